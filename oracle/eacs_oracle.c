@@ -1,0 +1,681 @@
+/*
+ * eacs_oracle.c -- CPU restatement of CST-SSM's EACS temporal hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker for the CUDA kernels in
+ * longvideo-main_b200/csrc: it is loaded by tests/, by __graft_entry__.smoke()
+ * and by bench.py's CPU-baseline / reference arm, never by the product path.
+ *
+ * Parity pin: every entry point below is checked against golden vectors made
+ * by running the reference's own PyTorch code (tests/golden/make_golden.py).
+ *
+ * Layouts (all row-major, complex = interleaved float pairs, i.e. complex64):
+ *   lam (H,N) complex, log_dt/D/mean/var (H), u (B,L,H), Bc/Cc (B,L,N) complex,
+ *   t (B,L), y (B,L,H), gate/resid (B,L), scan tensors (B,L,H,N) complex.
+ *
+ * Forward math is done in float with the reference's operation order (so the
+ * oracle reproduces the reference to a few ulp); the hand-derived backward of
+ * the gated cell is done in double.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+typedef struct { float re, im; } cf;
+typedef struct { double re, im; } cd;
+
+static inline cf cf_mul(cf a, cf b) {
+    cf r = {a.re * b.re - a.im * b.im, a.re * b.im + a.im * b.re};
+    return r;
+}
+static inline cf cf_add(cf a, cf b) { cf r = {a.re + b.re, a.im + b.im}; return r; }
+static inline cf cf_scale(cf a, float s) { cf r = {a.re * s, a.im * s}; return r; }
+
+/* 1/lam = conj(lam)/|lam|^2 (torch.reciprocal on complex64). */
+static inline cf cf_recip(cf z) {
+    float d = z.re * z.re + z.im * z.im;
+    cf r = {z.re / d, -z.im / d};
+    return r;
+}
+
+static inline cd cd_mul(cd a, cd b) {
+    cd r = {a.re * b.re - a.im * b.im, a.re * b.im + a.im * b.re};
+    return r;
+}
+static inline cd cd_conj(cd a) { cd r = {a.re, -a.im}; return r; }
+static inline cd cd_add(cd a, cd b) { cd r = {a.re + b.re, a.im + b.im}; return r; }
+static inline cd cd_sub(cd a, cd b) { cd r = {a.re - b.re, a.im - b.im}; return r; }
+static inline cd cd_scale(cd a, double s) { cd r = {a.re * s, a.im * s}; return r; }
+static inline cd cd_of(const float* p) { cd r = {p[0], p[1]}; return r; }
+static inline double cd_redot(cd a, cd b) { return a.re * b.re + a.im * b.im; } /* Re(conj(a) b) */
+
+static int g_threads = 0;
+void eacs_oracle_set_threads(int n) { g_threads = n; }
+static int nthreads(void) {
+#ifdef _OPENMP
+    return g_threads > 0 ? g_threads : omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+/* ZOH kernels, discretization.py:20-36 (zoh_kernels): z = lam*dt,
+ * dA = (expm1(a)+1)(cos b, sin b), E = complex_expm1(z), dB_bar = E * inv_lam. */
+static inline void zoh_f(cf lam, cf ilam, float dte, cf* dA, cf* dBbar) {
+    float a = lam.re * dte, b = lam.im * dte;
+    float em1 = expm1f(a);
+    float ea = em1 + 1.0f;
+    float sb = sinf(b), cb = cosf(b);
+    float im = ea * sb;
+    dA->re = ea * cb;
+    dA->im = im;
+    float sh = sinf(0.5f * b);
+    cf E = {em1 * cb - 2.0f * (sh * sh), im};
+    *dBbar = cf_mul(E, ilam);
+}
+
+/* effective_dt, discretization.py:63-82: clamp(dt*exp(log_dt), dt_min, dt_max). */
+static inline float eff_dt(float delta, float scale, float dt_min, float dt_max) {
+    float v = delta * scale;
+    if (v < dt_min) v = dt_min;
+    if (v > dt_max) v = dt_max;
+    return v;
+}
+
+/* ---------------------------------------------------------------------------
+ * scan_fwd: h_l = a_l * h_{l-1} + b_l (scan.py:36-44 sequential_scan_diag;
+ * eacs_scan_cuda.cu:23-38).  a, b, h: (B,L,H,N) complex.
+ * ------------------------------------------------------------------------- */
+int eacs_oracle_scan_fwd(const float* a, const float* b, float* h,
+                         int64_t B, int64_t L, int64_t H, int64_t N) {
+    int64_t C = H * N;
+#pragma omp parallel for num_threads(nthreads()) collapse(2)
+    for (int64_t bi = 0; bi < B; ++bi)
+        for (int64_t c = 0; c < C; ++c) {
+            cf s = {0.f, 0.f};
+            for (int64_t l = 0; l < L; ++l) {
+                int64_t o = ((bi * L + l) * C + c) * 2;
+                cf av = {a[o], a[o + 1]}, bv = {b[o], b[o + 1]};
+                s = cf_add(cf_mul(av, s), bv);
+                h[o] = s.re;
+                h[o + 1] = s.im;
+            }
+        }
+    return 0;
+}
+
+/* scan_bwd: reverse adjoint of the scan (eacs_scan_cuda.cu:40-60):
+ * s_l = g_l + conj(a_{l+1}) s_{l+1}; grad_b_l = s_l; grad_a_l = s_l conj(h_{l-1}). */
+int eacs_oracle_scan_bwd(const float* a, const float* h, const float* gh,
+                         float* ga, float* gb,
+                         int64_t B, int64_t L, int64_t H, int64_t N) {
+    int64_t C = H * N;
+#pragma omp parallel for num_threads(nthreads()) collapse(2)
+    for (int64_t bi = 0; bi < B; ++bi)
+        for (int64_t c = 0; c < C; ++c) {
+            cf s = {0.f, 0.f};
+            for (int64_t l = L - 1; l >= 0; --l) {
+                int64_t o = ((bi * L + l) * C + c) * 2;
+                s.re += gh[o];
+                s.im += gh[o + 1];
+                gb[o] = s.re;
+                gb[o + 1] = s.im;
+                cf hp = {0.f, 0.f};
+                if (l > 0) { hp.re = h[o - 2 * C]; hp.im = -h[o - 2 * C + 1]; }
+                cf g = cf_mul(s, hp);
+                ga[o] = g.re;
+                ga[o + 1] = g.im;
+                cf ac = {a[o], -a[o + 1]};
+                s = cf_mul(ac, s);
+            }
+        }
+    return 0;
+}
+
+/* ---------------------------------------------------------------------------
+ * Ungated continuous SSM core, continuous_ssm.py:44-55:
+ *   dt_l = max(t_l - t_{l-1}, 0) (dt_0 = dt_1), dt_eff = clamp(dt e^{log_dt}),
+ *   h_l = dA h_{l-1} + (dB_bar B_l) u_l,  y = Re sum_n C_l h_l + D u.
+ * ------------------------------------------------------------------------- */
+int eacs_oracle_ssm_fwd(const float* lam, const float* log_dt, const float* t,
+                        const float* Bc, const float* Cc, const float* u,
+                        const float* D, float* y,
+                        int64_t B, int64_t L, int64_t H, int64_t N,
+                        float dt_min, float dt_max) {
+#pragma omp parallel for num_threads(nthreads()) collapse(2)
+    for (int64_t bi = 0; bi < B; ++bi)
+        for (int64_t hh = 0; hh < H; ++hh) {
+            float scale = expf(log_dt[hh]);
+            cf* st = (cf*)calloc((size_t)N, sizeof(cf));
+            for (int64_t l = 0; l < L; ++l) {
+                float dt;
+                if (L == 1) dt = 0.f;
+                else {
+                    int64_t l1 = l == 0 ? 1 : l;
+                    dt = t[bi * L + l1] - t[bi * L + l1 - 1];
+                    if (dt < 0.f) dt = 0.f;
+                }
+                float dte = eff_dt(dt, scale, dt_min, dt_max);
+                float ul = u[(bi * L + l) * H + hh];
+                float acc = 0.f;
+                for (int64_t n = 0; n < N; ++n) {
+                    cf lm = {lam[(hh * N + n) * 2], lam[(hh * N + n) * 2 + 1]};
+                    cf dA, dBb;
+                    zoh_f(lm, cf_recip(lm), dte, &dA, &dBb);
+                    const float* bp = Bc + ((bi * L + l) * N + n) * 2;
+                    cf dB = cf_mul(dBb, (cf){bp[0], bp[1]});
+                    cf dBu = cf_scale(dB, ul);
+                    st[n] = cf_add(cf_mul(dA, st[n]), dBu);
+                    const float* cp = Cc + ((bi * L + l) * N + n) * 2;
+                    acc += cp[0] * st[n].re - cp[1] * st[n].im;
+                }
+                y[(bi * L + l) * H + hh] = acc + D[hh] * ul;
+            }
+            free(st);
+        }
+    return 0;
+}
+
+/* ---------------------------------------------------------------------------
+ * Gated EACS cell, inference (eacs.py:78-142 eacs_step with skip_compute and
+ * eacs.py:145-173 scan_range, including robust_guard).  Per batch row:
+ *   state (h_pi, t_pi, u_pi, B_pi, C_pi) initialised to (0, t_0-dt_init, u_0, B_0, C_0)
+ *   x_hat = dA h_pi + (dB_bar B_pi) u_pi,  y_hat = Re sum_n C_pi x_hat
+ *   r = ||(u-mu)/s - (y_hat-mu)/s|| / (||(u-mu)/s|| + eta),  gate = r > eps_l
+ *   commit: h_pi = dA h_pi + (dB_bar B_l) u_l, t/u/B/C_pi = current inputs
+ *   y = Re sum_n C_l h_cur + D u_l  (h_cur = committed update or x_hat)
+ * robust: eps_l = spike >= k ? eps*eps_factor : eps; spike counts consecutive
+ *   steps with r_l > r_{l-1}*spike_ratio.
+ * gate_mode: 0 = hard gate (inference / STE forward values), 1 = soft gate
+ *   sigmoid((r-eps)/max(T,1e-4)) blended into the state (eacs_cell_train.py:47-63).
+ * Outputs y (B,L,H), gate, resid (B,L).
+ * ------------------------------------------------------------------------- */
+static void cell_row(const float* lam, const float* log_dt, const float* u,
+                     const float* Bc, const float* Cc, const float* t,
+                     const float* D, const float* mean, const float* var,
+                     float eps, float eta, float var_eps, float dt_init,
+                     float dt_min, float dt_max, int robust, int robust_k,
+                     float spike_ratio, float eps_factor, int gate_mode, float T,
+                     int train_exp, float* y, float* gate, float* resid,
+                     int64_t L, int64_t H, int64_t N) {
+    cf* hpi = (cf*)calloc((size_t)(H * N), sizeof(cf));
+    cf* dA = (cf*)malloc(sizeof(cf) * (size_t)(H * N));
+    cf* dBb = (cf*)malloc(sizeof(cf) * (size_t)(H * N));
+    cf* xh = (cf*)malloc(sizeof(cf) * (size_t)(H * N));
+    cf* ilam = (cf*)malloc(sizeof(cf) * (size_t)(H * N));
+    float* upi = (float*)malloc(sizeof(float) * (size_t)H);
+    float* scale = (float*)malloc(sizeof(float) * (size_t)H);
+    float* sd = (float*)malloc(sizeof(float) * (size_t)H);
+    cf* Bpi = (cf*)malloc(sizeof(cf) * (size_t)N);
+    cf* Cpi = (cf*)malloc(sizeof(cf) * (size_t)N);
+    for (int64_t i = 0; i < H * N; ++i) {
+        cf lm = {lam[2 * i], lam[2 * i + 1]};
+        ilam[i] = cf_recip(lm);
+    }
+    for (int64_t hh = 0; hh < H; ++hh) {
+        scale[hh] = expf(log_dt[hh]);
+        sd[hh] = sqrtf(var[hh] + var_eps);
+        upi[hh] = u[hh];
+    }
+    for (int64_t n = 0; n < N; ++n) {
+        Bpi[n] = (cf){Bc[2 * n], Bc[2 * n + 1]};
+        Cpi[n] = (cf){Cc[2 * n], Cc[2 * n + 1]};
+    }
+    float tpi = t[0] - dt_init;
+    float spike = 0.f, prev_r = 0.f;
+    float eps_lo = eps * eps_factor;
+    float Tp = T > 1e-4f ? T : 1e-4f;
+    for (int64_t l = 0; l < L; ++l) {
+        float tl = t[l];
+        float delta = tl - tpi;
+        if (delta < 0.f) delta = 0.f;
+        double sdiff = 0.0, sobs = 0.0;
+        for (int64_t hh = 0; hh < H; ++hh) {
+            float dte = eff_dt(delta, scale[hh], dt_min, dt_max);
+            float yhat = 0.f;
+            for (int64_t n = 0; n < N; ++n) {
+                int64_t i = hh * N + n;
+                cf lm = {lam[2 * i], lam[2 * i + 1]};
+                if (train_exp) {
+                    /* eacs_cell_train.py:32-36: dA = exp(z), dB_bar = complex_expm1(z)/lam */
+                    float a = lm.re * dte, b = lm.im * dte;
+                    float e = expf(a);
+                    dA[i] = (cf){e * cosf(b), e * sinf(b)};
+                    float em1 = expm1f(a);
+                    float sb = sinf(b), cb = cosf(b);
+                    float sh = sinf(0.5f * b);
+                    cf E = {em1 * cb - 2.0f * (sh * sh), (em1 + 1.0f) * sb};
+                    dBb[i] = cf_mul(E, ilam[i]);
+                } else {
+                    zoh_f(lm, ilam[i], dte, &dA[i], &dBb[i]);
+                }
+                cf hf = cf_mul(dA[i], hpi[i]);
+                cf q = cf_mul(dBb[i], Bpi[n]);
+                xh[i] = cf_add(hf, cf_scale(q, upi[hh]));
+                yhat += Cpi[n].re * xh[i].re - Cpi[n].im * xh[i].im;
+            }
+            float ul = u[l * H + hh];
+            float obs = (ul - mean[hh]) / sd[hh];
+            float pred = (yhat - mean[hh]) / sd[hh];
+            float d = obs - pred;
+            sdiff += (double)d * d;
+            sobs += (double)obs * obs;
+        }
+        float r = sqrtf((float)sdiff) / (sqrtf((float)sobs) + eta);
+        float eps_l = eps;
+        if (robust) eps_l = (spike >= (float)robust_k) ? eps_lo : eps;
+        float g;
+        if (gate_mode == 1) g = 1.0f / (1.0f + expf(-((r - eps_l) / Tp)));
+        else g = (r > eps_l) ? 1.0f : 0.0f;
+        gate[l] = g;
+        resid[l] = r;
+        const float* Bl = Bc + l * N * 2;
+        const float* Cl = Cc + l * N * 2;
+        for (int64_t hh = 0; hh < H; ++hh) {
+            float ul = u[l * H + hh];
+            float acc = 0.f;
+            for (int64_t n = 0; n < N; ++n) {
+                int64_t i = hh * N + n;
+                cf hcur;
+                if (gate_mode == 1 || g > 0.5f) {
+                    cf hf = cf_mul(dA[i], hpi[i]);
+                    cf q = cf_mul(dBb[i], (cf){Bl[2 * n], Bl[2 * n + 1]});
+                    cf hu = cf_add(hf, cf_scale(q, ul));
+                    if (gate_mode == 1) {
+                        cf a1 = cf_scale(hu, g);
+                        hcur = cf_add(a1, cf_scale(xh[i], 1.0f - g));
+                        hpi[i] = cf_add(a1, cf_scale(hpi[i], 1.0f - g));
+                    } else {
+                        hcur = hu;
+                        hpi[i] = hu;
+                    }
+                } else {
+                    hcur = xh[i];
+                }
+                acc += Cl[2 * n] * hcur.re - Cl[2 * n + 1] * hcur.im;
+            }
+            y[l * H + hh] = acc + D[hh] * ul;
+        }
+        if (gate_mode == 1) {
+            for (int64_t hh = 0; hh < H; ++hh) upi[hh] = g * u[l * H + hh] + (1.0f - g) * upi[hh];
+            for (int64_t n = 0; n < N; ++n) {
+                Bpi[n].re = g * Bl[2 * n] + (1.0f - g) * Bpi[n].re;
+                Bpi[n].im = g * Bl[2 * n + 1] + (1.0f - g) * Bpi[n].im;
+                Cpi[n].re = g * Cl[2 * n] + (1.0f - g) * Cpi[n].re;
+                Cpi[n].im = g * Cl[2 * n + 1] + (1.0f - g) * Cpi[n].im;
+            }
+            tpi = g * tl + (1.0f - g) * tpi;
+        } else if (g > 0.5f) {
+            for (int64_t hh = 0; hh < H; ++hh) upi[hh] = u[l * H + hh];
+            for (int64_t n = 0; n < N; ++n) {
+                Bpi[n] = (cf){Bl[2 * n], Bl[2 * n + 1]};
+                Cpi[n] = (cf){Cl[2 * n], Cl[2 * n + 1]};
+            }
+            tpi = tl;
+        }
+        if (robust) {
+            if (l > 0) spike = (r > prev_r * spike_ratio) ? spike + 1.0f : 0.0f;
+            prev_r = r;
+        }
+    }
+    free(hpi); free(dA); free(dBb); free(xh); free(ilam); free(upi);
+    free(scale); free(sd); free(Bpi); free(Cpi);
+}
+
+int eacs_oracle_cell_fwd(const float* lam, const float* log_dt, const float* u,
+                         const float* Bc, const float* Cc, const float* t,
+                         const float* D, const float* mean, const float* var,
+                         float eps, float eta, float var_eps, float dt_init,
+                         float dt_min, float dt_max, int robust, int robust_k,
+                         float spike_ratio, float eps_factor, int gate_mode, float T,
+                         int train_exp, float* y, float* gate, float* resid,
+                         int64_t B, int64_t L, int64_t H, int64_t N) {
+#pragma omp parallel for num_threads(nthreads()) schedule(dynamic, 1)
+    for (int64_t bi = 0; bi < B; ++bi)
+        cell_row(lam, log_dt, u + bi * L * H, Bc + bi * L * N * 2, Cc + bi * L * N * 2,
+                 t + bi * L, D, mean, var, eps, eta, var_eps, dt_init, dt_min, dt_max,
+                 robust, robust_k, spike_ratio, eps_factor, gate_mode, T, train_exp,
+                 y + bi * L * H, gate + bi * L, resid + bi * L, L, H, N);
+    return 0;
+}
+
+/* ---------------------------------------------------------------------------
+ * Backward of GatedEACSCellFunction (eacs_cell_train.py:117-175): the VJP of
+ * _step_functional (eacs_cell_train.py:15-66) chained in reverse over L,
+ * derived by hand and evaluated in double.  Hard gates are pinned to the
+ * forward's gates for gate_mode 0 (STE); gate_mode 1 is the soft gate.
+ * Inputs: forward inputs, forward gates gs (B,L), upstream gy (B,L,H),
+ *   ggs, grs, gns (B,L) (any may be NULL = zero).
+ * Outputs (float, overwritten): du (B,L,H), dBc, dCc (B,L,N) complex, dt (B,L),
+ *   dlam (H,N) complex, dlog (H), dD (H), deps (1).
+ * ------------------------------------------------------------------------- */
+typedef struct {
+    double tpi, *upi;
+    cd *hpi, *Bpi, *Cpi;
+} dstate;
+
+int eacs_oracle_cell_bwd(const float* lam, const float* log_dt, const float* u,
+                         const float* Bc, const float* Cc, const float* t,
+                         const float* D, const float* mean, const float* var,
+                         float eps, float eta, float var_eps, float dt_init,
+                         float dt_max, float T, int gate_mode, const float* gs,
+                         const float* gy, const float* ggs, const float* grs,
+                         const float* gns, float* du, float* dBc, float* dCc,
+                         float* dt, float* dlam, float* dlog, float* dD, float* deps,
+                         int64_t B, int64_t L, int64_t H, int64_t N) {
+    const double dt_min = 1e-3;
+    const double Tp = T > 1e-4f ? (double)T : 1e-4;
+    int64_t HN = H * N;
+    double* acc_lam = (double*)calloc((size_t)(B * HN * 2), sizeof(double));
+    double* acc_log = (double*)calloc((size_t)(B * H), sizeof(double));
+    double* acc_D = (double*)calloc((size_t)(B * H), sizeof(double));
+    double* acc_eps = (double*)calloc((size_t)B, sizeof(double));
+
+#pragma omp parallel for num_threads(nthreads()) schedule(dynamic, 1)
+    for (int64_t bi = 0; bi < B; ++bi) {
+        const float* ub = u + bi * L * H;
+        const float* Bb = Bc + bi * L * N * 2;
+        const float* Cb = Cc + bi * L * N * 2;
+        const float* tb = t + bi * L;
+        /* Forward recompute of all states (double). */
+        dstate* st = (dstate*)malloc(sizeof(dstate) * (size_t)(L + 1));
+        for (int64_t l = 0; l <= L; ++l) {
+            st[l].upi = (double*)malloc(sizeof(double) * (size_t)H);
+            st[l].hpi = (cd*)malloc(sizeof(cd) * (size_t)HN);
+            st[l].Bpi = (cd*)malloc(sizeof(cd) * (size_t)N);
+            st[l].Cpi = (cd*)malloc(sizeof(cd) * (size_t)N);
+        }
+        st[0].tpi = (double)(tb[0] - dt_init);
+        for (int64_t hh = 0; hh < H; ++hh) st[0].upi[hh] = ub[hh];
+        for (int64_t i = 0; i < HN; ++i) st[0].hpi[i] = (cd){0, 0};
+        for (int64_t n = 0; n < N; ++n) {
+            st[0].Bpi[n] = cd_of(Bb + 2 * n);
+            st[0].Cpi[n] = cd_of(Cb + 2 * n);
+        }
+        cd* ilam = (cd*)malloc(sizeof(cd) * (size_t)HN);
+        for (int64_t i = 0; i < HN; ++i) {
+            double a = lam[2 * i], b = lam[2 * i + 1], d = a * a + b * b;
+            ilam[i] = (cd){a / d, -b / d};
+        }
+        double* sdv = (double*)malloc(sizeof(double) * (size_t)H);
+        double* sc = (double*)malloc(sizeof(double) * (size_t)H);
+        for (int64_t hh = 0; hh < H; ++hh) {
+            sdv[hh] = sqrt((double)var[hh] + (double)var_eps);
+            sc[hh] = exp((double)log_dt[hh]);
+        }
+        /* per-step scratch */
+        cd* dA = (cd*)malloc(sizeof(cd) * (size_t)HN);
+        cd* E = (cd*)malloc(sizeof(cd) * (size_t)HN);
+        cd* dB = (cd*)malloc(sizeof(cd) * (size_t)HN);
+        cd* hf = (cd*)malloc(sizeof(cd) * (size_t)HN);
+        cd* xh = (cd*)malloc(sizeof(cd) * (size_t)HN);
+        cd* hu = (cd*)malloc(sizeof(cd) * (size_t)HN);
+        cd* hcur = (cd*)malloc(sizeof(cd) * (size_t)HN);
+        double* dte = (double*)malloc(sizeof(double) * (size_t)H);
+        double* dte_raw = (double*)malloc(sizeof(double) * (size_t)H);
+        double* obs = (double*)malloc(sizeof(double) * (size_t)H);
+        double* dv = (double*)malloc(sizeof(double) * (size_t)H);
+
+        /* step function: fills per-step arrays for step l from state st[l]; returns
+         * r pieces through pointers; if adv, writes st[l+1]. */
+#define STEP_FWD(l, adv)                                                              \
+        do {                                                                          \
+            dstate* S = &st[l];                                                       \
+            double tl = tb[l];                                                        \
+            draw = tl - S->tpi;                                                       \
+            delta = draw > 0 ? draw : 0;                                              \
+            for (int64_t hh = 0; hh < H; ++hh) {                                      \
+                dte_raw[hh] = delta * sc[hh];                                         \
+                double v = dte_raw[hh];                                               \
+                if (v < dt_min) v = dt_min;                                           \
+                if (v > dt_max) v = dt_max;                                           \
+                dte[hh] = v;                                                          \
+            }                                                                         \
+            sdiff = 0; sobs = 0;                                                      \
+            for (int64_t hh = 0; hh < H; ++hh) {                                      \
+                double yh = 0;                                                        \
+                for (int64_t n = 0; n < N; ++n) {                                     \
+                    int64_t i = hh * N + n;                                           \
+                    double a = lam[2 * i] * dte[hh], b = lam[2 * i + 1] * dte[hh];    \
+                    double e = exp(a);                                                \
+                    dA[i] = (cd){e * cos(b), e * sin(b)};                             \
+                    E[i] = (cd){expm1(a) * cos(b) - 2 * sin(0.5 * b) * sin(0.5 * b),  \
+                                e * sin(b)};                                          \
+                    dB[i] = cd_mul(E[i], ilam[i]);                                    \
+                    hf[i] = cd_mul(dA[i], S->hpi[i]);                                 \
+                    xh[i] = cd_add(hf[i], cd_scale(cd_mul(dB[i], S->Bpi[n]), S->upi[hh])); \
+                    yh += S->Cpi[n].re * xh[i].re - S->Cpi[n].im * xh[i].im;          \
+                }                                                                     \
+                double ul = ub[l * H + hh];                                           \
+                obs[hh] = (ul - mean[hh]) / sdv[hh];                                  \
+                double pred = (yh - mean[hh]) / sdv[hh];                              \
+                dv[hh] = obs[hh] - pred;                                              \
+                sdiff += dv[hh] * dv[hh];                                             \
+                sobs += obs[hh] * obs[hh];                                            \
+            }                                                                         \
+            num = sqrt(sdiff); nobs = sqrt(sobs); den = nobs + eta;                   \
+            r = num / den;                                                            \
+            soft = 1.0 / (1.0 + exp(-((r - (double)eps) / Tp)));                      \
+            g = gate_mode == 1 ? soft : (double)gs[bi * L + l];                       \
+            for (int64_t hh = 0; hh < H; ++hh) {                                      \
+                double ul = ub[l * H + hh];                                           \
+                for (int64_t n = 0; n < N; ++n) {                                     \
+                    int64_t i = hh * N + n;                                           \
+                    hu[i] = cd_add(hf[i], cd_scale(cd_mul(dB[i], cd_of(Bb + 2 * (l * N + n))), ul)); \
+                    hcur[i] = cd_add(cd_scale(hu[i], g), cd_scale(xh[i], 1 - g));    \
+                }                                                                     \
+            }                                                                         \
+            if (adv) {                                                                \
+                dstate* S2 = &st[l + 1];                                              \
+                S2->tpi = g * tl + (1 - g) * S->tpi;                                  \
+                for (int64_t hh = 0; hh < H; ++hh)                                    \
+                    S2->upi[hh] = g * ub[l * H + hh] + (1 - g) * S->upi[hh];          \
+                for (int64_t i = 0; i < HN; ++i)                                      \
+                    S2->hpi[i] = cd_add(cd_scale(hu[i], g), cd_scale(S->hpi[i], 1 - g)); \
+                for (int64_t n = 0; n < N; ++n) {                                     \
+                    S2->Bpi[n] = cd_add(cd_scale(cd_of(Bb + 2 * (l * N + n)), g), cd_scale(S->Bpi[n], 1 - g)); \
+                    S2->Cpi[n] = cd_add(cd_scale(cd_of(Cb + 2 * (l * N + n)), g), cd_scale(S->Cpi[n], 1 - g)); \
+                }                                                                     \
+            }                                                                         \
+        } while (0)
+
+        double draw, delta, sdiff, sobs, num, nobs, den, r, soft, g;
+        for (int64_t l = 0; l < L; ++l) STEP_FWD(l, 1);
+
+        /* Adjoints of the carried state (state after step l). */
+        cd* ah = (cd*)calloc((size_t)HN, sizeof(cd));
+        double at = 0;
+        double* au = (double*)calloc((size_t)H, sizeof(double));
+        cd* aB = (cd*)calloc((size_t)N, sizeof(cd));
+        cd* aC = (cd*)calloc((size_t)N, sizeof(cd));
+        cd* ahn = (cd*)malloc(sizeof(cd) * (size_t)HN);
+        double* aun = (double*)malloc(sizeof(double) * (size_t)H);
+        cd* aBn = (cd*)malloc(sizeof(cd) * (size_t)N);
+        cd* aCn = (cd*)malloc(sizeof(cd) * (size_t)N);
+        double* dul = (double*)malloc(sizeof(double) * (size_t)H);
+        cd* dBl = (cd*)malloc(sizeof(cd) * (size_t)N);
+        cd* dCl = (cd*)malloc(sizeof(cd) * (size_t)N);
+        double* dtl = (double*)calloc((size_t)L, sizeof(double));
+        double* dub = (double*)calloc((size_t)(L * H), sizeof(double));
+        cd* dBb = (cd*)calloc((size_t)(L * N), sizeof(cd));
+        cd* dCb = (cd*)calloc((size_t)(L * N), sizeof(cd));
+        double* alam = acc_lam + bi * HN * 2;
+        double* alog = acc_log + bi * H;
+        double* aD = acc_D + bi * H;
+
+        for (int64_t l = L - 1; l >= 0; --l) {
+            STEP_FWD(l, 0);
+            dstate* S = &st[l];
+            double tl = tb[l];
+            double gyl_any = gy != NULL;
+            double gbar = ggs ? ggs[bi * L + l] : 0.0;
+            double rbar = grs ? grs[bi * L + l] : 0.0;
+            double nbar = gns ? gns[bi * L + l] : 0.0;
+            for (int64_t hh = 0; hh < H; ++hh) dul[hh] = 0;
+            for (int64_t n = 0; n < N; ++n) { dBl[n] = (cd){0, 0}; dCl[n] = (cd){0, 0}; }
+            /* y = Re sum C_l hcur + D u_l */
+            for (int64_t hh = 0; hh < H; ++hh) {
+                double yb = gyl_any ? gy[(bi * L + l) * H + hh] : 0.0;
+                double ul = ub[l * H + hh];
+                aD[hh] += yb * ul;
+                dul[hh] += yb * D[hh];
+            }
+            /* blends and the gate adjoint */
+            for (int64_t hh = 0; hh < H; ++hh) {
+                double yb = gyl_any ? gy[(bi * L + l) * H + hh] : 0.0;
+                for (int64_t n = 0; n < N; ++n) {
+                    int64_t i = hh * N + n;
+                    cd Cl = cd_of(Cb + 2 * (l * N + n));
+                    cd ahc = cd_scale(cd_conj(Cl), yb);
+                    /* dC_l += yb * conj(hcur) */
+                    dCl[n] = cd_add(dCl[n], cd_scale(cd_conj(hcur[i]), yb));
+                    gbar += cd_redot(ahc, cd_sub(hu[i], xh[i]));
+                    gbar += cd_redot(ah[i], cd_sub(hu[i], S->hpi[i]));
+                    /* store ahcur in hcur slot for later use */
+                    hcur[i] = ahc;
+                }
+            }
+            gbar += at * (tl - S->tpi);
+            for (int64_t hh = 0; hh < H; ++hh) gbar += au[hh] * (ub[l * H + hh] - S->upi[hh]);
+            for (int64_t n = 0; n < N; ++n) {
+                gbar += cd_redot(aB[n], cd_sub(cd_of(Bb + 2 * (l * N + n)), S->Bpi[n]));
+                gbar += cd_redot(aC[n], cd_sub(cd_of(Cb + 2 * (l * N + n)), S->Cpi[n]));
+            }
+            double dtl_l = g * at;
+            double atn = (1 - g) * at;
+            for (int64_t hh = 0; hh < H; ++hh) { dul[hh] += g * au[hh]; aun[hh] = (1 - g) * au[hh]; }
+            for (int64_t n = 0; n < N; ++n) {
+                dBl[n] = cd_add(dBl[n], cd_scale(aB[n], g));
+                aBn[n] = cd_scale(aB[n], 1 - g);
+                dCl[n] = cd_add(dCl[n], cd_scale(aC[n], g));
+                aCn[n] = cd_scale(aC[n], 1 - g);
+            }
+            /* gate -> soft -> r, eps */
+            double xbar = gbar * soft * (1 - soft);
+            rbar += xbar / Tp;
+            acc_eps[bi] += -xbar / Tp;
+            double numbar = rbar / den;
+            double denbar = -rbar * num / (den * den);
+            double numtbar = nbar / den;
+            for (int64_t hh = 0; hh < H; ++hh) {
+                double dbar = num > 0 ? numbar * dv[hh] / num : 0.0;
+                double obar = dbar + (nobs > 0 ? denbar * obs[hh] / nobs : 0.0);
+                double pbar = -dbar - (num > 0 ? numtbar * dv[hh] / num : 0.0);
+                dul[hh] += obar / sdv[hh];
+                obs[hh] = pbar / sdv[hh]; /* reuse as yhat_bar */
+            }
+            double deltabar = 0;
+            for (int64_t hh = 0; hh < H; ++hh) {
+                double ul = ub[l * H + hh];
+                double yhb = obs[hh];
+                double dtebar = 0;
+                for (int64_t n = 0; n < N; ++n) {
+                    int64_t i = hh * N + n;
+                    cd ahc = hcur[i];
+                    cd ahu = cd_add(cd_scale(ahc, g), cd_scale(ah[i], g));
+                    cd axh = cd_scale(ahc, 1 - g);
+                    cd ahp = cd_scale(ah[i], 1 - g);
+                    /* yhat = Re sum C_pi xhat */
+                    axh = cd_add(axh, cd_scale(cd_conj(S->Cpi[n]), yhb));
+                    aCn[n] = cd_add(aCn[n], cd_scale(cd_conj(xh[i]), yhb));
+                    /* xhat = hf + (dB B_pi) u_pi ; hupd = hf + (dB B_l) u_l */
+                    cd ahf = cd_add(axh, ahu);
+                    cd Bl = cd_of(Bb + 2 * (l * N + n));
+                    cd qpi = cd_mul(dB[i], S->Bpi[n]);
+                    cd ql = cd_mul(dB[i], Bl);
+                    cd aqpi = cd_scale(axh, S->upi[hh]);
+                    cd aql = cd_scale(ahu, ul);
+                    aun[hh] += cd_redot(axh, qpi);
+                    dul[hh] += cd_redot(ahu, ql);
+                    cd adB = cd_add(cd_mul(aqpi, cd_conj(S->Bpi[n])), cd_mul(aql, cd_conj(Bl)));
+                    aBn[n] = cd_add(aBn[n], cd_mul(cd_conj(dB[i]), aqpi));
+                    dBl[n] = cd_add(dBl[n], cd_mul(cd_conj(dB[i]), aql));
+                    /* hf = dA h_pi */
+                    ahp = cd_add(ahp, cd_mul(cd_conj(dA[i]), ahf));
+                    cd adA = cd_mul(cd_conj(S->hpi[i]), ahf);
+                    /* dB = E * ilam */
+                    cd aE = cd_mul(adB, cd_conj(ilam[i]));
+                    cd ail = cd_mul(adB, cd_conj(E[i]));
+                    cd il2 = cd_mul(ilam[i], ilam[i]);
+                    cd alm = cd_scale(cd_mul(cd_conj(il2), ail), -1.0);
+                    /* dA = exp(z), E = expm1(z): dz = conj(exp z)(adA + aE) */
+                    cd az = cd_mul(cd_conj(dA[i]), cd_add(adA, aE));
+                    alm = cd_add(alm, cd_scale(az, dte[hh]));
+                    cd lm = {lam[2 * i], lam[2 * i + 1]};
+                    dtebar += cd_redot(az, lm);
+                    alam[2 * i] += alm.re;
+                    alam[2 * i + 1] += alm.im;
+                    ahn[i] = ahp;
+                }
+                double m = (dte_raw[hh] >= dt_min && dte_raw[hh] <= (double)dt_max) ? 1.0 : 0.0;
+                double drb = m * dtebar;
+                deltabar += drb * sc[hh];
+                alog[hh] += drb * delta * sc[hh];
+            }
+            double mdel = draw >= 0 ? 1.0 : 0.0;
+            dtl_l += mdel * deltabar;
+            atn += -mdel * deltabar;
+            dtl[l] += dtl_l;
+            for (int64_t hh = 0; hh < H; ++hh) dub[l * H + hh] += dul[hh];
+            for (int64_t n = 0; n < N; ++n) {
+                dBb[l * N + n] = cd_add(dBb[l * N + n], dBl[n]);
+                dCb[l * N + n] = cd_add(dCb[l * N + n], dCl[n]);
+            }
+            /* roll adjoints */
+            cd* tmp = ah; ah = ahn; ahn = tmp;
+            at = atn;
+            double* tu = au; au = aun; aun = tu;
+            cd* tB = aB; aB = aBn; aBn = tB;
+            cd* tC = aC; aC = aCn; aCn = tC;
+        }
+        /* initial state: t_pi = t_0 - dt_init, u_pi = u_0, B_pi = B_0, C_pi = C_0 */
+        dtl[0] += at;
+        for (int64_t hh = 0; hh < H; ++hh) dub[hh] += au[hh];
+        for (int64_t n = 0; n < N; ++n) {
+            dBb[n] = cd_add(dBb[n], aB[n]);
+            dCb[n] = cd_add(dCb[n], aC[n]);
+        }
+        for (int64_t l = 0; l < L; ++l) {
+            dt[bi * L + l] = (float)dtl[l];
+            for (int64_t hh = 0; hh < H; ++hh) du[(bi * L + l) * H + hh] = (float)dub[l * H + hh];
+            for (int64_t n = 0; n < N; ++n) {
+                int64_t o = ((bi * L + l) * N + n) * 2;
+                dBc[o] = (float)dBb[l * N + n].re;
+                dBc[o + 1] = (float)dBb[l * N + n].im;
+                dCc[o] = (float)dCb[l * N + n].re;
+                dCc[o + 1] = (float)dCb[l * N + n].im;
+            }
+        }
+#undef STEP_FWD
+        for (int64_t l = 0; l <= L; ++l) {
+            free(st[l].upi); free(st[l].hpi); free(st[l].Bpi); free(st[l].Cpi);
+        }
+        free(st); free(ilam); free(sdv); free(sc); free(dA); free(E); free(dB); free(hf);
+        free(xh); free(hu); free(hcur); free(dte); free(dte_raw); free(obs); free(dv);
+        free(ah); free(au); free(aB); free(aC); free(ahn); free(aun);
+        free(aBn); free(aCn); free(dul); free(dBl); free(dCl); free(dtl); free(dub);
+        free(dBb); free(dCb);
+    }
+    /* deterministic cross-row reduction of the parameter gradients */
+    for (int64_t i = 0; i < HN * 2; ++i) {
+        double s = 0;
+        for (int64_t bi = 0; bi < B; ++bi) s += acc_lam[bi * HN * 2 + i];
+        dlam[i] = (float)s;
+    }
+    for (int64_t hh = 0; hh < H; ++hh) {
+        double s = 0, s2 = 0;
+        for (int64_t bi = 0; bi < B; ++bi) { s += acc_log[bi * H + hh]; s2 += acc_D[bi * H + hh]; }
+        dlog[hh] = (float)s;
+        dD[hh] = (float)s2;
+    }
+    double se = 0;
+    for (int64_t bi = 0; bi < B; ++bi) se += acc_eps[bi];
+    deps[0] = (float)se;
+    free(acc_lam); free(acc_log); free(acc_D); free(acc_eps);
+    return 0;
+}
+
+const char* eacs_oracle_version(void) { return "eacs-oracle 1"; }

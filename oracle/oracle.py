@@ -1,0 +1,173 @@
+"""ctypes binding of the CPU oracle (test infrastructure only).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference
+arm import this module; the product path never does.  All arrays are numpy,
+complex arrays are complex64 (interleaved float pairs), real arrays float32.
+Each function names the reference code it restates (paths inside the
+CST-SSM project, BitGao-ai/LongVideo-main).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libeacs_oracle.so")
+_lib = None
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_F = ctypes.c_float
+_I = ctypes.c_int
+
+
+def build() -> str:
+    """Compile eacs_oracle.c with the committed Makefile; returns the .so path."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.eacs_oracle_scan_fwd.argtypes = [_P, _P, _P, _I64, _I64, _I64, _I64]
+        L.eacs_oracle_scan_bwd.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64]
+        L.eacs_oracle_ssm_fwd.argtypes = [_P] * 8 + [_I64] * 4 + [_F, _F]
+        L.eacs_oracle_cell_fwd.argtypes = ([_P] * 9 + [_F] * 6 + [_I, _I, _F, _F, _I, _F, _I]
+                                           + [_P] * 3 + [_I64] * 4)
+        L.eacs_oracle_cell_bwd.argtypes = ([_P] * 9 + [_F] * 5 + [_F, _I] + [_P] * 5
+                                           + [_P] * 8 + [_I64] * 4)
+        L.eacs_oracle_set_threads.argtypes = [_I]
+        L.eacs_oracle_version.restype = ctypes.c_char_p
+        _lib = L
+    return _lib
+
+
+def set_threads(n: int) -> None:
+    """Number of OpenMP threads the oracle uses (0 = all available)."""
+    lib().eacs_oracle_set_threads(int(n))
+
+
+def _c(x, dtype):
+    return np.ascontiguousarray(np.asarray(x), dtype=dtype)
+
+
+def _ptr(x):
+    return None if x is None else x.ctypes.data_as(ctypes.c_void_p)
+
+
+def scan_fwd(a, b):
+    """sequential_scan_diag (cst_ssm/ops/scan.py:36-44): h_l = a_l h_{l-1} + b_l."""
+    a = _c(a, np.complex64)
+    b = _c(b, np.complex64)
+    B, L, H, N = a.shape
+    h = np.empty_like(a)
+    lib().eacs_oracle_scan_fwd(_ptr(a), _ptr(b), _ptr(h), B, L, H, N)
+    return h
+
+
+def scan_bwd(a, h, gh):
+    """Adjoint of the scan (cst_ssm/ops/csrc/eacs_scan_cuda.cu:40-60)."""
+    a = _c(a, np.complex64)
+    h = _c(h, np.complex64)
+    gh = _c(gh, np.complex64)
+    B, L, H, N = a.shape
+    ga = np.empty_like(a)
+    gb = np.empty_like(a)
+    lib().eacs_oracle_scan_bwd(_ptr(a), _ptr(h), _ptr(gh), _ptr(ga), _ptr(gb), B, L, H, N)
+    return ga, gb
+
+
+def ssm_fwd(lam, log_dt, t, Bc, Cc, u, D, dt_min=1e-3, dt_max=1e3):
+    """ContinuousSSMLayer core (cst_ssm/modules/continuous_ssm.py:44-55)."""
+    lam = _c(lam, np.complex64)
+    log_dt = _c(log_dt, np.float32)
+    t = _c(t, np.float32)
+    Bc = _c(Bc, np.complex64)
+    Cc = _c(Cc, np.complex64)
+    u = _c(u, np.float32)
+    D = _c(D, np.float32)
+    B, L, H = u.shape
+    N = lam.shape[1]
+    y = np.empty((B, L, H), np.float32)
+    lib().eacs_oracle_ssm_fwd(_ptr(lam), _ptr(log_dt), _ptr(t), _ptr(Bc), _ptr(Cc), _ptr(u),
+                              _ptr(D), _ptr(y), B, L, H, N, dt_min, dt_max)
+    return y
+
+
+def cell_fwd(lam, log_dt, u, Bc, Cc, t, D, mean, var, eps, eta, var_eps=1e-5,
+             dt_init=1.0, dt_min=1e-3, dt_max=1e3, robust=None, gate_mode=0, T=0.1,
+             train_exp=False):
+    """Gated EACS cell over L (cst_ssm/modules/eacs.py:78-173, scan_range).
+
+    robust: None or (k, spike_ratio, eps_factor) (eacs.py:67-71).
+    gate_mode 0: hard gate; 1: soft gate blended into the state
+    (cst_ssm/ops/eacs_cell_train.py:47-63).  train_exp selects the training
+    cell's dA = exp(z) (eacs_cell_train.py:33) instead of zoh_kernels' form.
+    Returns (y (B,L,H), gate (B,L), resid (B,L)).
+    """
+    lam = _c(lam, np.complex64)
+    u = _c(u, np.float32)
+    Bc = _c(Bc, np.complex64)
+    Cc = _c(Cc, np.complex64)
+    t = _c(t, np.float32)
+    log_dt = _c(log_dt, np.float32)
+    D = _c(D, np.float32)
+    mean = _c(mean, np.float32)
+    var = _c(var, np.float32)
+    B, L, H = u.shape
+    N = lam.shape[1]
+    y = np.empty((B, L, H), np.float32)
+    g = np.empty((B, L), np.float32)
+    r = np.empty((B, L), np.float32)
+    rk, rr, rf = (0, 2.0, 0.3) if robust is None else robust
+    lib().eacs_oracle_cell_fwd(_ptr(lam), _ptr(log_dt), _ptr(u), _ptr(Bc), _ptr(Cc), _ptr(t),
+                               _ptr(D), _ptr(mean), _ptr(var), eps, eta, var_eps, dt_init,
+                               dt_min, dt_max, 0 if robust is None else 1, int(rk), rr, rf,
+                               int(gate_mode), T, 1 if train_exp else 0,
+                               _ptr(y), _ptr(g), _ptr(r), B, L, H, N)
+    return y, g, r
+
+
+def cell_bwd(lam, log_dt, u, Bc, Cc, t, D, mean, var, eps, eta, var_eps, dt_init, dt_max,
+             T, gate_mode, gs, gy=None, ggs=None, grs=None, gns=None):
+    """Backward of GatedEACSCellFunction (cst_ssm/ops/eacs_cell_train.py:117-175).
+
+    Returns (du, dBc, dCc, dt, dlam, dlog_dt, dD, deps).
+    """
+    lam = _c(lam, np.complex64)
+    u = _c(u, np.float32)
+    Bc = _c(Bc, np.complex64)
+    Cc = _c(Cc, np.complex64)
+    t = _c(t, np.float32)
+    log_dt = _c(log_dt, np.float32)
+    D = _c(D, np.float32)
+    mean = _c(mean, np.float32)
+    var = _c(var, np.float32)
+    gs = _c(gs, np.float32)
+    gy = None if gy is None else _c(gy, np.float32)
+    ggs = None if ggs is None else _c(ggs, np.float32)
+    grs = None if grs is None else _c(grs, np.float32)
+    gns = None if gns is None else _c(gns, np.float32)
+    B, L, H = u.shape
+    N = lam.shape[1]
+    du = np.empty((B, L, H), np.float32)
+    dBc = np.empty((B, L, N), np.complex64)
+    dCc = np.empty((B, L, N), np.complex64)
+    dt = np.empty((B, L), np.float32)
+    dlam = np.empty((H, N), np.complex64)
+    dlog = np.empty((H,), np.float32)
+    dD = np.empty((H,), np.float32)
+    deps = np.empty((1,), np.float32)
+    lib().eacs_oracle_cell_bwd(_ptr(lam), _ptr(log_dt), _ptr(u), _ptr(Bc), _ptr(Cc), _ptr(t),
+                               _ptr(D), _ptr(mean), _ptr(var), eps, eta, var_eps, dt_init,
+                               dt_max, T, int(gate_mode), _ptr(gs), _ptr(gy), _ptr(ggs),
+                               _ptr(grs), _ptr(gns), _ptr(du), _ptr(dBc), _ptr(dCc), _ptr(dt),
+                               _ptr(dlam), _ptr(dlog), _ptr(dD), _ptr(deps), B, L, H, N)
+    return du, dBc, dCc, dt, dlam, dlog, dD, deps

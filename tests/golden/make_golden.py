@@ -1,0 +1,301 @@
+"""Generate golden vectors for the EACS hot path by running the reference.
+
+Runs the reference's own PyTorch implementation (CST-SSM, imported from a
+checkout given by --reference, default /root/reference) on small seeded inputs
+and writes the op-boundary inputs and outputs to tests/golden/*.npz.  The
+fixtures pin the CPU oracle (oracle/eacs_oracle.c) and the CUDA kernels; the
+tests that read them never import the reference.
+
+    python tests/golden/make_golden.py [--reference PATH]
+
+Reference functions exercised (paths inside the CST-SSM project):
+  ops/scan.py:36-44            sequential_scan_diag (+ autograd for the adjoint)
+  ops/discretization.py:20-82  zoh_kernels / zoh_discretize / effective_dt
+  modules/continuous_ssm.py:44-55  ungated layer core
+  modules/eacs.py:78-173       eacs_step / scan_range (+ RobustCfg)
+  ops/eacs_cell_train.py:81-199  GatedEACSCellFunction forward/backward
+"""
+from __future__ import annotations
+
+import argparse
+import math
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _np(x):
+    x = x.detach().cpu()
+    if x.is_complex():
+        return x.to(torch.complex64).numpy()
+    return x.to(torch.float32).numpy()
+
+
+def timestamps_exp(gen, B, L, mean=0.25, lo=1 / 30, hi=2.0):
+    """Cumulative dt with dt ~ Exponential(mean) clipped to [lo, hi]."""
+    dt = torch.empty(B, L).exponential_(1.0 / mean, generator=gen).clamp(lo, hi)
+    return torch.cumsum(dt, 1)
+
+
+def scan_cases(gen):
+    from cst_ssm.ops.scan import sequential_scan_diag, associative_scan_diag
+    out = {}
+    for name, (B, L, H, N) in {"scan_small": (2, 33, 5, 4), "scan_odd": (1, 7, 3, 3)}.items():
+        mag = torch.rand(B, L, H, N, generator=gen) * 0.3 + 0.69
+        ph = torch.rand(B, L, H, N, generator=gen) * 2 * math.pi
+        a = torch.polar(mag, ph).to(torch.complex64)
+        b = torch.complex(torch.randn(B, L, H, N, generator=gen),
+                          torch.randn(B, L, H, N, generator=gen))
+        gh = torch.complex(torch.randn(B, L, H, N, generator=gen),
+                           torch.randn(B, L, H, N, generator=gen))
+        a_ = a.clone().requires_grad_(True)
+        b_ = b.clone().requires_grad_(True)
+        h = sequential_scan_diag(a_, b_)
+        ga, gb = torch.autograd.grad(h, [a_, b_], gh)
+        h_assoc = associative_scan_diag(a, b)
+        out[name] = dict(a=_np(a), b=_np(b), h=_np(h), gh=_np(gh), ga=_np(ga), gb=_np(gb),
+                         h_assoc=_np(h_assoc))
+    return out
+
+
+def ssm_core(lam, log_dt, t, Bc, Cc, u, D):
+    """continuous_ssm.py:44-55 with the reference's own discretisation and scan."""
+    from cst_ssm.ops.discretization import effective_dt, zoh_discretize
+    from cst_ssm.ops.scan import sequential_scan_diag
+    dt = torch.zeros_like(t)
+    dt[:, 1:] = (t[:, 1:] - t[:, :-1]).clamp_min(0)
+    if t.shape[1] > 1:
+        dt[:, 0] = dt[:, 1]
+    dt_eff = effective_dt(dt.unsqueeze(-1), log_dt)
+    dA, dB = zoh_discretize(lam, dt_eff, Bc, inv_lam=torch.reciprocal(lam))
+    dBu = dB * u.unsqueeze(-1)
+    h = sequential_scan_diag(dA, dBu)
+    return torch.einsum("bln,blhn->blh", Cc, h).real + D * u
+
+
+def ssm_cases(gen):
+    from cst_ssm.ops.discretization import make_lambda
+    from cst_ssm.ops.spectral_init import BranchSpec, init_branch_lambda
+    out = {}
+    cases = {
+        # config 0: B=2, L=256, D=64 channels, N=16, tau log-uniform [0.5, 64] s.
+        "ssm_c0": (2, 256, 64, 16, 0.5, 64.0, False),
+        "ssm_odd": (3, 9, 7, 5, 0.1, 4.0, True),
+        "ssm_l1": (2, 1, 4, 4, 0.5, 4.0, False),
+    }
+    for name, (B, L, H, N, tmin, tmax, dup) in cases.items():
+        a_lnr, a_im = init_branch_lambda(BranchSpec(name, N, tmin, tmax), H, generator=gen)
+        lam = make_lambda(a_lnr, a_im).to(torch.complex64)
+        log_dt = torch.randn(H, generator=gen) * 0.3
+        t = timestamps_exp(gen, B, L)
+        if dup and L > 3:
+            t[:, 3] = t[:, 2]           # duplicate timestamp: dt = 0 -> dt_min clamp
+            t[0, 5] = t[0, 4] - 0.5     # decreasing timestamp: clamp_min(0)
+        s = 1.0 / math.sqrt(N)
+        Bc = torch.complex(torch.randn(B, L, N, generator=gen) * s,
+                           torch.randn(B, L, N, generator=gen) * s)
+        Cc = torch.complex(torch.randn(B, L, N, generator=gen) * s,
+                           torch.randn(B, L, N, generator=gen) * s)
+        u = torch.randn(B, L, H, generator=gen)
+        D = torch.randn(H, generator=gen)
+        y = ssm_core(lam, log_dt, t, Bc, Cc, u, D)
+        out[name] = dict(lam=_np(lam), log_dt=_np(log_dt), t=_np(t), Bc=_np(Bc), Cc=_np(Cc),
+                         u=_np(u), D=_np(D), y=_np(y))
+    return out
+
+
+def _layer_inputs(H, N, tmin, tmax, B, L, seed, dup_frames=False, ramp=False):
+    """Op-boundary tensors from the reference EACSLayer constructor (seeded)."""
+    from cst_ssm.modules.eacs import EACSLayer
+    from cst_ssm.modules.event_gate import EventGate
+    from cst_ssm.ops.spectral_init import BranchSpec
+    torch.manual_seed(seed)
+    layer = EACSLayer(H, BranchSpec("b", N, tmin, tmax), gate=EventGate(init_eps=0.12)).eval()
+    with torch.no_grad():
+        layer.log_dt_scale.normal_(0.0, 0.2)
+        layer.D.normal_(0.0, 1.0)
+        layer.obs_norm.running_mean.normal_(0.0, 0.1)
+        layer.obs_norm.running_var.uniform_(0.5, 1.5)
+    x = torch.randn(B, L, H)
+    if dup_frames:
+        # ablation_pareto.py-style duplicated frames: runs of identical features
+        for l in range(1, L):
+            if (l // 3) % 2 == 1:
+                x[:, l] = x[:, l - 1]
+    t = timestamps_exp(torch.Generator().manual_seed(seed + 1), B, L)
+    with torch.no_grad():
+        u, Bc, Cc = layer._project(layer.norm(x))
+        if ramp:
+            # Residual spikes for robust_guard: with a large running mean the
+            # residual scales with |u - y_hat|, so observations that grow
+            # geometrically over runs of 6 frames make r double step after step.
+            layer.obs_norm.running_mean.fill_(20.0)
+            v = torch.randn(B, 1, H)
+            k = (torch.arange(L) % 6).view(1, L, 1).float()
+            u = v * 0.05 * (2.6 ** k) + 0.01 * torch.randn(B, L, H)
+    return layer, u, Bc, Cc, t
+
+
+def _run_scan_range(layer, u, Bc, Cc, t, eps=None, robust=None):
+    from cst_ssm.modules.eacs import scan_range
+    lam = layer.lam().to(torch.complex64)
+    p = layer.step_params(lam)
+    if eps is not None:
+        p.eps = torch.tensor(float(eps))
+    state = (torch.zeros(u.shape[0], layer.H, layer.N, dtype=torch.complex64),
+             t[:, 0] - layer.dt_init, u[:, 0], Bc[:, 0], Cc[:, 0])
+    with torch.no_grad():
+        ys, gs, rs, ns, _ = scan_range(p, state, u, Bc, Cc, t, 0, u.shape[1],
+                                       robust=robust, skip_compute=robust is None)
+    return ys, gs, rs
+
+
+def _spike_hits(rs, robust):
+    """Number of steps whose threshold robust_guard lowered (eacs.py:155-170)."""
+    if robust is None:
+        return 0
+    hits = 0
+    for row in rs:
+        spike, prev = 0.0, None
+        for r in row.tolist():
+            if spike >= robust.k:
+                hits += 1
+            if prev is not None:
+                spike = spike + 1.0 if r > prev * robust.spike_ratio else 0.0
+            prev = r
+    return hits
+
+
+def _calibrate(layer, u, Bc, Cc, t, rate, robust=None, margin=2e-4):
+    """Bisect eps for a target update rate, then nudge it so no residual sits
+    within margin of the threshold (the gate comparison stays unambiguous)."""
+    _, _, rs = _run_scan_range(layer, u, Bc, Cc, t, eps=0.0, robust=robust)
+    lo, hi = 0.0, float(rs.max()) * 4
+    for _ in range(40):
+        mid = 0.5 * (lo + hi)
+        _, gs, _ = _run_scan_range(layer, u, Bc, Cc, t, eps=mid, robust=robust)
+        if float(gs.mean()) > rate:
+            lo = mid
+        else:
+            hi = mid
+    eps = 0.5 * (lo + hi)
+    for _ in range(200):
+        ys, gs, rs = _run_scan_range(layer, u, Bc, Cc, t, eps=eps, robust=robust)
+        gap = (rs - eps).abs()
+        if robust is not None:
+            gap = torch.minimum(gap, (rs - eps * robust.eps_factor).abs())
+        if float(gap.min()) > margin:
+            return eps, ys, gs, rs
+        eps *= 1.0 + 3 * margin
+    raise RuntimeError("could not calibrate eps away from residuals")
+
+
+def cell_cases():
+    from cst_ssm.modules.eacs import RobustCfg
+    out = {}
+    specs = {
+        # name: (H, N, tau_min, tau_max, B, L, seed, target update rate, robust, dup, ramp)
+        "cell_commit": (48, 16, 0.5, 4.0, 2, 64, 0, None, None, False, False),
+        "cell_wide": (256, 16, 0.5, 64.0, 2, 40, 1, None, None, False, False),
+        "cell_skip50": (48, 16, 0.5, 4.0, 2, 64, 2, 0.5, None, True, False),
+        "cell_skip30": (40, 8, 4.0, 32.0, 3, 48, 3, 0.3, None, True, False),
+        "cell_skip70": (33, 5, 32.0, 256.0, 2, 40, 4, 0.7, None, False, False),
+        "cell_n32": (24, 32, 0.5, 64.0, 2, 36, 5, 0.4, None, True, False),
+        "cell_robust": (32, 16, 0.5, 4.0, 2, 64, 6, 0.6, (3, 2.0, 0.3), False, True),
+        "cell_robust_k1": (32, 8, 0.5, 4.0, 2, 64, 7, 0.55, (1, 1.05, 0.5), True, False),
+        "cell_l1": (16, 4, 0.5, 4.0, 2, 1, 8, None, None, False, False),
+    }
+    for name, (H, N, tmin, tmax, B, L, seed, q, rb, dup, ramp) in specs.items():
+        layer, u, Bc, Cc, t = _layer_inputs(H, N, tmin, tmax, B, L, seed, dup, ramp)
+        robust = None if rb is None else RobustCfg(*rb)
+        if q is None:
+            eps = float(layer.gate.eps.detach())
+            ys, gs, rs = _run_scan_range(layer, u, Bc, Cc, t, robust=robust)
+        else:
+            eps, ys, gs, rs = _calibrate(layer, u, Bc, Cc, t, q, robust=robust)
+        d = dict(lam=_np(layer.lam()), log_dt=_np(layer.log_dt_scale), u=_np(u), Bc=_np(Bc),
+                 Cc=_np(Cc), t=_np(t), D=_np(layer.D), mean=_np(layer.obs_norm.running_mean),
+                 var=_np(layer.obs_norm.running_var),
+                 scalars=np.array([eps, layer.gate.norm_eta, layer.obs_norm.eps, layer.dt_init,
+                                   1e-3, layer.dt_max], np.float64),
+                 robust=np.array([-1, 0, 0] if rb is None else rb, np.float64),
+                 y=_np(ys), gate=_np(gs), resid=_np(rs))
+        out[name] = d
+        print(f"{name}: update rate {float(gs.mean()):.3f}, "
+              f"min|r-eps| {float((rs - eps).abs().min()):.2e}, "
+              f"robust-lowered steps {_spike_hits(rs, robust)}")
+    return out
+
+
+def train_cases():
+    from cst_ssm.ops.eacs_cell_train import GatedEACSCellFunction
+    out = {}
+    specs = {
+        # name: (H, N, B, L, seed, gate_mode, T, target update rate)
+        "train_ste": (6, 4, 2, 12, 10, "ste", 0.5, 0.5),
+        "train_ste_commit": (8, 4, 2, 10, 11, "ste", 0.3, None),
+        "train_soft": (5, 3, 2, 9, 12, "soft", 0.4, 0.5),
+    }
+    for name, (H, N, B, L, seed, mode, T, q) in specs.items():
+        layer, u, Bc, Cc, t = _layer_inputs(H, N, 0.5, 4.0, B, L, seed, dup_frames=True)
+        if q is None:
+            eps_v = float(layer.gate.eps.detach())
+        else:
+            eps_v, _, _, _ = _calibrate(layer, u, Bc, Cc, t, q)
+        g = torch.Generator().manual_seed(seed + 100)
+        lam = layer.lam().detach().to(torch.complex64).requires_grad_(True)
+        log_dt = layer.log_dt_scale.detach().clone().requires_grad_(True)
+        D = layer.D.detach().clone().requires_grad_(True)
+        eps = torch.tensor(eps_v).requires_grad_(True)
+        u_ = u.clone().requires_grad_(True)
+        Bc_ = Bc.clone().requires_grad_(True)
+        Cc_ = Cc.clone().requires_grad_(True)
+        t_ = t.clone().requires_grad_(True)
+        mean = layer.obs_norm.running_mean.detach()
+        var = layer.obs_norm.running_var.detach()
+        ys, gs, rs, ns = GatedEACSCellFunction.apply(
+            u_, Bc_, Cc_, t_, lam, log_dt, D, eps, mean, var, T, layer.gate.norm_eta,
+            layer.obs_norm.eps, layer.dt_init, mode, False, layer.dt_max)
+        gy = torch.randn(ys.shape, generator=g)
+        ggs = torch.randn(gs.shape, generator=g)
+        grs = torch.randn(rs.shape, generator=g)
+        gns = torch.randn(ns.shape, generator=g)
+        grads = torch.autograd.grad([ys, gs, rs, ns], [u_, Bc_, Cc_, t_, lam, log_dt, D, eps],
+                                    [gy, ggs, grs, gns])
+        names = ["du", "dBc", "dCc", "dt", "dlam", "dlog_dt", "dD", "deps"]
+        d = dict(lam=_np(lam), log_dt=_np(log_dt), u=_np(u), Bc=_np(Bc), Cc=_np(Cc), t=_np(t),
+                 D=_np(D), mean=_np(mean), var=_np(var),
+                 scalars=np.array([eps_v, layer.gate.norm_eta, layer.obs_norm.eps,
+                                   layer.dt_init, 1e-3, layer.dt_max, T], np.float64),
+                 gate_mode=np.array([0 if mode == "ste" else 1]),
+                 y=_np(ys), gate=_np(gs), resid=_np(rs), innov=_np(ns),
+                 gy=_np(gy), ggs=_np(ggs), grs=_np(grs), gns=_np(gns))
+        for k, v in zip(names, grads):
+            d[k] = _np(v)
+        out[name] = d
+        print(f"{name}: update rate {float(gs.mean()):.3f}")
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    gen = torch.Generator().manual_seed(1234)
+    groups = {"scan": scan_cases(gen), "ssm": ssm_cases(gen), "cell": cell_cases(),
+              "train": train_cases()}
+    for group, cases in groups.items():
+        flat = {f"{case}/{k}": v for case, d in cases.items() for k, v in d.items()}
+        path = os.path.join(HERE, f"{group}.npz")
+        np.savez_compressed(path, **flat)
+        print(f"wrote {path} ({os.path.getsize(path) / 1024:.0f} KiB)")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,69 @@
+"""The CPU oracle against golden vectors produced by the reference itself."""
+import numpy as np
+import pytest
+
+from golden_io import cases, cell_args, decisive, relerr
+from oracle import oracle
+
+SCAN = cases("scan")
+SSM = cases("ssm")
+CELL = cases("cell")
+TRAIN = cases("train")
+
+
+@pytest.mark.parametrize("name", sorted(SCAN))
+def test_scan_fwd_bwd(name):
+    d = SCAN[name]
+    h = oracle.scan_fwd(d["a"], d["b"])
+    assert relerr(h, d["h"]) < 1e-6
+    assert relerr(d["h_assoc"], d["h"]) < 1e-5  # reference's own two scans agree
+    ga, gb = oracle.scan_bwd(d["a"], d["h"], d["gh"])
+    assert relerr(ga, d["ga"]) < 1e-6
+    assert relerr(gb, d["gb"]) < 1e-6
+
+
+@pytest.mark.parametrize("name", sorted(SSM))
+def test_ssm_fwd(name):
+    d = SSM[name]
+    y = oracle.ssm_fwd(d["lam"], d["log_dt"], d["t"], d["Bc"], d["Cc"], d["u"], d["D"])
+    assert relerr(y, d["y"]) < 1e-5
+
+
+@pytest.mark.parametrize("name", sorted(CELL))
+def test_cell_fwd(name):
+    d = CELL[name]
+    a = cell_args(d)
+    y, g, r = oracle.cell_fwd(d["lam"], d["log_dt"], d["u"], d["Bc"], d["Cc"], d["t"], d["D"],
+                              d["mean"], d["var"], **a)
+    assert np.array_equal(g, d["gate"]), "gate masks differ"
+    assert decisive(d["resid"], a["eps"], a["robust"]).all()
+    assert relerr(r, d["resid"]) < 1e-5
+    assert relerr(y, d["y"]) < 1e-5
+
+
+@pytest.mark.parametrize("name", sorted(TRAIN))
+def test_train_fwd(name):
+    d = TRAIN[name]
+    eps, eta, var_eps, dt_init, dt_min, dt_max, T = [float(v) for v in d["scalars"]]
+    mode = int(d["gate_mode"][0])
+    y, g, r = oracle.cell_fwd(d["lam"], d["log_dt"], d["u"], d["Bc"], d["Cc"], d["t"], d["D"],
+                              d["mean"], d["var"], eps, eta, var_eps, dt_init, dt_min, dt_max,
+                              gate_mode=mode, T=T, train_exp=True)
+    tol_g = 0 if mode == 0 else 1e-5
+    assert np.max(np.abs(g - d["gate"])) <= tol_g
+    assert relerr(r, d["resid"]) < 1e-5
+    assert relerr(y, d["y"]) < 1e-5
+    assert np.array_equal(d["innov"], d["resid"])
+
+
+@pytest.mark.parametrize("name", sorted(TRAIN))
+def test_train_bwd(name):
+    d = TRAIN[name]
+    eps, eta, var_eps, dt_init, dt_min, dt_max, T = [float(v) for v in d["scalars"]]
+    mode = int(d["gate_mode"][0])
+    got = oracle.cell_bwd(d["lam"], d["log_dt"], d["u"], d["Bc"], d["Cc"], d["t"], d["D"],
+                          d["mean"], d["var"], eps, eta, var_eps, dt_init, dt_max, T, mode,
+                          d["gate"], d["gy"], d["ggs"], d["grs"], d["gns"])
+    names = ["du", "dBc", "dCc", "dt", "dlam", "dlog_dt", "dD", "deps"]
+    for k, v in zip(names, got):
+        assert relerr(v, d[k]) < 1e-4, (k, relerr(v, d[k]))
