@@ -1,0 +1,126 @@
+/*
+ * eacs_b200.h -- C ABI of the B200 (sm_100a) EACS temporal hot path.
+ *
+ * Plain pointers and sizes only.  Every pointer is a device pointer on the
+ * current CUDA device unless noted; `stream` is a cudaStream_t (NULL = legacy
+ * default stream).  Complex tensors are complex64 (interleaved float pairs).
+ * Shapes: lam (H,N), log_dt/D/mean/var (H), u (B,L,H), Bc/Cc (B,L,N),
+ * t (B,L), y (B,L,H), gate/resid (B,L), scan tensors (B,L,H,N).  All tensors
+ * are dense row-major (C-contiguous).
+ *
+ * Every entry point returns EACS_OK or an error code; a message for the last
+ * failure on the calling thread is available from eacs_last_error().  Nothing
+ * here allocates device memory unless stated: outputs and workspaces are the
+ * caller's.  Calls are asynchronous on `stream`.
+ *
+ * Reference interface each entry replaces (paths inside the CST-SSM project,
+ * BitGao-ai/LongVideo-main) is cited on the declaration.
+ */
+#ifndef EACS_B200_H
+#define EACS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define EACS_API __attribute__((visibility("default")))
+#else
+#define EACS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EACS_OK 0
+#define EACS_ERR_INVALID 1     /* bad shape, pointer, alignment or argument */
+#define EACS_ERR_CUDA 2        /* a CUDA runtime call or kernel launch failed */
+#define EACS_ERR_WORKSPACE 3   /* workspace missing or too small */
+#define EACS_ERR_TIMEOUT 4     /* a bounded device-side wait expired */
+#define EACS_ERR_UNSUPPORTED 5 /* shape outside what the kernels handle (e.g. N > 64) */
+
+/* element types of the `u` input */
+#define EACS_DTYPE_F32 0
+#define EACS_DTYPE_F16 1
+#define EACS_DTYPE_BF16 2
+
+/* Library version string. */
+EACS_API const char* eacs_version(void);
+
+/* Message describing the last failing call on this host thread ("" if none). */
+EACS_API const char* eacs_last_error(void);
+
+/* Synchronises `stream`, then reads and clears the device status word that
+ * kernels set instead of trapping (EACS_ERR_TIMEOUT for an expired bounded
+ * wait).  *status receives EACS_OK when nothing was recorded. */
+EACS_API int eacs_device_status(int* status, void* stream);
+
+/* Number of kernel launches this library has issued in this process (all
+ * devices).  Lets a caller prove the native path ran. */
+EACS_API uint64_t eacs_kernel_launches(void);
+
+/* Per host thread: when both events are non-NULL (cudaEvent_t), every later
+ * call records `start` just before and `stop` just after its dominant kernel
+ * (the chain kernel of eacs_cell_fwd / eacs_ssm_fwd, the scan kernel of
+ * eacs_scan_fwd / eacs_scan_bwd) on the call's stream.  NULL, NULL turns it
+ * off.  Used to time that kernel alone inside a larger call. */
+EACS_API int eacs_set_kernel_events(void* start, void* stop);
+
+/* Variable-step diagonal complex scan forward, h_l = a_l * h_{l-1} + b_l.
+ * Replaces scan_fwd(a, b) -> [h] (cst_ssm/ops/csrc/eacs_scan_cuda.cu:62-77,
+ * bound at eacs_scan_cuda.cu:98-101 and called from ops/scan_cuda.py:38-42).
+ * a, b, h: (B,L,H,N) complex64. */
+EACS_API int eacs_scan_fwd(const void* a, const void* b, void* h,
+                  int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
+
+/* Reverse adjoint of the scan: s_l = g_l + conj(a_{l+1}) s_{l+1},
+ * grad_b = s, grad_a = s * conj(h_{l-1}).
+ * Replaces scan_bwd(a, h, grad_h) -> [grad_a, grad_b]
+ * (cst_ssm/ops/csrc/eacs_scan_cuda.cu:79-96, called from ops/scan_cuda.py:44-49). */
+EACS_API int eacs_scan_bwd(const void* a, const void* h, const void* grad_h,
+                  void* grad_a, void* grad_b,
+                  int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
+
+/* Fused ungated continuous SSM core (ContinuousSSMLayer.forward,
+ * cst_ssm/modules/continuous_ssm.py:44-55 with ops/discretization.py:20-82):
+ * dt from timestamp differences (dt_0 = dt_1), ZOH discretisation, scan and
+ * readout y = Re sum_n C h + D u, with no (B,L,H,N) tensor in memory.
+ * lam (H,N) complex64, log_dt (H), t (B,L), Bc/Cc (B,L,N) complex64,
+ * u (B,L,H) of u_dtype, D (H); y (B,L,H) float32. */
+EACS_API int eacs_ssm_fwd(const void* lam, const float* log_dt, const float* t,
+                 const void* Bc, const void* Cc, const void* u, int u_dtype,
+                 const float* D, float* y,
+                 int64_t B, int64_t L, int64_t H, int64_t N,
+                 float dt_min, float dt_max, void* stream);
+
+/* Workspace bytes eacs_cell_fwd needs for these sizes. */
+EACS_API size_t eacs_cell_fwd_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+
+/* Gated EACS cell forward over all L (event gate, ZOH predict/update,
+ * commit, optional robust_guard).
+ * Replaces eacs_cell_fwd(lam, log_dt, u, Bc, Cc, t, Dp, mean, var, eps, eta,
+ * var_eps, dt_init, dt_min, dt_max) -> [y, gate, resid]
+ * (cst_ssm/ops/csrc/eacs_cell_cuda.cu:170-223, called from
+ * ops/eacs_gated_scan.py:35-49), and extends it with the semantics of
+ * modules/eacs.py:145-173 (scan_range): robust != 0 enables robust_guard
+ * (eps_l = eps*eps_factor after robust_k consecutive steps with
+ * r_l > r_{l-1}*spike_ratio, eacs.py:155-170); gate_mode 1 selects the soft
+ * gate sigmoid((r-eps)/max(T,1e-4)) blended into the state
+ * (ops/eacs_cell_train.py:47-63).  gate_mode 0 is the hard gate r > eps_l.
+ * Outputs y (B,L,H) float32, gate and resid (B,L) float32. */
+EACS_API int eacs_cell_fwd(const void* lam, const float* log_dt, const void* u, int u_dtype,
+                  const void* Bc, const void* Cc, const float* t, const float* D,
+                  const float* mean, const float* var,
+                  float eps, float eta, float var_eps, float dt_init,
+                  float dt_min, float dt_max,
+                  int robust, int robust_k, float spike_ratio, float eps_factor,
+                  int gate_mode, float temperature,
+                  float* y, float* gate, float* resid,
+                  void* workspace, size_t workspace_bytes,
+                  int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EACS_B200_H */

@@ -1,0 +1,104 @@
+// capi.cu -- the extern "C" entry points of libeacs_b200.so (include/eacs_b200.h).
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/eacs_b200.h"
+#include "eacs_host.h"
+
+namespace eacs {
+
+static thread_local std::string g_last_error;
+static std::atomic<uint64_t> g_launches{0};
+static thread_local cudaEvent_t g_ev_start = nullptr;
+static thread_local cudaEvent_t g_ev_stop = nullptr;
+
+void note_launch(int n) { g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed); }
+void mark_start(cudaStream_t s) {
+    if (g_ev_start && g_ev_stop) cudaEventRecord(g_ev_start, s);
+}
+void mark_stop(cudaStream_t s) {
+    if (g_ev_start && g_ev_stop) cudaEventRecord(g_ev_stop, s);
+}
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_check(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return EACS_OK;
+    return fail(EACS_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+}  // namespace eacs
+
+extern "C" {
+
+const char* eacs_version(void) { return "eacs_b200 0.1.0 (sm_100a)"; }
+
+const char* eacs_last_error(void) { return eacs::g_last_error.c_str(); }
+
+uint64_t eacs_kernel_launches(void) { return eacs::g_launches.load(std::memory_order_relaxed); }
+
+int eacs_set_kernel_events(void* start, void* stop) {
+    eacs::g_ev_start = static_cast<cudaEvent_t>(start);
+    eacs::g_ev_stop = static_cast<cudaEvent_t>(stop);
+    return EACS_OK;
+}
+
+int eacs_device_status(int* status, void* stream) {
+    if (!status) return eacs::fail(EACS_ERR_INVALID, "eacs_device_status: null status pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int a = 0, b = 0;
+    int rc = eacs::cuda_check(eacs::scan_read_status(&a, s), "eacs_device_status");
+    if (rc) return rc;
+    rc = eacs::cuda_check(eacs::cell_read_status(&b, s), "eacs_device_status");
+    if (rc) return rc;
+    *status = a ? a : b;
+    return EACS_OK;
+}
+
+int eacs_scan_fwd(const void* a, const void* b, void* h, int64_t B, int64_t L, int64_t H, int64_t N,
+                  void* stream) {
+    if (B < 0 || L < 0 || H < 0 || N < 0) return eacs::fail(EACS_ERR_INVALID, "eacs_scan_fwd: negative size");
+    return eacs::scan_fwd(a, b, h, B, L, H * N, static_cast<cudaStream_t>(stream));
+}
+
+int eacs_scan_bwd(const void* a, const void* h, const void* grad_h, void* grad_a, void* grad_b,
+                  int64_t B, int64_t L, int64_t H, int64_t N, void* stream) {
+    if (B < 0 || L < 0 || H < 0 || N < 0) return eacs::fail(EACS_ERR_INVALID, "eacs_scan_bwd: negative size");
+    return eacs::scan_bwd(a, h, grad_h, grad_a, grad_b, B, L, H * N, static_cast<cudaStream_t>(stream));
+}
+
+int eacs_ssm_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc, const void* Cc,
+                 const void* u, int u_dtype, const float* D, float* y, int64_t B, int64_t L, int64_t H,
+                 int64_t N, float dt_min, float dt_max, void* stream) {
+    return eacs::ssm_fwd(lam, log_dt, t, Bc, Cc, u, u_dtype, D, y, B, L, H, N, dt_min, dt_max,
+                         static_cast<cudaStream_t>(stream));
+}
+
+size_t eacs_cell_fwd_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
+    return eacs::cell_workspace_size(B, L, H, N);
+}
+
+int eacs_cell_fwd(const void* lam, const float* log_dt, const void* u, int u_dtype, const void* Bc,
+                  const void* Cc, const float* t, const float* D, const float* mean, const float* var,
+                  float eps, float eta, float var_eps, float dt_init, float dt_min, float dt_max,
+                  int robust, int robust_k, float spike_ratio, float eps_factor, int gate_mode,
+                  float temperature, float* y, float* gate, float* resid, void* workspace,
+                  size_t workspace_bytes, int64_t B, int64_t L, int64_t H, int64_t N, void* stream) {
+    eacs::CellCall c{lam,  log_dt, u,       u_dtype, Bc,     Cc,          t,           D,
+                     mean, var,    eps,     eta,     var_eps, dt_init,    dt_min,      dt_max,
+                     robust, robust_k, spike_ratio, eps_factor, gate_mode, temperature, y, gate,
+                     resid, workspace, workspace_bytes, B, L, H, N};
+    return eacs::cell_fwd(c, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

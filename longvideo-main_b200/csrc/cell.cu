@@ -1,0 +1,709 @@
+// cell.cu -- gated EACS cell and fused ungated continuous SSM (sm_100a).
+//
+// Semantics: cst_ssm/modules/eacs.py:78-173 (eacs_step / scan_range with
+// robust_guard), cst_ssm/ops/csrc/eacs_cell_cuda.cu:36-168 (the inference
+// kernel this replaces), cst_ssm/ops/eacs_cell_train.py:15-66 (soft gate) and
+// cst_ssm/modules/continuous_ssm.py:44-55 (ungated layer core).
+//
+// Gated forward = speculate, verify, repair:
+//  1. cell_chain<SPEC>: assume every frame commits.  Then t_pi = t_{l-1},
+//     u_pi = u_{l-1}, B_pi = B_{l-1}, C_pi = C_{l-1}, h_pi = h_{l-1} and the
+//     gated cell is a linear recurrence, run with one thread per (h, n) chain
+//     (state in registers, all of L, no (B,L,H,N) tensor anywhere).  Each step
+//     also forms the prediction x_hat, y_hat and the residual partial sums
+//     sum_h ((u-mu)/s - (y_hat-mu)/s)^2, sum_h ((u-mu)/s)^2 per h-tile.
+//  2. cell_resid: r_l per (b, l) from the partials (fixed summation order).
+//  3. cell_gates: per row, the robust_guard spike counter as a max-scan,
+//     gates g_l = r_l > eps_l and the first skipped step l*.  Everything
+//     before l* is exact; rows with no skip are done.
+//  4. cell_chain<REPLAY>: for rows with a skip, the committed state h_{l*-1}.
+//  5. cell_repair: for those rows, the exact sequential gated cell from l*
+//     (one CTA per row, one block reduction per step).
+// Frames with every step committing (update rate 1.0, the common case on
+// N(0,1) features) cost one pass of step 1.
+#include <algorithm>
+
+#include "eacs_common.cuh"
+#include "eacs_host.h"
+
+namespace eacs {
+namespace {
+
+constexpr int kThreads = 128;  // chain kernel CTA
+constexpr int kT = 32;         // steps per staged chunk
+constexpr int kRepair = 1024;  // repair kernel CTA
+
+enum Mode { SPEC = 0, UNGATED = 1, REPLAY = 2 };
+
+struct Args {
+    const float2* lam;
+    const float* log_dt;
+    const void* u;
+    const float2* Bc;
+    const float2* Cc;
+    const float* t;
+    const float* D;
+    const float* mean;
+    const float* var;
+    float eps, eta, var_eps, dt_init, dt_min, dt_max;
+    int robust, robust_k;
+    float spike_ratio, eps_lo;
+    int gate_mode;
+    float Tp;
+    float* y;
+    float* gate;
+    float* resid;
+    float2* part;  // [B][ntiles][L] (sum d^2, sum obs^2)
+    int4* row;     // [B] {l*, bits(spike after l*-1), bits(r_{l*-1}), 0}
+    float2* hpi;   // [B][H][N] committed state for the repair pass
+    float* upi;    // [B][H]
+    int B, L, H, N, ntiles;
+};
+
+// ---------------------------------------------------------------------------
+// 1 / 4: chain kernel.  Thread (hl, ln) of a CTA owns chains n = ln + LANES*j
+// (j < NPT) of channel h = tile*HT + hl; the n-sum of the readouts is a
+// shuffle butterfly inside the LANES-wide group.
+// ---------------------------------------------------------------------------
+template <int LANES, int NPT, int MODE, typename UT>
+__global__ void __launch_bounds__(kThreads, (NPT == 1 ? 6 : 4)) cell_chain(Args a) {
+    constexpr int HT = kThreads / LANES;
+    constexpr int NP = LANES * NPT;
+    constexpr int NW = kThreads / 32;
+    __shared__ float2 sB[kT][NP];
+    __shared__ float2 sC[kT][NP];
+    __shared__ float su[kT][HT];
+    __shared__ float sy[kT][HT];
+    __shared__ float st[kT];
+    __shared__ float2 sred[kT][NW];
+
+    const int tid = threadIdx.x;
+    const int ln = tid % LANES;
+    const int hl = tid / LANES;
+    const int tile = blockIdx.x;
+    const int b = blockIdx.y;
+    const int h0 = tile * HT;
+    const int h = h0 + hl;
+    const bool hv = h < a.H;
+    const int L = a.L, H = a.H, N = a.N;
+
+    int lstop = L;
+    if (MODE == REPLAY) {
+        lstop = a.row[b].x;
+        if (lstop >= L) return;  // row verified: nothing to repair
+    }
+
+    const UT* u = static_cast<const UT*>(a.u);
+    const size_t rowLH = static_cast<size_t>(b) * L;
+
+    float2 lam[NPT], ilam[NPT], hs[NPT], Bp[NPT], Cp[NPT];
+    bool nv[NPT];
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) {
+        const int n = ln + LANES * j;
+        nv[j] = hv && n < N;
+        lam[j] = nv[j] ? a.lam[static_cast<size_t>(h) * N + n] : make_float2(-1.f, 0.f);
+        ilam[j] = crecip(lam[j]);
+        hs[j] = make_float2(0.f, 0.f);
+        Bp[j] = nv[j] ? a.Bc[rowLH * N + n] : make_float2(0.f, 0.f);
+        Cp[j] = nv[j] ? a.Cc[rowLH * N + n] : make_float2(0.f, 0.f);
+    }
+    const float scale = hv ? expf(a.log_dt[h]) : 1.f;
+    const float sd = hv ? sqrtf(a.var[h] + a.var_eps) : 1.f;
+    const float mu = hv ? a.mean[h] : 0.f;
+    const float Dh = hv ? a.D[h] : 0.f;
+    float u_prev = hv ? to_f32(u[rowLH * H + h]) : 0.f;
+    const float t0 = a.t[rowLH];
+    float t_prev = t0 - a.dt_init;
+    float dt0 = 0.f;  // ungated: dt_0 = dt_1 (continuous_ssm.py:45-48)
+    if (MODE == UNGATED && L > 1) dt0 = fmaxf(a.t[rowLH + 1] - t0, 0.f);
+
+    for (int l0 = 0; l0 < lstop; l0 += kT) {
+        const int steps = min(kT, lstop - l0);
+        __syncthreads();
+        for (int idx = tid; idx < steps * N; idx += kThreads) {
+            const int i = idx / N, n = idx - (idx / N) * N;
+            const size_t o = (rowLH + l0 + i) * N + n;
+            sB[i][n] = a.Bc[o];
+            sC[i][n] = a.Cc[o];
+        }
+        for (int idx = tid; idx < steps * HT; idx += kThreads) {
+            const int i = idx / HT, k = idx - (idx / HT) * HT;
+            su[i][k] = (h0 + k < H) ? to_f32(u[(rowLH + l0 + i) * H + h0 + k]) : 0.f;
+        }
+        for (int i = tid; i < steps; i += kThreads) st[i] = a.t[rowLH + l0 + i];
+        __syncthreads();
+
+        for (int i = 0; i < steps; ++i) {
+            const float tl = st[i];
+            float delta;
+            if (MODE == UNGATED)
+                delta = (l0 + i == 0) ? dt0 : fmaxf(tl - t_prev, 0.f);
+            else
+                delta = fmaxf(tl - t_prev, 0.f);
+            const float dte = eff_dt(delta, scale, a.dt_min, a.dt_max);
+            const float ul = su[i][hl];
+            float yp = 0.f, yhp = 0.f;
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                if (!nv[j]) continue;
+                const int n = ln + LANES * j;
+                float2 dA, dB;
+                zoh(lam[j], ilam[j], dte, dA, dB);
+                const float2 Bl = sB[i][n];
+                const float2 P = cmul(dA, hs[j]);
+                const float2 qc = cmul(dB, Bl);
+                hs[j] = make_float2(fmaf(qc.x, ul, P.x), fmaf(qc.y, ul, P.y));
+                if (MODE != REPLAY) {
+                    const float2 Cl = sC[i][n];
+                    yp += cre_mul(Cl, hs[j]);
+                    if (MODE == SPEC) {
+                        const float2 qp = cmul(dB, Bp[j]);
+                        const float2 xh = make_float2(fmaf(qp.x, u_prev, P.x), fmaf(qp.y, u_prev, P.y));
+                        yhp += cre_mul(Cp[j], xh);
+                        Bp[j] = Bl;
+                        Cp[j] = Cl;
+                    }
+                }
+            }
+            if (MODE == SPEC) {
+                // Halving butterfly: lower half of the group ends with sum(yp),
+                // upper half with sum(yhp).
+                const bool up = (ln & (LANES / 2)) != 0;
+                const float send = up ? yp : yhp;
+                float v = (up ? yhp : yp) + __shfl_xor_sync(0xffffffffu, send, LANES / 2);
+#pragma unroll
+                for (int o = LANES / 4; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (ln == 0 && hv) sy[i][hl] = v + Dh * ul;
+                float v1 = 0.f, v2 = 0.f;
+                if (ln == LANES / 2 && hv) {
+                    const float obs = (ul - mu) / sd;
+                    const float pred = (v - mu) / sd;
+                    const float d = obs - pred;
+                    v1 = d * d;
+                    v2 = obs * obs;
+                }
+#pragma unroll
+                for (int o = LANES; o < 32; o <<= 1) {
+                    v1 += __shfl_xor_sync(0xffffffffu, v1, o);
+                    v2 += __shfl_xor_sync(0xffffffffu, v2, o);
+                }
+                if ((tid & 31) == LANES / 2) sred[i][tid >> 5] = make_float2(v1, v2);
+            } else if (MODE == UNGATED) {
+                float v = yp;
+#pragma unroll
+                for (int o = LANES / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (ln == 0 && hv) sy[i][hl] = v + Dh * ul;
+            }
+            u_prev = ul;
+            t_prev = tl;
+        }
+        if (MODE != REPLAY) {
+            __syncthreads();
+            for (int idx = tid; idx < steps * HT; idx += kThreads) {
+                const int i = idx / HT, k = idx - (idx / HT) * HT;
+                if (h0 + k < H) a.y[(rowLH + l0 + i) * H + h0 + k] = sy[i][k];
+            }
+            if (MODE == SPEC) {
+                for (int i = tid; i < steps; i += kThreads) {
+                    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+                    for (int w = 0; w < NW; ++w) {
+                        s1 += sred[i][w].x;
+                        s2 += sred[i][w].y;
+                    }
+                    a.part[(static_cast<size_t>(b) * a.ntiles + tile) * L + l0 + i] = make_float2(s1, s2);
+                }
+            }
+        }
+    }
+    if (MODE == REPLAY) {
+#pragma unroll
+        for (int j = 0; j < NPT; ++j)
+            if (nv[j]) a.hpi[(static_cast<size_t>(b) * H + h) * N + ln + LANES * j] = hs[j];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 2: residual per (b, l) from the h-tile partials.
+// ---------------------------------------------------------------------------
+__global__ void cell_resid(Args a) {
+    const int b = blockIdx.y;
+    const int l = blockIdx.x * blockDim.x + threadIdx.x;
+    if (l >= a.L) return;
+    float s1 = 0.f, s2 = 0.f;
+    const float2* p = a.part + static_cast<size_t>(b) * a.ntiles * a.L + l;
+    for (int k = 0; k < a.ntiles; ++k) {
+        const float2 v = p[static_cast<size_t>(k) * a.L];
+        s1 += v.x;
+        s2 += v.y;
+    }
+    a.resid[static_cast<size_t>(b) * a.L + l] = sqrtf(s1) / (sqrtf(s2) + a.eta);
+}
+
+// ---------------------------------------------------------------------------
+// 3: gates, robust_guard and the first skipped step, one CTA per row.
+// spike after step l is l - R_l with R_l the last step <= l that was not a
+// spike (r_l > r_{l-1} * spike_ratio), so it is a max-scan over the tile.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) cell_gates(Args a) {
+    __shared__ int swarp[32];
+    __shared__ float slast_r;
+    __shared__ int slast_R;
+    __shared__ int sfirst;
+    const int b = blockIdx.x;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, wid = tid >> 5;
+    const size_t rb = static_cast<size_t>(b) * a.L;
+    int carry_R = 0;       // R_{l0-1}
+    float carry_r = 0.f;   // r_{l0-1}
+    int lstar = a.L;
+    int4 rowv = make_int4(a.L, 0, 0, 0);
+    for (int l0 = 0; l0 < a.L; l0 += 1024) {
+        const int l = l0 + tid;
+        const bool valid = l < a.L;
+        const float r = valid ? a.resid[rb + l] : 0.f;
+        // previous residual
+        float rprev = __shfl_up_sync(0xffffffffu, r, 1);
+        __shared__ float sbound[32];
+        if (lane == 31) sbound[wid] = r;
+        __syncthreads();
+        if (lane == 0) rprev = (wid == 0) ? carry_r : sbound[wid - 1];
+        const bool f = valid && l >= 1 && (r > rprev * a.spike_ratio);
+        // inclusive max-scan of key = f ? -1 : l  (R_l), with the tile carry
+        int key = f ? -1 : (valid ? l : -1);
+        int x = key;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x = max(x, y);
+        }
+        if (lane == 31) swarp[wid] = x;
+        __syncthreads();
+        if (wid == 0) {
+            int w = swarp[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) w = max(w, y);
+            }
+            swarp[lane] = w;
+        }
+        __syncthreads();
+        const int pre_w = wid > 0 ? swarp[wid - 1] : -1;
+        const int incl = max(max(x, pre_w), carry_R);          // R_l
+        int excl = __shfl_up_sync(0xffffffffu, incl, 1);       // R_{l-1}
+        if (lane == 0) excl = max(pre_w, carry_R);
+        if (wid == 0 && lane == 0) excl = carry_R;
+        const float spike_prev = (l == 0) ? 0.f : static_cast<float>((l - 1) - excl);
+        float eps_l = a.eps;
+        if (a.robust && spike_prev >= static_cast<float>(a.robust_k)) eps_l = a.eps_lo;
+        const bool g = r > eps_l;
+        if (valid) a.gate[rb + l] = g ? 1.f : 0.f;
+        // first skipped step in this tile
+        if (tid == 0) sfirst = 0x7fffffff;
+        __syncthreads();
+        if (valid && !g) atomicMin(&sfirst, l);
+        if (l == min(a.L, l0 + 1024) - 1) {  // last step of the tile
+            slast_r = r;
+            slast_R = incl;
+        }
+        __syncthreads();
+        const int first = sfirst;
+        if (first != 0x7fffffff) {
+            if (l == first) {
+                rowv.x = first;
+                rowv.y = __float_as_int(spike_prev);
+                rowv.z = __float_as_int(rprev);
+                a.row[b] = rowv;
+            }
+            lstar = first;
+            break;
+        }
+        carry_r = slast_r;
+        carry_R = slast_R;
+        __syncthreads();
+    }
+    if (lstar == a.L && tid == 0) a.row[b] = rowv;
+}
+
+// ---------------------------------------------------------------------------
+// 5: exact sequential gated cell from l* (one CTA per row).
+// ---------------------------------------------------------------------------
+template <int LANES, int NPT, typename UT>
+__global__ void __launch_bounds__(kRepair) cell_repair(Args a) {
+    constexpr int HG = kRepair / LANES;  // channel groups per pass
+    constexpr int NP = LANES * NPT;
+    __shared__ float2 sBpi[NP];
+    __shared__ float2 sCpi[NP];
+    __shared__ float2 sred[32];
+    __shared__ float sg;
+
+    const int b = blockIdx.x;
+    const int L = a.L, H = a.H, N = a.N;
+    const int4 rowv = a.row[b];
+    const int lstar = rowv.x;
+    if (lstar >= L) return;
+    const int tid = threadIdx.x;
+    const int ln = tid % LANES, hg = tid / LANES;
+    const int lane = tid & 31, wid = tid >> 5;
+    const UT* u = static_cast<const UT*>(a.u);
+    const size_t rowLH = static_cast<size_t>(b) * L;
+    const int lp = lstar > 0 ? lstar - 1 : 0;
+    float2* hpi = a.hpi + static_cast<size_t>(b) * H * N;
+    float* upi = a.upi + static_cast<size_t>(b) * H;
+
+    for (int n = tid; n < N; n += kRepair) {
+        sBpi[n] = a.Bc[(rowLH + lp) * N + n];
+        sCpi[n] = a.Cc[(rowLH + lp) * N + n];
+    }
+    for (int hh = tid; hh < H; hh += kRepair) upi[hh] = to_f32(u[(rowLH + lp) * H + hh]);
+    float t_pi = lstar > 0 ? a.t[rowLH + lp] : a.t[rowLH] - a.dt_init;
+    float spike = __int_as_float(rowv.y);
+    float prev_r = __int_as_float(rowv.z);
+    __syncthreads();
+
+    for (int l = lstar; l < L; ++l) {
+        const float tl = a.t[rowLH + l];
+        const float delta = fmaxf(tl - t_pi, 0.f);
+        // phase A: prediction and residual
+        float acc1 = 0.f, acc2 = 0.f;
+        for (int h0 = 0; h0 < H; h0 += HG) {
+            const int h = h0 + hg;
+            const bool hv = h < H;
+            float yhp = 0.f;
+            float dte = 0.f, upv = 0.f;
+            if (hv) {
+                dte = eff_dt(delta, expf(a.log_dt[h]), a.dt_min, a.dt_max);
+                upv = upi[h];
+            }
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                const int n = ln + LANES * j;
+                if (hv && n < N) {
+                    const float2 lm = a.lam[static_cast<size_t>(h) * N + n];
+                    float2 dA, dB;
+                    zoh(lm, crecip(lm), dte, dA, dB);
+                    const float2 P = cmul(dA, hpi[static_cast<size_t>(h) * N + n]);
+                    const float2 q = cmul(dB, sBpi[n]);
+                    const float2 xh = make_float2(fmaf(q.x, upv, P.x), fmaf(q.y, upv, P.y));
+                    yhp += cre_mul(sCpi[n], xh);
+                }
+            }
+#pragma unroll
+            for (int o = LANES / 2; o > 0; o >>= 1) yhp += __shfl_xor_sync(0xffffffffu, yhp, o);
+            if (ln == 0 && hv) {
+                const float sd = sqrtf(a.var[h] + a.var_eps);
+                const float ul = to_f32(u[(rowLH + l) * H + h]);
+                const float obs = (ul - a.mean[h]) / sd;
+                const float pred = (yhp - a.mean[h]) / sd;
+                const float d = obs - pred;
+                acc1 += d * d;
+                acc2 += obs * obs;
+            }
+        }
+        acc1 = warp_sum(acc1);
+        acc2 = warp_sum(acc2);
+        if (lane == 0) sred[wid] = make_float2(acc1, acc2);
+        __syncthreads();
+        if (tid == 0) {
+            float s1 = 0.f, s2 = 0.f;
+            for (int w = 0; w < kRepair / 32; ++w) {
+                s1 += sred[w].x;
+                s2 += sred[w].y;
+            }
+            const float r = sqrtf(s1) / (sqrtf(s2) + a.eta);
+            float g;
+            if (a.gate_mode == 1) {
+                g = 1.0f / (1.0f + expf(-((r - a.eps) / a.Tp)));
+            } else {
+                float eps_l = a.eps;
+                if (a.robust && spike >= static_cast<float>(a.robust_k)) eps_l = a.eps_lo;
+                g = r > eps_l ? 1.f : 0.f;
+            }
+            if (a.robust) {
+                if (l > 0) spike = (r > prev_r * a.spike_ratio) ? spike + 1.f : 0.f;
+                prev_r = r;
+            }
+            a.gate[rowLH + l] = g;
+            a.resid[rowLH + l] = r;
+            sg = g;
+        }
+        __syncthreads();
+        const float g = sg;
+        const bool soft = a.gate_mode == 1;
+        const bool fire = soft || g > 0.5f;
+        // phase C: update / select / readout / commit h_pi, u_pi
+        for (int h0 = 0; h0 < H; h0 += HG) {
+            const int h = h0 + hg;
+            const bool hv = h < H;
+            float yp = 0.f, dte = 0.f, upv = 0.f, ul = 0.f;
+            if (hv) {
+                dte = eff_dt(delta, expf(a.log_dt[h]), a.dt_min, a.dt_max);
+                upv = upi[h];
+                ul = to_f32(u[(rowLH + l) * H + h]);
+            }
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                const int n = ln + LANES * j;
+                if (hv && n < N) {
+                    const size_t o = static_cast<size_t>(h) * N + n;
+                    const float2 lm = a.lam[o];
+                    float2 dA, dB;
+                    zoh(lm, crecip(lm), dte, dA, dB);
+                    const float2 hp = hpi[o];
+                    const float2 P = cmul(dA, hp);
+                    const float2 Cl = a.Cc[(rowLH + l) * N + n];
+                    float2 hc;
+                    if (fire) {
+                        const float2 qc = cmul(dB, a.Bc[(rowLH + l) * N + n]);
+                        const float2 hu = make_float2(fmaf(qc.x, ul, P.x), fmaf(qc.y, ul, P.y));
+                        if (soft) {
+                            const float2 qp = cmul(dB, sBpi[n]);
+                            const float2 xh = make_float2(fmaf(qp.x, upv, P.x), fmaf(qp.y, upv, P.y));
+                            const float2 gu = cscale(hu, g);
+                            hc = cadd(gu, cscale(xh, 1.f - g));
+                            hpi[o] = cadd(gu, cscale(hp, 1.f - g));
+                        } else {
+                            hc = hu;
+                            hpi[o] = hu;
+                        }
+                    } else {
+                        const float2 qp = cmul(dB, sBpi[n]);
+                        hc = make_float2(fmaf(qp.x, upv, P.x), fmaf(qp.y, upv, P.y));
+                    }
+                    yp += cre_mul(Cl, hc);
+                }
+            }
+#pragma unroll
+            for (int o = LANES / 2; o > 0; o >>= 1) yp += __shfl_xor_sync(0xffffffffu, yp, o);
+            if (ln == 0 && hv) {
+                a.y[(rowLH + l) * H + h] = yp + a.D[h] * ul;
+                if (soft) upi[h] = g * ul + (1.f - g) * upv;
+                else if (fire) upi[h] = ul;
+            }
+        }
+        __syncthreads();
+        if (soft) {
+            for (int n = tid; n < N; n += kRepair) {
+                const float2 Bl = a.Bc[(rowLH + l) * N + n], Cl = a.Cc[(rowLH + l) * N + n];
+                sBpi[n] = cadd(cscale(Bl, g), cscale(sBpi[n], 1.f - g));
+                sCpi[n] = cadd(cscale(Cl, g), cscale(sCpi[n], 1.f - g));
+            }
+            t_pi = g * tl + (1.f - g) * t_pi;
+        } else if (fire) {
+            for (int n = tid; n < N; n += kRepair) {
+                sBpi[n] = a.Bc[(rowLH + l) * N + n];
+                sCpi[n] = a.Cc[(rowLH + l) * N + n];
+            }
+            t_pi = tl;
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// dispatch
+// ---------------------------------------------------------------------------
+int lanes_for(int N, int* lanes, int* npt) {
+    if (N <= 4) { *lanes = 4; *npt = 1; }
+    else if (N <= 8) { *lanes = 8; *npt = 1; }
+    else if (N <= 16) { *lanes = 16; *npt = 1; }
+    else if (N <= 32) { *lanes = 32; *npt = 1; }
+    else if (N <= 64) { *lanes = 32; *npt = 2; }
+    else return 0;
+    return 1;
+}
+
+template <int LANES, int NPT, int MODE, typename UT>
+cudaError_t launch_chain(const Args& a, cudaStream_t s) {
+    dim3 grid(a.ntiles, a.B);
+    if (MODE != REPLAY) mark_start(s);
+    cell_chain<LANES, NPT, MODE, UT><<<grid, kThreads, 0, s>>>(a);
+    if (MODE != REPLAY) mark_stop(s);
+    note_launch();
+    return cudaGetLastError();
+}
+
+template <int MODE, typename UT>
+cudaError_t chain_by_n(const Args& a, cudaStream_t s) {
+    int lanes, npt;
+    lanes_for(a.N, &lanes, &npt);
+    if (lanes == 4) return launch_chain<4, 1, MODE, UT>(a, s);
+    if (lanes == 8) return launch_chain<8, 1, MODE, UT>(a, s);
+    if (lanes == 16) return launch_chain<16, 1, MODE, UT>(a, s);
+    if (npt == 1) return launch_chain<32, 1, MODE, UT>(a, s);
+    return launch_chain<32, 2, MODE, UT>(a, s);
+}
+
+template <int MODE>
+cudaError_t chain_dispatch(const Args& a, int dtype, cudaStream_t s) {
+    if (dtype == EACS_DTYPE_F16) return chain_by_n<MODE, __half>(a, s);
+    if (dtype == EACS_DTYPE_BF16) return chain_by_n<MODE, __nv_bfloat16>(a, s);
+    return chain_by_n<MODE, float>(a, s);
+}
+
+template <typename UT>
+cudaError_t repair_by_n(const Args& a, cudaStream_t s) {
+    int lanes, npt;
+    lanes_for(a.N, &lanes, &npt);
+    if (lanes == 4) cell_repair<4, 1, UT><<<a.B, kRepair, 0, s>>>(a);
+    else if (lanes == 8) cell_repair<8, 1, UT><<<a.B, kRepair, 0, s>>>(a);
+    else if (lanes == 16) cell_repair<16, 1, UT><<<a.B, kRepair, 0, s>>>(a);
+    else if (npt == 1) cell_repair<32, 1, UT><<<a.B, kRepair, 0, s>>>(a);
+    else cell_repair<32, 2, UT><<<a.B, kRepair, 0, s>>>(a);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t repair_dispatch(const Args& a, int dtype, cudaStream_t s) {
+    if (dtype == EACS_DTYPE_F16) return repair_by_n<__half>(a, s);
+    if (dtype == EACS_DTYPE_BF16) return repair_by_n<__nv_bfloat16>(a, s);
+    return repair_by_n<float>(a, s);
+}
+
+int tiles_for(int H, int N) {
+    int lanes, npt;
+    lanes_for(N, &lanes, &npt);
+    const int HT = kThreads / lanes;
+    return (H + HT - 1) / HT;
+}
+
+size_t align_up(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+struct WsLayout {
+    size_t part, row, hpi, upi, total;
+};
+WsLayout ws_layout(int64_t B, int64_t L, int64_t H, int64_t N) {
+    WsLayout w;
+    const int64_t nt = tiles_for(static_cast<int>(H), static_cast<int>(N));
+    w.part = 0;
+    w.row = w.part + align_up(static_cast<size_t>(B * nt * L) * sizeof(float2));
+    w.hpi = w.row + align_up(static_cast<size_t>(B) * sizeof(int4));
+    w.upi = w.hpi + align_up(static_cast<size_t>(B * H * N) * sizeof(float2));
+    w.total = w.upi + align_up(static_cast<size_t>(B * H) * sizeof(float));
+    return w;
+}
+
+int check_shape(const char* fn, int64_t B, int64_t L, int64_t H, int64_t N, int dtype) {
+    if (B < 0 || L < 0 || H < 0 || N < 0) return fail(EACS_ERR_INVALID, "%s: negative size", fn);
+    if (N > 64) return fail(EACS_ERR_UNSUPPORTED, "%s: N=%lld > 64 is not supported", fn, (long long)N);
+    if (B > 65535) return fail(EACS_ERR_UNSUPPORTED, "%s: B=%lld > 65535", fn, (long long)B);
+    if (L > (1LL << 30) || H > (1LL << 24)) return fail(EACS_ERR_UNSUPPORTED, "%s: L or H too large", fn);
+    if (dtype != EACS_DTYPE_F32 && dtype != EACS_DTYPE_F16 && dtype != EACS_DTYPE_BF16)
+        return fail(EACS_ERR_INVALID, "%s: unknown u dtype %d", fn, dtype);
+    return EACS_OK;
+}
+
+}  // namespace
+
+size_t cell_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
+    if (B <= 0 || L <= 0 || H <= 0 || N <= 0 || N > 64) return 0;
+    return ws_layout(B, L, H, N).total;
+}
+
+int cell_fwd(const CellCall& c, cudaStream_t stream) {
+    const char* fn = "eacs_cell_fwd";
+    int rc = check_shape(fn, c.B, c.L, c.H, c.N, c.u_dtype);
+    if (rc) return rc;
+    if (c.B == 0 || c.L == 0 || c.H == 0) return EACS_OK;
+    if (c.N == 0) return fail(EACS_ERR_INVALID, "%s: N must be positive", fn);
+    if (!c.lam || !c.log_dt || !c.u || !c.Bc || !c.Cc || !c.t || !c.D || !c.mean || !c.var ||
+        !c.y || !c.gate || !c.resid)
+        return fail(EACS_ERR_INVALID, "%s: null pointer argument", fn);
+    if (c.gate_mode != 0 && c.gate_mode != 1)
+        return fail(EACS_ERR_INVALID, "%s: gate_mode must be 0 (hard) or 1 (soft)", fn);
+    if (c.gate_mode == 1 && c.robust)
+        return fail(EACS_ERR_INVALID, "%s: robust_guard applies to the hard gate only", fn);
+    const WsLayout w = ws_layout(c.B, c.L, c.H, c.N);
+    if (!c.workspace || c.workspace_bytes < w.total)
+        return fail(EACS_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", fn, w.total,
+                    c.workspace_bytes);
+    Args a{};
+    a.lam = static_cast<const float2*>(c.lam);
+    a.log_dt = c.log_dt;
+    a.u = c.u;
+    a.Bc = static_cast<const float2*>(c.Bc);
+    a.Cc = static_cast<const float2*>(c.Cc);
+    a.t = c.t;
+    a.D = c.D;
+    a.mean = c.mean;
+    a.var = c.var;
+    a.eps = c.eps;
+    a.eta = c.eta;
+    a.var_eps = c.var_eps;
+    a.dt_init = c.dt_init;
+    a.dt_min = c.dt_min;
+    a.dt_max = c.dt_max;
+    a.robust = c.robust ? 1 : 0;
+    a.robust_k = c.robust_k;
+    a.spike_ratio = c.spike_ratio;
+    a.eps_lo = c.eps * c.eps_factor;
+    a.gate_mode = c.gate_mode;
+    a.Tp = c.temperature > 1e-4f ? c.temperature : 1e-4f;
+    a.y = c.y;
+    a.gate = c.gate;
+    a.resid = c.resid;
+    char* ws = static_cast<char*>(c.workspace);
+    a.part = reinterpret_cast<float2*>(ws + w.part);
+    a.row = reinterpret_cast<int4*>(ws + w.row);
+    a.hpi = reinterpret_cast<float2*>(ws + w.hpi);
+    a.upi = reinterpret_cast<float*>(ws + w.upi);
+    a.B = static_cast<int>(c.B);
+    a.L = static_cast<int>(c.L);
+    a.H = static_cast<int>(c.H);
+    a.N = static_cast<int>(c.N);
+    a.ntiles = tiles_for(a.H, a.N);
+
+    cudaError_t e;
+    if (c.gate_mode == 0) {
+        if ((e = chain_dispatch<SPEC>(a, c.u_dtype, stream)) != cudaSuccess) return cuda_check(e, fn);
+        cell_resid<<<dim3((a.L + 255) / 256, a.B), 256, 0, stream>>>(a);
+        note_launch();
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_check(e, fn);
+        cell_gates<<<a.B, 1024, 0, stream>>>(a);
+        note_launch();
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_check(e, fn);
+    } else {
+        // soft gate: the state is a continuous blend, so run the exact cell from l = 0
+        if ((e = cudaMemsetAsync(a.row, 0, static_cast<size_t>(a.B) * sizeof(int4), stream)) != cudaSuccess)
+            return cuda_check(e, fn);
+    }
+    if ((e = chain_dispatch<REPLAY>(a, c.u_dtype, stream)) != cudaSuccess) return cuda_check(e, fn);
+    if ((e = repair_dispatch(a, c.u_dtype, stream)) != cudaSuccess) return cuda_check(e, fn);
+    return EACS_OK;
+}
+
+int ssm_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc, const void* Cc,
+            const void* u, int u_dtype, const float* D, float* y, int64_t B, int64_t L, int64_t H,
+            int64_t N, float dt_min, float dt_max, cudaStream_t stream) {
+    const char* fn = "eacs_ssm_fwd";
+    int rc = check_shape(fn, B, L, H, N, u_dtype);
+    if (rc) return rc;
+    if (B == 0 || L == 0 || H == 0) return EACS_OK;
+    if (N == 0) return fail(EACS_ERR_INVALID, "%s: N must be positive", fn);
+    if (!lam || !log_dt || !t || !Bc || !Cc || !u || !D || !y)
+        return fail(EACS_ERR_INVALID, "%s: null pointer argument", fn);
+    Args a{};
+    a.lam = static_cast<const float2*>(lam);
+    a.log_dt = log_dt;
+    a.u = u;
+    a.Bc = static_cast<const float2*>(Bc);
+    a.Cc = static_cast<const float2*>(Cc);
+    a.t = t;
+    a.D = D;
+    a.dt_min = dt_min;
+    a.dt_max = dt_max;
+    a.y = y;
+    a.B = static_cast<int>(B);
+    a.L = static_cast<int>(L);
+    a.H = static_cast<int>(H);
+    a.N = static_cast<int>(N);
+    a.ntiles = tiles_for(a.H, a.N);
+    cudaError_t e = chain_dispatch<UNGATED>(a, u_dtype, stream);
+    return cuda_check(e, fn);
+}
+
+cudaError_t cell_read_status(int* out, cudaStream_t stream) { return read_clear_status(out, stream); }
+
+}  // namespace eacs

@@ -1,0 +1,60 @@
+// eacs_host.h -- host-side declarations shared by the translation units of
+// libeacs_b200.so (kernels launchers and the C ABI in capi.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace eacs {
+
+// Records `msg` as the calling thread's last error and returns `code`.
+int fail(int code, const char* fmt, ...);
+// Maps a CUDA error to EACS_ERR_CUDA with a message (EACS_OK when e == success).
+int cuda_check(cudaError_t e, const char* what);
+
+// Launch bookkeeping (capi.cu): count a launch; record the thread's optional
+// timing events around the dominant kernel of a call.
+void note_launch(int n = 1);
+void mark_start(cudaStream_t s);
+void mark_stop(cudaStream_t s);
+
+// scan.cu
+int scan_fwd(const void* a, const void* b, void* h, int64_t B, int64_t L, int64_t C,
+             cudaStream_t stream);
+int scan_bwd(const void* a, const void* h, const void* gh, void* ga, void* gb, int64_t B,
+             int64_t L, int64_t C, cudaStream_t stream);
+cudaError_t scan_read_status(int* out, cudaStream_t stream);
+
+// cell.cu
+struct CellCall {
+    const void* lam;
+    const float* log_dt;
+    const void* u;
+    int u_dtype;
+    const void* Bc;
+    const void* Cc;
+    const float* t;
+    const float* D;
+    const float* mean;
+    const float* var;
+    float eps, eta, var_eps, dt_init, dt_min, dt_max;
+    int robust, robust_k;
+    float spike_ratio, eps_factor;
+    int gate_mode;
+    float temperature;
+    float* y;
+    float* gate;
+    float* resid;
+    void* workspace;
+    size_t workspace_bytes;
+    int64_t B, L, H, N;
+};
+size_t cell_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+int cell_fwd(const CellCall& c, cudaStream_t stream);
+int ssm_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc,
+            const void* Cc, const void* u, int u_dtype, const float* D, float* y, int64_t B,
+            int64_t L, int64_t H, int64_t N, float dt_min, float dt_max, cudaStream_t stream);
+cudaError_t cell_read_status(int* out, cudaStream_t stream);
+
+}  // namespace eacs

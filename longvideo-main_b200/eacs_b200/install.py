@@ -1,0 +1,40 @@
+"""Point an imported reference CST-SSM package at the B200 kernels.
+
+The reference loads its CUDA extensions lazily through module globals and
+imports its fused operators inside the calling functions
+(cst_ssm/ops/scan_cuda.py:14-29, ops/eacs_gated_scan.py:16-28,
+modules/eacs.py:250, :321, :367, ops/scan.py:69), so replacing those globals
+makes ContinuousSSMLayer, EACSLayer and MultiScaleEACS run these kernels
+without any change to the reference's code.
+"""
+from __future__ import annotations
+
+import importlib
+
+
+def install(package: str = "cst_ssm") -> dict:
+    """Patch `package` (already importable) and return what was replaced."""
+    from .ops import eacs_gated_scan as ours_cell
+    from .ops import scan_cuda as ours_scan
+
+    patched = {}
+    ref_scan = importlib.import_module(f"{package}.ops.scan_cuda")
+    ref_scan._EXT = ours_scan._load()
+    ref_scan._TRIED = True
+    patched["scan_cuda._EXT"] = ref_scan._EXT
+
+    ref_cell = importlib.import_module(f"{package}.ops.eacs_gated_scan")
+    ref_cell._EXT = ours_cell._load()
+    ref_cell._TRIED = True
+    patched["eacs_gated_scan._EXT"] = ref_cell._EXT
+
+    try:
+        from .ops import eacs_cell_train as ours_train
+    except ImportError:
+        ours_train = None
+    if ours_train is not None:
+        ref_train = importlib.import_module(f"{package}.ops.eacs_cell_train")
+        ref_train.GatedEACSCellFunction = ours_train.GatedEACSCellFunction
+        ref_train.fused_gated_scan = ours_train.fused_gated_scan
+        patched["eacs_cell_train.fused_gated_scan"] = ours_train.fused_gated_scan
+    return patched

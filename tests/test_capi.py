@@ -1,0 +1,88 @@
+"""C ABI checks that need no GPU: the library loads, exports every symbol the
+header declares, and rejects bad arguments before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from eacs_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "eacs_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"EACS_API\s+[\w\s\*]+?\b(eacs_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert "eacs_cell_fwd" in syms and "eacs_scan_fwd" in syms and len(syms) >= 8
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert not missing, missing
+    # the Python binding covers the same set
+    assert set(declared_symbols()) == set(_lib.SIGNATURES)
+
+
+def test_version_and_last_error():
+    assert "sm_100a" in _lib.version()
+    assert isinstance(_lib.last_error(), str)
+
+
+def test_cell_rejects_unsupported_n_without_device():
+    L = _lib.lib()
+    rc = L.eacs_cell_fwd(*([None] * 3), 0, *([None] * 6), 0.1, 1e-6, 1e-5, 1.0, 1e-3, 1e3,
+                         0, 0, 2.0, 0.3, 0, 0.1, None, None, None, None, 0, 2, 8, 4, 65, None)
+    assert rc == _lib.EACS_ERR_UNSUPPORTED
+    assert "N=65" in _lib.last_error()
+
+
+def test_cell_rejects_missing_workspace_without_device():
+    L = _lib.lib()
+    p = 16  # any non-null pointer value; rejected before use
+    rc = L.eacs_cell_fwd(p, p, p, 0, p, p, p, p, p, p, 0.1, 1e-6, 1e-5, 1.0, 1e-3, 1e3,
+                         0, 0, 2.0, 0.3, 0, 0.1, p, p, p, None, 0, 2, 8, 4, 16, None)
+    assert rc == _lib.EACS_ERR_WORKSPACE
+    assert L.eacs_cell_fwd_workspace_size(2, 8, 4, 16) > 0
+    assert L.eacs_cell_fwd_workspace_size(2, 8, 4, 65) == 0
+
+
+def test_cell_rejects_bad_dtype_and_gate_mode():
+    L = _lib.lib()
+    p = 16
+    rc = L.eacs_cell_fwd(p, p, p, 7, p, p, p, p, p, p, 0.1, 1e-6, 1e-5, 1.0, 1e-3, 1e3,
+                         0, 0, 2.0, 0.3, 0, 0.1, p, p, p, p, 1 << 30, 2, 8, 4, 16, None)
+    assert rc == _lib.EACS_ERR_INVALID
+    rc = L.eacs_cell_fwd(p, p, p, 0, p, p, p, p, p, p, 0.1, 1e-6, 1e-5, 1.0, 1e-3, 1e3,
+                         0, 0, 2.0, 0.3, 3, 0.1, p, p, p, p, 1 << 30, 2, 8, 4, 16, None)
+    assert rc == _lib.EACS_ERR_INVALID
+
+
+def test_empty_shapes_are_noops():
+    L = _lib.lib()
+    assert L.eacs_scan_fwd(None, None, None, 0, 5, 3, 2, None) == _lib.EACS_OK
+    assert L.eacs_scan_bwd(None, None, None, None, None, 2, 0, 3, 2, None) == _lib.EACS_OK
+    assert L.eacs_ssm_fwd(None, None, None, None, None, None, 0, None, None, 2, 0, 3, 2,
+                          1e-3, 1e3, None) == _lib.EACS_OK
+
+
+def test_python_ops_reject_cpu_tensors():
+    from eacs_b200.ops.eacs_gated_scan import eacs_cell_forward
+    from eacs_b200.ops.scan_cuda import EXT
+    a = torch.zeros(1, 2, 3, 4, dtype=torch.complex64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        EXT.scan_fwd(a, a)
+    H, N = 3, 4
+    z = torch.zeros(H)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        eacs_cell_forward(torch.zeros(H, N, dtype=torch.complex64), z, torch.zeros(1, 2, H),
+                          torch.zeros(1, 2, N, dtype=torch.complex64),
+                          torch.zeros(1, 2, N, dtype=torch.complex64), torch.zeros(1, 2), z, z, z,
+                          0.1, 1e-6)
