@@ -292,6 +292,9 @@ def run_ours(args):
           for _ in range(args.steps)]
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
+    for a, b in kev:  # torch creates the CUDA event at its first record
+        a.record()
+        b.record()
     barrier()
     torch.cuda.synchronize()
     sampler.load = True
