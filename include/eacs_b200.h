@@ -119,6 +119,36 @@ EACS_API int eacs_cell_fwd(const void* lam, const float* log_dt, const void* u, 
                   void* workspace, size_t workspace_bytes,
                   int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
 
+/* Bytes of the library-owned scratch array behind eacs_cell_fwd_noalloc. */
+#define EACS_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* eacs_cell_fwd without a workspace argument: the gated cell's scratch
+ * (residual partials, row state, committed state) lives in a file-scope
+ * __device__ array of EACS_NOALLOC_SCRATCH_BYTES (32 MiB) inside the library,
+ * for callers that cannot allocate device memory -- a host that binds only
+ * this C ABI with no device allocator of its own, or a process whose device
+ * memory belongs to another allocator and must not see a cudaMalloc (which
+ * also synchronises the device).  No counterpart in the reference.
+ * Nothing is allocated by this call; the array is created when the library's
+ * device code is loaded and every GPU that loads it keeps it until exit.
+ * The first call on each device looks up the array's device address (with
+ * that device current); make that first call before any stream capture.
+ * Sizes whose scratch (eacs_cell_fwd_workspace_size) exceeds the array are
+ * rejected with EACS_ERR_WORKSPACE.  All calls share the one array per device
+ * and it keeps the last call's contents (every byte a call reads it writes
+ * first in that call), so calls that overlap on the GPU -- on different
+ * streams or host threads of the same device -- race; serialise them.
+ * Arguments and outputs are those of eacs_cell_fwd. */
+EACS_API int eacs_cell_fwd_noalloc(const void* lam, const float* log_dt, const void* u,
+                                   int u_dtype, const void* Bc, const void* Cc,
+                                   const float* t, const float* D, const float* mean,
+                                   const float* var, float eps, float eta, float var_eps,
+                                   float dt_init, float dt_min, float dt_max,
+                                   int robust, int robust_k, float spike_ratio,
+                                   float eps_factor, int gate_mode, float temperature,
+                                   float* y, float* gate, float* resid,
+                                   int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

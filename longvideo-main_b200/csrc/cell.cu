@@ -22,6 +22,7 @@
 // Frames with every step committing (update rate 1.0, the common case on
 // N(0,1) features) cost one pass of step 1.
 #include <algorithm>
+#include <mutex>
 
 #include "eacs_common.cuh"
 #include "eacs_host.h"
@@ -705,5 +706,54 @@ int ssm_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc
 }
 
 cudaError_t cell_read_status(int* out, cudaStream_t stream) { return read_clear_status(out, stream); }
+
+// ---------------------------------------------------------------------------
+// Gated cell with library-owned scratch, for callers that cannot allocate
+// device memory: a host that binds only this C ABI and has no device
+// allocator of its own, or a process whose device memory belongs to another
+// allocator (a framework's pool) where a stray cudaMalloc -- which also
+// synchronises the device -- is not allowed.  The scratch is this file-scope
+// array: every GPU that loads the library holds EACS_NOALLOC_SCRATCH_BYTES of
+// it until the process exits.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_cell_scratch[EACS_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+}  // namespace
+
+int cell_fwd_noalloc(const CellCall& c, cudaStream_t stream) {
+    const char* fn = "eacs_cell_fwd_noalloc";
+    const size_t need = cell_workspace_size(c.B, c.L, c.H, c.N);
+    if (need > EACS_NOALLOC_SCRATCH_BYTES)
+        return fail(EACS_ERR_WORKSPACE,
+                    "%s: B=%lld L=%lld H=%lld N=%lld needs %zu bytes of scratch, more than the "
+                    "%zu-byte static array; use eacs_cell_fwd with a caller workspace",
+                    fn, (long long)c.B, (long long)c.L, (long long)c.H, (long long)c.N, need,
+                    static_cast<size_t>(EACS_NOALLOC_SCRATCH_BYTES));
+    int dev = 0;
+    int rc = cuda_check(cudaGetDevice(&dev), fn);
+    if (rc) return rc;
+    if (dev < 0 || dev >= kMaxDevices) return fail(EACS_ERR_UNSUPPORTED, "%s: device %d", fn, dev);
+    void* scratch = nullptr;
+    {
+        // Set-up, once per device with that device current: the host-side name
+        // g_cell_scratch is a stand-in, not a device address.
+        std::lock_guard<std::mutex> lock(g_scratch_mu);
+        if (!g_scratch_addr[dev]) {
+            void* p = nullptr;
+            rc = cuda_check(cudaGetSymbolAddress(&p, g_cell_scratch), fn);
+            if (rc) return rc;
+            g_scratch_addr[dev] = p;
+        }
+        scratch = g_scratch_addr[dev];
+    }
+    CellCall c2 = c;
+    c2.workspace = scratch;
+    c2.workspace_bytes = EACS_NOALLOC_SCRATCH_BYTES;
+    return cell_fwd(c2, stream);
+}
 
 }  // namespace eacs

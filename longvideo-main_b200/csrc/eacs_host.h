@@ -52,6 +52,7 @@ struct CellCall {
 };
 size_t cell_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
 int cell_fwd(const CellCall& c, cudaStream_t stream);
+int cell_fwd_noalloc(const CellCall& c, cudaStream_t stream);
 int ssm_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc,
             const void* Cc, const void* u, int u_dtype, const float* D, float* y, int64_t B,
             int64_t L, int64_t H, int64_t N, float dt_min, float dt_max, cudaStream_t stream);
