@@ -81,6 +81,16 @@ EACS_API int eacs_scan_bwd(const void* a, const void* h, const void* grad_h,
                   void* grad_a, void* grad_b,
                   int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
 
+/* Zero-order-hold discretisation kernels: for lam (H,N) complex64 and
+ * dt (M,H) float32, dA = exp(lam dt) and dB_bar = expm1(lam dt) / lam, each
+ * (M,H,N) complex64, with expm1 in the branch-free form of
+ * cst_ssm/ops/discretization.py:10-17.
+ * Replaces zoh_kernels(lam, dt) -> (dA, dB_bar) (ops/discretization.py:20-36)
+ * for callers that want the discretisation materialised; the fused kernels
+ * below compute the same values in registers. */
+EACS_API int eacs_zoh_kernels(const void* lam, const float* dt, void* dA, void* dB_bar,
+                              int64_t M, int64_t H, int64_t N, void* stream);
+
 /* Fused ungated continuous SSM core (ContinuousSSMLayer.forward,
  * cst_ssm/modules/continuous_ssm.py:44-55 with ops/discretization.py:20-82):
  * dt from timestamp differences (dt_0 = dt_1), ZOH discretisation, scan and

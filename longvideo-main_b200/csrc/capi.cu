@@ -84,6 +84,11 @@ int eacs_ssm_fwd(const void* lam, const float* log_dt, const float* t, const voi
                          static_cast<cudaStream_t>(stream));
 }
 
+int eacs_zoh_kernels(const void* lam, const float* dt, void* dA, void* dB_bar, int64_t M, int64_t H,
+                     int64_t N, void* stream) {
+    return eacs::zoh_kernels(lam, dt, dA, dB_bar, M, H, N, static_cast<cudaStream_t>(stream));
+}
+
 size_t eacs_cell_fwd_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
     return eacs::cell_workspace_size(B, L, H, N);
 }

@@ -62,15 +62,66 @@ struct Args {
 };
 
 // ---------------------------------------------------------------------------
+// Transposed shuffle butterfly over the LANES lanes of a channel group.  A lane
+// enters with V partial sums; at each of the first log2(min(V, LANES)) levels
+// it keeps half of its values and trades the other half with its partner, so V
+// sums cost V-1 shuffles instead of V*log2(LANES).  Afterwards lane ln holds
+// the full sums of original indices held_index(ln) .. + V_REM-1; lanes that
+// differ only in the bits of the plain levels hold the same sums.
+// ---------------------------------------------------------------------------
+template <int V, int O>
+struct Bfly {
+    static __device__ __forceinline__ void run(float* v, int ln) {
+        if constexpr (O == 0) {
+            return;
+        } else if constexpr (V == 1) {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], O);
+            Bfly<1, O / 2>::run(v, ln);
+        } else {
+            const bool up = (ln & O) != 0;
+#pragma unroll
+            for (int k = 0; k < V / 2; ++k) {
+                const float send = up ? v[k] : v[k + V / 2];
+                const float keep = up ? v[k + V / 2] : v[k];
+                v[k] = keep + __shfl_xor_sync(0xffffffffu, send, O);
+            }
+            Bfly<V / 2, O / 2>::run(v, ln);
+        }
+    }
+};
+
+template <int V, int LANES>
+struct BflyShape {
+    static constexpr int levels(int v, int o) { return (o == 0 || v == 1) ? 0 : 1 + levels(v / 2, o / 2); }
+    static constexpr int kHalve = levels(V, LANES / 2);
+    static constexpr int kRem = V >> kHalve;                  // sums held per lane
+    static constexpr int kPlainMask = (LANES >> kHalve) - 1;  // bits of the plain levels
+    static __device__ __forceinline__ int held_index(int ln) {
+        int idx = 0;
+#pragma unroll
+        for (int j = 0; j < kHalve; ++j)
+            if (ln & (LANES >> (j + 1))) idx += V >> (j + 1);
+        return idx;
+    }
+};
+
+// ---------------------------------------------------------------------------
 // 1 / 4: chain kernel.  Thread (hl, ln) of a CTA owns chains n = ln + LANES*j
-// (j < NPT) of channel h = tile*HT + hl; the n-sum of the readouts is a
-// shuffle butterfly inside the LANES-wide group.
+// (j < NPT) of channel h = tile*HT + hl.  Steps run in groups of U: the U
+// discretisations are independent (the state enters only through two complex
+// FMAs per step), and the 2U readout sums of a group (y and y_hat) share one
+// transposed butterfly, after which the per-channel residual work of the U
+// steps is spread over the group's lanes instead of repeated by every lane.
 // ---------------------------------------------------------------------------
 template <int LANES, int NPT, int MODE, typename UT>
 __global__ void __launch_bounds__(kThreads, (NPT == 1 ? 6 : 4)) cell_chain(Args a) {
     constexpr int HT = kThreads / LANES;
     constexpr int NP = LANES * NPT;
     constexpr int NW = kThreads / 32;
+    constexpr int U = 4;
+    constexpr int NV = MODE == SPEC ? 2 * U : U;  // readout sums per group
+    using Shape = BflyShape<NV, LANES>;
+    static_assert(kT % U == 0, "chunk must hold whole step groups");
     __shared__ float2 sB[kT][NP];
     __shared__ float2 sC[kT][NP];
     __shared__ float su[kT][HT];
@@ -118,6 +169,8 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? 6 : 4)) cell_chain(Args 
     float t_prev = t0 - a.dt_init;
     float dt0 = 0.f;  // ungated: dt_0 = dt_1 (continuous_ssm.py:45-48)
     if (MODE == UNGATED && L > 1) dt0 = fmaxf(a.t[rowLH + 1] - t0, 0.f);
+    const int held = Shape::held_index(ln);
+    const bool writer = (ln & Shape::kPlainMask) == 0;
 
     for (int l0 = 0; l0 < lstop; l0 += kT) {
         const int steps = min(kT, lstop - l0);
@@ -135,69 +188,89 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? 6 : 4)) cell_chain(Args 
         for (int i = tid; i < steps; i += kThreads) st[i] = a.t[rowLH + l0 + i];
         __syncthreads();
 
-        for (int i = 0; i < steps; ++i) {
-            const float tl = st[i];
-            float delta;
-            if (MODE == UNGATED)
-                delta = (l0 + i == 0) ? dt0 : fmaxf(tl - t_prev, 0.f);
-            else
-                delta = fmaxf(tl - t_prev, 0.f);
-            const float dte = eff_dt(delta, scale, a.dt_min, a.dt_max);
-            const float ul = su[i][hl];
-            float yp = 0.f, yhp = 0.f;
+        for (int i0 = 0; i0 < steps; i0 += U) {
+            float vals[NV];
 #pragma unroll
-            for (int j = 0; j < NPT; ++j) {
-                if (!nv[j]) continue;
-                const int n = ln + LANES * j;
-                float2 dA, dB;
-                zoh(lam[j], ilam[j], dte, dA, dB);
-                const float2 Bl = sB[i][n];
-                const float2 P = cmul(dA, hs[j]);
-                const float2 qc = cmul(dB, Bl);
-                hs[j] = make_float2(fmaf(qc.x, ul, P.x), fmaf(qc.y, ul, P.y));
-                if (MODE != REPLAY) {
-                    const float2 Cl = sC[i][n];
-                    yp += cre_mul(Cl, hs[j]);
-                    if (MODE == SPEC) {
-                        const float2 qp = cmul(dB, Bp[j]);
-                        const float2 xh = make_float2(fmaf(qp.x, u_prev, P.x), fmaf(qp.y, u_prev, P.y));
-                        yhp += cre_mul(Cp[j], xh);
-                        Bp[j] = Bl;
-                        Cp[j] = Cl;
+            for (int uu = 0; uu < U; ++uu) {
+                const int i = i0 + uu;
+                const bool act = i < steps;  // uniform over the CTA
+                const float tl = act ? st[i] : t_prev;
+                const float ul = act ? su[i][hl] : 0.f;
+                float delta;
+                if (MODE == UNGATED)
+                    delta = (l0 + i == 0) ? dt0 : fmaxf(tl - t_prev, 0.f);
+                else
+                    delta = fmaxf(tl - t_prev, 0.f);
+                const float dte = eff_dt(delta, scale, a.dt_min, a.dt_max);
+                float yp = 0.f, yhp = 0.f;
+#pragma unroll
+                for (int j = 0; j < NPT; ++j) {
+                    if (!nv[j] || !act) continue;
+                    const int n = ln + LANES * j;
+                    float2 dA, dB;
+                    zoh(lam[j], ilam[j], dte, dA, dB);
+                    const float2 Bl = sB[i][n];
+                    const float2 P = cmul(dA, hs[j]);
+                    const float2 qc = cmul(dB, Bl);
+                    hs[j] = make_float2(fmaf(qc.x, ul, P.x), fmaf(qc.y, ul, P.y));
+                    if (MODE != REPLAY) {
+                        const float2 Cl = sC[i][n];
+                        yp += cre_mul(Cl, hs[j]);
+                        if (MODE == SPEC) {
+                            const float2 qp = cmul(dB, Bp[j]);
+                            const float2 xh = make_float2(fmaf(qp.x, u_prev, P.x), fmaf(qp.y, u_prev, P.y));
+                            yhp += cre_mul(Cp[j], xh);
+                            Bp[j] = Bl;
+                            Cp[j] = Cl;
+                        }
                     }
+                }
+                vals[uu] = yp;
+                if (MODE == SPEC) vals[U + uu] = yhp;
+                if (act) {
+                    u_prev = ul;
+                    t_prev = tl;
+                }
+            }
+            if (MODE == REPLAY) continue;
+            Bfly<NV, LANES / 2>::run(vals, ln);
+            float r1[Shape::kRem], r2[Shape::kRem];
+#pragma unroll
+            for (int k = 0; k < Shape::kRem; ++k) {
+                r1[k] = 0.f;
+                r2[k] = 0.f;
+                const int orig = held + k;
+                const int i = i0 + (orig % U);
+                if (orig < U) {  // output readout of step i
+                    if (writer && hv && i < steps) sy[i][hl] = vals[k] + Dh * su[i][hl];
+                } else if (MODE == SPEC && writer && hv && i < steps) {  // prediction of step i
+                    const float ul = su[i][hl];
+                    const float obs = (ul - mu) / sd;
+                    const float pred = (vals[k] - mu) / sd;
+                    const float d = obs - pred;
+                    r1[k] = d * d;
+                    r2[k] = obs * obs;
                 }
             }
             if (MODE == SPEC) {
-                // Halving butterfly: lower half of the group ends with sum(yp),
-                // upper half with sum(yhp).
-                const bool up = (ln & (LANES / 2)) != 0;
-                const float send = up ? yp : yhp;
-                float v = (up ? yhp : yp) + __shfl_xor_sync(0xffffffffu, send, LANES / 2);
-#pragma unroll
-                for (int o = LANES / 4; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (ln == 0 && hv) sy[i][hl] = v + Dh * ul;
-                float v1 = 0.f, v2 = 0.f;
-                if (ln == LANES / 2 && hv) {
-                    const float obs = (ul - mu) / sd;
-                    const float pred = (v - mu) / sd;
-                    const float d = obs - pred;
-                    v1 = d * d;
-                    v2 = obs * obs;
-                }
+                // sum over the channel groups of the warp (lanes with equal ln hold the same step)
 #pragma unroll
                 for (int o = LANES; o < 32; o <<= 1) {
-                    v1 += __shfl_xor_sync(0xffffffffu, v1, o);
-                    v2 += __shfl_xor_sync(0xffffffffu, v2, o);
-                }
-                if ((tid & 31) == LANES / 2) sred[i][tid >> 5] = make_float2(v1, v2);
-            } else if (MODE == UNGATED) {
-                float v = yp;
 #pragma unroll
-                for (int o = LANES / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (ln == 0 && hv) sy[i][hl] = v + Dh * ul;
+                    for (int k = 0; k < Shape::kRem; ++k) {
+                        r1[k] += __shfl_xor_sync(0xffffffffu, r1[k], o);
+                        r2[k] += __shfl_xor_sync(0xffffffffu, r2[k], o);
+                    }
+                }
+                if ((tid & 31) < LANES && writer) {
+#pragma unroll
+                    for (int k = 0; k < Shape::kRem; ++k) {
+                        const int orig = held + k;
+                        const int i = i0 + (orig % U);
+                        if (orig >= U && i < steps) sred[i][tid >> 5] = make_float2(r1[k], r2[k]);
+                    }
+                }
             }
-            u_prev = ul;
-            t_prev = tl;
         }
         if (MODE != REPLAY) {
             __syncthreads();
@@ -504,6 +577,26 @@ __global__ void __launch_bounds__(kRepair) cell_repair(Args a) {
 }
 
 // ---------------------------------------------------------------------------
+// zoh_kernels (discretization.py:20-36) on its own: dt (M,H) -> dA, dB_bar
+// (M,H,N).  One thread per output element.
+// ---------------------------------------------------------------------------
+__global__ void zoh_kernels_k(const float2* __restrict__ lam, const float* __restrict__ dt,
+                              float2* __restrict__ dA, float2* __restrict__ dB, int64_t M, int H,
+                              int N) {
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t HN = static_cast<int64_t>(H) * N;
+    if (idx >= M * HN) return;
+    const int64_t m = idx / HN;
+    const int64_t hn = idx - m * HN;
+    const int hh = static_cast<int>(hn / N);
+    const float2 lm = lam[hn];
+    float2 a_, b_;
+    zoh(lm, crecip(lm), dt[m * H + hh], a_, b_);
+    dA[idx] = a_;
+    dB[idx] = b_;
+}
+
+// ---------------------------------------------------------------------------
 // dispatch
 // ---------------------------------------------------------------------------
 int lanes_for(int N, int* lanes, int* npt) {
@@ -706,6 +799,22 @@ int ssm_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc
 }
 
 cudaError_t cell_read_status(int* out, cudaStream_t stream) { return read_clear_status(out, stream); }
+
+int zoh_kernels(const void* lam, const float* dt, void* dA, void* dBbar, int64_t M, int64_t H,
+                int64_t N, cudaStream_t stream) {
+    const char* fn = "eacs_zoh_kernels";
+    if (M < 0 || H < 0 || N < 0) return fail(EACS_ERR_INVALID, "%s: negative size", fn);
+    const int64_t n = M * H * N;
+    if (n == 0) return EACS_OK;
+    if (!lam || !dt || !dA || !dBbar) return fail(EACS_ERR_INVALID, "%s: null pointer", fn);
+    if (H > (1LL << 30) || N > (1LL << 30) || (n + 255) / 256 > 0x7fffffffLL)
+        return fail(EACS_ERR_UNSUPPORTED, "%s: too large", fn);
+    zoh_kernels_k<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
+        static_cast<const float2*>(lam), dt, static_cast<float2*>(dA), static_cast<float2*>(dBbar), M,
+        static_cast<int>(H), static_cast<int>(N));
+    note_launch();
+    return cuda_check(cudaGetLastError(), fn);
+}
 
 // ---------------------------------------------------------------------------
 // Gated cell with library-owned scratch, for callers that cannot allocate

@@ -57,5 +57,7 @@ int ssm_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc
             const void* Cc, const void* u, int u_dtype, const float* D, float* y, int64_t B,
             int64_t L, int64_t H, int64_t N, float dt_min, float dt_max, cudaStream_t stream);
 cudaError_t cell_read_status(int* out, cudaStream_t stream);
+int zoh_kernels(const void* lam, const float* dt, void* dA, void* dBbar, int64_t M, int64_t H,
+                int64_t N, cudaStream_t stream);
 
 }  // namespace eacs

@@ -38,6 +38,7 @@ SIGNATURES = {
     "eacs_scan_fwd": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "eacs_scan_bwd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "eacs_ssm_fwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _P, _P, _I64, _I64, _I64, _I64, _F, _F, _P]),
+    "eacs_zoh_kernels": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "eacs_cell_fwd_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I64, _I64]),
     "eacs_cell_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
                            _F, _F, _F, _F, _F, _F, _I, _I, _F, _F, _I, _F,
