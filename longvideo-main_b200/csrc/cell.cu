@@ -30,8 +30,15 @@
 namespace eacs {
 namespace {
 
-constexpr int kThreads = 128;  // chain kernel CTA
-constexpr int kT = 32;         // steps per staged chunk
+#ifndef EACS_CHAIN_THREADS
+#define EACS_CHAIN_THREADS 64
+#endif
+#ifndef EACS_CHAIN_U
+#define EACS_CHAIN_U 4
+#endif
+constexpr int kThreads = EACS_CHAIN_THREADS;  // chain kernel CTA
+constexpr int kMinBlocks = 768 / kThreads;    // keep 24 warps per SM resident
+constexpr int kT = 32;                         // steps per staged chunk
 constexpr int kRepair = 1024;  // repair kernel CTA
 
 enum Mode { SPEC = 0, UNGATED = 1, REPLAY = 2 };
@@ -114,11 +121,11 @@ struct BflyShape {
 // steps is spread over the group's lanes instead of repeated by every lane.
 // ---------------------------------------------------------------------------
 template <int LANES, int NPT, int MODE, typename UT>
-__global__ void __launch_bounds__(kThreads, (NPT == 1 ? 6 : 4)) cell_chain(Args a) {
+__global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks * 2 / 3)) cell_chain(Args a) {
     constexpr int HT = kThreads / LANES;
     constexpr int NP = LANES * NPT;
     constexpr int NW = kThreads / 32;
-    constexpr int U = 4;
+    constexpr int U = EACS_CHAIN_U;
     constexpr int NV = MODE == SPEC ? 2 * U : U;  // readout sums per group
     using Shape = BflyShape<NV, LANES>;
     static_assert(kT % U == 0, "chunk must hold whole step groups");
@@ -161,7 +168,9 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? 6 : 4)) cell_chain(Args 
         Cp[j] = nv[j] ? a.Cc[rowLH * N + n] : make_float2(0.f, 0.f);
     }
     const float scale = hv ? expf(a.log_dt[h]) : 1.f;
-    const float sd = hv ? sqrtf(a.var[h] + a.var_eps) : 1.f;
+    // 1/sqrt(var + var_eps): the residual standardises with a multiply
+    // (within one rounding of the reference's division)
+    const float rsd = hv ? 1.0f / sqrtf(a.var[h] + a.var_eps) : 1.f;
     const float mu = hv ? a.mean[h] : 0.f;
     const float Dh = hv ? a.D[h] : 0.f;
     float u_prev = hv ? to_f32(u[rowLH * H + h]) : 0.f;
@@ -175,14 +184,16 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? 6 : 4)) cell_chain(Args 
     for (int l0 = 0; l0 < lstop; l0 += kT) {
         const int steps = min(kT, lstop - l0);
         __syncthreads();
-        for (int idx = tid; idx < steps * N; idx += kThreads) {
-            const int i = idx / N, n = idx - (idx / N) * N;
-            const size_t o = (rowLH + l0 + i) * N + n;
-            sB[i][n] = a.Bc[o];
-            sC[i][n] = a.Cc[o];
+        for (int idx = tid; idx < steps * NP; idx += kThreads) {
+            const int i = idx / NP, n = idx % NP;  // NP, HT are powers of two
+            if (n < N) {
+                const size_t o = (rowLH + l0 + i) * N + n;
+                sB[i][n] = a.Bc[o];
+                sC[i][n] = a.Cc[o];
+            }
         }
         for (int idx = tid; idx < steps * HT; idx += kThreads) {
-            const int i = idx / HT, k = idx - (idx / HT) * HT;
+            const int i = idx / HT, k = idx % HT;
             su[i][k] = (h0 + k < H) ? to_f32(u[(rowLH + l0 + i) * H + h0 + k]) : 0.f;
         }
         for (int i = tid; i < steps; i += kThreads) st[i] = a.t[rowLH + l0 + i];
@@ -193,7 +204,10 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? 6 : 4)) cell_chain(Args 
 #pragma unroll
             for (int uu = 0; uu < U; ++uu) {
                 const int i = i0 + uu;
-                const bool act = i < steps;  // uniform over the CTA
+                // Steps past the end of the last chunk only matter to REPLAY,
+                // whose final state is kept; elsewhere they compute values that
+                // are never stored (each butterfly sum stays within its step).
+                const bool act = MODE == REPLAY ? i < steps : true;
                 const float tl = act ? st[i] : t_prev;
                 const float ul = act ? su[i][hl] : 0.f;
                 float delta;
@@ -245,8 +259,8 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? 6 : 4)) cell_chain(Args 
                     if (writer && hv && i < steps) sy[i][hl] = vals[k] + Dh * su[i][hl];
                 } else if (MODE == SPEC && writer && hv && i < steps) {  // prediction of step i
                     const float ul = su[i][hl];
-                    const float obs = (ul - mu) / sd;
-                    const float pred = (vals[k] - mu) / sd;
+                    const float obs = (ul - mu) * rsd;
+                    const float pred = (vals[k] - mu) * rsd;
                     const float d = obs - pred;
                     r1[k] = d * d;
                     r2[k] = obs * obs;
@@ -275,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? 6 : 4)) cell_chain(Args 
         if (MODE != REPLAY) {
             __syncthreads();
             for (int idx = tid; idx < steps * HT; idx += kThreads) {
-                const int i = idx / HT, k = idx - (idx / HT) * HT;
+                const int i = idx / HT, k = idx % HT;
                 if (h0 + k < H) a.y[(rowLH + l0 + i) * H + h0 + k] = sy[i][k];
             }
             if (MODE == SPEC) {

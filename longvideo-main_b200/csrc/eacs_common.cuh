@@ -53,87 +53,75 @@ __device__ __forceinline__ float2 crecip(float2 z) {
     return make_float2(z.x / d, -z.y / d);
 }
 
-// sin and cos of x.  Cody & Waite range reduction, x = k pi/2 + r, with a
-// three-part float split of pi/2 applied by FMA, then the Taylor series of
-// sin to r^9 and cos to r^10 on |r| <= pi/4 (truncation below 2.5e-9
-// relative) and the quadrant rotation by k mod 4.  Beyond |x| = 8192 the
-// three-part split loses accuracy, so CUDA's sincosf (Payne-Hanek reduction)
-// takes over.
-__device__ __forceinline__ void sincos_cw(float x, float& s, float& c) {
-    if (fabsf(x) > 8192.0f) {
-        sincosf(x, &s, &c);
-        return;
-    }
-    const float q = rintf(x * 0.636619772f);  // 2/pi
-    float r = fmaf(-q, 1.57079637e+00f, x);   // pi/2 = hi + mid + lo
-    r = fmaf(-q, -4.37113883e-08f, r);
-    r = fmaf(-q, -1.71512451e-15f, r);
-    const int k = __float2int_rn(q);
-    const float r2 = r * r;
-    // sin r = r + r^3 (-1/3! + r^2 (1/5! + r^2 (-1/7! + r^2 / 9!)))
-    float ps = fmaf(r2, 2.75573192e-06f, -1.98412698e-04f);
-    ps = fmaf(r2, ps, 8.33333333e-03f);
-    ps = fmaf(r2, ps, -1.66666667e-01f);
-    const float sr = fmaf(r * r2, ps, r);
-    // cos r = 1 + r^2 (-1/2! + r^2 (1/4! + r^2 (-1/6! + r^2 (1/8! - r^2 / 10!))))
-    float pc = fmaf(r2, -2.75573192e-07f, 2.48015873e-05f);
-    pc = fmaf(r2, pc, -1.38888889e-03f);
-    pc = fmaf(r2, pc, 4.16666667e-02f);
-    pc = fmaf(r2, pc, -0.5f);
-    const float cr = fmaf(r2, pc, 1.0f);
-    const float ss = (k & 1) ? cr : sr;
-    const float cc = (k & 1) ? sr : cr;
-    s = (k & 2) ? -ss : ss;
-    c = ((k + 1) & 2) ? -cc : cc;
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
-// expm1(a) and exp(a) together by Tang's table-free method: a = k ln2 + r with
-// a two-part float ln2 applied by FMA, |r| <= ln2/2, expm1(r) from its Taylor
-// series to r^8 (truncation below 1e-9 relative), then
-// e^a - 1 = 2^k expm1(r) + (2^k - 1) and e^a = 2^k expm1(r) + 2^k.
-// Below a = -87 the results are exactly -1 and 0, as float expm1 gives there.
+// e^a and e^a - 1.  e^a from the hardware base-2 exponential (about 2^-22
+// relative).  e^a - 1 from it when |a| >= 0.35, where the subtraction loses at
+// most a factor 2.3 of that, and below from the Taylor series of expm1 to a^8
+// (truncation below 3e-10 relative), which keeps small |a| -- the slow modes,
+// where dB_bar ~ dt -- relatively exact.
 __device__ __forceinline__ void expm1_exp(float a, float& em1, float& ea) {
-    const float ac = fminf(fmaxf(a, -87.0f), 88.0f);
-    const float k = rintf(ac * 1.44269502f);  // log2(e)
-    float r = fmaf(-k, 6.93147182e-01f, ac);   // ln2 = hi + lo
-    r = fmaf(-k, -1.90465421e-09f, r);
-    float p = fmaf(r, 2.48015873e-05f, 1.98412698e-04f);  // 1/8!, 1/7!
-    p = fmaf(r, p, 1.38888889e-03f);                      // 1/6!
-    p = fmaf(r, p, 8.33333333e-03f);                      // 1/5!
-    p = fmaf(r, p, 4.16666667e-02f);                      // 1/4!
-    p = fmaf(r, p, 1.66666667e-01f);                      // 1/3!
-    p = fmaf(r, p, 0.5f);                                 // 1/2!
-    p = fmaf(r * r, p, r);                                // expm1(r)
-    const float s2k = __int_as_float((__float2int_rn(k) + 127) << 23);
-    em1 = fmaf(s2k, p, s2k - 1.0f);
-    ea = fmaf(s2k, p, s2k);
-    if (a < -87.0f) {
-        em1 = -1.0f;
-        ea = 0.0f;
+    ea = ex2_approx(a * 1.44269504f);  // log2(e)
+    float p = fmaf(a, 2.48015873e-05f, 1.98412698e-04f);  // 1/8!, 1/7!
+    p = fmaf(a, p, 1.38888889e-03f);                      // 1/6!
+    p = fmaf(a, p, 8.33333333e-03f);                      // 1/5!
+    p = fmaf(a, p, 4.16666667e-02f);                      // 1/4!
+    p = fmaf(a, p, 1.66666667e-01f);                      // 1/3!
+    p = fmaf(a, p, 0.5f);                                 // 1/2!
+    p = fmaf(a * a, p, a);
+    em1 = fabsf(a) < 0.35f ? p : ea - 1.0f;
+}
+
+// sin b, cos b and 2 sin^2(b/2) = 1 - cos b.  Cody & Waite reduction
+// b = 2 pi k + r with a three-part float split of 2 pi applied by FMA
+// (|r| <= pi), then with h = r/2: s = sin h from its Taylor series to h^11
+// (truncation below 6e-8 on |h| <= pi/2, relative near 0) and c = cos h from
+// the hardware cosine (absolute error about 2^-21 on [-pi, pi]); finally
+// sin b = 2 s c, 2 sin^2(b/2) = 2 s^2, cos b = 1 - 2 s^2.  Every error term is
+// proportional to s, so expm1(z) built from these keeps its relative accuracy
+// as |z| -> 0.  |b| > 32768 takes CUDA's sincosf of b/2.
+__device__ __forceinline__ void trig_half(float b, float& sb, float& cb, float& vb) {
+    float s, c;
+    if (fabsf(b) > 32768.0f) {
+        sincosf(0.5f * b, &s, &c);
+    } else {
+        const float k = rintf(b * 0.159154943f);  // 1/(2 pi)
+        float r = fmaf(-k, 6.28318548e+00f, b);    // 2 pi = hi + mid + lo
+        r = fmaf(-k, -1.74845553e-07f, r);
+        r = fmaf(-k, -6.86049804e-15f, r);
+        const float h = 0.5f * r;
+        const float h2 = h * h;
+        // sin h = h + h^3 (-1/3! + h^2 (1/5! + h^2 (-1/7! + h^2 (1/9! - h^2/11!))))
+        float ps = fmaf(h2, -2.50521084e-08f, 2.75573192e-06f);
+        ps = fmaf(h2, ps, -1.98412698e-04f);
+        ps = fmaf(h2, ps, 8.33333333e-03f);
+        ps = fmaf(h2, ps, -1.66666667e-01f);
+        s = fmaf(h * h2, ps, h);
+        c = __cosf(h);
     }
-    if (a != a) em1 = ea = a;  // NaN in, NaN out
+    const float s2 = s + s;
+    sb = s2 * c;
+    vb = s2 * s;
+    cb = 1.0f - vb;
 }
 
 // Zero-order-hold kernels of one chain (discretization.py:20-36):
 //   z = lam * dt,  dA = e^z,  dB_bar = expm1(z) / lam
 // with expm1(z) = (expm1(a) cos b - 2 sin^2(b/2), e^a sin b), the branch-free
-// form of discretization.py:10-17.  sin b and cos b come from the half angle
-// (sin b = 2 s c, cos b = 1 - 2 s^2 with s, c = sin, cos of b/2), so one
-// sincos evaluation serves all three trigonometric terms.
+// form of discretization.py:10-17.
 __device__ __forceinline__ void zoh(float2 lam, float2 ilam, float dte, float2& dA, float2& dBbar) {
     const float a = lam.x * dte;
     const float b = lam.y * dte;
-    float em1, ea;
+    float em1, ea, sb, cb, vb;
     expm1_exp(a, em1, ea);
-    float s, c;
-    sincos_cw(0.5f * b, s, c);
-    const float s2 = s + s;
-    const float sb = s2 * c;
-    const float cb = fmaf(-s2, s, 1.0f);
+    trig_half(b, sb, cb, vb);
     const float im = ea * sb;
     dA = make_float2(ea * cb, im);
-    const float2 E = make_float2(fmaf(em1, cb, -(s2 * s)), im);
-    dBbar = cmul(E, ilam);
+    dBbar = cmul(make_float2(fmaf(em1, cb, -vb), im), ilam);
 }
 
 // effective_dt (discretization.py:63-82): clamp(delta * scale, dt_min, dt_max)

@@ -12,7 +12,8 @@ import threading
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libeacs_b200.so")
+# EACS_B200_LIB may point at another build of the same library.
+LIB_PATH = os.environ.get("EACS_B200_LIB") or os.path.join(_HERE, "libeacs_b200.so")
 
 EACS_OK = 0
 EACS_ERR_INVALID = 1
