@@ -31,7 +31,7 @@ namespace eacs {
 namespace {
 
 #ifndef EACS_CHAIN_THREADS
-#define EACS_CHAIN_THREADS 64
+#define EACS_CHAIN_THREADS 128
 #endif
 #ifndef EACS_CHAIN_U
 #define EACS_CHAIN_U 4
@@ -184,13 +184,13 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
     for (int l0 = 0; l0 < lstop; l0 += kT) {
         const int steps = min(kT, lstop - l0);
         __syncthreads();
+        // padded chains (n >= N) read zeros: with lam = -1 and B = C = 0
+        // their state stays 0 and they add exact zeros, without a branch
         for (int idx = tid; idx < steps * NP; idx += kThreads) {
             const int i = idx / NP, n = idx % NP;  // NP, HT are powers of two
-            if (n < N) {
-                const size_t o = (rowLH + l0 + i) * N + n;
-                sB[i][n] = a.Bc[o];
-                sC[i][n] = a.Cc[o];
-            }
+            const size_t o = (rowLH + l0 + i) * N + n;
+            sB[i][n] = n < N ? a.Bc[o] : make_float2(0.f, 0.f);
+            sC[i][n] = n < N ? a.Cc[o] : make_float2(0.f, 0.f);
         }
         for (int idx = tid; idx < steps * HT; idx += kThreads) {
             const int i = idx / HT, k = idx % HT;
@@ -217,16 +217,21 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                     delta = fmaxf(tl - t_prev, 0.f);
                 const float dte = eff_dt(delta, scale, a.dt_min, a.dt_max);
                 float yp = 0.f, yhp = 0.f;
+                // Branch-free: channels past H stage u = 0 and padded chains
+                // stage B = C = 0, so both keep a zero state and add zeros.
 #pragma unroll
                 for (int j = 0; j < NPT; ++j) {
-                    if (!nv[j] || !act) continue;
                     const int n = ln + LANES * j;
                     float2 dA, dB;
                     zoh(lam[j], ilam[j], dte, dA, dB);
                     const float2 Bl = sB[i][n];
                     const float2 P = cmul(dA, hs[j]);
                     const float2 qc = cmul(dB, Bl);
-                    hs[j] = make_float2(fmaf(qc.x, ul, P.x), fmaf(qc.y, ul, P.y));
+                    const float2 hn = make_float2(fmaf(qc.x, ul, P.x), fmaf(qc.y, ul, P.y));
+                    if (MODE == REPLAY)
+                        hs[j] = act ? hn : hs[j];
+                    else
+                        hs[j] = hn;
                     if (MODE != REPLAY) {
                         const float2 Cl = sC[i][n];
                         yp += cre_mul(Cl, hs[j]);
@@ -613,7 +618,25 @@ __global__ void zoh_kernels_k(const float2* __restrict__ lam, const float* __res
 // ---------------------------------------------------------------------------
 // dispatch
 // ---------------------------------------------------------------------------
+#ifndef EACS_CHAIN_NPT
+#define EACS_CHAIN_NPT 2
+#endif
 int lanes_for(int N, int* lanes, int* npt) {
+    if (EACS_CHAIN_NPT == 4) {
+        if (N <= 16) { *lanes = 4; *npt = 4; }
+        else if (N <= 32) { *lanes = 8; *npt = 4; }
+        else if (N <= 64) { *lanes = 16; *npt = 4; }
+        else return 0;
+        return 1;
+    }
+    if (EACS_CHAIN_NPT == 2) {
+        if (N <= 8) { *lanes = 4; *npt = 2; }
+        else if (N <= 16) { *lanes = 8; *npt = 2; }
+        else if (N <= 32) { *lanes = 16; *npt = 2; }
+        else if (N <= 64) { *lanes = 32; *npt = 2; }
+        else return 0;
+        return 1;
+    }
     if (N <= 4) { *lanes = 4; *npt = 1; }
     else if (N <= 8) { *lanes = 8; *npt = 1; }
     else if (N <= 16) { *lanes = 16; *npt = 1; }
@@ -637,11 +660,22 @@ template <int MODE, typename UT>
 cudaError_t chain_by_n(const Args& a, cudaStream_t s) {
     int lanes, npt;
     lanes_for(a.N, &lanes, &npt);
+#if EACS_CHAIN_NPT == 4
+    if (lanes == 4) return launch_chain<4, 4, MODE, UT>(a, s);
+    if (lanes == 8) return launch_chain<8, 4, MODE, UT>(a, s);
+    return launch_chain<16, 4, MODE, UT>(a, s);
+#elif EACS_CHAIN_NPT == 2
+    if (lanes == 4) return launch_chain<4, 2, MODE, UT>(a, s);
+    if (lanes == 8) return launch_chain<8, 2, MODE, UT>(a, s);
+    if (lanes == 16) return launch_chain<16, 2, MODE, UT>(a, s);
+    return launch_chain<32, 2, MODE, UT>(a, s);
+#else
     if (lanes == 4) return launch_chain<4, 1, MODE, UT>(a, s);
     if (lanes == 8) return launch_chain<8, 1, MODE, UT>(a, s);
     if (lanes == 16) return launch_chain<16, 1, MODE, UT>(a, s);
     if (npt == 1) return launch_chain<32, 1, MODE, UT>(a, s);
     return launch_chain<32, 2, MODE, UT>(a, s);
+#endif
 }
 
 template <int MODE>
@@ -655,6 +689,10 @@ template <typename UT>
 cudaError_t repair_by_n(const Args& a, cudaStream_t s) {
     int lanes, npt;
     lanes_for(a.N, &lanes, &npt);
+    while (npt > 1 && lanes < 32) {  // the repair pass keeps one chain per lane
+        lanes *= 2;
+        npt /= 2;
+    }
     if (lanes == 4) cell_repair<4, 1, UT><<<a.B, kRepair, 0, s>>>(a);
     else if (lanes == 8) cell_repair<8, 1, UT><<<a.B, kRepair, 0, s>>>(a);
     else if (lanes == 16) cell_repair<16, 1, UT><<<a.B, kRepair, 0, s>>>(a);

@@ -78,31 +78,29 @@ __device__ __forceinline__ void expm1_exp(float a, float& em1, float& ea) {
 
 // sin b, cos b and 2 sin^2(b/2) = 1 - cos b.  Cody & Waite reduction
 // b = 2 pi k + r with a three-part float split of 2 pi applied by FMA
-// (|r| <= pi), then with h = r/2: s = sin h from its Taylor series to h^11
-// (truncation below 6e-8 on |h| <= pi/2, relative near 0) and c = cos h from
-// the hardware cosine (absolute error about 2^-21 on [-pi, pi]); finally
-// sin b = 2 s c, 2 sin^2(b/2) = 2 s^2, cos b = 1 - 2 s^2.  Every error term is
-// proportional to s, so expm1(z) built from these keeps its relative accuracy
-// as |z| -> 0.  |b| > 32768 takes CUDA's sincosf of b/2.
+// (|r| <= pi; each FMA rounds once, so r keeps an absolute error near
+// ulp(pi) and stays relatively exact when small while |k| < ~1e4, and
+// absolutely within ~1e-7 up to |b| ~ 1e6), then with h = r/2:
+// s = sin h from its Taylor series to h^11 (truncation below 6e-8 on
+// |h| <= pi/2, relative near 0) and c = cos h from the hardware cosine
+// (absolute error about 2^-21 on [-pi, pi]); finally sin b = 2 s c,
+// 2 sin^2(b/2) = 2 s^2, cos b = 1 - 2 s^2.  Every error term is proportional
+// to s, so expm1(z) built from these keeps its relative accuracy as |z| -> 0.
+// Branch-free, so unrolled steps and chains interleave.
 __device__ __forceinline__ void trig_half(float b, float& sb, float& cb, float& vb) {
-    float s, c;
-    if (fabsf(b) > 32768.0f) {
-        sincosf(0.5f * b, &s, &c);
-    } else {
-        const float k = rintf(b * 0.159154943f);  // 1/(2 pi)
-        float r = fmaf(-k, 6.28318548e+00f, b);    // 2 pi = hi + mid + lo
-        r = fmaf(-k, -1.74845553e-07f, r);
-        r = fmaf(-k, -6.86049804e-15f, r);
-        const float h = 0.5f * r;
-        const float h2 = h * h;
-        // sin h = h + h^3 (-1/3! + h^2 (1/5! + h^2 (-1/7! + h^2 (1/9! - h^2/11!))))
-        float ps = fmaf(h2, -2.50521084e-08f, 2.75573192e-06f);
-        ps = fmaf(h2, ps, -1.98412698e-04f);
-        ps = fmaf(h2, ps, 8.33333333e-03f);
-        ps = fmaf(h2, ps, -1.66666667e-01f);
-        s = fmaf(h * h2, ps, h);
-        c = __cosf(h);
-    }
+    const float k = rintf(b * 0.159154943f);  // 1/(2 pi)
+    float r = fmaf(-k, 6.28318548e+00f, b);    // 2 pi = hi + mid + lo
+    r = fmaf(-k, -1.74845553e-07f, r);
+    r = fmaf(-k, -6.86049804e-15f, r);
+    const float h = 0.5f * r;
+    const float h2 = h * h;
+    // sin h = h + h^3 (-1/3! + h^2 (1/5! + h^2 (-1/7! + h^2 (1/9! - h^2/11!))))
+    float ps = fmaf(h2, -2.50521084e-08f, 2.75573192e-06f);
+    ps = fmaf(h2, ps, -1.98412698e-04f);
+    ps = fmaf(h2, ps, 8.33333333e-03f);
+    ps = fmaf(h2, ps, -1.66666667e-01f);
+    const float s = fmaf(h * h2, ps, h);
+    const float c = __cosf(h);
     const float s2 = s + s;
     sb = s2 * c;
     vb = s2 * s;
