@@ -129,6 +129,50 @@ EACS_API int eacs_cell_fwd(const void* lam, const float* log_dt, const void* u, 
                   void* workspace, size_t workspace_bytes,
                   int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
 
+/* Training forward of the gated cell: eacs_cell_fwd plus, in `stats`
+ * (B,L,2) float32, the two norms of each step's residual
+ * (||obs - pred||, ||obs||) that the backward needs.  gate_mode 0 gives the
+ * straight-through forward (hard gate values), 1 the soft gate.
+ * Replaces the forward of GatedEACSCellFunction
+ * (cst_ssm/ops/eacs_cell_train.py:81-115: ys, gs, rs; its fourth output, the
+ * stop-target innovation, has the values of rs). */
+EACS_API int eacs_cell_train_fwd(const void* lam, const float* log_dt, const void* u, int u_dtype,
+                                 const void* Bc, const void* Cc, const float* t, const float* D,
+                                 const float* mean, const float* var,
+                                 float eps, float eta, float var_eps, float dt_init,
+                                 float dt_min, float dt_max, int gate_mode, float temperature,
+                                 float* y, float* gate, float* resid, float* stats,
+                                 void* workspace, size_t workspace_bytes,
+                                 int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
+
+/* Workspace bytes eacs_cell_train_bwd needs for these sizes (0 if the sizes
+ * are unsupported). */
+EACS_API size_t eacs_cell_train_bwd_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+
+/* Backward of the gated cell: the vector-Jacobian product of the whole L-step
+ * scan with the forward's gate values pinned (STE) or soft.
+ * Replaces GatedEACSCellFunction.backward (cst_ssm/ops/eacs_cell_train.py:
+ * 117-175).  Inputs are the forward's inputs and its gate, resid and stats
+ * outputs, and the upstream gradients gy (B,L,H) and ggs, grs, gns (B,L) of
+ * ys, gs, rs and the innovation (each of the last three may be NULL = 0).
+ * Outputs (overwritten, float32 / complex64): du (B,L,H), dBc, dCc (B,L,N),
+ * dt (B,L), dlam (H,N), dlog_dt (H), dD (H), deps (1).  temperature is T of
+ * sigmoid((r - eps)/max(T, 1e-4)).  Rows are handled by one thread-block
+ * cluster of up to 16 CTAs of at most 512 threads (H*lanes <= 8192, lanes = 8
+ * for N <= 16, 16 for N <= 32, 32 for N <= 64). */
+EACS_API int eacs_cell_train_bwd(const void* lam, const float* log_dt, const void* u, int u_dtype,
+                                 const void* Bc, const void* Cc, const float* t, const float* D,
+                                 const float* mean, const float* var,
+                                 float eps, float eta, float var_eps, float dt_init,
+                                 float dt_min, float dt_max, float temperature,
+                                 const float* gate, const float* resid, const float* stats,
+                                 const float* gy, const float* ggs, const float* grs,
+                                 const float* gns,
+                                 float* du, void* dBc, void* dCc, float* dt, void* dlam,
+                                 float* dlog_dt, float* dD, float* deps,
+                                 void* workspace, size_t workspace_bytes,
+                                 int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
+
 /* Bytes of the library-owned scratch array behind eacs_cell_fwd_noalloc. */
 #define EACS_NOALLOC_SCRATCH_BYTES (32u << 20)
 

@@ -61,7 +61,10 @@ int eacs_device_status(int* status, void* stream) {
     if (rc) return rc;
     rc = eacs::cuda_check(eacs::cell_read_status(&b, s), "eacs_device_status");
     if (rc) return rc;
-    *status = a ? a : b;
+    int c = 0;
+    rc = eacs::cuda_check(eacs::train_read_status(&c, s), "eacs_device_status");
+    if (rc) return rc;
+    *status = a ? a : (b ? b : c);
     return EACS_OK;
 }
 
@@ -104,6 +107,43 @@ int eacs_cell_fwd(const void* lam, const float* log_dt, const void* u, int u_dty
                      robust, robust_k, spike_ratio, eps_factor, gate_mode, temperature, y, gate,
                      resid, workspace, workspace_bytes, B, L, H, N};
     return eacs::cell_fwd(c, static_cast<cudaStream_t>(stream));
+}
+
+int eacs_cell_train_fwd(const void* lam, const float* log_dt, const void* u, int u_dtype, const void* Bc,
+                        const void* Cc, const float* t, const float* D, const float* mean,
+                        const float* var, float eps, float eta, float var_eps, float dt_init,
+                        float dt_min, float dt_max, int gate_mode, float temperature, float* y,
+                        float* gate, float* resid, float* stats, void* workspace,
+                        size_t workspace_bytes, int64_t B, int64_t L, int64_t H, int64_t N,
+                        void* stream) {
+    if (!stats) return eacs::fail(EACS_ERR_INVALID, "eacs_cell_train_fwd: null stats");
+    eacs::CellCall c{lam,  log_dt, u,       u_dtype, Bc,     Cc,      t,      D,
+                     mean, var,    eps,     eta,     var_eps, dt_init, dt_min, dt_max,
+                     0,    3,      2.0f,    0.3f,    gate_mode, temperature, y, gate,
+                     resid, workspace, workspace_bytes, B, L, H, N};
+    c.stats = stats;
+    return eacs::cell_fwd(c, static_cast<cudaStream_t>(stream));
+}
+
+size_t eacs_cell_train_bwd_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
+    return eacs::train_workspace_size(B, L, H, N);
+}
+
+int eacs_cell_train_bwd(const void* lam, const float* log_dt, const void* u, int u_dtype, const void* Bc,
+                        const void* Cc, const float* t, const float* D, const float* mean,
+                        const float* var, float eps, float eta, float var_eps, float dt_init,
+                        float dt_min, float dt_max, float temperature, const float* gate,
+                        const float* resid, const float* stats, const float* gy, const float* ggs,
+                        const float* grs, const float* gns, float* du, void* dBc, void* dCc,
+                        float* dt, void* dlam, float* dlog_dt, float* dD, float* deps,
+                        void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t H,
+                        int64_t N, void* stream) {
+    eacs::TrainBwdCall c{lam,   log_dt, u,     u_dtype, Bc,      Cc,     t,      D,       mean,
+                         var,   eps,    eta,   var_eps, dt_init, dt_min, dt_max, temperature,
+                         gate,  resid,  stats, gy,      ggs,     grs,    gns,    du,      dBc,
+                         dCc,   dt,     dlam,  dlog_dt, dD,      deps,   workspace, workspace_bytes,
+                         B,     L,      H,     N};
+    return eacs::train_bwd(c, static_cast<cudaStream_t>(stream));
 }
 
 int eacs_cell_fwd_noalloc(const void* lam, const float* log_dt, const void* u, int u_dtype,

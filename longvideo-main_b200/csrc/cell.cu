@@ -61,6 +61,7 @@ struct Args {
     float* y;
     float* gate;
     float* resid;
+    float2* stats; // [B][L] (||obs - pred||, ||obs||) when non-null (training forward)
     float2* part;  // [B][ntiles][L] (sum d^2, sum obs^2)
     int4* row;     // [B] {l*, bits(spike after l*-1), bits(r_{l*-1}), 0}
     float2* hpi;   // [B][H][N] committed state for the repair pass
@@ -331,7 +332,9 @@ __global__ void cell_resid(Args a) {
         s1 += v.x;
         s2 += v.y;
     }
-    a.resid[static_cast<size_t>(b) * a.L + l] = sqrtf(s1) / (sqrtf(s2) + a.eta);
+    const float num = sqrtf(s1), nobs = sqrtf(s2);
+    a.resid[static_cast<size_t>(b) * a.L + l] = num / (nobs + a.eta);
+    if (a.stats) a.stats[static_cast<size_t>(b) * a.L + l] = make_float2(num, nobs);
 }
 
 // ---------------------------------------------------------------------------
@@ -506,6 +509,7 @@ __global__ void __launch_bounds__(kRepair) cell_repair(Args a) {
                 s2 += sred[w].y;
             }
             const float r = sqrtf(s1) / (sqrtf(s2) + a.eta);
+            if (a.stats) a.stats[rowLH + l] = make_float2(sqrtf(s1), sqrtf(s2));
             float g;
             if (a.gate_mode == 1) {
                 g = 1.0f / (1.0f + expf(-((r - a.eps) / a.Tp)));
@@ -790,6 +794,7 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
     a.y = c.y;
     a.gate = c.gate;
     a.resid = c.resid;
+    a.stats = static_cast<float2*>(c.stats);
     char* ws = static_cast<char*>(c.workspace);
     a.part = reinterpret_cast<float2*>(ws + w.part);
     a.row = reinterpret_cast<int4*>(ws + w.row);

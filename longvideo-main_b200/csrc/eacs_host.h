@@ -49,6 +49,7 @@ struct CellCall {
     void* workspace;
     size_t workspace_bytes;
     int64_t B, L, H, N;
+    void* stats = nullptr;  // optional (B,L) float2 (||obs-pred||, ||obs||)
 };
 size_t cell_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
 int cell_fwd(const CellCall& c, cudaStream_t stream);
@@ -59,5 +60,41 @@ int ssm_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc
 cudaError_t cell_read_status(int* out, cudaStream_t stream);
 int zoh_kernels(const void* lam, const float* dt, void* dA, void* dBbar, int64_t M, int64_t H,
                 int64_t N, cudaStream_t stream);
+
+// train.cu
+struct TrainBwdCall {
+    const void* lam;
+    const float* log_dt;
+    const void* u;
+    int u_dtype;
+    const void* Bc;
+    const void* Cc;
+    const float* t;
+    const float* D;
+    const float* mean;
+    const float* var;
+    float eps, eta, var_eps, dt_init, dt_min, dt_max, temperature;
+    const float* gates;
+    const float* resid;
+    const void* stats;
+    const float* gy;
+    const float* ggs;
+    const float* grs;
+    const float* gns;
+    float* du;
+    void* dBc;
+    void* dCc;
+    float* dt;
+    void* dlam;
+    float* dlog;
+    float* dD;
+    float* deps;
+    void* workspace;
+    size_t workspace_bytes;
+    int64_t B, L, H, N;
+};
+size_t train_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+int train_bwd(const TrainBwdCall& c, cudaStream_t stream);
+cudaError_t train_read_status(int* out, cudaStream_t stream);
 
 }  // namespace eacs

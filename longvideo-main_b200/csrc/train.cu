@@ -1,0 +1,800 @@
+// train.cu -- backward of the gated EACS cell (GatedEACSCellFunction) on sm_100a.
+//
+// Reference: cst_ssm/ops/eacs_cell_train.py:117-175 runs, per step in reverse,
+// torch.autograd.grad of _step_functional (eacs_cell_train.py:15-66) with the
+// forward's hard gates pinned (STE) or the soft gate.  This file evaluates the
+// same vector-Jacobian product by hand (the derivation is restated in the CPU
+// oracle, oracle/eacs_oracle.c, eacs_oracle_cell_bwd, and checked there
+// against the reference's autograd):
+//
+//   per step l (reverse), chain (h, n), with hf = dA h_pi, q = dB_bar B,
+//   x_hat = hf + q_pi u_pi, h_upd = hf + q_l u_l, h_cur = g h_upd + (1-g) x_hat
+//     g_bar  = g_gs + sum Re(conj(a_hcur)(h_upd - x_hat)) + sum Re(conj(a_h)(h_upd - h_pi))
+//              + a_t (t_l - t_pi) + sum a_u (u_l - u_pi) + sum Re(conj(a_B)(B_l - B_pi)) + ...C
+//     r_bar  = g_rs + g_bar s(1-s)/T,  s = sigmoid((r - eps)/T)
+//     then the residual, readout, blend, ZOH and clamp adjoints.
+//
+// Only g_bar couples the chains of a row within a step: every other row-level
+// carry (the adjoints of t_pi, u_pi, B_pi, C_pi) is linear, so each chain (or
+// channel) carries its own share and adds its share's term to the g_bar sum.
+// A row is one thread-block cluster; g_bar is one float reduced per step
+// through distributed shared memory.  States come from checkpoints every kK
+// steps written by a gated forward pass, recomputed into shared memory one
+// chunk at a time.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+
+#include "eacs_common.cuh"
+#include "eacs_host.h"
+
+namespace cg = cooperative_groups;
+
+namespace eacs {
+namespace {
+
+constexpr int kK = 16;          // steps per checkpoint / recompute chunk
+constexpr int kCkThreads = 128; // checkpoint kernel CTA
+
+struct TArgs {
+    const float2* lam;
+    const float* log_dt;
+    const void* u;
+    const float2* Bc;
+    const float2* Cc;
+    const float* t;
+    const float* D;
+    const float* mean;
+    const float* var;
+    float eps, eta, var_eps, dt_init, dt_min, dt_max, Tp;
+    const float* gates;   // (B,L) forward gate values (hard 0/1 for STE, soft values for soft)
+    const float* resid;   // (B,L)
+    const float2* stats;  // (B,L) (||obs - pred||, ||obs||)
+    const float* gy;      // (B,L,H)
+    const float* ggs;     // (B,L) or null
+    const float* grs;
+    const float* gns;
+    float* du;            // (B,L,H)
+    float2* dBc;          // (B,L,N)
+    float2* dCc;
+    float* dt;            // (B,L)
+    float2* dlam;         // (H,N)
+    float* dlog;          // (H)
+    float* dD;            // (H)
+    float* deps;          // (1)
+    // workspace
+    float2* ck_h;         // [B][nK][H][N] state before step k*kK
+    float* ck_u;          // [B][nK][H]    u_pi before step k*kK
+    float4* ck_row;       // [B][nK]       (t_pi, -, -, -)
+    float2* ck_bc;        // [B][nK][2][N] B_pi, C_pi before step k*kK
+    float2* pB;           // [B][CL][L][N] per-CTA partials of dBc
+    float2* pC;
+    float* pt;            // [B][CL][L]
+    float2* plam;         // [B][H][N]
+    float* plog;          // [B][H]
+    float* pD;            // [B][H]
+    float* peps;          // [B]
+    int B, L, H, N, nK, CL, HC;
+};
+
+template <int LANES>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+    for (int o = LANES / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// Gated forward with known gates, writing checkpoints.  Thread layout as the
+// chain kernel: (hl, ln) owns chains n = ln + LANES*j of channel h.
+// ---------------------------------------------------------------------------
+template <int LANES, int NPT, typename UT>
+__global__ void __launch_bounds__(kCkThreads) train_ckpt(TArgs a) {
+    constexpr int HT = kCkThreads / LANES;
+    const int tid = threadIdx.x, ln = tid % LANES, hl = tid / LANES;
+    const int b = blockIdx.y, h = blockIdx.x * HT + hl;
+    const bool hv = h < a.H;
+    const int L = a.L, H = a.H, N = a.N;
+    const UT* u = static_cast<const UT*>(a.u);
+    const size_t rowL = static_cast<size_t>(b) * L;
+    float2 lam[NPT], ilam[NPT], hs[NPT], Bp[NPT], Cp[NPT];
+    bool nv[NPT];
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) {
+        const int n = ln + LANES * j;
+        nv[j] = hv && n < N;
+        lam[j] = nv[j] ? a.lam[static_cast<size_t>(h) * N + n] : make_float2(-1.f, 0.f);
+        ilam[j] = crecip(lam[j]);
+        hs[j] = make_float2(0.f, 0.f);
+        Bp[j] = nv[j] ? a.Bc[rowL * N + n] : make_float2(0.f, 0.f);
+        Cp[j] = nv[j] ? a.Cc[rowL * N + n] : make_float2(0.f, 0.f);
+    }
+    const float scale = hv ? expf(a.log_dt[h]) : 1.f;
+    float u_pi = hv ? to_f32(u[rowL * H + h]) : 0.f;
+    float t_pi = a.t[rowL] - a.dt_init;
+    const bool row_writer = blockIdx.x == 0 && tid == 0;
+    for (int l = 0; l < L; ++l) {
+        if (l % kK == 0) {
+            const int k = l / kK;
+#pragma unroll
+            for (int j = 0; j < NPT; ++j)
+                if (nv[j]) a.ck_h[((static_cast<size_t>(b) * a.nK + k) * H + h) * N + ln + LANES * j] = hs[j];
+            if (hv && ln == 0) a.ck_u[(static_cast<size_t>(b) * a.nK + k) * H + h] = u_pi;
+            if (row_writer) a.ck_row[static_cast<size_t>(b) * a.nK + k] = make_float4(t_pi, 0.f, 0.f, 0.f);
+            if (blockIdx.x == 0 && hl == 0) {
+#pragma unroll
+                for (int j = 0; j < NPT; ++j) {
+                    const int n = ln + LANES * j;
+                    if (n < N) {
+                        const size_t o = ((static_cast<size_t>(b) * a.nK + k) * 2) * N + n;
+                        a.ck_bc[o] = Bp[j];
+                        a.ck_bc[o + N] = Cp[j];
+                    }
+                }
+            }
+        }
+        const float g = a.gates[rowL + l];
+        const float tl = a.t[rowL + l];
+        const float ul = hv ? to_f32(u[(rowL + l) * H + h]) : 0.f;
+        const float dte = eff_dt(fmaxf(tl - t_pi, 0.f), scale, a.dt_min, a.dt_max);
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            const float2 Bl = nv[j] ? a.Bc[(rowL + l) * N + n] : make_float2(0.f, 0.f);
+            const float2 Cl = nv[j] ? a.Cc[(rowL + l) * N + n] : make_float2(0.f, 0.f);
+            float2 dA, dB;
+            zoh(lam[j], ilam[j], dte, dA, dB);
+            const float2 hf = cmul(dA, hs[j]);
+            const float2 ql = cmul(dB, Bl);
+            const float2 hu = make_float2(fmaf(ql.x, ul, hf.x), fmaf(ql.y, ul, hf.y));
+            const float2 gu = cscale(hu, g);
+            hs[j] = cadd(gu, cscale(hs[j], 1.f - g));
+            Bp[j] = cadd(cscale(Bl, g), cscale(Bp[j], 1.f - g));
+            Cp[j] = cadd(cscale(Cl, g), cscale(Cp[j], 1.f - g));
+        }
+        u_pi = g * ul + (1.f - g) * u_pi;
+        t_pi = g * tl + (1.f - g) * t_pi;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// cluster helpers (distributed shared memory)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_cluster_f32(float* local_addr, int cta, float v) {
+    uint32_t la = smem_u32(local_addr), ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(cta));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Backward: one cluster of CL CTAs per row, CTA c owns channels
+// [c*HC, (c+1)*HC); thread (hl, ln) owns chains n = ln + LANES*j.
+// ---------------------------------------------------------------------------
+template <int LANES, int NPT, typename UT>
+__global__ void train_bwd(TArgs a) {
+    constexpr int NP = LANES * NPT;
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int T = blockDim.x;
+    const int NW = T / 32;
+    const int HC = a.HC;
+    // shared layout
+    float2* sh = reinterpret_cast<float2*>(smem);                 // [kK][T][NPT]
+    float2* sBpi = sh + kK * T * NPT;                             // [kK][NP]
+    float2* sCpi = sBpi + kK * NP;
+    float2* sBl = sCpi + kK * NP;
+    float2* sCl = sBl + kK * NP;
+    float2* soB = sCl + kK * NP;                                  // [kK][NW][NP]
+    float2* soC = soB + kK * NW * NP;
+    float2* sstat = soC + kK * NW * NP;                           // [kK]
+    float* f = reinterpret_cast<float*>(sstat + kK);
+    float* supi = f;  f += kK * HC;                               // [kK][HC]
+    float* sul = f;   f += kK * HC;
+    float* sgy = f;   f += kK * HC;
+    float* stl = f;   f += kK;
+    float* stpi = f;  f += kK;
+    float* sgt = f;   f += kK;
+    float* sres = f;  f += kK;
+    float* sgg = f;   f += kK;                                    // g_gs
+    float* sgr = f;   f += kK;                                    // g_rs
+    float* sgn = f;   f += kK;                                    // g_ns
+    float* sot = f;   f += kK * NW;                               // [kK][NW]
+    float* sred = f;  f += 32;
+    float* sslot = f; f += 2 * 16;                                // [2][16] cluster partials of g_bar
+    float* sbc = f;   f += 4;
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int crank = static_cast<int>(cluster.block_rank());
+    const int CL = a.CL;
+    const int tid = threadIdx.x, ln = tid % LANES, hl = tid / LANES;
+    const int lane = tid & 31, wid = tid >> 5;
+    const int b = blockIdx.y;
+    const int h = crank * HC + hl;
+    const bool hv = hl < HC && h < a.H;
+    const int L = a.L, H = a.H, N = a.N;
+    const UT* u = static_cast<const UT*>(a.u);
+    const size_t rowL = static_cast<size_t>(b) * L;
+
+    float2 lam[NPT], ilam[NPT], ah[NPT], vB[NPT], vC[NPT], glam[NPT];
+    bool nv[NPT];
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) {
+        const int n = ln + LANES * j;
+        nv[j] = hv && n < N;
+        lam[j] = nv[j] ? a.lam[static_cast<size_t>(h) * N + n] : make_float2(-1.f, 0.f);
+        ilam[j] = crecip(lam[j]);
+        ah[j] = vB[j] = vC[j] = glam[j] = make_float2(0.f, 0.f);
+    }
+    const float scale = hv ? expf(a.log_dt[h]) : 1.f;
+    const float sd = hv ? sqrtf(a.var[h] + a.var_eps) : 1.f;
+    const float mu = hv ? a.mean[h] : 0.f;
+    const float Dh = hv ? a.D[h] : 0.f;
+    float vu = 0.f, vt = 0.f, glog = 0.f, gD = 0.f, geps = 0.f;
+    cluster_sync_all();  // every CTA of the cluster is running before any DSMEM store
+
+    for (int k = a.nK - 1; k >= 0; --k) {
+        const int l0 = k * kK;
+        const int steps = min(kK, L - l0);
+        __syncthreads();
+        // ---- stage per-step inputs of the chunk ----
+        for (int idx = tid; idx < steps * NP; idx += T) {
+            const int i = idx / NP, n = idx % NP;
+            const size_t o = (rowL + l0 + i) * N + n;
+            sBl[i * NP + n] = n < N ? a.Bc[o] : make_float2(0.f, 0.f);
+            sCl[i * NP + n] = n < N ? a.Cc[o] : make_float2(0.f, 0.f);
+        }
+        for (int idx = tid; idx < steps * HC; idx += T) {
+            const int i = idx / HC, c = idx % HC, hh = crank * HC + c;
+            const bool ok = hh < H;
+            sul[i * HC + c] = ok ? to_f32(u[(rowL + l0 + i) * H + hh]) : 0.f;
+            sgy[i * HC + c] = ok ? a.gy[(rowL + l0 + i) * H + hh] : 0.f;
+        }
+        for (int i = tid; i < steps; i += T) {
+            const size_t o = rowL + l0 + i;
+            stl[i] = a.t[o];
+            sgt[i] = a.gates[o];
+            sres[i] = a.resid[o];
+            sstat[i] = a.stats[o];
+            sgg[i] = a.ggs ? a.ggs[o] : 0.f;
+            sgr[i] = a.grs ? a.grs[o] : 0.f;
+            sgn[i] = a.gns ? a.gns[o] : 0.f;
+        }
+        // ---- forward recompute of the chunk from its checkpoint ----
+        float2 hs[NPT], Bp[NPT], Cp[NPT];
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            const size_t o = ((static_cast<size_t>(b) * a.nK + k) * H + (hv ? h : 0)) * N + (n < N ? n : 0);
+            hs[j] = nv[j] ? a.ck_h[o] : make_float2(0.f, 0.f);
+            const size_t ob = ((static_cast<size_t>(b) * a.nK + k) * 2) * N + (n < N ? n : 0);
+            Bp[j] = n < N ? a.ck_bc[ob] : make_float2(0.f, 0.f);
+            Cp[j] = n < N ? a.ck_bc[ob + N] : make_float2(0.f, 0.f);
+        }
+        float u_pi = hv ? a.ck_u[(static_cast<size_t>(b) * a.nK + k) * H + h] : 0.f;
+        float t_pi = a.ck_row[static_cast<size_t>(b) * a.nK + k].x;
+        __syncthreads();
+        for (int i = 0; i < steps; ++i) {
+            const float g = sgt[i], tl = stl[i];
+            const float ul = hv ? sul[i * HC + hl] : 0.f;
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) sh[(i * T + tid) * NPT + j] = hs[j];
+            if (hl == 0) {
+#pragma unroll
+                for (int j = 0; j < NPT; ++j) {
+                    sBpi[i * NP + ln + LANES * j] = Bp[j];
+                    sCpi[i * NP + ln + LANES * j] = Cp[j];
+                }
+            }
+            if (hv && ln == 0) supi[i * HC + hl] = u_pi;
+            if (tid == 0) stpi[i] = t_pi;
+            const float dte = eff_dt(fmaxf(tl - t_pi, 0.f), scale, a.dt_min, a.dt_max);
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                const int n = ln + LANES * j;
+                const float2 Bl = sBl[i * NP + n], Cl = sCl[i * NP + n];
+                float2 dA, dB;
+                zoh(lam[j], ilam[j], dte, dA, dB);
+                const float2 hf = cmul(dA, hs[j]);
+                const float2 ql = cmul(dB, Bl);
+                const float2 hu = make_float2(fmaf(ql.x, ul, hf.x), fmaf(ql.y, ul, hf.y));
+                hs[j] = cadd(cscale(hu, g), cscale(hs[j], 1.f - g));
+                Bp[j] = cadd(cscale(Bl, g), cscale(Bp[j], 1.f - g));
+                Cp[j] = cadd(cscale(Cl, g), cscale(Cp[j], 1.f - g));
+            }
+            u_pi = g * ul + (1.f - g) * u_pi;
+            t_pi = g * tl + (1.f - g) * t_pi;
+        }
+        __syncthreads();
+
+        // ---- reverse over the chunk ----
+        for (int i = steps - 1; i >= 0; --i) {
+            const int l = l0 + i;
+            const float g = sgt[i], tl = stl[i], tpi = stpi[i];
+            const float ul = hv ? sul[i * HC + hl] : 0.f;
+            const float upi = hv ? supi[i * HC + hl] : 0.f;
+            const float yb = hv ? sgy[i * HC + hl] : 0.f;
+            const float draw = tl - tpi;
+            const float delta = fmaxf(draw, 0.f);
+            const float mdel = draw >= 0.f ? 1.f : 0.f;
+            const float dte_raw = delta * scale;
+            const float dte = fminf(fmaxf(dte_raw, a.dt_min), a.dt_max);
+            const float mdt = (dte_raw >= a.dt_min && dte_raw <= a.dt_max) ? 1.f : 0.f;
+            float2 hp[NPT], dA[NPT], E[NPT], dB[NPT], xh[NPT], hu[NPT], hc[NPT], qp[NPT], ql[NPT];
+            float yhp = 0.f;
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                const int n = ln + LANES * j;
+                hp[j] = sh[(i * T + tid) * NPT + j];
+                const float2 Bl = sBl[i * NP + n], Bpi = sBpi[i * NP + n], Cpi = sCpi[i * NP + n];
+                const float a_ = lam[j].x * dte, b_ = lam[j].y * dte;
+                float em1, ea, sb, cb, vb;
+                expm1_exp(a_, em1, ea);
+                trig_half(b_, sb, cb, vb);
+                dA[j] = make_float2(ea * cb, ea * sb);
+                E[j] = make_float2(fmaf(em1, cb, -vb), ea * sb);
+                dB[j] = cmul(E[j], ilam[j]);
+                const float2 hf = cmul(dA[j], hp[j]);
+                qp[j] = cmul(dB[j], Bpi);
+                ql[j] = cmul(dB[j], Bl);
+                xh[j] = make_float2(fmaf(qp[j].x, upi, hf.x), fmaf(qp[j].y, upi, hf.y));
+                hu[j] = make_float2(fmaf(ql[j].x, ul, hf.x), fmaf(ql[j].y, ul, hf.y));
+                hc[j] = cadd(cscale(hu[j], g), cscale(xh[j], 1.f - g));
+                yhp += cre_mul(Cpi, xh[j]);
+            }
+            const float yhat = group_sum<LANES>(yhp);
+            const float obs = (ul - mu) / sd;
+            const float pred = (yhat - mu) / sd;
+            const float dv = obs - pred;
+            // local share of g_bar
+            float gl = 0.f;
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                const int n = ln + LANES * j;
+                const float2 Cl = sCl[i * NP + n], Bl = sBl[i * NP + n];
+                const float2 Bpi = sBpi[i * NP + n], Cpi = sCpi[i * NP + n];
+                const float2 ahc = make_float2(yb * Cl.x, -yb * Cl.y);  // yb conj(C_l)
+                const float2 d1 = make_float2(hu[j].x - xh[j].x, hu[j].y - xh[j].y);
+                const float2 d2 = make_float2(hu[j].x - hp[j].x, hu[j].y - hp[j].y);
+                gl += ahc.x * d1.x + ahc.y * d1.y;
+                gl += ah[j].x * d2.x + ah[j].y * d2.y;
+                gl += vB[j].x * (Bl.x - Bpi.x) + vB[j].y * (Bl.y - Bpi.y);
+                gl += vC[j].x * (Cl.x - Cpi.x) + vC[j].y * (Cl.y - Cpi.y);
+            }
+            if (ln == 0 && hv) gl += vu * (ul - upi) + vt * (tl - tpi);
+            // sigmoid slope of the gate at this step (row-uniform)
+            const float soft = 1.0f / (1.0f + expf(-((sres[i] - a.eps) / a.Tp)));
+            const float slope = soft * (1.f - soft);
+            float gbar = sgg[i];
+            if (slope != 0.f) {
+                gl = warp_sum(gl);
+                if (lane == 0) sred[wid] = gl;
+                __syncthreads();
+                if (tid == 0) {
+                    float sacc = 0.f;
+                    for (int w = 0; w < NW; ++w) sacc += sred[w];
+                    sbc[0] = sacc;
+                }
+                __syncthreads();
+                const int par = l & 1;
+                if (tid < CL) st_cluster_f32(&sslot[par * 16 + crank], tid, sbc[0]);
+                cluster_sync_all();
+                float tot = 0.f;
+                for (int c = 0; c < CL; ++c) tot += sslot[par * 16 + c];
+                gbar += tot;
+            }
+            const float xbar = gbar * slope;
+            const float rbar = sgr[i] + xbar / a.Tp;
+            if (crank == 0 && tid == 0) geps += -xbar / a.Tp;
+            const float2 st = sstat[i];
+            const float num = st.x, nobs = st.y, den = nobs + a.eta;
+            const float numbar = rbar / den;
+            const float denbar = -rbar * num / (den * den);
+            const float numtbar = sgn[i] / den;
+            const float dbar = num > 0.f ? numbar * dv / num : 0.f;
+            const float obar = dbar + (nobs > 0.f ? denbar * obs / nobs : 0.f);
+            const float pbar = -dbar - (num > 0.f ? numtbar * dv / num : 0.f);
+            const float yhbar = pbar / sd;
+            float s_u_pi = 0.f, s_u_l = 0.f, s_dte = 0.f;
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                const int n = ln + LANES * j;
+                const float2 Cl = sCl[i * NP + n], Bl = sBl[i * NP + n];
+                const float2 Bpi = sBpi[i * NP + n], Cpi = sCpi[i * NP + n];
+                const float2 ahc = make_float2(yb * Cl.x, -yb * Cl.y);
+                // x_hat and h_upd adjoints
+                const float2 axh = make_float2((1.f - g) * ahc.x + yhbar * Cpi.x,
+                                               (1.f - g) * ahc.y - yhbar * Cpi.y);
+                const float2 ahu = make_float2(g * (ahc.x + ah[j].x), g * (ahc.y + ah[j].y));
+                const float2 ahf = cadd(axh, ahu);
+                s_u_pi += axh.x * qp[j].x + axh.y * qp[j].y;
+                s_u_l += ahu.x * ql[j].x + ahu.y * ql[j].y;
+                const float2 aqp = cscale(axh, upi), aql = cscale(ahu, ul);
+                // dB_bar adjoint
+                const float2 adB = cadd(cmul(aqp, make_float2(Bpi.x, -Bpi.y)),
+                                        cmul(aql, make_float2(Bl.x, -Bl.y)));
+                const float2 cdB = make_float2(dB[j].x, -dB[j].y);
+                const float2 outB = cadd(cscale(vB[j], g), cmul(cdB, aql));
+                vB[j] = cadd(cscale(vB[j], 1.f - g), cmul(cdB, aqp));
+                const float2 outC = cadd(cscale(vC[j], g), make_float2(yb * hc[j].x, -yb * hc[j].y));
+                vC[j] = cadd(cscale(vC[j], 1.f - g), make_float2(yhbar * xh[j].x, -yhbar * xh[j].y));
+                // state adjoint for the previous step
+                const float2 cdA = make_float2(dA[j].x, -dA[j].y);
+                const float2 adA = cmul(make_float2(hp[j].x, -hp[j].y), ahf);
+                ah[j] = cadd(cscale(ah[j], 1.f - g), cmul(cdA, ahf));
+                // dB_bar = E * ilam
+                const float2 aE = cmul(adB, make_float2(ilam[j].x, -ilam[j].y));
+                const float2 ail = cmul(adB, make_float2(E[j].x, -E[j].y));
+                const float2 il2 = cmul(ilam[j], ilam[j]);
+                float2 alm = cmul(make_float2(-il2.x, il2.y), ail);  // -conj(ilam^2) ail
+                const float2 az = cmul(cdA, cadd(adA, aE));
+                alm = cadd(alm, cscale(az, dte));
+                s_dte += az.x * lam[j].x + az.y * lam[j].y;
+                if (nv[j]) glam[j] = cadd(glam[j], alm);
+                // per-(step, n) partials over this warp's channel groups
+                float2 ob = nv[j] ? outB : make_float2(0.f, 0.f);
+                float2 oc = nv[j] ? outC : make_float2(0.f, 0.f);
+#pragma unroll
+                for (int o = LANES; o < 32; o <<= 1) {
+                    ob.x += __shfl_xor_sync(0xffffffffu, ob.x, o);
+                    ob.y += __shfl_xor_sync(0xffffffffu, ob.y, o);
+                    oc.x += __shfl_xor_sync(0xffffffffu, oc.x, o);
+                    oc.y += __shfl_xor_sync(0xffffffffu, oc.y, o);
+                }
+                if (lane < LANES) {
+                    soB[(i * NW + wid) * NP + n] = ob;
+                    soC[(i * NW + wid) * NP + n] = oc;
+                }
+            }
+            s_u_pi = group_sum<LANES>(s_u_pi);
+            s_u_l = group_sum<LANES>(s_u_l);
+            s_dte = group_sum<LANES>(s_dte);
+            float out_t = 0.f;
+            if (hv) {
+                const float dub = yb * Dh + obar / sd + g * vu + s_u_l;
+                vu = (1.f - g) * vu + s_u_pi;
+                const float drb = mdt * s_dte;
+                const float dlt = drb * scale;  // this channel's share of delta_bar
+                glog += drb * delta * scale;
+                gD += yb * ul;
+                out_t = g * vt + mdel * dlt;
+                vt = (1.f - g) * vt - mdel * dlt;
+                if (ln == 0) a.du[(rowL + l) * H + h] = dub;
+            }
+            float ot = (ln == 0) ? out_t : 0.f;
+            ot = warp_sum(ot);
+            if (lane == 0) sot[i * NW + wid] = ot;
+        }
+        // ---- chunk end: per-CTA partials of dBc, dCc, dt ----
+        __syncthreads();
+        for (int idx = tid; idx < steps * NP; idx += T) {
+            const int i = idx / NP, n = idx % NP;
+            if (n >= N) continue;
+            float2 sb = make_float2(0.f, 0.f), sc = make_float2(0.f, 0.f);
+            for (int w = 0; w < NW; ++w) {
+                sb = cadd(sb, soB[(i * NW + w) * NP + n]);
+                sc = cadd(sc, soC[(i * NW + w) * NP + n]);
+            }
+            const size_t o = ((static_cast<size_t>(b) * CL + crank) * L + l0 + i) * N + n;
+            a.pB[o] = sb;
+            a.pC[o] = sc;
+        }
+        for (int i = tid; i < steps; i += T) {
+            float s = 0.f;
+            for (int w = 0; w < NW; ++w) s += sot[i * NW + w];
+            a.pt[(static_cast<size_t>(b) * CL + crank) * L + l0 + i] = s;
+        }
+    }
+    // ---- initial state (t_0 - dt_init, u_0, B_0, C_0) ----
+    __syncthreads();
+    if (hv && ln == 0) a.du[rowL * H + h] += vu;
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) {
+        const int n = ln + LANES * j;
+        float2 ob = nv[j] ? vB[j] : make_float2(0.f, 0.f);
+        float2 oc = nv[j] ? vC[j] : make_float2(0.f, 0.f);
+#pragma unroll
+        for (int o = LANES; o < 32; o <<= 1) {
+            ob.x += __shfl_xor_sync(0xffffffffu, ob.x, o);
+            ob.y += __shfl_xor_sync(0xffffffffu, ob.y, o);
+            oc.x += __shfl_xor_sync(0xffffffffu, oc.x, o);
+            oc.y += __shfl_xor_sync(0xffffffffu, oc.y, o);
+        }
+        if (lane < LANES) {
+            soB[wid * NP + n] = ob;
+            soC[wid * NP + n] = oc;
+        }
+    }
+    float ot = (hv && ln == 0) ? vt : 0.f;
+    ot = warp_sum(ot);
+    if (lane == 0) sot[wid] = ot;
+    __syncthreads();
+    for (int n = tid; n < N; n += T) {
+        float2 sb = make_float2(0.f, 0.f), sc = make_float2(0.f, 0.f);
+        for (int w = 0; w < NW; ++w) {
+            sb = cadd(sb, soB[w * NP + n]);
+            sc = cadd(sc, soC[w * NP + n]);
+        }
+        const size_t o = ((static_cast<size_t>(b) * CL + crank) * L) * N + n;
+        a.pB[o] = cadd(a.pB[o], sb);
+        a.pC[o] = cadd(a.pC[o], sc);
+    }
+    if (tid == 0) {
+        float s = 0.f;
+        for (int w = 0; w < NW; ++w) s += sot[w];
+        a.pt[(static_cast<size_t>(b) * CL + crank) * L] += s;
+    }
+    // ---- per-row parameter partials ----
+#pragma unroll
+    for (int j = 0; j < NPT; ++j)
+        if (nv[j]) a.plam[(static_cast<size_t>(b) * H + h) * N + ln + LANES * j] = glam[j];
+    if (hv && ln == 0) {
+        a.plog[static_cast<size_t>(b) * H + h] = glog;
+        a.pD[static_cast<size_t>(b) * H + h] = gD;
+    }
+    if (crank == 0 && tid == 0) a.peps[b] = geps;
+    cluster_sync_all();  // no CTA leaves while a peer may still write its slots
+}
+
+// ---------------------------------------------------------------------------
+// post pass: sum per-CTA and per-row partials
+// ---------------------------------------------------------------------------
+__global__ void train_post_rows(TArgs a) {
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t BLN = static_cast<int64_t>(a.B) * a.L * a.N;
+    if (idx < BLN) {
+        const int64_t b = idx / (static_cast<int64_t>(a.L) * a.N);
+        const int64_t ln = idx % (static_cast<int64_t>(a.L) * a.N);
+        float2 sb = make_float2(0.f, 0.f), sc = make_float2(0.f, 0.f);
+        for (int c = 0; c < a.CL; ++c) {
+            const size_t o = (static_cast<size_t>(b) * a.CL + c) * a.L * a.N + ln;
+            sb = cadd(sb, a.pB[o]);
+            sc = cadd(sc, a.pC[o]);
+        }
+        a.dBc[idx] = sb;
+        a.dCc[idx] = sc;
+    }
+    const int64_t BL = static_cast<int64_t>(a.B) * a.L;
+    if (idx < BL) {
+        const int64_t b = idx / a.L, l = idx % a.L;
+        float s = 0.f;
+        for (int c = 0; c < a.CL; ++c) s += a.pt[(static_cast<size_t>(b) * a.CL + c) * a.L + l];
+        a.dt[idx] = s;
+    }
+}
+
+__global__ void train_post_params(TArgs a) {
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t HN = static_cast<int64_t>(a.H) * a.N;
+    if (idx < HN) {
+        float2 s = make_float2(0.f, 0.f);
+        for (int b = 0; b < a.B; ++b) s = cadd(s, a.plam[static_cast<size_t>(b) * HN + idx]);
+        a.dlam[idx] = s;
+    }
+    if (idx < a.H) {
+        float s1 = 0.f, s2 = 0.f;
+        for (int b = 0; b < a.B; ++b) {
+            s1 += a.plog[static_cast<size_t>(b) * a.H + idx];
+            s2 += a.pD[static_cast<size_t>(b) * a.H + idx];
+        }
+        a.dlog[idx] = s1;
+        a.dD[idx] = s2;
+    }
+    if (idx == 0) {
+        float s = 0.f;
+        for (int b = 0; b < a.B; ++b) s += a.peps[b];
+        a.deps[0] = s;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+int lanes_train(int N, int* lanes, int* npt) {
+    if (N <= 8) { *lanes = 4; *npt = 2; }
+    else if (N <= 16) { *lanes = 8; *npt = 2; }
+    else if (N <= 32) { *lanes = 16; *npt = 2; }
+    else if (N <= 64) { *lanes = 32; *npt = 2; }
+    else return 0;
+    return 1;
+}
+
+// Cluster size and channels per CTA: the smallest power-of-two cluster (up to
+// 16) whose CTAs hold at most 512 threads (train_bwd needs ~118 registers a
+// thread, so 512 threads is the most one SM can hold).
+bool train_shape(int64_t H, int lanes, int* CL, int* HC, int* T) {
+    for (int cl = 1; cl <= 16; cl *= 2) {
+        const int64_t hc = (H + cl - 1) / cl;
+        const int64_t t = ((hc * lanes + 31) / 32) * 32;
+        if (t <= 512) {
+            *CL = cl;
+            *HC = static_cast<int>(hc);
+            *T = static_cast<int>(t);
+            return true;
+        }
+    }
+    return false;
+}
+
+size_t smem_bytes(int T, int NPT, int NP, int HC) {
+    const int NW = T / 32;
+    size_t s = 0;
+    s += sizeof(float2) * kK * T * NPT;
+    s += sizeof(float2) * kK * NP * 4;
+    s += sizeof(float2) * kK * NW * NP * 2;
+    s += sizeof(float2) * kK;
+    s += sizeof(float) * (kK * HC * 3 + kK * 7 + kK * NW + 32 + 32 + 4);
+    return s;
+}
+
+size_t al(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+struct TWs {
+    size_t ck_h, ck_u, ck_row, ck_bc, pB, pC, pt, plam, plog, pD, peps, total;
+};
+TWs tws(int64_t B, int64_t L, int64_t H, int64_t N, int CL) {
+    TWs w{};
+    const int64_t nK = (L + kK - 1) / kK;
+    size_t o = 0;
+    w.ck_h = o; o += al(sizeof(float2) * B * nK * H * N);
+    w.ck_u = o; o += al(sizeof(float) * B * nK * H);
+    w.ck_row = o; o += al(sizeof(float4) * B * nK);
+    w.ck_bc = o; o += al(sizeof(float2) * B * nK * 2 * N);
+    w.pB = o; o += al(sizeof(float2) * B * CL * L * N);
+    w.pC = o; o += al(sizeof(float2) * B * CL * L * N);
+    w.pt = o; o += al(sizeof(float) * B * CL * L);
+    w.plam = o; o += al(sizeof(float2) * B * H * N);
+    w.plog = o; o += al(sizeof(float) * B * H);
+    w.pD = o; o += al(sizeof(float) * B * H);
+    w.peps = o; o += al(sizeof(float) * B);
+    w.total = o;
+    return w;
+}
+
+template <int LANES, int NPT, typename UT>
+cudaError_t launch_train(TArgs& a, int T, cudaStream_t s) {
+    constexpr int NP = LANES * NPT;
+    {
+        dim3 grid((a.H + kCkThreads / LANES - 1) / (kCkThreads / LANES), a.B);
+        train_ckpt<LANES, NPT, UT><<<grid, kCkThreads, 0, s>>>(a);
+        note_launch();
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    const size_t smem = smem_bytes(T, NPT, NP, a.HC);
+    auto kern = train_bwd<LANES, NPT, UT>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    if (a.CL > 8) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.CL, a.B);
+    cfg.blockDim = dim3(T);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = a.CL;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    mark_start(s);
+    e = cudaLaunchKernelEx(&cfg, kern, a);
+    mark_stop(s);
+    note_launch();
+    if (e != cudaSuccess) return e;
+    const int64_t n1 = std::max<int64_t>(static_cast<int64_t>(a.B) * a.L * a.N, static_cast<int64_t>(a.B) * a.L);
+    train_post_rows<<<static_cast<unsigned>((n1 + 255) / 256), 256, 0, s>>>(a);
+    note_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const int64_t n2 = std::max<int64_t>(static_cast<int64_t>(a.H) * a.N, 1);
+    train_post_params<<<static_cast<unsigned>((n2 + 255) / 256), 256, 0, s>>>(a);
+    note_launch();
+    return cudaGetLastError();
+}
+
+template <typename UT>
+cudaError_t train_by_n(TArgs& a, int T, cudaStream_t s) {
+    int lanes, npt;
+    lanes_train(a.N, &lanes, &npt);
+    if (lanes == 4) return launch_train<4, 2, UT>(a, T, s);
+    if (lanes == 8) return launch_train<8, 2, UT>(a, T, s);
+    if (lanes == 16) return launch_train<16, 2, UT>(a, T, s);
+    return launch_train<32, 2, UT>(a, T, s);
+}
+
+}  // namespace
+
+size_t train_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
+    int lanes, npt, CL, HC, T;
+    if (B <= 0 || L <= 0 || H <= 0 || N <= 0 || !lanes_train(static_cast<int>(N), &lanes, &npt)) return 0;
+    if (!train_shape(H, lanes, &CL, &HC, &T)) return 0;
+    return tws(B, L, H, N, CL).total;
+}
+
+int train_bwd(const TrainBwdCall& c, cudaStream_t stream) {
+    const char* fn = "eacs_cell_train_bwd";
+    if (c.B < 0 || c.L < 0 || c.H < 0 || c.N < 0) return fail(EACS_ERR_INVALID, "%s: negative size", fn);
+    if (c.B == 0 || c.L == 0 || c.H == 0) return EACS_OK;
+    int lanes, npt, CL, HC, T;
+    if (c.N <= 0 || !lanes_train(static_cast<int>(c.N), &lanes, &npt))
+        return fail(EACS_ERR_UNSUPPORTED, "%s: N=%lld outside 1..64", fn, (long long)c.N);
+    if (!train_shape(c.H, lanes, &CL, &HC, &T))
+        return fail(EACS_ERR_UNSUPPORTED, "%s: H=%lld needs more than 16 CTAs of 512 threads per row", fn,
+                    (long long)c.H);
+    if (c.B > 65535 || c.L > (1LL << 30)) return fail(EACS_ERR_UNSUPPORTED, "%s: B or L too large", fn);
+    if (c.u_dtype != EACS_DTYPE_F32 && c.u_dtype != EACS_DTYPE_F16 && c.u_dtype != EACS_DTYPE_BF16)
+        return fail(EACS_ERR_INVALID, "%s: unknown u dtype %d", fn, c.u_dtype);
+    if (!c.lam || !c.log_dt || !c.u || !c.Bc || !c.Cc || !c.t || !c.D || !c.mean || !c.var || !c.gates ||
+        !c.resid || !c.stats || !c.gy || !c.du || !c.dBc || !c.dCc || !c.dt || !c.dlam || !c.dlog ||
+        !c.dD || !c.deps)
+        return fail(EACS_ERR_INVALID, "%s: null pointer argument", fn);
+    const TWs w = tws(c.B, c.L, c.H, c.N, CL);
+    if (!c.workspace || c.workspace_bytes < w.total)
+        return fail(EACS_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", fn, w.total,
+                    c.workspace_bytes);
+    TArgs a{};
+    a.lam = static_cast<const float2*>(c.lam);
+    a.log_dt = c.log_dt;
+    a.u = c.u;
+    a.Bc = static_cast<const float2*>(c.Bc);
+    a.Cc = static_cast<const float2*>(c.Cc);
+    a.t = c.t;
+    a.D = c.D;
+    a.mean = c.mean;
+    a.var = c.var;
+    a.eps = c.eps;
+    a.eta = c.eta;
+    a.var_eps = c.var_eps;
+    a.dt_init = c.dt_init;
+    a.dt_min = c.dt_min;
+    a.dt_max = c.dt_max;
+    a.Tp = c.temperature > 1e-4f ? c.temperature : 1e-4f;
+    a.gates = c.gates;
+    a.resid = c.resid;
+    a.stats = static_cast<const float2*>(c.stats);
+    a.gy = c.gy;
+    a.ggs = c.ggs;
+    a.grs = c.grs;
+    a.gns = c.gns;
+    a.du = c.du;
+    a.dBc = static_cast<float2*>(c.dBc);
+    a.dCc = static_cast<float2*>(c.dCc);
+    a.dt = c.dt;
+    a.dlam = static_cast<float2*>(c.dlam);
+    a.dlog = c.dlog;
+    a.dD = c.dD;
+    a.deps = c.deps;
+    char* ws = static_cast<char*>(c.workspace);
+    a.ck_h = reinterpret_cast<float2*>(ws + w.ck_h);
+    a.ck_u = reinterpret_cast<float*>(ws + w.ck_u);
+    a.ck_row = reinterpret_cast<float4*>(ws + w.ck_row);
+    a.ck_bc = reinterpret_cast<float2*>(ws + w.ck_bc);
+    a.pB = reinterpret_cast<float2*>(ws + w.pB);
+    a.pC = reinterpret_cast<float2*>(ws + w.pC);
+    a.pt = reinterpret_cast<float*>(ws + w.pt);
+    a.plam = reinterpret_cast<float2*>(ws + w.plam);
+    a.plog = reinterpret_cast<float*>(ws + w.plog);
+    a.pD = reinterpret_cast<float*>(ws + w.pD);
+    a.peps = reinterpret_cast<float*>(ws + w.peps);
+    a.B = static_cast<int>(c.B);
+    a.L = static_cast<int>(c.L);
+    a.H = static_cast<int>(c.H);
+    a.N = static_cast<int>(c.N);
+    a.nK = static_cast<int>((c.L + kK - 1) / kK);
+    a.CL = CL;
+    a.HC = HC;
+    cudaError_t e;
+    if (c.u_dtype == EACS_DTYPE_F16) e = train_by_n<__half>(a, T, stream);
+    else if (c.u_dtype == EACS_DTYPE_BF16) e = train_by_n<__nv_bfloat16>(a, T, stream);
+    else e = train_by_n<float>(a, T, stream);
+    return cuda_check(e, fn);
+}
+
+cudaError_t train_read_status(int* out, cudaStream_t stream) { return read_clear_status(out, stream); }
+
+}  // namespace eacs

@@ -44,6 +44,15 @@ SIGNATURES = {
     "eacs_cell_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
                            _F, _F, _F, _F, _F, _F, _I, _I, _F, _F, _I, _F,
                            _P, _P, _P, _P, ctypes.c_size_t, _I64, _I64, _I64, _I64, _P]),
+    "eacs_cell_train_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
+                                 _F, _F, _F, _F, _F, _F, _I, _F,
+                                 _P, _P, _P, _P, _P, ctypes.c_size_t, _I64, _I64, _I64, _I64, _P]),
+    "eacs_cell_train_bwd_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I64, _I64]),
+    "eacs_cell_train_bwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
+                                 _F, _F, _F, _F, _F, _F, _F,
+                                 _P, _P, _P, _P, _P, _P, _P,
+                                 _P, _P, _P, _P, _P, _P, _P, _P,
+                                 _P, ctypes.c_size_t, _I64, _I64, _I64, _I64, _P]),
     "eacs_cell_fwd_noalloc": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
                                    _F, _F, _F, _F, _F, _F, _I, _I, _F, _F, _I, _F,
                                    _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
