@@ -33,7 +33,7 @@ namespace cg = cooperative_groups;
 namespace eacs {
 namespace {
 
-constexpr int kK = 16;          // steps per checkpoint / recompute chunk
+constexpr int kKMax = 16;       // steps per checkpoint / recompute chunk (at most)
 constexpr int kCkThreads = 128; // checkpoint kernel CTA
 
 struct TArgs {
@@ -75,6 +75,7 @@ struct TArgs {
     float* pD;            // [B][H]
     float* peps;          // [B]
     int B, L, H, N, nK, CL, HC;
+    int K;                // steps per checkpoint / recompute chunk
 };
 
 template <int LANES>
@@ -114,8 +115,8 @@ __global__ void __launch_bounds__(kCkThreads) train_ckpt(TArgs a) {
     float t_pi = a.t[rowL] - a.dt_init;
     const bool row_writer = blockIdx.x == 0 && tid == 0;
     for (int l = 0; l < L; ++l) {
-        if (l % kK == 0) {
-            const int k = l / kK;
+        if (l % a.K == 0) {
+            const int k = l / a.K;
 #pragma unroll
             for (int j = 0; j < NPT; ++j)
                 if (nv[j]) a.ck_h[((static_cast<size_t>(b) * a.nK + k) * H + h) * N + ln + LANES * j] = hs[j];
@@ -180,6 +181,7 @@ __global__ void train_bwd(TArgs a) {
     const int T = blockDim.x;
     const int NW = T / 32;
     const int HC = a.HC;
+    const int kK = a.K;
     // shared layout
     float2* sh = reinterpret_cast<float2*>(smem);                 // [kK][T][NPT]
     float2* sBpi = sh + kK * T * NPT;                             // [kK][NP]
@@ -617,7 +619,7 @@ bool train_shape(int64_t H, int lanes, int* CL, int* HC, int* T) {
     return false;
 }
 
-size_t smem_bytes(int T, int NPT, int NP, int HC) {
+size_t smem_bytes(int T, int NPT, int NP, int HC, int kK) {
     const int NW = T / 32;
     size_t s = 0;
     s += sizeof(float2) * kK * T * NPT;
@@ -630,10 +632,18 @@ size_t smem_bytes(int T, int NPT, int NP, int HC) {
 
 size_t al(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+// Chunk length: the largest power of two up to kKMax whose shared-memory
+// footprint fits in 200 KiB.
+int chunk_len(int T, int NPT, int NP, int HC) {
+    for (int k = kKMax; k >= 1; k /= 2)
+        if (smem_bytes(T, NPT, NP, HC, k) <= 200u * 1024u) return k;
+    return 0;
+}
+
 struct TWs {
     size_t ck_h, ck_u, ck_row, ck_bc, pB, pC, pt, plam, plog, pD, peps, total;
 };
-TWs tws(int64_t B, int64_t L, int64_t H, int64_t N, int CL) {
+TWs tws(int64_t B, int64_t L, int64_t H, int64_t N, int CL, int kK) {
     TWs w{};
     const int64_t nK = (L + kK - 1) / kK;
     size_t o = 0;
@@ -662,7 +672,7 @@ cudaError_t launch_train(TArgs& a, int T, cudaStream_t s) {
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    const size_t smem = smem_bytes(T, NPT, NP, a.HC);
+    const size_t smem = smem_bytes(T, NPT, NP, a.HC, a.K);
     auto kern = train_bwd<LANES, NPT, UT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
@@ -713,7 +723,9 @@ size_t train_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
     int lanes, npt, CL, HC, T;
     if (B <= 0 || L <= 0 || H <= 0 || N <= 0 || !lanes_train(static_cast<int>(N), &lanes, &npt)) return 0;
     if (!train_shape(H, lanes, &CL, &HC, &T)) return 0;
-    return tws(B, L, H, N, CL).total;
+    const int K = chunk_len(T, npt, lanes * npt, HC);
+    if (K == 0) return 0;
+    return tws(B, L, H, N, CL, K).total;
 }
 
 int train_bwd(const TrainBwdCall& c, cudaStream_t stream) {
@@ -733,7 +745,9 @@ int train_bwd(const TrainBwdCall& c, cudaStream_t stream) {
         !c.resid || !c.stats || !c.gy || !c.du || !c.dBc || !c.dCc || !c.dt || !c.dlam || !c.dlog ||
         !c.dD || !c.deps)
         return fail(EACS_ERR_INVALID, "%s: null pointer argument", fn);
-    const TWs w = tws(c.B, c.L, c.H, c.N, CL);
+    const int K = chunk_len(T, npt, lanes * npt, HC);
+    if (K == 0) return fail(EACS_ERR_UNSUPPORTED, "%s: shared memory too small for H=%lld", fn, (long long)c.H);
+    const TWs w = tws(c.B, c.L, c.H, c.N, CL, K);
     if (!c.workspace || c.workspace_bytes < w.total)
         return fail(EACS_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", fn, w.total,
                     c.workspace_bytes);
@@ -785,7 +799,8 @@ int train_bwd(const TrainBwdCall& c, cudaStream_t stream) {
     a.L = static_cast<int>(c.L);
     a.H = static_cast<int>(c.H);
     a.N = static_cast<int>(c.N);
-    a.nK = static_cast<int>((c.L + kK - 1) / kK);
+    a.K = K;
+    a.nK = static_cast<int>((c.L + K - 1) / K);
     a.CL = CL;
     a.HC = HC;
     cudaError_t e;
