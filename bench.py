@@ -64,6 +64,10 @@ def parse():
                     help="budget of the CPU baseline sample (rank 0, N=1)")
     ap.add_argument("--profile", action="store_true",
                     help="device-timed section only (no e2e, no CPU sample): for ncu captures")
+    ap.add_argument("--workload", choices=["cell", "scan", "ssm", "train", "multiscale"],
+                    default="cell", help="cell (default) is the headline; the others are the "
+                    "materialised scan, the fused ungated SSM, the training step and the "
+                    "three-branch multiscale cell")
     return ap.parse_args()
 
 
@@ -369,6 +373,26 @@ def run_ours(args):
     if os.path.exists(tpath):
         traffic = json.load(open(tpath)).get("dram_bytes_per_launch")
 
+    # ---- the reference's own CUDA kernel (K3), when built for sm_100a -----
+    ref_cuda = None
+    if rank == 0 and world == 1 and not args.profile:
+        from bench_workloads import load_ref, timed
+        ref = load_ref("ref_eacs_cell_cuda")
+        if ref is not None:
+            u32 = d["u"].float()  # its wrapper casts u to float32 (eacs_gated_scan.py:44-49)
+            def ref_op():
+                return ref.eacs_cell_fwd(d["lam"], d["log_dt"], u32, d["Bc"], d["Cc"], d["t"], d["D"],
+                                         d["mean"], d["var"], eps, ETA, VAR_EPS, DT_INIT, DT_MIN, DT_MAX)
+            r_ms, _ = timed(ref_op, 3, 1, flush)
+            yr, gr, rr = ref_op()
+            op()
+            torch.cuda.synchronize()
+            ref_cuda = {"kernel": "reference eacs_cell_fwd_kernel (K3), sm_100a build",
+                        "value": UPDATES / (statistics.median(r_ms) / 1e3) / 1e9, "unit": UNIT,
+                        "ms_per_step": statistics.median(r_ms),
+                        "y_max_rel_diff": float((yr - y).abs().max() / yr.abs().max()),
+                        "gates_equal": bool(torch.equal(gr, gate))}
+
     line = None
     if rank == 0:
         line = {
@@ -387,6 +411,8 @@ def run_ours(args):
             "gpu_launches": launches,
             "clocks": sampler.summary(),
         }
+        if ref_cuda is not None:
+            line["reference_cuda"] = ref_cuda
         if world == 1 and not args.profile:
             host = oracle_sample_inputs(d)
             cores = cpu_cores()
@@ -407,6 +433,9 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "cell":
+        from bench_workloads import run_workload
+        return run_workload(args)
     return run_ours(args)
 
 

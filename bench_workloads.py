@@ -1,0 +1,238 @@
+"""Secondary bench.py workloads (one GPU): the materialised scan, the fused
+ungated SSM, the training step and the three-branch multiscale cell.
+
+Each prints one JSON line like bench.py's headline (state updates/s, the
+dominant kernel's HBM roofline) and, where the reference's own CUDA kernels
+were built into oracle/_ref (oracle/build_ref.py), times them on the same
+tensors for comparison.  Inputs are seeded synthetic data with the BASELINE
+config shapes; L2 is flushed between timed steps.
+"""
+from __future__ import annotations
+
+import importlib.machinery
+import importlib.util
+import json
+import math
+import os
+import statistics
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+UNIT = "Gstate-updates/s"
+
+
+def load_ref(name: str):
+    """The reference's extension built for sm_100a, or None."""
+    path = os.path.join(ROOT, "oracle", "_ref", name, name + ".so")
+    if not os.path.exists(path):
+        return None
+    loader = importlib.machinery.ExtensionFileLoader(name, path)
+    spec = importlib.util.spec_from_loader(name, loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
+    return mod
+
+
+def peak_hbm():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return json.load(open(p))["hbm_gbs"], "measured"
+    return 6650.0, "fallback"
+
+
+def timed(fn, steps, warmup, flush, kernel_events=False):
+    """Per-step device times (ms) of fn, L2 flushed before each step; with
+    kernel_events the library's events around its dominant kernel too."""
+    from eacs_b200 import _lib
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in ev + kev:
+        a.record()
+        b.record()
+    torch.cuda.synchronize()
+    for k in range(steps):
+        flush.zero_()
+        ev[k][0].record()
+        if kernel_events:
+            _lib.set_kernel_events(*kev[k])
+        fn()
+        if kernel_events:
+            _lib.set_kernel_events(None, None)
+        ev[k][1].record()
+    torch.cuda.synchronize()
+    step = [a.elapsed_time(b) for a, b in ev]
+    kern = [a.elapsed_time(b) for a, b in kev] if kernel_events else None
+    return step, kern
+
+
+def lam_init(g, H, N, tmin, tmax, imag_scale=1.0):
+    log_tau = torch.empty(H, N).uniform_(math.log(tmin), math.log(tmax), generator=g)
+    im = (math.pi * imag_scale * torch.arange(N, dtype=torch.float32)).expand(H, N)
+    return torch.complex(-torch.exp(-log_tau), im.contiguous())
+
+
+def times_exp(g, B, L, mean):
+    dt = torch.empty(B, L).exponential_(1.0 / mean, generator=g).clamp(1 / 30, 2.0)
+    return torch.cumsum(dt, 1)
+
+
+def cell_inputs(g, B, L, H, N, tau, dev, u_dtype, mean_dt=0.25):
+    s = 1.0 / math.sqrt(2 * N)
+    d = dict(lam=lam_init(g, H, N, *tau), log_dt=torch.zeros(H),
+             u=torch.randn(B, L, H, generator=g).to(u_dtype),
+             Bc=torch.complex(torch.randn(B, L, N, generator=g) * s, torch.randn(B, L, N, generator=g) * s),
+             Cc=torch.complex(torch.randn(B, L, N, generator=g) * s, torch.randn(B, L, N, generator=g) * s),
+             t=times_exp(g, B, L, mean_dt), D=torch.randn(H, generator=g),
+             mean=torch.zeros(H), var=torch.ones(H))
+    return {k: v.to(dev) for k, v in d.items()}
+
+
+def line(metric, value, steps, warmup, ms, config, **extra):
+    out = {"metric": metric, "value": value, "unit": UNIT, "n_gpus": 1, "steps": steps,
+           "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config}
+    out.update(extra)
+    print(json.dumps(out), flush=True)
+
+
+# ----------------------------------------------------------------------------
+def wl_scan(args, dev, flush):
+    """scan_fwd / scan_bwd on one branch of config 2 at L=4096 (24 / 40 B per update)."""
+    from eacs_b200.ops.scan_cuda import EXT
+    B, L, H, N = 4, 4096, 1024, 16
+    g = torch.Generator().manual_seed(7)
+    mag = (0.69 + 0.3 * torch.rand(B, L, H, N, generator=g))
+    ph = 6.283185 * torch.rand(B, L, H, N, generator=g)
+    a = torch.polar(mag, ph).to(dev)
+    b = torch.complex(torch.randn(B, L, H, N, generator=g), torch.randn(B, L, H, N, generator=g)).to(dev)
+    gh = torch.complex(torch.randn(B, L, H, N, generator=g), torch.randn(B, L, H, N, generator=g)).to(dev)
+    upd = B * L * H * N
+    peak, src = peak_hbm()
+    h = EXT.scan_fwd(a, b)[0]
+    fs, fk = timed(lambda: EXT.scan_fwd(a, b), args.steps, args.warmup, flush, True)
+    bs, bk = timed(lambda: EXT.scan_bwd(a, h, gh), args.steps, args.warmup, flush, True)
+    fk_s, bk_s = statistics.median(fk) / 1e3, statistics.median(bk) / 1e3
+    extra = {}
+    ref = load_ref("ref_eacs_scan_cuda")
+    if ref is not None:
+        rf, _ = timed(lambda: ref.scan_fwd(a, b), max(3, args.steps // 5), 2, flush)
+        rb, _ = timed(lambda: ref.scan_bwd(a, h, gh), max(3, args.steps // 5), 2, flush)
+        hr = ref.scan_fwd(a, b)[0]
+        extra["reference_cuda"] = {
+            "kernel": "reference scan_fwd_kernel / scan_bwd_kernel (sm_100a build)",
+            "fwd_gupdates_per_s": upd / (statistics.median(rf) / 1e3) / 1e9,
+            "bwd_gupdates_per_s": upd / (statistics.median(rb) / 1e3) / 1e9,
+            "fwd_ms": statistics.median(rf), "bwd_ms": statistics.median(rb),
+            "max_abs_diff_h": float((hr - h).abs().max())}
+    line("EACS scan_fwd Gstate-updates/s (materialised a, b -> h)", upd / fk_s / 1e9, args.steps,
+         args.warmup, statistics.median(fs),
+         {"workload": "scan_fwd/scan_bwd complex64 (B,L,H,N)", "B": B, "L": L, "H": H, "N": N,
+          "l2": "flushed between steps"},
+         roofline={"bound": "hbm", "unit": "GB/s", "peak": peak, "peak_source": src,
+                   "fwd": {"achieved": 24 * upd / fk_s / 1e9, "frac": 24 * upd / fk_s / 1e9 / peak,
+                           "kernel_ms": fk_s * 1e3, "bytes_per_update": 24},
+                   "bwd": {"achieved": 40 * upd / bk_s / 1e9, "frac": 40 * upd / bk_s / 1e9 / peak,
+                           "kernel_ms": bk_s * 1e3, "bytes_per_update": 40}},
+         bwd_gupdates_per_s=upd / bk_s / 1e9, **extra)
+
+
+def wl_ssm(args, dev, flush):
+    """Fused ungated continuous SSM forward, one branch of config 2 (bf16 u)."""
+    from eacs_b200.ops.continuous_ssm import ssm_forward
+    B, L, H, N = 4, 16384, 1024, 16
+    g = torch.Generator().manual_seed(8)
+    d = cell_inputs(g, B, L, H, N, (0.5, 64.0), dev, torch.bfloat16)
+    upd = B * L * H * N
+    fn = lambda: ssm_forward(d["lam"], d["log_dt"], d["t"], d["Bc"], d["Cc"], d["u"], d["D"])
+    st, kt = timed(fn, args.steps, args.warmup, flush, True)
+    k_s = statistics.median(kt) / 1e3
+    alg = B * L * H * 2 + 2 * B * L * N * 8 + B * L * 4 + B * L * H * 4
+    peak, src = peak_hbm()
+    line("EACS fused ungated SSM Gstate-updates/s", upd / (statistics.median(st) / 1e3) / 1e9,
+         args.steps, args.warmup, statistics.median(st),
+         {"workload": "ContinuousSSMLayer core fused (dt, ZOH, scan, readout)", "B": B, "L": L,
+          "H": H, "N": N, "u_dtype": "bf16", "l2": "flushed between steps"},
+         roofline={"bound": "hbm", "achieved": alg / k_s / 1e9, "peak": peak, "unit": "GB/s",
+                   "frac": alg / k_s / 1e9 / peak, "peak_source": src, "kernel_ms": k_s * 1e3,
+                   "alg_bytes_per_launch": alg})
+
+
+def wl_train(args, dev, flush):
+    """Config 3: GatedEACSCellFunction forward + backward, B=8 L=8192 H=768 N=16, bf16 u."""
+    from eacs_b200.ops.eacs_cell_train import fused_gated_scan
+    B, L, H, N = 8, 8192, 768, 16
+    g = torch.Generator().manual_seed(9)
+    d = cell_inputs(g, B, L, H, N, (0.5, 4.0), dev, torch.bfloat16)
+    gy = torch.randn(B, L, H, generator=g).to(dev)
+    leaves = {k: d[k].clone().requires_grad_(True) for k in ("u", "Bc", "Cc", "lam", "log_dt", "D")}
+    eps = torch.tensor(0.12, device=dev, requires_grad=True)
+
+    def step():
+        y, gs, rs = fused_gated_scan(leaves["u"], leaves["Bc"], leaves["Cc"], d["t"], leaves["lam"],
+                                     leaves["log_dt"], leaves["D"], eps, d["mean"], d["var"], 0.1, 1e-6)
+        torch.autograd.backward([y], [gy])
+
+    st, kt = timed(step, max(3, args.steps // 10), 2, flush, True)
+    upd = B * L * H * N
+    rate = float(fused_gated_scan(leaves["u"], leaves["Bc"], leaves["Cc"], d["t"], leaves["lam"],
+                                  leaves["log_dt"], leaves["D"], eps, d["mean"], d["var"], 0.1,
+                                  1e-6)[1].mean())
+    line("EACS gated cell training fwd+bwd Gstate-updates/s", upd / (statistics.median(st) / 1e3) / 1e9,
+         len(st), 2, statistics.median(st),
+         {"workload": "GatedEACSCellFunction fwd+bwd (STE, T=0.1)", "B": B, "L": L, "H": H, "N": N,
+          "u_dtype": "bf16", "update_rate": rate, "l2": "flushed between steps"},
+         backward_kernel_ms=statistics.median(kt),
+         note="kernel_ms is the cluster backward kernel (train_bwd) alone")
+
+
+def wl_multiscale(args, dev, flush):
+    """Config 2: three gated branches (tau bands [0.5,4], [4,32], [32,256] s) + fusion."""
+    from eacs_b200.ops.eacs_gated_scan import cell_forward_into, workspace_bytes
+    B, L, H, N = 4, 16384, 1024, 16
+    g = torch.Generator().manual_seed(10)
+    bands = [(0.5, 4.0), (4.0, 32.0), (32.0, 256.0)]
+    x = torch.randn(B, L, H, generator=g).to(torch.bfloat16).to(dev)
+    br = [cell_inputs(g, B, L, H, N, tb, dev, torch.bfloat16) for tb in bands]
+    for d in br:  # one video: every branch sees the same timestamps
+        d["t"] = br[0]["t"]
+    fusion = torch.nn.Linear(H, 3).to(dev)
+    norm = torch.nn.LayerNorm(H).to(dev)
+    ys = [torch.empty(B, L, H, device=dev) for _ in bands]
+    gts = [torch.empty(B, L, device=dev) for _ in bands]
+    rss = [torch.empty(B, L, device=dev) for _ in bands]
+    ws = torch.empty(workspace_bytes(B, L, H, N), dtype=torch.uint8, device=dev)
+    dt_max = [max(1e3, 10 * tb[1]) for tb in bands]
+
+    @torch.no_grad()
+    def step():
+        for i, d in enumerate(br):
+            cell_forward_into(d["lam"], d["log_dt"], d["u"], d["Bc"], d["Cc"], d["t"], d["D"],
+                              d["mean"], d["var"], 0.12, 1e-6, 1e-5, 1.0, 1e-3, dt_max[i], None, "hard",
+                              0.1, ys[i], gts[i], rss[i], ws)
+        w = torch.softmax(fusion(x.float()), dim=-1)
+        fused = ys[0] * w[..., 0:1] + ys[1] * w[..., 1:2] + ys[2] * w[..., 2:3]
+        return norm(x.float() + fused)
+
+    st, kt = timed(step, max(3, args.steps // 5), 2, flush, False)
+    upd = 3 * B * L * H * N
+    line("EACS MultiScaleEACS (3 branches) Gstate-updates/s", upd / (statistics.median(st) / 1e3) / 1e9,
+         len(st), 2, statistics.median(st),
+         {"workload": "MultiScaleEACS: 3 gated branches + softmax fusion + LayerNorm", "B": B, "L": L,
+          "H": H, "N": N, "u_dtype": "bf16", "update_rates": [float(x.mean()) for x in gts],
+          "l2": "flushed between steps"},
+         note="branch outputs fused in PyTorch (fusion Linear, softmax, LayerNorm)")
+
+
+def run_workload(args):
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    {"scan": wl_scan, "ssm": wl_ssm, "train": wl_train, "multiscale": wl_multiscale}[args.workload](
+        args, dev, flush)
+    from eacs_b200 import _lib
+    assert _lib.device_status() == 0
+    return 0
