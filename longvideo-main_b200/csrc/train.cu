@@ -182,29 +182,31 @@ __global__ void train_bwd(TArgs a) {
     const int NW = T / 32;
     const int HC = a.HC;
     const int kK = a.K;
-    // shared layout
-    float2* sh = reinterpret_cast<float2*>(smem);                 // [kK][T][NPT]
-    float2* sBpi = sh + kK * T * NPT;                             // [kK][NP]
+    // shared layout (see smem_bytes)
+    float2* sh = reinterpret_cast<float2*>(smem);                 // [kK][T][NPT] h_pi
+    float2* sdA = sh + kK * T * NPT;                              // [kK][T][NPT] dA
+    float2* sdB = sdA + kK * T * NPT;                             // [kK][T][NPT] dB_bar
+    float2* sBpi = sdB + kK * T * NPT;                            // [kK][NP]
     float2* sCpi = sBpi + kK * NP;
     float2* sBl = sCpi + kK * NP;
     float2* sCl = sBl + kK * NP;
     float2* soB = sCl + kK * NP;                                  // [kK][NW][NP]
     float2* soC = soB + kK * NW * NP;
-    float2* sstat = soC + kK * NW * NP;                           // [kK]
-    float* f = reinterpret_cast<float*>(sstat + kK);
+    float4* srow = reinterpret_cast<float4*>(soC + kK * NW * NP); // [kK] 1/den, num/den^2, 1/num, 1/nobs
+    float4* sslot = srow + kK;                                    // [2][16/4] cluster partials of g_bar
+    float* f = reinterpret_cast<float*>(sslot + 8);
     float* supi = f;  f += kK * HC;                               // [kK][HC]
     float* sul = f;   f += kK * HC;
     float* sgy = f;   f += kK * HC;
     float* stl = f;   f += kK;
     float* stpi = f;  f += kK;
     float* sgt = f;   f += kK;
-    float* sres = f;  f += kK;
+    float* sslp = f;  f += kK;                                    // sigmoid slope / T
     float* sgg = f;   f += kK;                                    // g_gs
     float* sgr = f;   f += kK;                                    // g_rs
     float* sgn = f;   f += kK;                                    // g_ns
     float* sot = f;   f += kK * NW;                               // [kK][NW]
     float* sred = f;  f += 32;
-    float* sslot = f; f += 2 * 16;                                // [2][16] cluster partials of g_bar
     float* sbc = f;   f += 4;
 
     cg::cluster_group cluster = cg::this_cluster();
@@ -215,6 +217,7 @@ __global__ void train_bwd(TArgs a) {
     const int b = blockIdx.y;
     const int h = crank * HC + hl;
     const bool hv = hl < HC && h < a.H;
+    const bool row_owner = hl == 0;  // tracks the row-level B_pi, C_pi in the recompute
     const int L = a.L, H = a.H, N = a.N;
     const UT* u = static_cast<const UT*>(a.u);
     const size_t rowL = static_cast<size_t>(b) * L;
@@ -230,7 +233,7 @@ __global__ void train_bwd(TArgs a) {
         ah[j] = vB[j] = vC[j] = glam[j] = make_float2(0.f, 0.f);
     }
     const float scale = hv ? expf(a.log_dt[h]) : 1.f;
-    const float sd = hv ? sqrtf(a.var[h] + a.var_eps) : 1.f;
+    const float rsd = hv ? 1.0f / sqrtf(a.var[h] + a.var_eps) : 1.f;
     const float mu = hv ? a.mean[h] : 0.f;
     const float Dh = hv ? a.D[h] : 0.f;
     float vu = 0.f, vt = 0.f, glog = 0.f, gD = 0.f, geps = 0.f;
@@ -257,8 +260,13 @@ __global__ void train_bwd(TArgs a) {
             const size_t o = rowL + l0 + i;
             stl[i] = a.t[o];
             sgt[i] = a.gates[o];
-            sres[i] = a.resid[o];
-            sstat[i] = a.stats[o];
+            const float soft = 1.0f / (1.0f + expf(-((a.resid[o] - a.eps) / a.Tp)));
+            sslp[i] = soft * (1.f - soft) / a.Tp;
+            const float2 st = a.stats[o];
+            const float num = st.x, nobs = st.y, den = nobs + a.eta;
+            const float rden = 1.0f / den;
+            srow[i] = make_float4(rden, num * rden * rden, num > 0.f ? 1.0f / num : 0.f,
+                                  nobs > 0.f ? 1.0f / nobs : 0.f);
             sgg[i] = a.ggs ? a.ggs[o] : 0.f;
             sgr[i] = a.grs ? a.grs[o] : 0.f;
             sgn[i] = a.gns ? a.gns[o] : 0.f;
@@ -270,9 +278,12 @@ __global__ void train_bwd(TArgs a) {
             const int n = ln + LANES * j;
             const size_t o = ((static_cast<size_t>(b) * a.nK + k) * H + (hv ? h : 0)) * N + (n < N ? n : 0);
             hs[j] = nv[j] ? a.ck_h[o] : make_float2(0.f, 0.f);
-            const size_t ob = ((static_cast<size_t>(b) * a.nK + k) * 2) * N + (n < N ? n : 0);
-            Bp[j] = n < N ? a.ck_bc[ob] : make_float2(0.f, 0.f);
-            Cp[j] = n < N ? a.ck_bc[ob + N] : make_float2(0.f, 0.f);
+            Bp[j] = Cp[j] = make_float2(0.f, 0.f);
+            if (row_owner && n < N) {
+                const size_t ob = ((static_cast<size_t>(b) * a.nK + k) * 2) * N + n;
+                Bp[j] = a.ck_bc[ob];
+                Cp[j] = a.ck_bc[ob + N];
+            }
         }
         float u_pi = hv ? a.ck_u[(static_cast<size_t>(b) * a.nK + k) * H + h] : 0.f;
         float t_pi = a.ck_row[static_cast<size_t>(b) * a.nK + k].x;
@@ -280,30 +291,34 @@ __global__ void train_bwd(TArgs a) {
         for (int i = 0; i < steps; ++i) {
             const float g = sgt[i], tl = stl[i];
             const float ul = hv ? sul[i * HC + hl] : 0.f;
-#pragma unroll
-            for (int j = 0; j < NPT; ++j) sh[(i * T + tid) * NPT + j] = hs[j];
-            if (hl == 0) {
-#pragma unroll
-                for (int j = 0; j < NPT; ++j) {
-                    sBpi[i * NP + ln + LANES * j] = Bp[j];
-                    sCpi[i * NP + ln + LANES * j] = Cp[j];
-                }
-            }
             if (hv && ln == 0) supi[i * HC + hl] = u_pi;
             if (tid == 0) stpi[i] = t_pi;
             const float dte = eff_dt(fmaxf(tl - t_pi, 0.f), scale, a.dt_min, a.dt_max);
 #pragma unroll
             for (int j = 0; j < NPT; ++j) {
                 const int n = ln + LANES * j;
-                const float2 Bl = sBl[i * NP + n], Cl = sCl[i * NP + n];
+                const size_t so = (static_cast<size_t>(i) * T + tid) * NPT + j;
+                sh[so] = hs[j];
+                const float2 Bl = sBl[i * NP + n];
                 float2 dA, dB;
                 zoh(lam[j], ilam[j], dte, dA, dB);
+                sdA[so] = dA;
+                sdB[so] = dB;
                 const float2 hf = cmul(dA, hs[j]);
                 const float2 ql = cmul(dB, Bl);
                 const float2 hu = make_float2(fmaf(ql.x, ul, hf.x), fmaf(ql.y, ul, hf.y));
                 hs[j] = cadd(cscale(hu, g), cscale(hs[j], 1.f - g));
-                Bp[j] = cadd(cscale(Bl, g), cscale(Bp[j], 1.f - g));
-                Cp[j] = cadd(cscale(Cl, g), cscale(Cp[j], 1.f - g));
+            }
+            if (row_owner) {  // warp 0 only: row-level B_pi, C_pi before each step
+#pragma unroll
+                for (int j = 0; j < NPT; ++j) {
+                    const int n = ln + LANES * j;
+                    sBpi[i * NP + n] = Bp[j];
+                    sCpi[i * NP + n] = Cp[j];
+                    const float2 Bl = sBl[i * NP + n], Cl = sCl[i * NP + n];
+                    Bp[j] = cadd(cscale(Bl, g), cscale(Bp[j], 1.f - g));
+                    Cp[j] = cadd(cscale(Cl, g), cscale(Cp[j], 1.f - g));
+                }
             }
             u_pi = g * ul + (1.f - g) * u_pi;
             t_pi = g * tl + (1.f - g) * t_pi;
@@ -323,51 +338,36 @@ __global__ void train_bwd(TArgs a) {
             const float dte_raw = delta * scale;
             const float dte = fminf(fmaxf(dte_raw, a.dt_min), a.dt_max);
             const float mdt = (dte_raw >= a.dt_min && dte_raw <= a.dt_max) ? 1.f : 0.f;
-            float2 hp[NPT], dA[NPT], E[NPT], dB[NPT], xh[NPT], hu[NPT], hc[NPT], qp[NPT], ql[NPT];
-            float yhp = 0.f;
+            float2 hp[NPT], dA[NPT], dB[NPT], xh[NPT], hu[NPT], qp[NPT], ql[NPT];
+            float yhp = 0.f, gl = 0.f;
 #pragma unroll
             for (int j = 0; j < NPT; ++j) {
                 const int n = ln + LANES * j;
-                hp[j] = sh[(i * T + tid) * NPT + j];
-                const float2 Bl = sBl[i * NP + n], Bpi = sBpi[i * NP + n], Cpi = sCpi[i * NP + n];
-                const float a_ = lam[j].x * dte, b_ = lam[j].y * dte;
-                float em1, ea, sb, cb, vb;
-                expm1_exp(a_, em1, ea);
-                trig_half(b_, sb, cb, vb);
-                dA[j] = make_float2(ea * cb, ea * sb);
-                E[j] = make_float2(fmaf(em1, cb, -vb), ea * sb);
-                dB[j] = cmul(E[j], ilam[j]);
+                const size_t so = (static_cast<size_t>(i) * T + tid) * NPT + j;
+                hp[j] = sh[so];
+                dA[j] = sdA[so];
+                dB[j] = sdB[so];
+                const float2 Bl = sBl[i * NP + n], Bpi = sBpi[i * NP + n];
+                const float2 Cl = sCl[i * NP + n], Cpi = sCpi[i * NP + n];
                 const float2 hf = cmul(dA[j], hp[j]);
                 qp[j] = cmul(dB[j], Bpi);
                 ql[j] = cmul(dB[j], Bl);
                 xh[j] = make_float2(fmaf(qp[j].x, upi, hf.x), fmaf(qp[j].y, upi, hf.y));
                 hu[j] = make_float2(fmaf(ql[j].x, ul, hf.x), fmaf(ql[j].y, ul, hf.y));
-                hc[j] = cadd(cscale(hu[j], g), cscale(xh[j], 1.f - g));
                 yhp += cre_mul(Cpi, xh[j]);
-            }
-            const float yhat = group_sum<LANES>(yhp);
-            const float obs = (ul - mu) / sd;
-            const float pred = (yhat - mu) / sd;
-            const float dv = obs - pred;
-            // local share of g_bar
-            float gl = 0.f;
-#pragma unroll
-            for (int j = 0; j < NPT; ++j) {
-                const int n = ln + LANES * j;
-                const float2 Cl = sCl[i * NP + n], Bl = sBl[i * NP + n];
-                const float2 Bpi = sBpi[i * NP + n], Cpi = sCpi[i * NP + n];
+                // local share of g_bar
                 const float2 ahc = make_float2(yb * Cl.x, -yb * Cl.y);  // yb conj(C_l)
-                const float2 d1 = make_float2(hu[j].x - xh[j].x, hu[j].y - xh[j].y);
-                const float2 d2 = make_float2(hu[j].x - hp[j].x, hu[j].y - hp[j].y);
-                gl += ahc.x * d1.x + ahc.y * d1.y;
-                gl += ah[j].x * d2.x + ah[j].y * d2.y;
+                gl += ahc.x * (hu[j].x - xh[j].x) + ahc.y * (hu[j].y - xh[j].y);
+                gl += ah[j].x * (hu[j].x - hp[j].x) + ah[j].y * (hu[j].y - hp[j].y);
                 gl += vB[j].x * (Bl.x - Bpi.x) + vB[j].y * (Bl.y - Bpi.y);
                 gl += vC[j].x * (Cl.x - Cpi.x) + vC[j].y * (Cl.y - Cpi.y);
             }
+            const float yhat = group_sum<LANES>(yhp);
+            const float obs = (ul - mu) * rsd;
+            const float pred = (yhat - mu) * rsd;
+            const float dv = obs - pred;
             if (ln == 0 && hv) gl += vu * (ul - upi) + vt * (tl - tpi);
-            // sigmoid slope of the gate at this step (row-uniform)
-            const float soft = 1.0f / (1.0f + expf(-((sres[i] - a.eps) / a.Tp)));
-            const float slope = soft * (1.f - soft);
+            const float slope = sslp[i];  // row-uniform
             float gbar = sgg[i];
             if (slope != 0.f) {
                 gl = warp_sum(gl);
@@ -380,24 +380,31 @@ __global__ void train_bwd(TArgs a) {
                 }
                 __syncthreads();
                 const int par = l & 1;
-                if (tid < CL) st_cluster_f32(&sslot[par * 16 + crank], tid, sbc[0]);
+                float* slots = reinterpret_cast<float*>(sslot + par * 4);
+                if (tid < CL) st_cluster_f32(&slots[crank], tid, sbc[0]);
                 cluster_sync_all();
                 float tot = 0.f;
-                for (int c = 0; c < CL; ++c) tot += sslot[par * 16 + c];
+                if (CL >= 4) {
+                    for (int c4 = 0; c4 < CL / 4; ++c4) {
+                        const float4 v = sslot[par * 4 + c4];
+                        tot += (v.x + v.y) + (v.z + v.w);
+                    }
+                } else {
+                    for (int c = 0; c < CL; ++c) tot += slots[c];
+                }
                 gbar += tot;
             }
-            const float xbar = gbar * slope;
-            const float rbar = sgr[i] + xbar / a.Tp;
-            if (crank == 0 && tid == 0) geps += -xbar / a.Tp;
-            const float2 st = sstat[i];
-            const float num = st.x, nobs = st.y, den = nobs + a.eta;
-            const float numbar = rbar / den;
-            const float denbar = -rbar * num / (den * den);
-            const float numtbar = sgn[i] / den;
-            const float dbar = num > 0.f ? numbar * dv / num : 0.f;
-            const float obar = dbar + (nobs > 0.f ? denbar * obs / nobs : 0.f);
-            const float pbar = -dbar - (num > 0.f ? numtbar * dv / num : 0.f);
-            const float yhbar = pbar / sd;
+            const float xbar = gbar * slope;  // already divided by T
+            const float rbar = sgr[i] + xbar;
+            if (crank == 0 && tid == 0) geps -= xbar;
+            const float4 rw = srow[i];  // 1/den, num/den^2, 1/num, 1/nobs
+            const float numbar = rbar * rw.x;
+            const float denbar = -rbar * rw.y;
+            const float numtbar = sgn[i] * rw.x;
+            const float dbar = numbar * dv * rw.z;
+            const float obar = dbar + denbar * obs * rw.w;
+            const float pbar = -dbar - numtbar * dv * rw.z;
+            const float yhbar = pbar * rsd;
             float s_u_pi = 0.f, s_u_l = 0.f, s_dte = 0.f;
 #pragma unroll
             for (int j = 0; j < NPT; ++j) {
@@ -405,6 +412,7 @@ __global__ void train_bwd(TArgs a) {
                 const float2 Cl = sCl[i * NP + n], Bl = sBl[i * NP + n];
                 const float2 Bpi = sBpi[i * NP + n], Cpi = sCpi[i * NP + n];
                 const float2 ahc = make_float2(yb * Cl.x, -yb * Cl.y);
+                const float2 hc = cadd(cscale(hu[j], g), cscale(xh[j], 1.f - g));
                 // x_hat and h_upd adjoints
                 const float2 axh = make_float2((1.f - g) * ahc.x + yhbar * Cpi.x,
                                                (1.f - g) * ahc.y - yhbar * Cpi.y);
@@ -413,21 +421,21 @@ __global__ void train_bwd(TArgs a) {
                 s_u_pi += axh.x * qp[j].x + axh.y * qp[j].y;
                 s_u_l += ahu.x * ql[j].x + ahu.y * ql[j].y;
                 const float2 aqp = cscale(axh, upi), aql = cscale(ahu, ul);
-                // dB_bar adjoint
                 const float2 adB = cadd(cmul(aqp, make_float2(Bpi.x, -Bpi.y)),
                                         cmul(aql, make_float2(Bl.x, -Bl.y)));
                 const float2 cdB = make_float2(dB[j].x, -dB[j].y);
                 const float2 outB = cadd(cscale(vB[j], g), cmul(cdB, aql));
                 vB[j] = cadd(cscale(vB[j], 1.f - g), cmul(cdB, aqp));
-                const float2 outC = cadd(cscale(vC[j], g), make_float2(yb * hc[j].x, -yb * hc[j].y));
+                const float2 outC = cadd(cscale(vC[j], g), make_float2(yb * hc.x, -yb * hc.y));
                 vC[j] = cadd(cscale(vC[j], 1.f - g), make_float2(yhbar * xh[j].x, -yhbar * xh[j].y));
                 // state adjoint for the previous step
                 const float2 cdA = make_float2(dA[j].x, -dA[j].y);
                 const float2 adA = cmul(make_float2(hp[j].x, -hp[j].y), ahf);
                 ah[j] = cadd(cscale(ah[j], 1.f - g), cmul(cdA, ahf));
-                // dB_bar = E * ilam
+                // dB_bar = E * ilam with E = expm1(z) = dB_bar * lam
+                const float2 E = cmul(dB[j], lam[j]);
                 const float2 aE = cmul(adB, make_float2(ilam[j].x, -ilam[j].y));
-                const float2 ail = cmul(adB, make_float2(E[j].x, -E[j].y));
+                const float2 ail = cmul(adB, make_float2(E.x, -E.y));
                 const float2 il2 = cmul(ilam[j], ilam[j]);
                 float2 alm = cmul(make_float2(-il2.x, il2.y), ail);  // -conj(ilam^2) ail
                 const float2 az = cmul(cdA, cadd(adA, aE));
@@ -454,7 +462,7 @@ __global__ void train_bwd(TArgs a) {
             s_dte = group_sum<LANES>(s_dte);
             float out_t = 0.f;
             if (hv) {
-                const float dub = yb * Dh + obar / sd + g * vu + s_u_l;
+                const float dub = yb * Dh + obar * rsd + g * vu + s_u_l;
                 vu = (1.f - g) * vu + s_u_pi;
                 const float drb = mdt * s_dte;
                 const float dlt = drb * scale;  // this channel's share of delta_bar
@@ -622,11 +630,11 @@ bool train_shape(int64_t H, int lanes, int* CL, int* HC, int* T) {
 size_t smem_bytes(int T, int NPT, int NP, int HC, int kK) {
     const int NW = T / 32;
     size_t s = 0;
-    s += sizeof(float2) * kK * T * NPT;
-    s += sizeof(float2) * kK * NP * 4;
-    s += sizeof(float2) * kK * NW * NP * 2;
-    s += sizeof(float2) * kK;
-    s += sizeof(float) * (kK * HC * 3 + kK * 7 + kK * NW + 32 + 32 + 4);
+    s += sizeof(float2) * kK * T * NPT * 3;   // h_pi, dA, dB_bar
+    s += sizeof(float2) * kK * NP * 4;        // B_pi, C_pi, B_l, C_l
+    s += sizeof(float2) * kK * NW * NP * 2;   // dBc, dCc partials
+    s += sizeof(float4) * (kK + 8);           // row constants, cluster slots
+    s += sizeof(float) * (kK * HC * 3 + kK * 7 + kK * NW + 32 + 4);
     return s;
 }
 
