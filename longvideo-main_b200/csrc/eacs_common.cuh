@@ -133,7 +133,8 @@ template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return _
 template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
 
 // ----------------------------------------------------------------------------
-// mbarrier + TMA (cp.async.bulk[.tensor]) wrappers.  No cluster multicast.
+// mbarrier + TMA (cp.async.bulk[.tensor]) wrappers; every copy targets this
+// CTA's own shared memory from this GPU's memory.
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
