@@ -170,6 +170,39 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
     return false;
 }
 
+// Bounded wait on an mbarrier phase completed by other CTAs of the cluster
+// (acquire at cluster scope, so their st.async data is visible afterwards).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t phase) {
+    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(phase)
+            : "memory");
+        if (ok) return true;
+    }
+    set_status(EACS_ERR_TIMEOUT);
+    return false;
+}
+
+// Address of `local` in the shared memory of CTA `cta` of this cluster.
+__device__ __forceinline__ uint32_t mapa_u32(const void* local, int cta) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(cta));
+    return ra;
+}
+
+// Store a float into another CTA's shared memory, counting 4 bytes of
+// transaction on that CTA's mbarrier (both addresses from mapa_u32).
+__device__ __forceinline__ void st_async_f32(uint32_t raddr, float v, uint32_t rbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr),
+                 "r"(__float_as_uint(v)), "r"(rbar)
+                 : "memory");
+}
+
 // 3-D tiled TMA load global -> shared, completion counted on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_t* bar, int x, int y, int z) {
     asm volatile(

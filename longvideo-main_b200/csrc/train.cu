@@ -18,7 +18,9 @@
 // carry (the adjoints of t_pi, u_pi, B_pi, C_pi) is linear, so each chain (or
 // channel) carries its own share and adds its share's term to the g_bar sum.
 // A row is one thread-block cluster; g_bar is one float reduced per step
-// through distributed shared memory.  States come from checkpoints every kK
+// through distributed shared memory: every warp sends its partial to every
+// CTA with st.async, which counts the bytes on that CTA's mbarrier, and each
+// CTA waits on its own barrier (no cluster-wide barrier per step).  States come from checkpoints every kK
 // steps written by a gated forward pass, recomputed into shared memory one
 // chunk at a time.
 #include <cooperative_groups.h>
@@ -161,11 +163,6 @@ __global__ void __launch_bounds__(kCkThreads) train_ckpt(TArgs a) {
 // ---------------------------------------------------------------------------
 // cluster helpers (distributed shared memory)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void st_cluster_f32(float* local_addr, int cta, float v) {
-    uint32_t la = smem_u32(local_addr), ra;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(cta));
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
-}
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -193,8 +190,9 @@ __global__ void train_bwd(TArgs a) {
     float2* soB = sCl + kK * NP;                                  // [kK][NW][NP]
     float2* soC = soB + kK * NW * NP;
     float4* srow = reinterpret_cast<float4*>(soC + kK * NW * NP); // [kK] 1/den, num/den^2, 1/num, 1/nobs
-    float4* sslot = srow + kK;                                    // [2][16/4] cluster partials of g_bar
-    float* f = reinterpret_cast<float*>(sslot + 8);
+    uint64_t* rbar = reinterpret_cast<uint64_t*>(srow + kK);      // [2] reduction mbarriers
+    float* slots = reinterpret_cast<float*>(rbar + 2);            // [2][CL*NW] partials of g_bar
+    float* f = slots + 2 * 16 * 32;
     float* supi = f;  f += kK * HC;                               // [kK][HC]
     float* sul = f;   f += kK * HC;
     float* sgy = f;   f += kK * HC;
@@ -206,8 +204,6 @@ __global__ void train_bwd(TArgs a) {
     float* sgr = f;   f += kK;                                    // g_rs
     float* sgn = f;   f += kK;                                    // g_ns
     float* sot = f;   f += kK * NW;                               // [kK][NW]
-    float* sred = f;  f += 32;
-    float* sbc = f;   f += 4;
 
     cg::cluster_group cluster = cg::this_cluster();
     const int crank = static_cast<int>(cluster.block_rank());
@@ -237,7 +233,24 @@ __global__ void train_bwd(TArgs a) {
     const float mu = hv ? a.mean[h] : 0.f;
     const float Dh = hv ? a.D[h] : 0.f;
     float vu = 0.f, vt = 0.f, glog = 0.f, gD = 0.f, geps = 0.f;
-    cluster_sync_all();  // every CTA of the cluster is running before any DSMEM store
+    if (tid == 0) {
+        mbar_init(&rbar[0], 1);
+        mbar_init(&rbar[1], 1);
+        fence_mbar_init();
+    }
+    // every CTA of the cluster is running, with its barriers initialised,
+    // before any remote store
+    cluster_sync_all();
+    const int nslot = CL * NW;                 // one partial per (source CTA, warp)
+    uint32_t rslot[2] = {0u, 0u}, rbarr[2] = {0u, 0u};
+    if (lane < CL) {                           // lane c sends to CTA c
+        rslot[0] = mapa_u32(&slots[crank * NW + wid], lane);
+        rslot[1] = mapa_u32(&slots[16 * 32 + crank * NW + wid], lane);
+        rbarr[0] = mapa_u32(&rbar[0], lane);
+        rbarr[1] = mapa_u32(&rbar[1], lane);
+    }
+    int nred = 0;                              // reductions done so far
+    bool failed = false;
 
     for (int k = a.nK - 1; k >= 0; --k) {
         const int l0 = k * kK;
@@ -369,30 +382,21 @@ __global__ void train_bwd(TArgs a) {
             if (ln == 0 && hv) gl += vu * (ul - upi) + vt * (tl - tpi);
             const float slope = sslp[i];  // row-uniform
             float gbar = sgg[i];
-            if (slope != 0.f) {
+            if (slope != 0.f && !failed) {
+                // warp partial -> every CTA's slot for (this CTA, this warp),
+                // counted on that CTA's barrier; then wait for all CL*NW partials
                 gl = warp_sum(gl);
-                if (lane == 0) sred[wid] = gl;
-                __syncthreads();
-                if (tid == 0) {
-                    float sacc = 0.f;
-                    for (int w = 0; w < NW; ++w) sacc += sred[w];
-                    sbc[0] = sacc;
-                }
-                __syncthreads();
-                const int par = l & 1;
-                float* slots = reinterpret_cast<float*>(sslot + par * 4);
-                if (tid < CL) st_cluster_f32(&slots[crank], tid, sbc[0]);
-                cluster_sync_all();
+                const int par = nred & 1;
+                const uint32_t phase = (nred >> 1) & 1;
+                if (tid == 0) mbar_expect_tx(&rbar[par], static_cast<uint32_t>(nslot) * 4u);
+                if (lane < CL) st_async_f32(rslot[par], gl, rbarr[par]);
+                if (!mbar_wait_cluster(&rbar[par], phase)) failed = true;
+                const float* sl = slots + par * 16 * 32;
                 float tot = 0.f;
-                if (CL >= 4) {
-                    for (int c4 = 0; c4 < CL / 4; ++c4) {
-                        const float4 v = sslot[par * 4 + c4];
-                        tot += (v.x + v.y) + (v.z + v.w);
-                    }
-                } else {
-                    for (int c = 0; c < CL; ++c) tot += slots[c];
-                }
+                for (int q = lane; q < nslot; q += 32) tot += sl[q];
+                tot = warp_sum(tot);
                 gbar += tot;
+                ++nred;
             }
             const float xbar = gbar * slope;  // already divided by T
             const float rbar = sgr[i] + xbar;
@@ -633,8 +637,9 @@ size_t smem_bytes(int T, int NPT, int NP, int HC, int kK) {
     s += sizeof(float2) * kK * T * NPT * 3;   // h_pi, dA, dB_bar
     s += sizeof(float2) * kK * NP * 4;        // B_pi, C_pi, B_l, C_l
     s += sizeof(float2) * kK * NW * NP * 2;   // dBc, dCc partials
-    s += sizeof(float4) * (kK + 8);           // row constants, cluster slots
-    s += sizeof(float) * (kK * HC * 3 + kK * 7 + kK * NW + 32 + 4);
+    s += sizeof(float4) * kK + 16;            // row constants, 2 mbarriers
+    s += sizeof(float) * 2 * 16 * 32;         // reduction slots
+    s += sizeof(float) * (kK * HC * 3 + kK * 7 + kK * NW);
     return s;
 }
 
