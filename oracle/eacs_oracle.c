@@ -180,6 +180,140 @@ int eacs_oracle_ssm_fwd(const float* lam, const float* log_dt, const float* t,
 }
 
 /* ---------------------------------------------------------------------------
+ * Backward of the ungated core (autograd of continuous_ssm.py:44-55 through
+ * effective_dt, zoh_discretize, the scan and the readout), in double.
+ * Upstream gy (B,L,H).  Outputs (float, overwritten): du (B,L,H), dBc, dCc
+ * (B,L,N) complex, dt (B,L), dlam (H,N) complex, dlog (H), dD (H).
+ * ------------------------------------------------------------------------- */
+int eacs_oracle_ssm_bwd(const float* lam, const float* log_dt, const float* t,
+                        const float* Bc, const float* Cc, const float* u,
+                        const float* D, const float* gy, float* du, float* dBc,
+                        float* dCc, float* dtg, float* dlam, float* dlog, float* dD,
+                        int64_t B, int64_t L, int64_t H, int64_t N,
+                        float dt_min, float dt_max) {
+    double* alam = (double*)calloc((size_t)(B * H * N * 2), sizeof(double));
+    double* alog = (double*)calloc((size_t)(B * H), sizeof(double));
+    double* aD = (double*)calloc((size_t)(B * H), sizeof(double));
+#pragma omp parallel for num_threads(nthreads()) schedule(dynamic, 1)
+    for (int64_t bi = 0; bi < B; ++bi) {
+        const float* tb = t + bi * L;
+        double* dtraw = (double*)malloc(sizeof(double) * (size_t)L);   /* dt before the clamp */
+        double* mdt = (double*)malloc(sizeof(double) * (size_t)L);     /* clamp_min(0) mask of t-diff */
+        for (int64_t l = 0; l < L; ++l) {
+            if (L == 1) { dtraw[l] = 0; mdt[l] = 0; continue; }
+            int64_t l1 = l == 0 ? 1 : l;
+            double d = (double)tb[l1] - (double)tb[l1 - 1];
+            mdt[l] = d >= 0 ? 1.0 : 0.0;
+            dtraw[l] = d > 0 ? d : 0;
+        }
+        double* dtbar = (double*)calloc((size_t)L, sizeof(double));
+        cd* gBr = (cd*)calloc((size_t)(L * N), sizeof(cd));
+        cd* gCr = (cd*)calloc((size_t)(L * N), sizeof(cd));
+        cd* hs = (cd*)malloc(sizeof(cd) * (size_t)((L + 1) * N));
+        for (int64_t hh = 0; hh < H; ++hh) {
+            double sc = exp((double)log_dt[hh]);
+            /* forward states (double) */
+            for (int64_t n = 0; n < N; ++n) hs[n] = (cd){0, 0};
+            for (int64_t l = 0; l < L; ++l) {
+                double v = dtraw[l] * sc, dte = v < dt_min ? dt_min : (v > dt_max ? dt_max : v);
+                double ul = u[(bi * L + l) * H + hh];
+                for (int64_t n = 0; n < N; ++n) {
+                    int64_t i = hh * N + n;
+                    double a = lam[2 * i] * dte, b = lam[2 * i + 1] * dte, e = exp(a);
+                    cd dA = {e * cos(b), e * sin(b)};
+                    cd E = {expm1(a) * cos(b) - 2 * sin(0.5 * b) * sin(0.5 * b), e * sin(b)};
+                    double lr = lam[2 * i], li = lam[2 * i + 1], dd = lr * lr + li * li;
+                    cd il = {lr / dd, -li / dd};
+                    cd dB = cd_mul(E, il);
+                    cd q = cd_mul(dB, cd_of(Bc + ((bi * L + l) * N + n) * 2));
+                    hs[(l + 1) * N + n] = cd_add(cd_mul(dA, hs[l * N + n]), cd_scale(q, ul));
+                }
+            }
+            /* reverse */
+            cd* s = (cd*)calloc((size_t)N, sizeof(cd));
+            for (int64_t l = L - 1; l >= 0; --l) {
+                double v = dtraw[l] * sc, dte = v < dt_min ? dt_min : (v > dt_max ? dt_max : v);
+                double m = (v >= dt_min && v <= dt_max) ? 1.0 : 0.0;
+                double ul = u[(bi * L + l) * H + hh];
+                double yb = gy[(bi * L + l) * H + hh];
+                double dub = yb * D[hh];
+                aD[bi * H + hh] += yb * ul;
+                double dtebar = 0;
+                for (int64_t n = 0; n < N; ++n) {
+                    int64_t i = hh * N + n;
+                    double lr = lam[2 * i], li = lam[2 * i + 1], dd = lr * lr + li * li;
+                    double a = lr * dte, b = li * dte, e = exp(a);
+                    cd dA = {e * cos(b), e * sin(b)};
+                    cd E = {expm1(a) * cos(b) - 2 * sin(0.5 * b) * sin(0.5 * b), e * sin(b)};
+                    cd il = {lr / dd, -li / dd};
+                    cd dB = cd_mul(E, il);
+                    cd Bl = cd_of(Bc + ((bi * L + l) * N + n) * 2);
+                    cd Cl = cd_of(Cc + ((bi * L + l) * N + n) * 2);
+                    /* adjoint of h_l: readout + carried */
+                    s[n] = cd_add(s[n], cd_scale(cd_conj(Cl), yb));
+                    cd hl = hs[(l + 1) * N + n], hp = hs[l * N + n];
+                    /* dC_l += yb conj(h_l) */
+                    gCr[l * N + n] = cd_add(gCr[l * N + n], cd_scale(cd_conj(hl), yb));
+                    cd q = cd_mul(dB, Bl);
+                    dub += cd_redot(s[n], q);
+                    cd aq = cd_scale(s[n], ul);
+                    gBr[l * N + n] = cd_add(gBr[l * N + n], cd_mul(cd_conj(dB), aq));
+                    cd adB = cd_mul(aq, cd_conj(Bl));
+                    cd adA = cd_mul(cd_conj(hp), s[n]);
+                    cd aE = cd_mul(adB, cd_conj(il));
+                    cd ail = cd_mul(adB, cd_conj(E));
+                    cd il2 = cd_mul(il, il);
+                    cd alm = cd_scale(cd_mul(cd_conj(il2), ail), -1.0);
+                    cd az = cd_mul(cd_conj(dA), cd_add(adA, aE));
+                    alm = cd_add(alm, cd_scale(az, dte));
+                    dtebar += cd_redot(az, (cd){lr, li});
+                    alam[(bi * H * N + i) * 2] += alm.re;
+                    alam[(bi * H * N + i) * 2 + 1] += alm.im;
+                    s[n] = cd_mul(cd_conj(dA), s[n]);
+                }
+                du[(bi * L + l) * H + hh] = (float)dub;
+                double drb = m * dtebar;
+                alog[bi * H + hh] += drb * dtraw[l] * sc;
+                dtbar[l] += drb * sc;
+            }
+            free(s);
+        }
+        /* dt_l = max(t_l - t_{l-1}, 0), dt_0 = dt_1 */
+        for (int64_t l = 0; l < L; ++l) dtg[bi * L + l] = 0;
+        if (L > 1) {
+            for (int64_t l = 0; l < L; ++l) {
+                int64_t l1 = l == 0 ? 1 : l;
+                double g = dtbar[l] * mdt[l];
+                dtg[bi * L + l1] += (float)g;
+                dtg[bi * L + l1 - 1] -= (float)g;
+            }
+        }
+        for (int64_t l = 0; l < L; ++l)
+            for (int64_t n = 0; n < N; ++n) {
+                int64_t o = ((bi * L + l) * N + n) * 2;
+                dBc[o] = (float)gBr[l * N + n].re;
+                dBc[o + 1] = (float)gBr[l * N + n].im;
+                dCc[o] = (float)gCr[l * N + n].re;
+                dCc[o + 1] = (float)gCr[l * N + n].im;
+            }
+        free(dtraw); free(mdt); free(dtbar); free(hs); free(gBr); free(gCr);
+    }
+    for (int64_t i = 0; i < H * N * 2; ++i) {
+        double s2 = 0;
+        for (int64_t bi = 0; bi < B; ++bi) s2 += alam[bi * H * N * 2 + i];
+        dlam[i] = (float)s2;
+    }
+    for (int64_t hh = 0; hh < H; ++hh) {
+        double s1 = 0, s2 = 0;
+        for (int64_t bi = 0; bi < B; ++bi) { s1 += alog[bi * H + hh]; s2 += aD[bi * H + hh]; }
+        dlog[hh] = (float)s1;
+        dD[hh] = (float)s2;
+    }
+    free(alam); free(alog); free(aD);
+    return 0;
+}
+
+/* ---------------------------------------------------------------------------
  * Gated EACS cell, inference (eacs.py:78-142 eacs_step with skip_compute and
  * eacs.py:145-173 scan_range, including robust_guard).  Per batch row:
  *   state (h_pi, t_pi, u_pi, B_pi, C_pi) initialised to (0, t_0-dt_init, u_0, B_0, C_0)

@@ -39,6 +39,7 @@ def lib():
         L.eacs_oracle_scan_fwd.argtypes = [_P, _P, _P, _I64, _I64, _I64, _I64]
         L.eacs_oracle_scan_bwd.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64]
         L.eacs_oracle_ssm_fwd.argtypes = [_P] * 8 + [_I64] * 4 + [_F, _F]
+        L.eacs_oracle_ssm_bwd.argtypes = [_P] * 15 + [_I64] * 4 + [_F, _F]
         L.eacs_oracle_cell_fwd.argtypes = ([_P] * 9 + [_F] * 6 + [_I, _I, _F, _F, _I, _F, _I]
                                            + [_P] * 3 + [_I64] * 4)
         L.eacs_oracle_cell_bwd.argtypes = ([_P] * 9 + [_F] * 5 + [_F, _I] + [_P] * 5
@@ -99,6 +100,33 @@ def ssm_fwd(lam, log_dt, t, Bc, Cc, u, D, dt_min=1e-3, dt_max=1e3):
     lib().eacs_oracle_ssm_fwd(_ptr(lam), _ptr(log_dt), _ptr(t), _ptr(Bc), _ptr(Cc), _ptr(u),
                               _ptr(D), _ptr(y), B, L, H, N, dt_min, dt_max)
     return y
+
+
+def ssm_bwd(lam, log_dt, t, Bc, Cc, u, D, gy, dt_min=1e-3, dt_max=1e3):
+    """Backward of the ungated core (autograd of continuous_ssm.py:44-55).
+
+    Returns (du, dBc, dCc, dt, dlam, dlog_dt, dD)."""
+    lam = _c(lam, np.complex64)
+    log_dt = _c(log_dt, np.float32)
+    t = _c(t, np.float32)
+    Bc = _c(Bc, np.complex64)
+    Cc = _c(Cc, np.complex64)
+    u = _c(u, np.float32)
+    D = _c(D, np.float32)
+    gy = _c(gy, np.float32)
+    B, L, H = u.shape
+    N = lam.shape[1]
+    du = np.empty((B, L, H), np.float32)
+    dBc = np.empty((B, L, N), np.complex64)
+    dCc = np.empty((B, L, N), np.complex64)
+    dt = np.empty((B, L), np.float32)
+    dlam = np.empty((H, N), np.complex64)
+    dlog = np.empty((H,), np.float32)
+    dD = np.empty((H,), np.float32)
+    lib().eacs_oracle_ssm_bwd(_ptr(lam), _ptr(log_dt), _ptr(t), _ptr(Bc), _ptr(Cc), _ptr(u), _ptr(D),
+                              _ptr(gy), _ptr(du), _ptr(dBc), _ptr(dCc), _ptr(dt), _ptr(dlam),
+                              _ptr(dlog), _ptr(dD), B, L, H, N, dt_min, dt_max)
+    return du, dBc, dCc, dt, dlam, dlog, dD
 
 
 def cell_fwd(lam, log_dt, u, Bc, Cc, t, D, mean, var, eps, eta, var_eps=1e-5,

@@ -102,9 +102,13 @@ def ssm_cases(gen):
                            torch.randn(B, L, N, generator=gen) * s)
         u = torch.randn(B, L, H, generator=gen)
         D = torch.randn(H, generator=gen)
-        y = ssm_core(lam, log_dt, t, Bc, Cc, u, D)
+        gy = torch.randn(B, L, H, generator=gen)
+        leaves = [x.clone().requires_grad_(True) for x in (lam, log_dt, t, Bc, Cc, u, D)]
+        y = ssm_core(*leaves)
+        grads = torch.autograd.grad(y, leaves, gy)
+        gl = dict(zip(["dlam", "dlog_dt", "dt", "dBc", "dCc", "du", "dD"], grads))
         out[name] = dict(lam=_np(lam), log_dt=_np(log_dt), t=_np(t), Bc=_np(Bc), Cc=_np(Cc),
-                         u=_np(u), D=_np(D), y=_np(y))
+                         u=_np(u), D=_np(D), y=_np(y), gy=_np(gy), **{k: _np(v) for k, v in gl.items()})
     return out
 
 

@@ -29,6 +29,16 @@ def test_ssm_fwd(name):
     assert relerr(y, d["y"]) < 1e-5
 
 
+@pytest.mark.parametrize("name", sorted(SSM))
+def test_ssm_bwd(name):
+    d = SSM[name]
+    got = oracle.ssm_bwd(d["lam"], d["log_dt"], d["t"], d["Bc"], d["Cc"], d["u"], d["D"], d["gy"])
+    # gradient tolerance 1e-3 (the L=1 case has |dlam| ~ 1e-7, where the
+    # reference's own float32 autograd differs from the double oracle by 2.5e-4)
+    for k, v in zip(["du", "dBc", "dCc", "dt", "dlam", "dlog_dt", "dD"], got):
+        assert relerr(v, d[k]) < 1e-3, (k, relerr(v, d[k]))
+
+
 @pytest.mark.parametrize("name", sorted(CELL))
 def test_cell_fwd(name):
     d = CELL[name]
