@@ -103,6 +103,43 @@ EACS_API int eacs_ssm_fwd(const void* lam, const float* log_dt, const float* t,
                  int64_t B, int64_t L, int64_t H, int64_t N,
                  float dt_min, float dt_max, void* stream);
 
+/* Bytes of the state checkpoints eacs_ssm_train_fwd writes for these sizes:
+ * one (B,H,N) complex64 state every 8 steps, B*ceil(L/8)*H*N*8 bytes
+ * (0 if the sizes are unsupported). */
+EACS_API size_t eacs_ssm_ckpt_size(int64_t B, int64_t L, int64_t H, int64_t N);
+
+/* Training forward of the fused ungated core: eacs_ssm_fwd, and also the
+ * state before every 8th step into `ckpt` (ckpt_bytes >= eacs_ssm_ckpt_size)
+ * for eacs_ssm_bwd.  Replaces the forward of ContinuousSSMLayer's core under
+ * autograd (cst_ssm/modules/continuous_ssm.py:44-55), which keeps dA, dB*u
+ * and h, three (B,L,H,N) complex64 tensors, for its backward
+ * (ops/scan_cuda.py:36-49 saves a and h). */
+EACS_API int eacs_ssm_train_fwd(const void* lam, const float* log_dt, const float* t,
+                                const void* Bc, const void* Cc, const void* u, int u_dtype,
+                                const float* D, float* y, void* ckpt, size_t ckpt_bytes,
+                                int64_t B, int64_t L, int64_t H, int64_t N,
+                                float dt_min, float dt_max, void* stream);
+
+/* Workspace bytes eacs_ssm_bwd needs for these sizes (0 if unsupported). */
+EACS_API size_t eacs_ssm_bwd_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+
+/* Backward of the fused ungated core: given the forward's inputs, its
+ * checkpoints and gy = dLoss/dy (B,L,H) float32, writes du (B,L,H) float32,
+ * dBc, dCc (B,L,N) complex64, dt (B,L) float32 (the gradient of the
+ * timestamps t), dlam (H,N) complex64, dlog_dt (H) and dD (H) float32, all
+ * overwritten.  Replaces what autograd runs for continuous_ssm.py:44-55:
+ * the readout's backward, scan_bwd (ops/csrc/eacs_scan_cuda.cu:79-96 via
+ * ops/scan_cuda.py:44-49) and the backward of zoh_discretize /
+ * effective_dt / the timestamp differences (ops/discretization.py:20-82).
+ * Deterministic: partial sums are added in a fixed order. */
+EACS_API int eacs_ssm_bwd(const void* lam, const float* log_dt, const float* t,
+                          const void* Bc, const void* Cc, const void* u, int u_dtype,
+                          const float* D, const float* gy, const void* ckpt, size_t ckpt_bytes,
+                          float* du, void* dBc, void* dCc, float* dt, void* dlam,
+                          float* dlog_dt, float* dD, void* workspace, size_t workspace_bytes,
+                          int64_t B, int64_t L, int64_t H, int64_t N,
+                          float dt_min, float dt_max, void* stream);
+
 /* Workspace bytes eacs_cell_fwd needs for these sizes. */
 EACS_API size_t eacs_cell_fwd_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
 

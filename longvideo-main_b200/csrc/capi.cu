@@ -84,7 +84,35 @@ int eacs_ssm_fwd(const void* lam, const float* log_dt, const float* t, const voi
                  const void* u, int u_dtype, const float* D, float* y, int64_t B, int64_t L, int64_t H,
                  int64_t N, float dt_min, float dt_max, void* stream) {
     return eacs::ssm_fwd(lam, log_dt, t, Bc, Cc, u, u_dtype, D, y, B, L, H, N, dt_min, dt_max,
-                         static_cast<cudaStream_t>(stream));
+                         nullptr, 0, static_cast<cudaStream_t>(stream));
+}
+
+size_t eacs_ssm_ckpt_size(int64_t B, int64_t L, int64_t H, int64_t N) {
+    return eacs::ssm_ckpt_size(B, L, H, N);
+}
+
+int eacs_ssm_train_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc,
+                       const void* Cc, const void* u, int u_dtype, const float* D, float* y,
+                       void* ckpt, size_t ckpt_bytes, int64_t B, int64_t L, int64_t H, int64_t N,
+                       float dt_min, float dt_max, void* stream) {
+    if (!ckpt) return eacs::fail(EACS_ERR_INVALID, "eacs_ssm_train_fwd: null checkpoint buffer");
+    return eacs::ssm_fwd(lam, log_dt, t, Bc, Cc, u, u_dtype, D, y, B, L, H, N, dt_min, dt_max,
+                         ckpt, ckpt_bytes, static_cast<cudaStream_t>(stream));
+}
+
+size_t eacs_ssm_bwd_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
+    return eacs::ssm_bwd_workspace_size(B, L, H, N);
+}
+
+int eacs_ssm_bwd(const void* lam, const float* log_dt, const float* t, const void* Bc, const void* Cc,
+                 const void* u, int u_dtype, const float* D, const float* gy, const void* ckpt,
+                 size_t ckpt_bytes, float* du, void* dBc, void* dCc, float* dt, void* dlam,
+                 float* dlog_dt, float* dD, void* workspace, size_t workspace_bytes, int64_t B,
+                 int64_t L, int64_t H, int64_t N, float dt_min, float dt_max, void* stream) {
+    eacs::SsmBwdCall c{lam, log_dt, t,  Bc,   Cc,      u,  u_dtype, D,         gy,
+                       ckpt, ckpt_bytes, du, dBc, dCc, dt, dlam, dlog_dt, dD, workspace,
+                       workspace_bytes, B, L, H, N, dt_min, dt_max};
+    return eacs::ssm_bwd(c, static_cast<cudaStream_t>(stream));
 }
 
 int eacs_zoh_kernels(const void* lam, const float* dt, void* dA, void* dB_bar, int64_t M, int64_t H,

@@ -66,7 +66,8 @@ struct Args {
     int4* row;     // [B] {l*, bits(spike after l*-1), bits(r_{l*-1}), 0}
     float2* hpi;   // [B][H][N] committed state for the repair pass
     float* upi;    // [B][H]
-    int B, L, H, N, ntiles;
+    float2* ck;    // UNGATED, optional: [B][nK][H][N] state before step k*kSsmCk
+    int B, L, H, N, ntiles, nK;
 };
 
 // ---------------------------------------------------------------------------
@@ -130,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
     constexpr int NV = MODE == SPEC ? 2 * U : U;  // readout sums per group
     using Shape = BflyShape<NV, LANES>;
     static_assert(kT % U == 0, "chunk must hold whole step groups");
+    static_assert(kT % kSsmCk == 0 && kSsmCk % U == 0, "checkpoints fall on step-group starts");
     __shared__ float2 sB[kT][NP];
     __shared__ float2 sC[kT][NP];
     __shared__ float su[kT][HT];
@@ -201,6 +203,13 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
         __syncthreads();
 
         for (int i0 = 0; i0 < steps; i0 += U) {
+            if (MODE == UNGATED && a.ck != nullptr && ((l0 + i0) % kSsmCk) == 0) {
+                // training forward: checkpoint of the state before step l0 + i0
+                const size_t ko = (static_cast<size_t>(b) * a.nK + (l0 + i0) / kSsmCk) * H + h;
+#pragma unroll
+                for (int j = 0; j < NPT; ++j)
+                    if (nv[j]) a.ck[ko * N + ln + LANES * j] = hs[j];
+            }
             float vals[NV];
 #pragma unroll
             for (int uu = 0; uu < U; ++uu) {
@@ -825,17 +834,29 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
     return EACS_OK;
 }
 
+size_t ssm_ckpt_size(int64_t B, int64_t L, int64_t H, int64_t N) {
+    if (B <= 0 || L <= 0 || H <= 0 || N <= 0 || N > 64) return 0;
+    return static_cast<size_t>(B) * static_cast<size_t>((L + kSsmCk - 1) / kSsmCk) *
+           static_cast<size_t>(H) * static_cast<size_t>(N) * sizeof(float2);
+}
+
 int ssm_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc, const void* Cc,
             const void* u, int u_dtype, const float* D, float* y, int64_t B, int64_t L, int64_t H,
-            int64_t N, float dt_min, float dt_max, cudaStream_t stream) {
-    const char* fn = "eacs_ssm_fwd";
+            int64_t N, float dt_min, float dt_max, void* ckpt, size_t ckpt_bytes,
+            cudaStream_t stream) {
+    const char* fn = ckpt ? "eacs_ssm_train_fwd" : "eacs_ssm_fwd";
     int rc = check_shape(fn, B, L, H, N, u_dtype);
     if (rc) return rc;
     if (B == 0 || L == 0 || H == 0) return EACS_OK;
     if (N == 0) return fail(EACS_ERR_INVALID, "%s: N must be positive", fn);
     if (!lam || !log_dt || !t || !Bc || !Cc || !u || !D || !y)
         return fail(EACS_ERR_INVALID, "%s: null pointer argument", fn);
+    if (ckpt && ckpt_bytes < ssm_ckpt_size(B, L, H, N))
+        return fail(EACS_ERR_WORKSPACE, "%s: checkpoint buffer of %zu bytes needed, %zu given", fn,
+                    ssm_ckpt_size(B, L, H, N), ckpt_bytes);
     Args a{};
+    a.ck = static_cast<float2*>(ckpt);
+    a.nK = static_cast<int>((L + kSsmCk - 1) / kSsmCk);
     a.lam = static_cast<const float2*>(lam);
     a.log_dt = log_dt;
     a.u = u;

@@ -26,6 +26,10 @@ int scan_bwd(const void* a, const void* h, const void* gh, void* ga, void* gb, i
              int64_t L, int64_t C, cudaStream_t stream);
 cudaError_t scan_read_status(int* out, cudaStream_t stream);
 
+// Steps between the state checkpoints of the ungated training forward
+// (eacs_ssm_train_fwd); the backward recomputes one such chunk at a time.
+constexpr int kSsmCk = 8;
+
 // cell.cu
 struct CellCall {
     const void* lam;
@@ -54,9 +58,13 @@ struct CellCall {
 size_t cell_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
 int cell_fwd(const CellCall& c, cudaStream_t stream);
 int cell_fwd_noalloc(const CellCall& c, cudaStream_t stream);
+// ckpt == nullptr: inference; otherwise also writes the state before every
+// kSsmCk-th step to ckpt ([B][ceil(L/kSsmCk)][H][N] complex64).
 int ssm_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc,
             const void* Cc, const void* u, int u_dtype, const float* D, float* y, int64_t B,
-            int64_t L, int64_t H, int64_t N, float dt_min, float dt_max, cudaStream_t stream);
+            int64_t L, int64_t H, int64_t N, float dt_min, float dt_max, void* ckpt,
+            size_t ckpt_bytes, cudaStream_t stream);
+size_t ssm_ckpt_size(int64_t B, int64_t L, int64_t H, int64_t N);
 cudaError_t cell_read_status(int* out, cudaStream_t stream);
 int zoh_kernels(const void* lam, const float* dt, void* dA, void* dBbar, int64_t M, int64_t H,
                 int64_t N, cudaStream_t stream);
@@ -94,6 +102,34 @@ struct TrainBwdCall {
     int64_t B, L, H, N;
 };
 size_t train_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+
+// ssm_train.cu
+struct SsmBwdCall {
+    const void* lam;
+    const float* log_dt;
+    const float* t;
+    const void* Bc;
+    const void* Cc;
+    const void* u;
+    int u_dtype;
+    const float* D;
+    const float* gy;
+    const void* ckpt;
+    size_t ckpt_bytes;
+    float* du;
+    void* dBc;
+    void* dCc;
+    float* dt;
+    void* dlam;
+    float* dlog;
+    float* dD;
+    void* workspace;
+    size_t workspace_bytes;
+    int64_t B, L, H, N;
+    float dt_min, dt_max;
+};
+size_t ssm_bwd_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+int ssm_bwd(const SsmBwdCall& c, cudaStream_t stream);
 int train_bwd(const TrainBwdCall& c, cudaStream_t stream);
 cudaError_t train_read_status(int* out, cudaStream_t stream);
 

@@ -28,6 +28,7 @@ _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _F = ctypes.c_float
 _I = ctypes.c_int
+_SZ = ctypes.c_size_t
 
 # name -> (restype, argtypes); mirrors include/eacs_b200.h
 SIGNATURES = {
@@ -40,6 +41,13 @@ SIGNATURES = {
     "eacs_scan_bwd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "eacs_ssm_fwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _P, _P, _I64, _I64, _I64, _I64, _F, _F, _P]),
     "eacs_zoh_kernels": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "eacs_ssm_ckpt_size": (_SZ, [_I64, _I64, _I64, _I64]),
+    "eacs_ssm_train_fwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ,
+                                _I64, _I64, _I64, _I64, _F, _F, _P]),
+    "eacs_ssm_bwd_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
+    "eacs_ssm_bwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ,
+                          _P, _P, _P, _P, _P, _P, _P, _P, _SZ,
+                          _I64, _I64, _I64, _I64, _F, _F, _P]),
     "eacs_cell_fwd_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I64, _I64]),
     "eacs_cell_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
                            _F, _F, _F, _F, _F, _F, _I, _I, _F, _F, _I, _F,

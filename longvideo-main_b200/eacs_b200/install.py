@@ -12,8 +12,12 @@ from __future__ import annotations
 import importlib
 
 
-def install(package: str = "cst_ssm") -> dict:
-    """Patch `package` (already importable) and return what was replaced."""
+def install(package: str = "cst_ssm", fuse_ungated: bool = False) -> dict:
+    """Patch `package` (already importable) and return what was replaced.
+
+    fuse_ungated: also bind ContinuousSSMLayer.forward to the fused ungated
+    core (eacs_b200.ops.continuous_ssm.layer_forward), which needs no
+    (B,L,H,N) tensors, instead of only swapping its scan extension."""
     from .ops import eacs_gated_scan as ours_cell
     from .ops import scan_cuda as ours_scan
 
@@ -37,4 +41,10 @@ def install(package: str = "cst_ssm") -> dict:
         ref_train.GatedEACSCellFunction = ours_train.GatedEACSCellFunction
         ref_train.fused_gated_scan = ours_train.fused_gated_scan
         patched["eacs_cell_train.fused_gated_scan"] = ours_train.fused_gated_scan
+    if fuse_ungated:
+        from .ops import continuous_ssm as ours_ssm
+
+        ref_layer = importlib.import_module(f"{package}.modules.continuous_ssm")
+        ref_layer.ContinuousSSMLayer.forward = ours_ssm.layer_forward
+        patched["continuous_ssm.ContinuousSSMLayer.forward"] = ours_ssm.layer_forward
     return patched
