@@ -64,7 +64,9 @@ def parse():
                     help="budget of the CPU baseline sample (rank 0, N=1)")
     ap.add_argument("--profile", action="store_true",
                     help="device-timed section only (no e2e, no CPU sample): for ncu captures")
-    ap.add_argument("--workload", choices=["cell", "scan", "ssm", "train", "multiscale"],
+    ap.add_argument("--shape", default=None,
+                    help="B,L,H,N override for --workload ssm_train (e.g. a small case for ncu)")
+    ap.add_argument("--workload", choices=["cell", "scan", "ssm", "ssm_train", "train", "multiscale"],
                     default="cell", help="cell (default) is the headline; the others are the "
                     "materialised scan, the fused ungated SSM, the training step and the "
                     "three-branch multiscale cell")

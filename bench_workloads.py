@@ -161,6 +161,119 @@ def wl_ssm(args, dev, flush):
                    "alg_bytes_per_launch": alg})
 
 
+class _RefScan(torch.autograd.Function):
+    """The reference's _SelectiveScanCUDA (cst_ssm/ops/scan_cuda.py:36-49) over its
+    own K1/K2 kernels built for sm_100a."""
+
+    @staticmethod
+    def forward(ctx, a, b, ext):
+        h = ext.scan_fwd(a.contiguous(), b.contiguous())[0]
+        ctx.save_for_backward(a, h)
+        ctx.ext = ext
+        return h
+
+    @staticmethod
+    def backward(ctx, gh):
+        a, h = ctx.saved_tensors
+        ga, gb = ctx.ext.scan_bwd(a, h, gh.contiguous())
+        return ga, gb, None
+
+
+def ref_ssm_core(lam, log_dt, t, Bc, Cc, u, D, ext):
+    """ContinuousSSMLayer's core as the reference computes it under autograd
+    (continuous_ssm.py:44-55 with discretization.py:10-82): materialised dt_eff,
+    dA, dB, dB*u (B,L,H,N) complex64, the scan, the einsum readout."""
+    dt = torch.zeros_like(t)
+    dt[:, 1:] = (t[:, 1:] - t[:, :-1]).clamp_min(0)
+    dt[:, 0] = dt[:, 1]
+    dte = (dt.unsqueeze(-1) * torch.exp(log_dt)).clamp_min(1e-3).clamp_max(1e3)
+    z = lam * dte.unsqueeze(-1).to(torch.complex64)
+    dA = torch.exp(z)
+    em1 = torch.complex(torch.expm1(z.real) * torch.cos(z.imag) - 2 * torch.sin(0.5 * z.imag) ** 2,
+                        torch.exp(z.real) * torch.sin(z.imag))
+    dB = em1 * torch.reciprocal(lam) * Bc.unsqueeze(2)
+    dBu = dB * u.float().unsqueeze(-1)
+    h = _RefScan.apply(dA, dBu, ext)
+    return torch.einsum("bln,blhn->blh", Cc, h).real + D * u.float()
+
+
+def wl_ssm_train(args, dev, flush):
+    """Fused ungated SSM core, forward + backward (SSMCoreFunction), one branch of
+    config 2 (B=4 L=16384 H=1024 N=16, bf16 u); beside it, at B=1 L=4096 (where
+    its materialised (B,L,H,N) tensors fit), the reference's autograd path over
+    its own scan kernels and ours on the same tensors."""
+    from eacs_b200 import _lib
+    from eacs_b200.ops.continuous_ssm import _backward, _forward, _prepare, ssm_forward
+
+    def make(B, L, H, N, seed):
+        g = torch.Generator().manual_seed(seed)
+        d = cell_inputs(g, B, L, H, N, (0.5, 64.0), dev, torch.bfloat16)
+        gy = torch.randn(B, L, H, generator=g).to(dev)
+        leaves = {k: d[k].clone().requires_grad_(True) for k in ("lam", "log_dt", "Bc", "Cc", "u", "D")}
+        return d, gy, leaves
+
+    def ours(d, gy, lv):
+        y = ssm_forward(lv["lam"], lv["log_dt"], d["t"], lv["Bc"], lv["Cc"], lv["u"], lv["D"])
+        torch.autograd.backward([y], [gy])
+
+    B, L, H, N = 4, 16384, 1024, 16
+    if getattr(args, "shape", None):
+        B, L, H, N = (int(v) for v in args.shape.split(","))
+    d, gy, lv = make(B, L, H, N, 11)
+    nsteps = max(3, args.steps // 10)
+    st, _ = timed(lambda: ours(d, gy, lv), nsteps, 2, flush, False)
+    upd = B * L * H * N
+    n0 = _lib.kernel_launches()
+    ours(d, gy, lv)
+    torch.cuda.synchronize()
+    launches = _lib.kernel_launches() - n0
+    # the two chain kernels on their own (autograd runs the backward on its
+    # own thread, where the library's per-thread timing events are not set)
+    dev_, prep = _prepare(*(lv[k].detach() if k in lv else d[k]
+                            for k in ("lam", "log_dt", "t", "Bc", "Cc", "u", "D")))
+    _, ck = _forward(prep, dev_, 1e-3, 1e3, True)
+    _, fk = timed(lambda: _forward(prep, dev_, 1e-3, 1e3, True), nsteps, 2, flush, True)
+    _, kt = timed(lambda: _backward(prep, ck, gy, 1e-3, 1e3), nsteps, 2, flush, True)
+    k_s = statistics.median(kt) / 1e3
+    # backward chain kernel algorithmic bytes: inputs re-read (u bf16, gy fp32, Bc, Cc, t),
+    # checkpoints read, du fp32 written, per-tile dB/dC partials written
+    lanes = 4 if N <= 8 else 8 if N <= 16 else 16 if N <= 32 else 32
+    ntiles = -(-H // (128 // lanes))  # backward CTAs per row: 128 threads, `lanes` per channel
+    alg = (B * L * H * (2 + 4 + 4) + 2 * B * L * N * 8 + B * L * 4 + B * ((L + 7) // 8) * H * N * 8
+           + B * ntiles * L * N * 16)
+    peak, src = peak_hbm()
+    extra = {}
+    ext = None if args.profile else load_ref("ref_eacs_scan_cuda")
+    if ext is not None:
+        Bs, Ls = 1, 4096
+        d2, gy2, lv2 = make(Bs, Ls, H, N, 12)
+
+        def ref():
+            y = ref_ssm_core(lv2["lam"], lv2["log_dt"], d2["t"], lv2["Bc"], lv2["Cc"], lv2["u"], lv2["D"], ext)
+            torch.autograd.backward([y], [gy2])
+
+        rt, _ = timed(ref, 3, 1, flush, False)
+        ot, _ = timed(lambda: ours(d2, gy2, lv2), 5, 2, flush, False)
+        u2 = Bs * Ls * H * N
+        extra["reference_torch_autograd_gpu"] = {
+            "workload": "reference autograd path (torch ops + its K1/K2 scan kernels)",
+            "B": Bs, "L": Ls, "H": H, "N": N, "ms_per_step": statistics.median(rt),
+            "Gstate_updates_per_s": u2 / (statistics.median(rt) / 1e3) / 1e9,
+            "ours_same_shape_ms": statistics.median(ot),
+            "ours_same_shape_Gstate_updates_per_s": u2 / (statistics.median(ot) / 1e3) / 1e9}
+    line("EACS fused ungated SSM training fwd+bwd Gstate-updates/s",
+         upd / (statistics.median(st) / 1e3) / 1e9, len(st), 2, statistics.median(st),
+         {"workload": "ContinuousSSMLayer core fwd+bwd fused (checkpoint every 8 steps)", "B": B,
+          "L": L, "H": H, "N": N, "u_dtype": "bf16", "l2": "flushed between steps"},
+         roofline={"bound": "issue (FP32/MUFU); hbm fraction shown", "achieved": alg / k_s / 1e9,
+                   "peak": peak, "unit": "GB/s", "frac": alg / k_s / 1e9 / peak, "peak_source": src,
+                   "kernel": "ssm_bwd_chain", "kernel_ms": k_s * 1e3,
+                   "kernel_Gstate_updates_per_s": upd / k_s / 1e9, "alg_bytes_per_launch": alg,
+                   "forward_chain_kernel_ms": statistics.median(fk),
+                   "forward_chain_Gstate_updates_per_s": upd / (statistics.median(fk) / 1e3) / 1e9},
+         gpu_launches=launches, **extra)
+
+
 def wl_train(args, dev, flush):
     """Config 3: GatedEACSCellFunction forward + backward, B=8 L=8192 H=768 N=16, bf16 u."""
     from eacs_b200.ops.eacs_cell_train import fused_gated_scan
@@ -176,7 +289,17 @@ def wl_train(args, dev, flush):
                                      leaves["log_dt"], leaves["D"], eps, d["mean"], d["var"], 0.1, 1e-6)
         torch.autograd.backward([y], [gy])
 
-    st, kt = timed(step, max(3, args.steps // 10), 2, flush, True)
+    nsteps = max(3, args.steps // 10)
+    st, _ = timed(step, nsteps, 2, flush, False)
+    # the backward kernel on its own (autograd runs it on its own thread, where
+    # the library's per-thread timing events are not set)
+    from eacs_b200.ops.eacs_cell_train import _train_bwd, _train_fwd
+    det = {k: v.detach() for k, v in leaves.items()}
+    _, gs_, rs_, stats_, prep = _train_fwd(det["u"], det["Bc"], det["Cc"], d["t"], det["lam"],
+                                           det["log_dt"], det["D"], 0.12, d["mean"], d["var"], 0.1,
+                                           1e-6, 1e-5, 1.0, "ste", 1e3)
+    _, kt = timed(lambda: _train_bwd(prep, gs_, rs_, stats_, 0.12, 0.1, 1e-6, 1e-5, 1.0, 1e3, gy,
+                                     None, None, None), nsteps, 2, flush, True)
     upd = B * L * H * N
     rate = float(fused_gated_scan(leaves["u"], leaves["Bc"], leaves["Cc"], d["t"], leaves["lam"],
                                   leaves["log_dt"], leaves["D"], eps, d["mean"], d["var"], 0.1,
@@ -186,7 +309,8 @@ def wl_train(args, dev, flush):
          {"workload": "GatedEACSCellFunction fwd+bwd (STE, T=0.1)", "B": B, "L": L, "H": H, "N": N,
           "u_dtype": "bf16", "update_rate": rate, "l2": "flushed between steps"},
          backward_kernel_ms=statistics.median(kt),
-         note="kernel_ms is the cluster backward kernel (train_bwd) alone")
+         backward_kernel_Gstate_updates_per_s=upd / (statistics.median(kt) / 1e3) / 1e9,
+         note="backward_kernel_ms is the cluster backward kernel (train_bwd) alone")
 
 
 def wl_multiscale(args, dev, flush):
@@ -231,7 +355,8 @@ def run_workload(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    {"scan": wl_scan, "ssm": wl_ssm, "train": wl_train, "multiscale": wl_multiscale}[args.workload](
+    {"scan": wl_scan, "ssm": wl_ssm, "ssm_train": wl_ssm_train, "train": wl_train,
+     "multiscale": wl_multiscale}[args.workload](
         args, dev, flush)
     from eacs_b200 import _lib
     assert _lib.device_status() == 0

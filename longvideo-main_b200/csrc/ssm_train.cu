@@ -23,11 +23,12 @@
 // chain kernel (eacs_ssm_train_fwd).  One CTA per (row, tile of channels)
 // walks the chunks from last to first: it recomputes the chunk forward from
 // its checkpoint into shared memory (h_{l-1}, dA, dB_bar per chain and step),
-// then runs the chunk in reverse.  Sums over n (du, ddte) use a transposed
-// shuffle butterfly within a channel group; sums over h (dB, dC) a transposed
-// butterfly across the warp's channel groups, then shared memory across
-// warps, then one partial per (row, tile, step) in the workspace.  Post
-// kernels add the tile and row partials in a fixed order (deterministic).
+// then runs the chunk in reverse, while the next chunk's inputs load into
+// registers.  Sums over n (du, ddte) use a transposed shuffle butterfly
+// within a channel group; each chain's dB, dC terms go to its own shared
+// slot and the chunk's output pass sums them over the CTA's channels, one
+// partial per (row, tile, step) in the workspace.  Post kernels add the tile
+// and row partials in a fixed order (deterministic).
 #include <algorithm>
 
 #include "eacs_common.cuh"
@@ -120,38 +121,37 @@ template <int LANES, int NPT>
 struct BwdSmem {
     static constexpr int HT = kBT / LANES;
     static constexpr int NP = LANES * NPT;
-    static constexpr int NW = kBT / 32;
     static constexpr size_t kAB = static_cast<size_t>(kK) * NPT * kBT * sizeof(float4);
     static constexpr size_t kH = static_cast<size_t>(kK) * NPT * kBT * sizeof(float2);
     static constexpr size_t kBC = 2ull * kK * NP * sizeof(float2);
-    static constexpr size_t kRed = static_cast<size_t>(kK) * NW * NP * sizeof(float4);
     static constexpr size_t kRow = 4ull * kK * HT * sizeof(float) + kK * sizeof(float);
-    static constexpr size_t bytes = kAB + kH + kBC + kRed + kRow;
+    static constexpr size_t bytes = kAB + kH + kBC + kRow;
 };
 
 template <int LANES, int NPT, typename UT>
-__global__ void __launch_bounds__(kBT, 3) ssm_bwd_chain(SArgs a) {
+__global__ void __launch_bounds__(kBT, NPT == 1 ? 5 : 4) ssm_bwd_chain(SArgs a) {
     using SM = BwdSmem<LANES, NPT>;
-    constexpr int HT = SM::HT, NP = SM::NP, NW = SM::NW, U = kU;
-    constexpr int VN = 2 * U;            // per group: du and ddte of U steps (sum over n)
-    constexpr int VH = 4 * NPT * U;      // per group: dB, dC of U steps and NPT chains (sum over h)
+    constexpr int HT = SM::HT, NP = SM::NP, U = kU;
+    constexpr int VN = 2 * U;                      // per group: du and ddte of U steps (sum over n)
+    constexpr int PB = (kK * NP + kBT - 1) / kBT;  // prefetched B, C entries per thread
+    constexpr int PU = (kK * HT + kBT - 1) / kBT;  // prefetched u, gy entries per thread
     using SN = FoldShape<VN, LANES / 2, 1>;
-    using SH = FoldShape<VH, 16, LANES, 4>;
-    static_assert(SH::kRem % 4 == 0, "over-h sums are stored as float4 (dB, dC)");
 
     extern __shared__ __align__(16) unsigned char smem[];
-    float4* sAB = reinterpret_cast<float4*>(smem);                     // [kK][NPT][kBT] (dA, dB_bar)
+    // [kK][NPT][kBT]: (dA, dB_bar) from the recompute; the reverse step
+    // overwrites its own slot with (u w conj(dB_bar), gy conj(h)), which the
+    // chunk's output pass then sums over the CTA's channels
+    float4* sAB = reinterpret_cast<float4*>(smem);
     float2* sH = reinterpret_cast<float2*>(smem + SM::kAB);            // [kK][NPT][kBT] h_{l-1}
     float2* sB = reinterpret_cast<float2*>(smem + SM::kAB + SM::kH);   // [kK][NP]
     float2* sC = sB + kK * NP;                                         // [kK][NP]
-    float4* sred = reinterpret_cast<float4*>(sC + kK * NP);            // [kK][NW][NP]
-    float* su = reinterpret_cast<float*>(sred + kK * NW * NP);         // [kK][HT]
+    float* su = reinterpret_cast<float*>(sC + kK * NP);                // [kK][HT]
     float* sg = su + kK * HT;                                          // [kK][HT] gy
     float* sdu = sg + kK * HT;                                         // [kK][HT]
     float* sdt = sdu + kK * HT;                                        // [kK][HT]
     float* sdel = sdt + kK * HT;                                       // [kK] dt before the clamp
 
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int tid = threadIdx.x;
     const int ln = tid % LANES, hl = tid / LANES;
     const int tile = blockIdx.x, b = blockIdx.y;
     const int h0 = tile * HT, h = h0 + hl;
@@ -175,41 +175,105 @@ __global__ void __launch_bounds__(kBT, 3) ssm_bwd_chain(SArgs a) {
     const float dt0 = L > 1 ? fmaxf(a.t[rowL + 1] - a.t[rowL], 0.f) : 0.f;
     const int heldN = SN::held(ln);
     const bool wN = SN::writer(ln);
-    const int heldH = SH::held(lane);
-    const bool wH = SH::writer(lane);
     float glog = 0.f, gD = 0.f;
 
-    for (int k = a.nK - 1; k >= 0; --k) {
+    // Registers holding the next chunk's inputs, loaded while the current
+    // chunk runs; steps past L and padded chains read zeros.
+    float2 pB[PB], pC[PB], pck[NPT];
+    UT pu[PU];
+    float pg[PU], pt1 = 0.f, pt0 = 0.f;  // raw loads; converted when staged
+    const UT uzero = static_cast<UT>(0.f);
+    auto prefetch = [&](int k) {
         const int l0 = k * kK;
         const int steps = min(kK, L - l0);
-        __syncthreads();  // the previous chunk is done with shared memory
-        // ---- stage the chunk; steps past L and padded chains read zeros ----
-        for (int idx = tid; idx < kK * NP; idx += kBT) {
+#pragma unroll
+        for (int r = 0; r < PB; ++r) {
+            const int idx = tid + r * kBT;
             const int i = idx / NP, n = idx % NP;
-            const bool ok = i < steps && n < N;
+            const bool ok = idx < kK * NP && i < steps && n < N;
             const size_t o = (rowL + l0 + i) * N + n;
-            sB[idx] = ok ? a.Bc[o] : make_float2(0.f, 0.f);
-            sC[idx] = ok ? a.Cc[o] : make_float2(0.f, 0.f);
+            pB[r] = ok ? a.Bc[o] : make_float2(0.f, 0.f);
+            pC[r] = ok ? a.Cc[o] : make_float2(0.f, 0.f);
         }
-        for (int idx = tid; idx < kK * HT; idx += kBT) {
+#pragma unroll
+        for (int r = 0; r < PU; ++r) {
+            const int idx = tid + r * kBT;
             const int i = idx / HT, c = idx % HT;
-            const bool ok = i < steps && h0 + c < H;
+            const bool ok = idx < kK * HT && i < steps && h0 + c < H;
             const size_t o = (rowL + l0 + i) * H + h0 + c;
-            su[idx] = ok ? to_f32(u[o]) : 0.f;
-            sg[idx] = ok ? a.gy[o] : 0.f;
+            pu[r] = ok ? u[o] : uzero;
+            pg[r] = ok ? a.gy[o] : 0.f;
         }
-        if (tid < kK) {
-            const int l = l0 + tid;
-            float d = 0.f;
-            if (tid < steps) d = l == 0 ? dt0 : fmaxf(a.t[rowL + l] - a.t[rowL + l - 1], 0.f);
-            sdel[tid] = d;
+        if (tid < kK && tid < steps && l0 + tid > 0) {
+            pt1 = a.t[rowL + l0 + tid];
+            pt0 = a.t[rowL + l0 + tid - 1];
         }
-        float2 hs[NPT];
         const size_t ko = (static_cast<size_t>(b) * a.nK + k) * H + (hv ? h : 0);
 #pragma unroll
         for (int j = 0; j < NPT; ++j)
-            hs[j] = nv[j] ? a.ck[ko * N + ln + LANES * j] : make_float2(0.f, 0.f);
+            pck[j] = nv[j] ? a.ck[ko * N + ln + LANES * j] : make_float2(0.f, 0.f);
+    };
+    // Chunk outputs: dB, dC summed over the CTA's channels, du, and the
+    // channels' sum of d(dt_l) per step.
+    auto emit = [&](int k) {
+        const int l0 = k * kK;
+        const int steps = min(kK, L - l0);
+        for (int idx = tid; idx < steps * N; idx += kBT) {
+            const int i = idx / N, n = idx % N;
+            const float4* src = sAB + (i * NPT + n / LANES) * kBT + n % LANES;
+            float4 acc = src[0];
+#pragma unroll
+            for (int c = 1; c < HT; ++c) {
+                const float4 v = src[c * LANES];
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+            a.part[((static_cast<size_t>(b) * a.ntiles + tile) * L + l0 + i) * N + n] = acc;
+        }
+        for (int idx = tid; idx < steps * HT; idx += kBT) {
+            const int i = idx / HT, c = idx % HT;
+            if (h0 + c < H) a.du[(rowL + l0 + i) * H + h0 + c] = sdu[idx];
+        }
+        if (tid < steps) {
+            float sum = 0.f;
+#pragma unroll
+            for (int c = 0; c < HT; ++c) sum += sdt[tid * HT + c];
+            a.pt[(static_cast<size_t>(b) * a.ntiles + tile) * L + l0 + tid] = sum;
+        }
+    };
+
+    prefetch(a.nK - 1);
+    for (int k = a.nK - 1; k >= 0; --k) {
+        __syncthreads();  // the reverse pass of chunk k+1 is done everywhere
+        if (k + 1 < a.nK) emit(k + 1);
+        // ---- stage chunk k from the prefetch registers ----
+#pragma unroll
+        for (int r = 0; r < PB; ++r) {
+            const int idx = tid + r * kBT;
+            if (idx < kK * NP) {
+                sB[idx] = pB[r];
+                sC[idx] = pC[r];
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < PU; ++r) {
+            const int idx = tid + r * kBT;
+            if (idx < kK * HT) {
+                su[idx] = to_f32(pu[r]);
+                sg[idx] = pg[r];
+            }
+        }
+        if (tid < kK) {
+            const int l = k * kK + tid;
+            sdel[tid] = l >= L ? 0.f : (l == 0 ? dt0 : fmaxf(pt1 - pt0, 0.f));
+        }
+        float2 hs[NPT];
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) hs[j] = pck[j];
         __syncthreads();
+        if (k > 0) prefetch(k - 1);
 
         // ---- forward recompute of the chunk from its checkpoint ----
 #pragma unroll
@@ -233,7 +297,7 @@ __global__ void __launch_bounds__(kBT, 3) ssm_bwd_chain(SArgs a) {
 #pragma unroll 1
         for (int g = kK / U - 1; g >= 0; --g) {
             const int i0 = g * U;
-            float vn[VN], vh[VH];
+            float vn[VN];
 #pragma unroll
             for (int uu = U - 1; uu >= 0; --uu) {
                 const int i = i0 + uu;
@@ -262,11 +326,9 @@ __global__ void __launch_bounds__(kBT, 3) ssm_bwd_chain(SArgs a) {
                     acc2[j] = make_float2(fmaf(dte, az.x, acc2[j].x), fmaf(dte, az.y, acc2[j].y));
                     dzn = fmaf(az.x, lam[j].x, fmaf(az.y, lam[j].y, dzn));
                     const float2 uw = cscale(w, ul);
-                    const int v0 = (uu * NPT + j) * 4;
-                    vh[v0 + 0] = uw.x * dB.x + uw.y * dB.y;  // u w conj(dB_bar)
-                    vh[v0 + 1] = uw.y * dB.x - uw.x * dB.y;
-                    vh[v0 + 2] = yb * hs[j].x;               // gy conj(h_l)
-                    vh[v0 + 3] = -yb * hs[j].y;
+                    // (u w conj(dB_bar), gy conj(h_l)) into this chain's slot
+                    sAB[si] = make_float4(uw.x * dB.x + uw.y * dB.y, uw.y * dB.x - uw.x * dB.y,
+                                          yb * hs[j].x, -yb * hs[j].y);
                     s[j] = make_float2(dA.x * w.x + dA.y * w.y, dA.x * w.y - dA.y * w.x);  // conj(dA) w
                     hs[j] = hp;
                 }
@@ -291,44 +353,10 @@ __global__ void __launch_bounds__(kBT, 3) ssm_bwd_chain(SArgs a) {
                     }
                 }
             }
-            // sums over the warp's channel groups: dB, dC per (step, n)
-            Fold<VH, 16, LANES, 4>::run(vh, lane);
-            if (wH) {
-#pragma unroll
-                for (int r = 0; r < SH::kRem; r += 4) {
-                    const int orig = heldH + r;
-                    const int j = (orig / 4) % NPT, uu = orig / (4 * NPT);
-                    sred[((i0 + uu) * NW + wid) * NP + ln + LANES * j] =
-                        make_float4(vh[r], vh[r + 1], vh[r + 2], vh[r + 3]);
-                }
-            }
-        }
-        __syncthreads();
-        // ---- chunk outputs ----
-        for (int idx = tid; idx < steps * N; idx += kBT) {
-            const int i = idx / N, n = idx % N;
-            float4 acc = sred[(i * NW) * NP + n];
-#pragma unroll
-            for (int w = 1; w < NW; ++w) {
-                const float4 v = sred[(i * NW + w) * NP + n];
-                acc.x += v.x;
-                acc.y += v.y;
-                acc.z += v.z;
-                acc.w += v.w;
-            }
-            a.part[((static_cast<size_t>(b) * a.ntiles + tile) * L + l0 + i) * N + n] = acc;
-        }
-        for (int idx = tid; idx < steps * HT; idx += kBT) {
-            const int i = idx / HT, c = idx % HT;
-            if (h0 + c < H) a.du[(rowL + l0 + i) * H + h0 + c] = sdu[idx];
-        }
-        if (tid < steps) {
-            float sum = 0.f;
-#pragma unroll
-            for (int c = 0; c < HT; ++c) sum += sdt[tid * HT + c];
-            a.pt[(static_cast<size_t>(b) * a.ntiles + tile) * L + l0 + tid] = sum;
         }
     }
+    __syncthreads();
+    emit(0);
     // ---- per-row parameter partials ----
 #pragma unroll
     for (int o = LANES / 2; o > 0; o >>= 1) glog += __shfl_xor_sync(0xffffffffu, glog, o);
@@ -410,12 +438,23 @@ __global__ void ssm_post_params(SArgs a) {
     }
 }
 
+#ifndef EACS_SSMBWD_NPT
+#define EACS_SSMBWD_NPT 2
+#endif
+// Thread layout of the backward: LANES threads per channel, NPT chains each.
+void bwd_shape(int N, int* lanes, int* npt) {
+    *npt = EACS_SSMBWD_NPT;
+    if (EACS_SSMBWD_NPT == 1) {
+        *lanes = N <= 4 ? 4 : N <= 8 ? 8 : N <= 16 ? 16 : 32;
+        if (N > 32) *npt = 2;
+    } else {
+        *lanes = N <= 8 ? 4 : N <= 16 ? 8 : N <= 32 ? 16 : 32;
+    }
+}
 int bwd_lanes(int N) {
-    if (N <= 8) return 4;
-    if (N <= 16) return 8;
-    if (N <= 32) return 16;
-    if (N <= 64) return 32;
-    return 0;
+    int lanes, npt;
+    bwd_shape(N, &lanes, &npt);
+    return lanes;
 }
 
 size_t align_up(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -435,9 +474,8 @@ SWs ws_layout(int64_t B, int64_t L, int64_t H, int64_t N) {
     return w;
 }
 
-template <int LANES, typename UT>
+template <int LANES, int NPT, typename UT>
 cudaError_t launch_bwd(const SArgs& a, cudaStream_t s) {
-    constexpr int NPT = 2;
     const size_t smem = BwdSmem<LANES, NPT>::bytes;
     cudaError_t e = cudaFuncSetAttribute(ssm_bwd_chain<LANES, NPT, UT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -451,12 +489,23 @@ cudaError_t launch_bwd(const SArgs& a, cudaStream_t s) {
 
 template <typename UT>
 cudaError_t bwd_by_n(const SArgs& a, cudaStream_t s) {
-    switch (bwd_lanes(a.N)) {
-        case 4: return launch_bwd<4, UT>(a, s);
-        case 8: return launch_bwd<8, UT>(a, s);
-        case 16: return launch_bwd<16, UT>(a, s);
-        default: return launch_bwd<32, UT>(a, s);
+    int lanes, npt;
+    bwd_shape(a.N, &lanes, &npt);
+#if EACS_SSMBWD_NPT == 1
+    switch (lanes) {
+        case 4: return launch_bwd<4, 1, UT>(a, s);
+        case 8: return launch_bwd<8, 1, UT>(a, s);
+        case 16: return launch_bwd<16, 1, UT>(a, s);
+        default: return npt == 1 ? launch_bwd<32, 1, UT>(a, s) : launch_bwd<32, 2, UT>(a, s);
     }
+#else
+    switch (lanes) {
+        case 4: return launch_bwd<4, 2, UT>(a, s);
+        case 8: return launch_bwd<8, 2, UT>(a, s);
+        case 16: return launch_bwd<16, 2, UT>(a, s);
+        default: return launch_bwd<32, 2, UT>(a, s);
+    }
+#endif
 }
 
 }  // namespace

@@ -12,12 +12,16 @@ from __future__ import annotations
 import importlib
 
 
-def install(package: str = "cst_ssm", fuse_ungated: bool = False) -> dict:
+def install(package: str = "cst_ssm", fuse_ungated: bool = False,
+            layer_dispatch: bool = False) -> dict:
     """Patch `package` (already importable) and return what was replaced.
 
     fuse_ungated: also bind ContinuousSSMLayer.forward to the fused ungated
     core (eacs_b200.ops.continuous_ssm.layer_forward), which needs no
-    (B,L,H,N) tensors, instead of only swapping its scan extension."""
+    (B,L,H,N) tensors, instead of only swapping its scan extension.
+    layer_dispatch: also bind EACSLayer._cuda_fused_ok / _forward_fused to
+    eacs_b200.ops.eacs_layer, so eval-mode layers with robust_guard run the
+    fused kernel instead of the Python step loop."""
     from .ops import eacs_gated_scan as ours_cell
     from .ops import scan_cuda as ours_scan
 
@@ -47,4 +51,11 @@ def install(package: str = "cst_ssm", fuse_ungated: bool = False) -> dict:
         ref_layer = importlib.import_module(f"{package}.modules.continuous_ssm")
         ref_layer.ContinuousSSMLayer.forward = ours_ssm.layer_forward
         patched["continuous_ssm.ContinuousSSMLayer.forward"] = ours_ssm.layer_forward
+    if layer_dispatch:
+        from .ops import eacs_layer as ours_layer
+
+        ref_eacs = importlib.import_module(f"{package}.modules.eacs")
+        ref_eacs.EACSLayer._cuda_fused_ok = ours_layer.cuda_fused_ok
+        ref_eacs.EACSLayer._forward_fused = ours_layer.forward_fused
+        patched["eacs.EACSLayer._forward_fused"] = ours_layer.forward_fused
     return patched

@@ -1,0 +1,99 @@
+"""eacs_b200.install() against an unmodified reference checkout (CPU only).
+
+Runs only where the reference is importable: the checkout given by the
+CST_SSM_REFERENCE environment variable, default /root/reference.  Checks that
+every hook the reference's lazy loaders and dispatch go through is replaced,
+that the replaced layer paths keep the reference's CPU behaviour where the
+reference falls back (EACSLayer on CPU) and that the fused ungated layer
+refuses CPU tensors instead of silently running elsewhere.
+"""
+import importlib
+import os
+import sys
+
+import pytest
+import torch
+
+REF = os.environ.get("CST_SSM_REFERENCE", "/root/reference")
+pytestmark = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "cst_ssm")),
+                                reason="reference checkout not present")
+
+
+@pytest.fixture()
+def ref_pkg():
+    sys.path.insert(0, REF)
+    try:
+        mods = {n: importlib.import_module(f"cst_ssm.{n}") for n in
+                ("ops.scan_cuda", "ops.eacs_gated_scan", "ops.eacs_cell_train",
+                 "modules.continuous_ssm", "modules.eacs")}
+    except ImportError as e:
+        sys.path.remove(REF)
+        pytest.skip(f"reference not importable: {e}")
+    saved = {
+        "scan": (mods["ops.scan_cuda"]._EXT, mods["ops.scan_cuda"]._TRIED),
+        "cell": (mods["ops.eacs_gated_scan"]._EXT, mods["ops.eacs_gated_scan"]._TRIED),
+        "train": (mods["ops.eacs_cell_train"].GatedEACSCellFunction,
+                  mods["ops.eacs_cell_train"].fused_gated_scan),
+        "ssm_fwd": mods["modules.continuous_ssm"].ContinuousSSMLayer.forward,
+        "ok": mods["modules.eacs"].EACSLayer._cuda_fused_ok,
+        "fused": mods["modules.eacs"].EACSLayer._forward_fused,
+    }
+    yield mods
+    mods["ops.scan_cuda"]._EXT, mods["ops.scan_cuda"]._TRIED = saved["scan"]
+    mods["ops.eacs_gated_scan"]._EXT, mods["ops.eacs_gated_scan"]._TRIED = saved["cell"]
+    (mods["ops.eacs_cell_train"].GatedEACSCellFunction,
+     mods["ops.eacs_cell_train"].fused_gated_scan) = saved["train"]
+    mods["modules.continuous_ssm"].ContinuousSSMLayer.forward = saved["ssm_fwd"]
+    mods["modules.eacs"].EACSLayer._cuda_fused_ok = saved["ok"]
+    mods["modules.eacs"].EACSLayer._forward_fused = saved["fused"]
+    sys.path.remove(REF)
+
+
+def test_install_replaces_every_hook(ref_pkg):
+    import eacs_b200
+    from eacs_b200.ops import continuous_ssm, eacs_cell_train, eacs_layer
+    from eacs_b200.ops import eacs_gated_scan as ours_cell
+    from eacs_b200.ops import scan_cuda as ours_scan
+
+    patched = eacs_b200.install("cst_ssm", fuse_ungated=True, layer_dispatch=True)
+    assert ref_pkg["ops.scan_cuda"]._EXT is ours_scan.EXT and ref_pkg["ops.scan_cuda"]._TRIED
+    assert ref_pkg["ops.eacs_gated_scan"]._EXT is ours_cell.EXT
+    assert ref_pkg["ops.eacs_cell_train"].fused_gated_scan is eacs_cell_train.fused_gated_scan
+    assert (ref_pkg["ops.eacs_cell_train"].GatedEACSCellFunction
+            is eacs_cell_train.GatedEACSCellFunction)
+    assert ref_pkg["modules.continuous_ssm"].ContinuousSSMLayer.forward is continuous_ssm.layer_forward
+    assert ref_pkg["modules.eacs"].EACSLayer._forward_fused is eacs_layer.forward_fused
+    assert len(patched) == 5
+    # the extension objects expose the reference's method names
+    for name in ("scan_fwd", "scan_bwd"):
+        assert callable(getattr(ours_scan.EXT, name))
+    assert callable(ours_cell.EXT.eacs_cell_fwd)
+
+
+def test_robust_layer_on_cpu_keeps_reference_path(ref_pkg):
+    """On CPU the patched dispatch declines (as the reference's does) and the
+    reference's step loop runs, with robust_guard."""
+    import eacs_b200
+    from cst_ssm.ops.spectral_init import BranchSpec
+
+    eacs_b200.install("cst_ssm", layer_dispatch=True)
+    EACSLayer = ref_pkg["modules.eacs"].EACSLayer
+    torch.manual_seed(0)
+    layer = EACSLayer(16, BranchSpec("t", n_state=4, tau_min=0.5, tau_max=4.0), robust_guard=True).eval()
+    x = torch.randn(2, 12, 16)
+    t = torch.cumsum(torch.full((2, 12), 0.25), 1)
+    assert not layer._cuda_fused_ok(x)
+    out = layer(x, t)
+    assert out.y.shape == (2, 12, 16) and out.gates.shape == (2, 12)
+    assert torch.equal(out.innovation, out.residual)
+
+
+def test_fused_ungated_layer_refuses_cpu(ref_pkg):
+    import eacs_b200
+    from cst_ssm.ops.spectral_init import BranchSpec
+
+    eacs_b200.install("cst_ssm", fuse_ungated=True)
+    layer = ref_pkg["modules.continuous_ssm"].ContinuousSSMLayer(
+        16, BranchSpec("t", n_state=4, tau_min=0.5, tau_max=4.0))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        layer(torch.randn(1, 5, 16), torch.cumsum(torch.full((1, 5), 0.25), 1))
