@@ -210,6 +210,49 @@ EACS_API int eacs_cell_train_bwd(const void* lam, const float* log_dt, const voi
                                  void* workspace, size_t workspace_bytes,
                                  int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
 
+/* Workspace bytes eacs_cell_commits needs (eacs_cell_fwd's plus one int per
+ * (b, l)); 0 if the sizes are unsupported. */
+EACS_API size_t eacs_cell_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+
+/* Gated cell (hard gate, optional robust_guard) that also records the
+ * committed state after every step, for continuous-time queries.
+ * Replaces EACSLayer.run_with_commits / _commit_range
+ * (cst_ssm/modules/eacs.py:386-439) after the projections: outputs y, gate,
+ * resid as eacs_cell_fwd, and commit_h (B,L,H,N) complex64 = h_pi after step
+ * l, commit_t (B,L) = t_pi, commit_u (B,L,H) float32 = u_pi, commit_B,
+ * commit_C (B,L,N) complex64 = B_pi, C_pi. */
+EACS_API int eacs_cell_commits(const void* lam, const float* log_dt, const void* u, int u_dtype,
+                               const void* Bc, const void* Cc, const float* t, const float* D,
+                               const float* mean, const float* var,
+                               float eps, float eta, float var_eps, float dt_init,
+                               float dt_min, float dt_max,
+                               int robust, int robust_k, float spike_ratio, float eps_factor,
+                               float* y, float* gate, float* resid,
+                               void* commit_h, float* commit_t, float* commit_u,
+                               void* commit_B, void* commit_C,
+                               void* workspace, size_t workspace_bytes,
+                               int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
+
+/* Segment index of each query time: the last frame k with frame_t[b,k] <= t*
+ * (binary search, clamped to [0, L-1]); frame_t (B,L) ascending, t_query
+ * (B,Q), idx (B,Q) int32.  Replaces segment_index
+ * (cst_ssm/modules/continuous_query.py:12-17). */
+EACS_API int eacs_query_index(const float* frame_t, const float* t_query, int32_t* idx,
+                              int64_t B, int64_t L, int64_t Q, void* stream);
+
+/* Readout at query times from recorded commits: per (b, q) the commits of
+ * frame idx[b,q] (clamped to [0, L-1]) evolved by delta = max(t* - t_pi, 0):
+ * y (B,Q,H) float32 = Re sum_n C_pi (dA h_pi + dB_bar B_pi u_pi) + D u_pi.
+ * Replaces readout_from_commits before its proj_out
+ * (cst_ssm/modules/continuous_query.py:20-61). */
+EACS_API int eacs_query_readout(const void* lam, const float* log_dt, const float* D,
+                                const void* commit_h, const float* commit_t,
+                                const float* commit_u, const void* commit_B,
+                                const void* commit_C, const float* t_query,
+                                const int32_t* idx, float* y,
+                                int64_t B, int64_t L, int64_t Q, int64_t H, int64_t N,
+                                float dt_min, float dt_max, void* stream);
+
 /* Bytes of the library-owned scratch array behind eacs_cell_fwd_noalloc. */
 #define EACS_NOALLOC_SCRATCH_BYTES (32u << 20)
 

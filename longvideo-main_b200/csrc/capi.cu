@@ -174,6 +174,46 @@ int eacs_cell_train_bwd(const void* lam, const float* log_dt, const void* u, int
     return eacs::train_bwd(c, static_cast<cudaStream_t>(stream));
 }
 
+size_t eacs_cell_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
+    return eacs::cell_commits_workspace_size(B, L, H, N);
+}
+
+int eacs_cell_commits(const void* lam, const float* log_dt, const void* u, int u_dtype, const void* Bc,
+                      const void* Cc, const float* t, const float* D, const float* mean,
+                      const float* var, float eps, float eta, float var_eps, float dt_init,
+                      float dt_min, float dt_max, int robust, int robust_k, float spike_ratio,
+                      float eps_factor, float* y, float* gate, float* resid, void* commit_h,
+                      float* commit_t, float* commit_u, void* commit_B, void* commit_C,
+                      void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t H,
+                      int64_t N, void* stream) {
+    if (!commit_h) return eacs::fail(EACS_ERR_INVALID, "eacs_cell_commits: null commit_h");
+    eacs::CellCall c{lam,  log_dt, u,       u_dtype, Bc,     Cc,          t,           D,
+                     mean, var,    eps,     eta,     var_eps, dt_init,    dt_min,      dt_max,
+                     robust, robust_k, spike_ratio, eps_factor, 0, 0.1f, y, gate,
+                     resid, workspace, workspace_bytes, B, L, H, N};
+    c.commit_h = commit_h;
+    c.commit_t = commit_t;
+    c.commit_u = commit_u;
+    c.commit_B = commit_B;
+    c.commit_C = commit_C;
+    return eacs::cell_fwd(c, static_cast<cudaStream_t>(stream));
+}
+
+int eacs_query_index(const float* frame_t, const float* t_query, int32_t* idx, int64_t B, int64_t L,
+                     int64_t Q, void* stream) {
+    return eacs::query_index(frame_t, t_query, idx, B, L, Q, static_cast<cudaStream_t>(stream));
+}
+
+int eacs_query_readout(const void* lam, const float* log_dt, const float* D, const void* commit_h,
+                       const float* commit_t, const float* commit_u, const void* commit_B,
+                       const void* commit_C, const float* t_query, const int32_t* idx, float* y,
+                       int64_t B, int64_t L, int64_t Q, int64_t H, int64_t N, float dt_min,
+                       float dt_max, void* stream) {
+    return eacs::query_readout(lam, log_dt, D, commit_h, commit_t, commit_u, commit_B, commit_C,
+                               t_query, idx, y, B, L, Q, H, N, dt_min, dt_max,
+                               static_cast<cudaStream_t>(stream));
+}
+
 int eacs_cell_fwd_noalloc(const void* lam, const float* log_dt, const void* u, int u_dtype,
                           const void* Bc, const void* Cc, const float* t, const float* D,
                           const float* mean, const float* var, float eps, float eta, float var_eps,

@@ -67,6 +67,13 @@ struct Args {
     float2* hpi;   // [B][H][N] committed state for the repair pass
     float* upi;    // [B][H]
     float2* ck;    // UNGATED, optional: [B][nK][H][N] state before step k*kSsmCk
+    // optional per-frame commits (hard gate): committed state after each step
+    float2* commit_h;  // (B,L,H,N)
+    float* commit_t;   // (B,L)
+    float* commit_u;   // (B,L,H)
+    float2* commit_B;  // (B,L,N)
+    float2* commit_C;
+    int* cidx;         // [B][L] last committed step <= l (-1: the initial state)
     int B, L, H, N, ntiles, nK;
 };
 
@@ -242,6 +249,10 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                         hs[j] = act ? hn : hs[j];
                     else
                         hs[j] = hn;
+                    // commits: under the all-commit assumption h_pi after step l is h_l;
+                    // rows that skip get their steps from l* on rewritten by the repair
+                    if (MODE == SPEC && a.commit_h != nullptr && nv[j] && i < steps)
+                        a.commit_h[((rowLH + l0 + i) * H + h) * N + n] = hn;
                     if (MODE != REPLAY) {
                         const float2 Cl = sC[i][n];
                         yp += cre_mul(Cl, hs[j]);
@@ -560,7 +571,7 @@ __global__ void __launch_bounds__(kRepair) cell_repair(Args a) {
                     const float2 hp = hpi[o];
                     const float2 P = cmul(dA, hp);
                     const float2 Cl = a.Cc[(rowLH + l) * N + n];
-                    float2 hc;
+                    float2 hc, hn = hp;
                     if (fire) {
                         const float2 qc = cmul(dB, a.Bc[(rowLH + l) * N + n]);
                         const float2 hu = make_float2(fmaf(qc.x, ul, P.x), fmaf(qc.y, ul, P.y));
@@ -569,15 +580,17 @@ __global__ void __launch_bounds__(kRepair) cell_repair(Args a) {
                             const float2 xh = make_float2(fmaf(qp.x, upv, P.x), fmaf(qp.y, upv, P.y));
                             const float2 gu = cscale(hu, g);
                             hc = cadd(gu, cscale(xh, 1.f - g));
-                            hpi[o] = cadd(gu, cscale(hp, 1.f - g));
+                            hn = cadd(gu, cscale(hp, 1.f - g));
                         } else {
                             hc = hu;
-                            hpi[o] = hu;
+                            hn = hu;
                         }
+                        hpi[o] = hn;
                     } else {
                         const float2 qp = cmul(dB, sBpi[n]);
                         hc = make_float2(fmaf(qp.x, upv, P.x), fmaf(qp.y, upv, P.y));
                     }
+                    if (a.commit_h != nullptr) a.commit_h[((rowLH + l) * H + h) * N + n] = hn;
                     yp += cre_mul(Cl, hc);
                 }
             }
@@ -605,6 +618,65 @@ __global__ void __launch_bounds__(kRepair) cell_repair(Args a) {
             t_pi = tl;
         }
         __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 6 (commits): per row, the last committed step c(l) <= l as a max-scan of
+// (g_l > 0.5 ? l : -1), and t_pi after each step; then u_pi, B_pi, C_pi are
+// the inputs at max(c(l), 0) (the initial state holds step 0's u, B, C and
+// t_0 - dt_init), gathered one (b, l) per CTA.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) commit_index(Args a) {
+    __shared__ int swarp[32];
+    __shared__ int scarry;
+    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const size_t rb = static_cast<size_t>(b) * a.L;
+    const float t_init = a.t[rb] - a.dt_init;
+    if (tid == 0) scarry = -1;
+    for (int l0 = 0; l0 < a.L; l0 += 1024) {
+        const int l = l0 + tid;
+        const bool valid = l < a.L;
+        int x = (valid && a.gate[rb + l] > 0.5f) ? l : -1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x = max(x, y);
+        }
+        if (lane == 31) swarp[wid] = x;
+        __syncthreads();
+        if (wid == 0) {
+            int w = swarp[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) w = max(w, y);
+            }
+            swarp[lane] = w;
+        }
+        __syncthreads();
+        const int c = max(max(x, wid > 0 ? swarp[wid - 1] : -1), scarry);
+        if (valid) {
+            a.cidx[rb + l] = c;
+            a.commit_t[rb + l] = c < 0 ? t_init : a.t[rb + c];
+        }
+        __syncthreads();
+        if (tid == 1023) scarry = c;
+        __syncthreads();
+    }
+}
+
+template <typename UT>
+__global__ void commit_gather(Args a) {
+    const int l = blockIdx.x, b = blockIdx.y;
+    const size_t row = static_cast<size_t>(b) * a.L + l;
+    const int c = max(a.cidx[row], 0);
+    const size_t src = static_cast<size_t>(b) * a.L + c;
+    const UT* u = static_cast<const UT*>(a.u);
+    for (int h = threadIdx.x; h < a.H; h += blockDim.x) a.commit_u[row * a.H + h] = to_f32(u[src * a.H + h]);
+    for (int n = threadIdx.x; n < a.N; n += blockDim.x) {
+        a.commit_B[row * a.N + n] = a.Bc[src * a.N + n];
+        a.commit_C[row * a.N + n] = a.Cc[src * a.N + n];
     }
 }
 
@@ -731,7 +803,7 @@ int tiles_for(int H, int N) {
 size_t align_up(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 struct WsLayout {
-    size_t part, row, hpi, upi, total;
+    size_t part, row, hpi, upi, total, cidx, total_commits;
 };
 WsLayout ws_layout(int64_t B, int64_t L, int64_t H, int64_t N) {
     WsLayout w;
@@ -741,6 +813,9 @@ WsLayout ws_layout(int64_t B, int64_t L, int64_t H, int64_t N) {
     w.hpi = w.row + align_up(static_cast<size_t>(B) * sizeof(int4));
     w.upi = w.hpi + align_up(static_cast<size_t>(B * H * N) * sizeof(float2));
     w.total = w.upi + align_up(static_cast<size_t>(B * H) * sizeof(float));
+    // commit recording also keeps the last committed step per (b, l)
+    w.cidx = w.total;
+    w.total_commits = w.cidx + align_up(static_cast<size_t>(B * L) * sizeof(int));
     return w;
 }
 
@@ -761,8 +836,14 @@ size_t cell_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
     return ws_layout(B, L, H, N).total;
 }
 
+size_t cell_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
+    if (B <= 0 || L <= 0 || H <= 0 || N <= 0 || N > 64) return 0;
+    return ws_layout(B, L, H, N).total_commits;
+}
+
 int cell_fwd(const CellCall& c, cudaStream_t stream) {
-    const char* fn = "eacs_cell_fwd";
+    const bool commits = c.commit_h != nullptr;
+    const char* fn = commits ? "eacs_cell_commits" : "eacs_cell_fwd";
     int rc = check_shape(fn, c.B, c.L, c.H, c.N, c.u_dtype);
     if (rc) return rc;
     if (c.B == 0 || c.L == 0 || c.H == 0) return EACS_OK;
@@ -774,9 +855,14 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
         return fail(EACS_ERR_INVALID, "%s: gate_mode must be 0 (hard) or 1 (soft)", fn);
     if (c.gate_mode == 1 && c.robust)
         return fail(EACS_ERR_INVALID, "%s: robust_guard applies to the hard gate only", fn);
+    if (commits && (!c.commit_t || !c.commit_u || !c.commit_B || !c.commit_C))
+        return fail(EACS_ERR_INVALID, "%s: null commit output", fn);
+    if (commits && c.gate_mode != 0)
+        return fail(EACS_ERR_INVALID, "%s: commits are recorded for the hard gate only", fn);
     const WsLayout w = ws_layout(c.B, c.L, c.H, c.N);
-    if (!c.workspace || c.workspace_bytes < w.total)
-        return fail(EACS_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", fn, w.total,
+    const size_t need = commits ? w.total_commits : w.total;
+    if (!c.workspace || c.workspace_bytes < need)
+        return fail(EACS_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", fn, need,
                     c.workspace_bytes);
     Args a{};
     a.lam = static_cast<const float2*>(c.lam);
@@ -809,6 +895,14 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
     a.row = reinterpret_cast<int4*>(ws + w.row);
     a.hpi = reinterpret_cast<float2*>(ws + w.hpi);
     a.upi = reinterpret_cast<float*>(ws + w.upi);
+    if (commits) {
+        a.commit_h = static_cast<float2*>(c.commit_h);
+        a.commit_t = c.commit_t;
+        a.commit_u = c.commit_u;
+        a.commit_B = static_cast<float2*>(c.commit_B);
+        a.commit_C = static_cast<float2*>(c.commit_C);
+        a.cidx = reinterpret_cast<int*>(ws + w.cidx);
+    }
     a.B = static_cast<int>(c.B);
     a.L = static_cast<int>(c.L);
     a.H = static_cast<int>(c.H);
@@ -831,6 +925,15 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
     }
     if ((e = chain_dispatch<REPLAY>(a, c.u_dtype, stream)) != cudaSuccess) return cuda_check(e, fn);
     if ((e = repair_dispatch(a, c.u_dtype, stream)) != cudaSuccess) return cuda_check(e, fn);
+    if (commits) {
+        commit_index<<<a.B, 1024, 0, stream>>>(a);
+        const dim3 grid(a.L, a.B);
+        if (c.u_dtype == EACS_DTYPE_F16) commit_gather<__half><<<grid, 256, 0, stream>>>(a);
+        else if (c.u_dtype == EACS_DTYPE_BF16) commit_gather<__nv_bfloat16><<<grid, 256, 0, stream>>>(a);
+        else commit_gather<float><<<grid, 256, 0, stream>>>(a);
+        note_launch(2);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_check(e, fn);
+    }
     return EACS_OK;
 }
 

@@ -54,8 +54,15 @@ struct CellCall {
     size_t workspace_bytes;
     int64_t B, L, H, N;
     void* stats = nullptr;  // optional (B,L) float2 (||obs-pred||, ||obs||)
+    // optional per-frame commits (hard gate; workspace cell_commits_workspace_size)
+    void* commit_h = nullptr;  // (B,L,H,N) complex64
+    float* commit_t = nullptr; // (B,L)
+    float* commit_u = nullptr; // (B,L,H)
+    void* commit_B = nullptr;  // (B,L,N) complex64
+    void* commit_C = nullptr;
 };
 size_t cell_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+size_t cell_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
 int cell_fwd(const CellCall& c, cudaStream_t stream);
 int cell_fwd_noalloc(const CellCall& c, cudaStream_t stream);
 // ckpt == nullptr: inference; otherwise also writes the state before every
@@ -68,6 +75,15 @@ size_t ssm_ckpt_size(int64_t B, int64_t L, int64_t H, int64_t N);
 cudaError_t cell_read_status(int* out, cudaStream_t stream);
 int zoh_kernels(const void* lam, const float* dt, void* dA, void* dBbar, int64_t M, int64_t H,
                 int64_t N, cudaStream_t stream);
+
+// query.cu: continuous-time queries over recorded commits
+int query_index(const float* frame_t, const float* t_query, int* idx, int64_t B, int64_t L,
+                int64_t Q, cudaStream_t stream);
+int query_readout(const void* lam, const float* log_dt, const float* D, const void* commit_h,
+                  const float* commit_t, const float* commit_u, const void* commit_B,
+                  const void* commit_C, const float* t_query, const int* idx, float* y, int64_t B,
+                  int64_t L, int64_t Q, int64_t H, int64_t N, float dt_min, float dt_max,
+                  cudaStream_t stream);
 
 // train.cu
 struct TrainBwdCall {

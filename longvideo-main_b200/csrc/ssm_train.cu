@@ -69,54 +69,6 @@ struct SArgs {
     int B, L, H, N, ntiles, nK;
 };
 
-// Transposed butterfly over the lane offsets O, O/2, ..., S.  A lane enters
-// with V partial sums; at each level while V > M it keeps half and trades the
-// other half with its partner (V-M shuffles for V sums down to M); once M
-// values are left the remaining levels are plain reductions of all M.
-template <int V, int O, int S, int M = 1>
-struct Fold {
-    static __device__ __forceinline__ void run(float* v, int lane) {
-        if constexpr (O >= S && O > 0) {
-            if constexpr (V <= M) {
-#pragma unroll
-                for (int k = 0; k < V; ++k) v[k] += __shfl_xor_sync(0xffffffffu, v[k], O);
-                Fold<V, O / 2, S, M>::run(v, lane);
-            } else {
-                const bool up = (lane & O) != 0;
-#pragma unroll
-                for (int k = 0; k < V / 2; ++k) {
-                    const float send = up ? v[k] : v[k + V / 2];
-                    const float keep = up ? v[k + V / 2] : v[k];
-                    v[k] = keep + __shfl_xor_sync(0xffffffffu, send, O);
-                }
-                Fold<V / 2, O / 2, S, M>::run(v, lane);
-            }
-        }
-    }
-};
-
-template <int V, int O, int S, int M = 1>
-struct FoldShape {
-    static constexpr int levels(int v, int o) { return (o < S || o == 0 || v <= M) ? 0 : 1 + levels(v / 2, o / 2); }
-    static constexpr int kHalve = levels(V, O);
-    static constexpr int kRem = V >> kHalve;  // sums a lane holds afterwards
-    // first original index of the sums lane `lane` holds
-    static __device__ __forceinline__ int held(int lane) {
-        int idx = 0;
-#pragma unroll
-        for (int j = 0; j < kHalve; ++j)
-            if (lane & (O >> j)) idx += V >> (j + 1);
-        return idx;
-    }
-    // one lane per distinct set of sums: the bits of the plain levels are zero
-    static __device__ __forceinline__ bool writer(int lane) {
-        bool w = true;
-#pragma unroll
-        for (int o = O >> kHalve; o >= S && o > 0; o >>= 1) w = w && !(lane & o);
-        return w;
-    }
-};
-
 template <int LANES, int NPT>
 struct BwdSmem {
     static constexpr int HT = kBT / LANES;

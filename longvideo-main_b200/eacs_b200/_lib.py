@@ -44,6 +44,12 @@ SIGNATURES = {
     "eacs_ssm_ckpt_size": (_SZ, [_I64, _I64, _I64, _I64]),
     "eacs_ssm_train_fwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ,
                                 _I64, _I64, _I64, _I64, _F, _F, _P]),
+    "eacs_cell_commits_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
+    "eacs_cell_commits": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _F, _F, _F, _F, _F, _F,
+                               _I, _I, _F, _F, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ,
+                               _I64, _I64, _I64, _I64, _P]),
+    "eacs_query_index": (_I, [_P, _P, _P, _I64, _I64, _I64, _P]),
+    "eacs_query_readout": (_I, [_P] * 11 + [_I64] * 5 + [_F, _F, _P]),
     "eacs_ssm_bwd_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
     "eacs_ssm_bwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _SZ,
                           _P, _P, _P, _P, _P, _P, _P, _P, _SZ,

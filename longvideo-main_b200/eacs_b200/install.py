@@ -13,7 +13,7 @@ import importlib
 
 
 def install(package: str = "cst_ssm", fuse_ungated: bool = False,
-            layer_dispatch: bool = False) -> dict:
+            layer_dispatch: bool = False, queries: bool = False) -> dict:
     """Patch `package` (already importable) and return what was replaced.
 
     fuse_ungated: also bind ContinuousSSMLayer.forward to the fused ungated
@@ -21,7 +21,11 @@ def install(package: str = "cst_ssm", fuse_ungated: bool = False,
     (B,L,H,N) tensors, instead of only swapping its scan extension.
     layer_dispatch: also bind EACSLayer._cuda_fused_ok / _forward_fused to
     eacs_b200.ops.eacs_layer, so eval-mode layers with robust_guard run the
-    fused kernel instead of the Python step loop."""
+    fused kernel instead of the Python step loop.
+    queries: also route EACSLayer.run_with_commits and the continuous-query
+    functions (segment_index, readout_from_commits) through the commit and
+    readout kernels where no gradient has to flow through the commits; the
+    reference's own code runs otherwise."""
     from .ops import eacs_gated_scan as ours_cell
     from .ops import scan_cuda as ours_scan
 
@@ -51,6 +55,18 @@ def install(package: str = "cst_ssm", fuse_ungated: bool = False,
         ref_layer = importlib.import_module(f"{package}.modules.continuous_ssm")
         ref_layer.ContinuousSSMLayer.forward = ours_ssm.layer_forward
         patched["continuous_ssm.ContinuousSSMLayer.forward"] = ours_ssm.layer_forward
+    if queries:
+        from .ops import continuous_query as ours_q
+
+        ref_eacs = importlib.import_module(f"{package}.modules.eacs")
+        ref_q = importlib.import_module(f"{package}.modules.continuous_query")
+        for owner, name, make in ((ref_eacs.EACSLayer, "run_with_commits", ours_q.make_run_with_commits),
+                                  (ref_q, "readout_from_commits", ours_q.make_readout_from_commits),
+                                  (ref_q, "segment_index", ours_q.make_segment_index)):
+            current = getattr(owner, name)
+            if not hasattr(current, "__wrapped__"):  # installing twice keeps one wrapper
+                setattr(owner, name, make(current))
+            patched[f"{owner.__name__.split('.')[-1]}.{name}"] = getattr(owner, name)
     if layer_dispatch:
         from .ops import eacs_layer as ours_layer
 

@@ -334,6 +334,7 @@ static void cell_row(const float* lam, const float* log_dt, const float* u,
                      float dt_min, float dt_max, int robust, int robust_k,
                      float spike_ratio, float eps_factor, int gate_mode, float T,
                      int train_exp, float* y, float* gate, float* resid,
+                     float* ch, float* ct, float* cu, float* cB, float* cC,
                      int64_t L, int64_t H, int64_t N) {
     cf* hpi = (cf*)calloc((size_t)(H * N), sizeof(cf));
     cf* dA = (cf*)malloc(sizeof(cf) * (size_t)(H * N));
@@ -450,6 +451,21 @@ static void cell_row(const float* lam, const float* log_dt, const float* u,
             }
             tpi = tl;
         }
+        if (ch) {
+            /* commits after step l (eacs.py:386-402): the committed state */
+            for (int64_t i = 0; i < H * N; ++i) {
+                ch[(l * H * N + i) * 2] = hpi[i].re;
+                ch[(l * H * N + i) * 2 + 1] = hpi[i].im;
+            }
+            ct[l] = tpi;
+            for (int64_t hh = 0; hh < H; ++hh) cu[l * H + hh] = upi[hh];
+            for (int64_t n = 0; n < N; ++n) {
+                cB[(l * N + n) * 2] = Bpi[n].re;
+                cB[(l * N + n) * 2 + 1] = Bpi[n].im;
+                cC[(l * N + n) * 2] = Cpi[n].re;
+                cC[(l * N + n) * 2 + 1] = Cpi[n].im;
+            }
+        }
         if (robust) {
             if (l > 0) spike = (r > prev_r * spike_ratio) ? spike + 1.0f : 0.0f;
             prev_r = r;
@@ -472,7 +488,89 @@ int eacs_oracle_cell_fwd(const float* lam, const float* log_dt, const float* u,
         cell_row(lam, log_dt, u + bi * L * H, Bc + bi * L * N * 2, Cc + bi * L * N * 2,
                  t + bi * L, D, mean, var, eps, eta, var_eps, dt_init, dt_min, dt_max,
                  robust, robust_k, spike_ratio, eps_factor, gate_mode, T, train_exp,
-                 y + bi * L * H, gate + bi * L, resid + bi * L, L, H, N);
+                 y + bi * L * H, gate + bi * L, resid + bi * L, NULL, NULL, NULL, NULL, NULL,
+                 L, H, N);
+    return 0;
+}
+
+/* ---------------------------------------------------------------------------
+ * Gated cell with per-frame commits (EACSLayer.run_with_commits /
+ * _commit_range, eacs.py:386-439): eacs_oracle_cell_fwd plus, after every
+ * step, the committed state h_pi (B,L,H,N) complex, t_pi (B,L), u_pi (B,L,H),
+ * B_pi, C_pi (B,L,N) complex.
+ * ------------------------------------------------------------------------- */
+int eacs_oracle_cell_commits(const float* lam, const float* log_dt, const float* u,
+                             const float* Bc, const float* Cc, const float* t,
+                             const float* D, const float* mean, const float* var,
+                             float eps, float eta, float var_eps, float dt_init,
+                             float dt_min, float dt_max, int robust, int robust_k,
+                             float spike_ratio, float eps_factor,
+                             float* y, float* gate, float* resid,
+                             float* ch, float* ct, float* cu, float* cB, float* cC,
+                             int64_t B, int64_t L, int64_t H, int64_t N) {
+#pragma omp parallel for num_threads(nthreads()) schedule(dynamic, 1)
+    for (int64_t bi = 0; bi < B; ++bi)
+        cell_row(lam, log_dt, u + bi * L * H, Bc + bi * L * N * 2, Cc + bi * L * N * 2,
+                 t + bi * L, D, mean, var, eps, eta, var_eps, dt_init, dt_min, dt_max,
+                 robust, robust_k, spike_ratio, eps_factor, 0, 0.1f, 0,
+                 y + bi * L * H, gate + bi * L, resid + bi * L,
+                 ch + bi * L * H * N * 2, ct + bi * L, cu + bi * L * H,
+                 cB + bi * L * N * 2, cC + bi * L * N * 2, L, H, N);
+    return 0;
+}
+
+/* ---------------------------------------------------------------------------
+ * Continuous-time query readout (continuous_query.py:12-61).  Per query
+ * (b, q): k = last frame with frame_t <= t_query (searchsorted right, minus 1,
+ * clamped to [0, L-1]) unless idx is given; then from the commits at k:
+ *   delta = max(t_q - t_pi, 0), dte = clamp(delta e^log_dt, dt_min, dt_max)
+ *   x* = dA h_pi + dB_bar B_pi u_pi,  y = Re sum_n C_pi x* + D u_pi
+ * Output y (B,Q,H) (before the layer's proj_out).
+ * ------------------------------------------------------------------------- */
+static int64_t segment_index(const float* ft, int64_t L, float tq) {
+    int64_t lo = 0, hi = L;  /* first index with ft > tq */
+    while (lo < hi) {
+        int64_t mid = (lo + hi) / 2;
+        if (ft[mid] <= tq) lo = mid + 1; else hi = mid;
+    }
+    int64_t k = lo - 1;
+    return k < 0 ? 0 : (k > L - 1 ? L - 1 : k);
+}
+
+int eacs_oracle_query_readout(const float* lam, const float* log_dt, const float* D,
+                              const float* ch, const float* ct, const float* cu,
+                              const float* cB, const float* cC, const float* frame_t,
+                              const float* t_query, const int32_t* idx, float* y,
+                              int64_t B, int64_t L, int64_t Q, int64_t H, int64_t N,
+                              float dt_min, float dt_max) {
+#pragma omp parallel for num_threads(nthreads()) schedule(dynamic, 1)
+    for (int64_t bi = 0; bi < B; ++bi) {
+        for (int64_t q = 0; q < Q; ++q) {
+            float tq = t_query[bi * Q + q];
+            int64_t k = idx ? idx[bi * Q + q] : segment_index(frame_t + bi * L, L, tq);
+            int64_t row = bi * L + k;
+            float delta = tq - ct[row];
+            if (delta < 0.f) delta = 0.f;
+            for (int64_t hh = 0; hh < H; ++hh) {
+                float dte = eff_dt(delta, expf(log_dt[hh]), dt_min, dt_max);
+                float upi = cu[row * H + hh];
+                float acc = 0.f;
+                for (int64_t n = 0; n < N; ++n) {
+                    int64_t i = hh * N + n;
+                    cf lm = {lam[2 * i], lam[2 * i + 1]};
+                    cf dA, dBb;
+                    zoh_f(lm, cf_recip(lm), dte, &dA, &dBb);
+                    int64_t o = (row * H + hh) * N + n;
+                    cf hp = {ch[2 * o], ch[2 * o + 1]};
+                    cf Bp = {cB[(row * N + n) * 2], cB[(row * N + n) * 2 + 1]};
+                    cf Cp = {cC[(row * N + n) * 2], cC[(row * N + n) * 2 + 1]};
+                    cf xs = cf_add(cf_mul(dA, hp), cf_scale(cf_mul(dBb, Bp), upi));
+                    acc += Cp.re * xs.re - Cp.im * xs.im;
+                }
+                y[(bi * Q + q) * H + hh] = acc + D[hh] * upi;
+            }
+        }
+    }
     return 0;
 }
 

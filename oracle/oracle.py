@@ -44,6 +44,9 @@ def lib():
                                            + [_P] * 3 + [_I64] * 4)
         L.eacs_oracle_cell_bwd.argtypes = ([_P] * 9 + [_F] * 5 + [_F, _I] + [_P] * 5
                                            + [_P] * 8 + [_I64] * 4)
+        L.eacs_oracle_cell_commits.argtypes = ([_P] * 9 + [_F] * 6 + [_I, _I, _F, _F]
+                                               + [_P] * 8 + [_I64] * 4)
+        L.eacs_oracle_query_readout.argtypes = [_P] * 12 + [_I64] * 5 + [_F, _F]
         L.eacs_oracle_set_threads.argtypes = [_I]
         L.eacs_oracle_version.restype = ctypes.c_char_p
         _lib = L
@@ -199,3 +202,59 @@ def cell_bwd(lam, log_dt, u, Bc, Cc, t, D, mean, var, eps, eta, var_eps, dt_init
                                _ptr(grs), _ptr(gns), _ptr(du), _ptr(dBc), _ptr(dCc), _ptr(dt),
                                _ptr(dlam), _ptr(dlog), _ptr(dD), _ptr(deps), B, L, H, N)
     return du, dBc, dCc, dt, dlam, dlog, dD, deps
+
+
+def cell_commits(lam, log_dt, u, Bc, Cc, t, D, mean, var, eps, eta, var_eps=1e-5,
+                 dt_init=1.0, dt_min=1e-3, dt_max=1e3, robust=None):
+    """Hard-gate cell recording per-frame commits (cst_ssm/modules/eacs.py:386-439).
+
+    Returns (y, gate, resid, h (B,L,H,N), t_pi (B,L), u_pi (B,L,H), B_pi, C_pi (B,L,N))."""
+    lam = _c(lam, np.complex64)
+    u = _c(u, np.float32)
+    Bc = _c(Bc, np.complex64)
+    Cc = _c(Cc, np.complex64)
+    t = _c(t, np.float32)
+    log_dt = _c(log_dt, np.float32)
+    D = _c(D, np.float32)
+    mean = _c(mean, np.float32)
+    var = _c(var, np.float32)
+    B, L, H = u.shape
+    N = lam.shape[1]
+    y = np.empty((B, L, H), np.float32)
+    g = np.empty((B, L), np.float32)
+    r = np.empty((B, L), np.float32)
+    ch = np.empty((B, L, H, N), np.complex64)
+    ct = np.empty((B, L), np.float32)
+    cu = np.empty((B, L, H), np.float32)
+    cB = np.empty((B, L, N), np.complex64)
+    cC = np.empty((B, L, N), np.complex64)
+    rk, rr, rf = (0, 2.0, 0.3) if robust is None else robust
+    lib().eacs_oracle_cell_commits(_ptr(lam), _ptr(log_dt), _ptr(u), _ptr(Bc), _ptr(Cc), _ptr(t),
+                                   _ptr(D), _ptr(mean), _ptr(var), eps, eta, var_eps, dt_init,
+                                   dt_min, dt_max, 0 if robust is None else 1, int(rk), rr, rf,
+                                   _ptr(y), _ptr(g), _ptr(r), _ptr(ch), _ptr(ct), _ptr(cu),
+                                   _ptr(cB), _ptr(cC), B, L, H, N)
+    return y, g, r, ch, ct, cu, cB, cC
+
+
+def query_readout(lam, log_dt, D, ch, ct, cu, cB, cC, frame_t, t_query, idx=None,
+                  dt_min=1e-3, dt_max=1e3):
+    """readout_from_commits before proj_out (cst_ssm/modules/continuous_query.py:20-61)."""
+    lam = _c(lam, np.complex64)
+    log_dt = _c(log_dt, np.float32)
+    D = _c(D, np.float32)
+    ch = _c(ch, np.complex64)
+    ct = _c(ct, np.float32)
+    cu = _c(cu, np.float32)
+    cB = _c(cB, np.complex64)
+    cC = _c(cC, np.complex64)
+    frame_t = _c(frame_t, np.float32)
+    t_query = _c(t_query, np.float32)
+    idx = None if idx is None else _c(idx, np.int32)
+    B, L, H, N = ch.shape
+    Q = t_query.shape[1]
+    y = np.empty((B, Q, H), np.float32)
+    lib().eacs_oracle_query_readout(_ptr(lam), _ptr(log_dt), _ptr(D), _ptr(ch), _ptr(ct), _ptr(cu),
+                                    _ptr(cB), _ptr(cC), _ptr(frame_t), _ptr(t_query), _ptr(idx),
+                                    _ptr(y), B, L, Q, H, N, dt_min, dt_max)
+    return y

@@ -14,6 +14,10 @@ Reference functions exercised (paths inside the CST-SSM project):
   modules/continuous_ssm.py:44-55  ungated layer core
   modules/eacs.py:78-173       eacs_step / scan_range (+ RobustCfg)
   ops/eacs_cell_train.py:81-199  GatedEACSCellFunction forward/backward
+  modules/eacs.py:386-439      run_with_commits (per-frame commits)
+  modules/continuous_query.py:12-61  segment_index / readout_from_commits
+
+    python tests/golden/make_golden.py --groups query   # rewrite one group only
 """
 from __future__ import annotations
 
@@ -285,15 +289,81 @@ def train_cases():
     return out
 
 
+def query_cases():
+    """EACSLayer.run_with_commits (eacs.py:404-439) and readout_from_commits
+    (continuous_query.py:20-61) on seeded layers, eval mode.  The layer's
+    proj_out is set to the identity so the readout is the core's value."""
+    from cst_ssm.modules.continuous_query import readout_from_commits
+    out = {}
+    specs = {
+        # name: (H, N, tau_min, tau_max, B, L, Q, seed, target update rate)
+        "query_skip": (24, 8, 0.5, 4.0, 2, 40, 29, 20, 0.5),
+        "query_commit": (16, 16, 0.5, 64.0, 2, 24, 17, 21, None),
+        "query_n5": (12, 5, 4.0, 32.0, 3, 19, 11, 22, 0.3),
+    }
+    for name, (H, N, tmin, tmax, B, L, Q, seed, q) in specs.items():
+        layer, u, Bc, Cc, t = _layer_inputs(H, N, tmin, tmax, B, L, seed, dup_frames=True)
+        torch.manual_seed(seed + 7)
+        x = torch.randn(B, L, H)
+        for l in range(1, L):
+            if (l // 3) % 2 == 1:
+                x[:, l] = x[:, l - 1]
+        with torch.no_grad():
+            u, Bc, Cc = layer._project(layer.norm(x))
+            layer.proj_out.weight.copy_(torch.eye(H))
+            layer.proj_out.bias.zero_()
+        eps = float(layer.gate.eps.detach()) if q is None else _calibrate(layer, u, Bc, Cc, t, q)[0]
+        orig = layer.step_params
+
+        def step_params(lam, _orig=orig, _eps=eps):
+            p = _orig(lam)
+            p.eps = torch.tensor(_eps)
+            return p
+
+        layer.step_params = step_params
+        g = torch.Generator().manual_seed(seed + 50)
+        # queries: inside segments, on frames, before the first and after the last frame
+        tq = t[:, :1] - 0.3 + (t[:, -1:] - t[:, :1] + 0.8) * torch.rand(B, Q, generator=g)
+        tq[:, 0] = t[:, 0] - 0.2
+        tq[:, 1] = t[:, 5]
+        tq[:, 2] = t[:, -1] + 0.4
+        tq = tq.sort(dim=1).values
+        with torch.no_grad():
+            res, commits = layer.run_with_commits(x, t)
+            yq = readout_from_commits(layer, commits, tq)
+            yf = readout_from_commits(layer, commits, commits["frame_t"])
+        d = dict(lam=_np(layer.lam()), log_dt=_np(layer.log_dt_scale), u=_np(u), Bc=_np(Bc),
+                 Cc=_np(Cc), t=_np(t), D=_np(layer.D), mean=_np(layer.obs_norm.running_mean),
+                 var=_np(layer.obs_norm.running_var),
+                 scalars=np.array([eps, layer.gate.norm_eta, layer.obs_norm.eps, layer.dt_init,
+                                   1e-3, layer.dt_max], np.float64),
+                 y=_np(res.y - x), gate=_np(res.gates), resid=_np(res.residual),
+                 ch=_np(commits["h"]), ct=_np(commits["t"]), cu=_np(commits["u"]),
+                 cB=_np(commits["B"]), cC=_np(commits["C"]), t_query=_np(tq), yq=_np(yq),
+                 yf=_np(yf))
+        out[name] = d
+        print(f"{name}: update rate {float(res.gates.mean()):.3f}, "
+              f"min|r-eps| {float((res.residual - eps).abs().min()):.2e}")
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--groups", default="scan,ssm,cell,train,query",
+                    help="comma-separated groups to (re)write")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     gen = torch.Generator().manual_seed(1234)
-    groups = {"scan": scan_cases(gen), "ssm": ssm_cases(gen), "cell": cell_cases(),
-              "train": train_cases()}
+    makers = {"scan": lambda: scan_cases(gen), "ssm": lambda: ssm_cases(gen),
+              "cell": cell_cases, "train": train_cases, "query": query_cases}
+    want = args.groups.split(",")
+    groups = {}
+    for name in ("scan", "ssm", "cell", "train", "query"):  # fixed order: gen is shared
+        cases = makers[name]()
+        if name in want:
+            groups[name] = cases
     for group, cases in groups.items():
         flat = {f"{case}/{k}": v for case, d in cases.items() for k, v in d.items()}
         path = os.path.join(HERE, f"{group}.npz")

@@ -147,3 +147,33 @@ def test_continuous_ssm_layer_forward_and_grads():
     assert relerr(layer.a_imag.grad.cpu().numpy(), dlam.imag) < 1e-3
     lam_re = d["lam"].real
     assert relerr(layer.a_log_neg_real.grad.cpu().numpy(), dlam.real * lam_re) < 1e-3
+
+
+def test_run_with_commits_and_continuous_query():
+    from eacs_b200.ops.continuous_query import (continuous_query, readout_from_commits,
+                                                run_with_commits)
+    from test_gpu_kernels import _calibrated_eps
+
+    d = cell_inputs(2, 50, 32, 16, seed=51)
+    eps = _calibrated_eps(d, 0.5)
+    layer = StandInLayer(dict(d, eps=eps), None).eval()
+    x = torch.from_numpy(d["u"]).to(DEV)
+    t = torch.from_numpy(d["t"]).to(DEV)
+    out, commits = run_with_commits(layer, x, t)
+    ref = oracle.cell_commits(**d, eps=eps, eta=1e-6)
+    assert isinstance(out, EACSOutput) and out.innovation is None
+    assert np.array_equal(out.gates.cpu().numpy(), ref[1])
+    assert relerr(out.y.cpu().numpy(), ref[0]) < 1e-4
+    for k, r in zip(("h", "t", "u", "B", "C"), ref[3:]):
+        assert relerr(commits[k].cpu().numpy(), r) < 1e-4, k
+    tq = t[:, :20] + 0.07
+    yq = readout_from_commits(layer, commits, tq)
+    yq_ref = oracle.query_readout(d["lam"], d["log_dt"], d["D"], *ref[3:], d["t"], tq.cpu().numpy())
+    assert relerr(yq.cpu().numpy(), yq_ref) < 1e-4
+    assert torch.equal(continuous_query(layer, x, t, tq), yq)
+    # queries at the frame times themselves use each frame's own commits
+    yf = readout_from_commits(layer, commits, commits["frame_t"])
+    B, L = d["t"].shape
+    idx = np.broadcast_to(np.arange(L, dtype=np.int32), (B, L))
+    yf_ref = oracle.query_readout(d["lam"], d["log_dt"], d["D"], *ref[3:], d["t"], d["t"], idx=idx)
+    assert relerr(yf.cpu().numpy(), yf_ref) < 1e-4

@@ -25,7 +25,7 @@ def ref_pkg():
     try:
         mods = {n: importlib.import_module(f"cst_ssm.{n}") for n in
                 ("ops.scan_cuda", "ops.eacs_gated_scan", "ops.eacs_cell_train",
-                 "modules.continuous_ssm", "modules.eacs")}
+                 "modules.continuous_ssm", "modules.eacs", "modules.continuous_query")}
     except ImportError as e:
         sys.path.remove(REF)
         pytest.skip(f"reference not importable: {e}")
@@ -37,6 +37,9 @@ def ref_pkg():
         "ssm_fwd": mods["modules.continuous_ssm"].ContinuousSSMLayer.forward,
         "ok": mods["modules.eacs"].EACSLayer._cuda_fused_ok,
         "fused": mods["modules.eacs"].EACSLayer._forward_fused,
+        "rwc": mods["modules.eacs"].EACSLayer.run_with_commits,
+        "rfc": mods["modules.continuous_query"].readout_from_commits,
+        "seg": mods["modules.continuous_query"].segment_index,
     }
     yield mods
     mods["ops.scan_cuda"]._EXT, mods["ops.scan_cuda"]._TRIED = saved["scan"]
@@ -46,6 +49,9 @@ def ref_pkg():
     mods["modules.continuous_ssm"].ContinuousSSMLayer.forward = saved["ssm_fwd"]
     mods["modules.eacs"].EACSLayer._cuda_fused_ok = saved["ok"]
     mods["modules.eacs"].EACSLayer._forward_fused = saved["fused"]
+    mods["modules.eacs"].EACSLayer.run_with_commits = saved["rwc"]
+    mods["modules.continuous_query"].readout_from_commits = saved["rfc"]
+    mods["modules.continuous_query"].segment_index = saved["seg"]
     sys.path.remove(REF)
 
 
@@ -97,3 +103,29 @@ def test_fused_ungated_layer_refuses_cpu(ref_pkg):
         16, BranchSpec("t", n_state=4, tau_min=0.5, tau_max=4.0))
     with pytest.raises(RuntimeError, match="CUDA"):
         layer(torch.randn(1, 5, 16), torch.cumsum(torch.full((1, 5), 0.25), 1))
+
+
+def test_query_dispatch_keeps_reference_on_cpu_and_with_grad(ref_pkg):
+    """Commits and query readouts: on CPU tensors (and wherever gradients must
+    flow through the commits) the reference's own functions still run."""
+    import eacs_b200
+    from cst_ssm.ops.spectral_init import BranchSpec
+
+    eacs_b200.install("cst_ssm", queries=True)
+    eacs_b200.install("cst_ssm", queries=True)  # idempotent
+    cq = ref_pkg["modules.continuous_query"]
+    EACSLayer = ref_pkg["modules.eacs"].EACSLayer
+    assert EACSLayer.run_with_commits.__wrapped__ is not None
+    assert not hasattr(EACSLayer.run_with_commits.__wrapped__, "__wrapped__")
+    torch.manual_seed(0)
+    layer = EACSLayer(8, BranchSpec("t", n_state=4, tau_min=0.5, tau_max=4.0)).eval()
+    x = torch.randn(2, 10, 8)
+    t = torch.cumsum(torch.full((2, 10), 0.25), 1)
+    tq = t[:, :5] + 0.1
+    with torch.no_grad():
+        out, commits = layer.run_with_commits(x, t)
+        y = cq.readout_from_commits(layer, commits, tq)
+        y2 = cq.continuous_query(layer, x, t, tq)
+    assert commits["h"].shape == (2, 10, 8, 4) and y.shape == (2, 5, 8)
+    assert torch.allclose(y, y2)
+    assert torch.equal(cq.segment_index(t, tq), torch.arange(5).expand(2, 5))

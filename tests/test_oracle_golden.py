@@ -77,3 +77,31 @@ def test_train_bwd(name):
     names = ["du", "dBc", "dCc", "dt", "dlam", "dlog_dt", "dD", "deps"]
     for k, v in zip(names, got):
         assert relerr(v, d[k]) < 1e-4, (k, relerr(v, d[k]))
+
+
+QUERY = cases("query")
+
+
+@pytest.mark.parametrize("name", sorted(QUERY))
+def test_commits_and_query_readout(name):
+    """run_with_commits + readout_from_commits (eacs.py:386-439,
+    continuous_query.py:12-61): gates bit-exact (eps calibrated away from the
+    residuals), commits and readouts to 1e-5."""
+    d = QUERY[name]
+    eps, eta, var_eps, dt_init, dt_min, dt_max = [float(v) for v in d["scalars"]]
+    y, g, r, ch, ct, cu, cB, cC = oracle.cell_commits(
+        d["lam"], d["log_dt"], d["u"], d["Bc"], d["Cc"], d["t"], d["D"], d["mean"], d["var"],
+        eps, eta, var_eps, dt_init, dt_min, dt_max)
+    assert np.array_equal(g, d["gate"])
+    assert relerr(r, d["resid"]) < 1e-5
+    assert relerr(y, d["y"]) < 1e-5
+    for got, key in zip((ch, ct, cu, cB, cC), ("ch", "ct", "cu", "cB", "cC")):
+        assert relerr(got, d[key]) < 1e-5, key
+    yq = oracle.query_readout(d["lam"], d["log_dt"], d["D"], d["ch"], d["ct"], d["cu"], d["cB"],
+                              d["cC"], d["t"], d["t_query"], dt_min=dt_min, dt_max=dt_max)
+    assert relerr(yq, d["yq"]) < 1e-5
+    B, L = d["t"].shape
+    idx = np.broadcast_to(np.arange(L, dtype=np.int32), (B, L))
+    yf = oracle.query_readout(d["lam"], d["log_dt"], d["D"], d["ch"], d["ct"], d["cu"], d["cB"],
+                              d["cC"], d["t"], d["t"], idx=idx, dt_min=dt_min, dt_max=dt_max)
+    assert relerr(yf, d["yf"]) < 1e-5
