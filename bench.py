@@ -45,6 +45,9 @@ UPDATES = B * L * H * N
 # Minimal (algorithmic) bytes of one call: read u (fp16), Bc, Cc (complex64),
 # t (fp32); write y (fp32), gate, resid (fp32).
 ALG_BYTES = B * L * H * 2 + 2 * B * L * N * 8 + B * L * 4 + B * L * H * 4 + 2 * B * L * 4
+# Issue slots per state update of cell_chain<SPEC> at this workload: ncu
+# smsp__inst_executed.sum x 32 / updates = 1,051,860,480 x 32 / 402,653,184.
+INSTR_PER_UPDATE = 83.6
 CONFIG = {
     "workload": "gated EACS cell inference forward (event gate + ZOH predict/update + commit), "
                 "B=8 L=4096 H=768 N=16",
@@ -388,6 +391,12 @@ def run_ours(args):
     tpath = os.path.join(ROOT, "profiles", "cell_chain_c1_traffic.json")
     if os.path.exists(tpath):
         traffic = json.load(open(tpath)).get("dram_bytes_per_launch")
+    # The chain kernel is bound by instruction issue (FP32 + MUFU), not HBM:
+    # its issue roofline from the ncu instruction count per state update.
+    n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
+    clk = sampler.summary().get("sm_mhz") or 1965.0
+    issue_peak = n_sm * 4 * 32 * clk * 1e6  # 4 warp-instructions per SM clock, 32 lanes
+    issue_achieved = UPDATES / kmean_s * INSTR_PER_UPDATE
 
     # ---- the reference's own CUDA kernel (K3), when built for sm_100a -----
     ref_cuda = None
@@ -421,7 +430,12 @@ def run_ours(args):
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
                          "kernel": "cell_chain<SPEC> (speculative all-commit gated chain)",
                          "kernel_ms": 1e3 * kmean_s, "alg_bytes_per_launch": ALG_BYTES,
-                         "kernel_gupdates_per_s": UPDATES / kmean_s / 1e9},
+                         "kernel_gupdates_per_s": UPDATES / kmean_s / 1e9,
+                         "issue": {"achieved_Tinstr_s": issue_achieved / 1e12,
+                                   "peak_Tinstr_s": issue_peak / 1e12,
+                                   "frac": issue_achieved / issue_peak,
+                                   "instr_per_update": INSTR_PER_UPDATE,
+                                   "peak_basis": f"{n_sm} SMs x 128 lanes x median SM clock"}},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,

@@ -253,6 +253,33 @@ EACS_API int eacs_query_readout(const void* lam, const float* log_dt, const floa
                                 int64_t B, int64_t L, int64_t Q, int64_t H, int64_t N,
                                 float dt_min, float dt_max, void* stream);
 
+/* K steps of one EACS branch with explicit state, per row (streaming).
+ * Replaces the per-branch body of temporal_step (cst_ssm/modules/streaming.py:
+ * 45-85: first-observation commit, valid masks, CPI-modulated threshold) over
+ * eacs_step (modules/eacs.py:78-142), after the projections.
+ * Inputs u (B,K,H) of u_dtype, Bc/Cc (B,K,N) complex64, t (B,K), valid (B,K)
+ * uint8 or NULL (all valid), cpi (B,K) or NULL.  State in: h (B,H,N)
+ * complex64, t (B), u (B,H), B/C (B,N) complex64, initialized (B) uint8;
+ * state out: the same shapes in separate buffers (the input state is not
+ * modified).  Outputs y (B,K,H) = Re sum_n C h_cur + D u (zeros where not
+ * valid), gate (1 on a row's first valid step), resid, innov (resid where the
+ * row was already initialised, else 0), all (B,K) float32.  gate_mode 0 hard
+ * (r > eps_l), 1 soft sigmoid((r - eps_l)/max(T, 1e-4)); cpi_modulation m > 0
+ * with cpi: eps_l = max(eps (1 - m clamp(cpi, 0, 1)), 1e-3).  No workspace. */
+EACS_API int eacs_stream_chunk(const void* lam, const float* log_dt, const float* D,
+                               const float* mean, const float* var,
+                               const void* u, int u_dtype, const void* Bc, const void* Cc,
+                               const float* t, const uint8_t* valid, const float* cpi,
+                               const void* h_in, const float* t_in, const float* u_in,
+                               const void* B_in, const void* C_in, const uint8_t* init_in,
+                               void* h_out, float* t_out, float* u_out, void* B_out,
+                               void* C_out, uint8_t* init_out,
+                               float* y, float* gate, float* resid, float* innov,
+                               float eps, float eta, float var_eps, float dt_init,
+                               float dt_min, float dt_max, float cpi_modulation,
+                               int gate_mode, float temperature,
+                               int64_t B, int64_t K, int64_t H, int64_t N, void* stream);
+
 /* Bytes of the library-owned scratch array behind eacs_cell_fwd_noalloc. */
 #define EACS_NOALLOC_SCRATCH_BYTES (32u << 20)
 

@@ -214,6 +214,23 @@ int eacs_query_readout(const void* lam, const float* log_dt, const float* D, con
                                static_cast<cudaStream_t>(stream));
 }
 
+int eacs_stream_chunk(const void* lam, const float* log_dt, const float* D, const float* mean,
+                      const float* var, const void* u, int u_dtype, const void* Bc, const void* Cc,
+                      const float* t, const uint8_t* valid, const float* cpi, const void* h_in,
+                      const float* t_in, const float* u_in, const void* B_in, const void* C_in,
+                      const uint8_t* init_in, void* h_out, float* t_out, float* u_out, void* B_out,
+                      void* C_out, uint8_t* init_out, float* y, float* gate, float* resid,
+                      float* innov, float eps, float eta, float var_eps, float dt_init, float dt_min,
+                      float dt_max, float cpi_modulation, int gate_mode, float temperature,
+                      int64_t B, int64_t K, int64_t H, int64_t N, void* stream) {
+    eacs::StreamCall c{lam,   log_dt, D,       mean,    var,      u,      u_dtype, Bc,    Cc,
+                       t,     valid,  cpi,     h_in,    t_in,     u_in,   B_in,    C_in,  init_in,
+                       h_out, t_out,  u_out,   B_out,   C_out,    init_out, y,     gate,  resid,
+                       innov, eps,    eta,     var_eps, dt_init,  dt_min, dt_max,  cpi_modulation,
+                       temperature, gate_mode, B, K, H, N};
+    return eacs::stream_chunk(c, static_cast<cudaStream_t>(stream));
+}
+
 int eacs_cell_fwd_noalloc(const void* lam, const float* log_dt, const void* u, int u_dtype,
                           const void* Bc, const void* Cc, const float* t, const float* D,
                           const float* mean, const float* var, float eps, float eta, float var_eps,

@@ -85,6 +85,42 @@ int query_readout(const void* lam, const float* log_dt, const float* D, const vo
                   int64_t L, int64_t Q, int64_t H, int64_t N, float dt_min, float dt_max,
                   cudaStream_t stream);
 
+// stream.cu: gated steps with explicit branch state
+struct StreamCall {
+    const void* lam;
+    const float* log_dt;
+    const float* D;
+    const float* mean;
+    const float* var;
+    const void* u;
+    int u_dtype;
+    const void* Bc;
+    const void* Cc;
+    const float* t;
+    const uint8_t* valid;
+    const float* cpi;
+    const void* h_in;
+    const float* t_in;
+    const float* u_in;
+    const void* B_in;
+    const void* C_in;
+    const uint8_t* init_in;
+    void* h_out;
+    float* t_out;
+    float* u_out;
+    void* B_out;
+    void* C_out;
+    uint8_t* init_out;
+    float* y;
+    float* gate;
+    float* resid;
+    float* innov;
+    float eps, eta, var_eps, dt_init, dt_min, dt_max, cpi_modulation, temperature;
+    int gate_mode;
+    int64_t B, K, H, N;
+};
+int stream_chunk(const StreamCall& c, cudaStream_t stream);
+
 // train.cu
 struct TrainBwdCall {
     const void* lam;

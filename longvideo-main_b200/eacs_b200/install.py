@@ -13,7 +13,8 @@ import importlib
 
 
 def install(package: str = "cst_ssm", fuse_ungated: bool = False,
-            layer_dispatch: bool = False, queries: bool = False) -> dict:
+            layer_dispatch: bool = False, queries: bool = False,
+            streaming: bool = False) -> dict:
     """Patch `package` (already importable) and return what was replaced.
 
     fuse_ungated: also bind ContinuousSSMLayer.forward to the fused ungated
@@ -25,7 +26,10 @@ def install(package: str = "cst_ssm", fuse_ungated: bool = False,
     queries: also route EACSLayer.run_with_commits and the continuous-query
     functions (segment_index, readout_from_commits) through the commit and
     readout kernels where no gradient has to flow through the commits; the
-    reference's own code runs otherwise."""
+    reference's own code runs otherwise.
+    streaming: also route temporal_step (modules/streaming.py, and the name
+    models/adaptive_path.py imported from it) through the streaming step
+    kernel under the same rule."""
     from .ops import eacs_gated_scan as ours_cell
     from .ops import scan_cuda as ours_scan
 
@@ -67,6 +71,18 @@ def install(package: str = "cst_ssm", fuse_ungated: bool = False,
             if not hasattr(current, "__wrapped__"):  # installing twice keeps one wrapper
                 setattr(owner, name, make(current))
             patched[f"{owner.__name__.split('.')[-1]}.{name}"] = getattr(owner, name)
+    if streaming:
+        from .ops import streaming as ours_s
+
+        for mod_name in (f"{package}.modules.streaming", f"{package}.models.adaptive_path"):
+            try:
+                mod = importlib.import_module(mod_name)
+            except ImportError:  # the model package may be absent
+                continue
+            current = mod.temporal_step
+            if not hasattr(current, "__wrapped__"):
+                mod.temporal_step = ours_s.make_temporal_step(current)
+            patched[f"{mod_name.split('.')[-1]}.temporal_step"] = mod.temporal_step
     if layer_dispatch:
         from .ops import eacs_layer as ours_layer
 

@@ -575,6 +575,122 @@ int eacs_oracle_query_readout(const float* lam, const float* log_dt, const float
 }
 
 /* ---------------------------------------------------------------------------
+ * Streaming steps with explicit branch state (streaming.py:45-85 per branch,
+ * over eacs_step eacs.py:78-142 and EventGate.forward event_gate.py:86-105).
+ * Per row and step k (valid masks, first observation of a row commits with
+ * itself as predecessor, CPI-modulated threshold, hard or soft gate):
+ *   state in (h, t, u, B, C, init) -> state out; outputs y (before proj_out),
+ *   gate (1 on the first step), resid, innov (resid once initialised).
+ * ------------------------------------------------------------------------- */
+int eacs_oracle_stream_chunk(const float* lam, const float* log_dt, const float* D,
+                             const float* mean, const float* var, const float* u,
+                             const float* Bc, const float* Cc, const float* t,
+                             const uint8_t* valid, const float* cpi,
+                             const float* h_in, const float* t_in, const float* u_in,
+                             const float* B_in, const float* C_in, const uint8_t* init_in,
+                             float* h_out, float* t_out, float* u_out, float* B_out,
+                             float* C_out, uint8_t* init_out, float* y, float* gate,
+                             float* resid, float* innov, float eps, float eta, float var_eps,
+                             float dt_init, float dt_min, float dt_max, float cpi_mod,
+                             int gate_mode, float T, int64_t B, int64_t K, int64_t H,
+                             int64_t N) {
+    float Tp = T > 1e-4f ? T : 1e-4f;
+#pragma omp parallel for num_threads(nthreads()) schedule(dynamic, 1)
+    for (int64_t bi = 0; bi < B; ++bi) {
+        cf* h = (cf*)(h_out + bi * H * N * 2);
+        float* up = u_out + bi * H;
+        cf* Bp = (cf*)(B_out + bi * N * 2);
+        cf* Cp = (cf*)(C_out + bi * N * 2);
+        memcpy(h, h_in + bi * H * N * 2, sizeof(float) * (size_t)(H * N * 2));
+        memcpy(up, u_in + bi * H, sizeof(float) * (size_t)H);
+        memcpy(Bp, B_in + bi * N * 2, sizeof(float) * (size_t)(N * 2));
+        memcpy(Cp, C_in + bi * N * 2, sizeof(float) * (size_t)(N * 2));
+        float tp = t_in[bi];
+        int init = init_in[bi] != 0;
+        cf* dA = (cf*)malloc(sizeof(cf) * (size_t)(H * N));
+        cf* dBb = (cf*)malloc(sizeof(cf) * (size_t)(H * N));
+        for (int64_t k = 0; k < K; ++k) {
+            int64_t rk = bi * K + k;
+            if (valid && !valid[rk]) {
+                for (int64_t hh = 0; hh < H; ++hh) y[rk * H + hh] = 0.f;
+                gate[rk] = resid[rk] = innov[rk] = 0.f;
+                continue;
+            }
+            const float* ul = u + rk * H;
+            const float* Bl = Bc + rk * N * 2;
+            const float* Cl = Cc + rk * N * 2;
+            float tl = t[rk];
+            int first = !init;
+            if (first) {
+                for (int64_t hh = 0; hh < H; ++hh) up[hh] = ul[hh];
+                for (int64_t n = 0; n < N; ++n) {
+                    Bp[n] = (cf){Bl[2 * n], Bl[2 * n + 1]};
+                    Cp[n] = (cf){Cl[2 * n], Cl[2 * n + 1]};
+                }
+                tp = tl - dt_init;
+            }
+            float delta = tl - tp;
+            if (delta < 0.f) delta = 0.f;
+            double sdiff = 0.0, sobs = 0.0;
+            for (int64_t hh = 0; hh < H; ++hh) {
+                float dte = eff_dt(delta, expf(log_dt[hh]), dt_min, dt_max);
+                float yhat = 0.f;
+                for (int64_t n = 0; n < N; ++n) {
+                    int64_t i = hh * N + n;
+                    cf lm = {lam[2 * i], lam[2 * i + 1]};
+                    zoh_f(lm, cf_recip(lm), dte, &dA[i], &dBb[i]);
+                    cf xh = cf_add(cf_mul(dA[i], h[i]), cf_scale(cf_mul(dBb[i], Bp[n]), up[hh]));
+                    yhat += Cp[n].re * xh.re - Cp[n].im * xh.im;
+                }
+                float sd = sqrtf(var[hh] + var_eps);
+                float obs = (ul[hh] - mean[hh]) / sd;
+                float pred = (yhat - mean[hh]) / sd;
+                float d = obs - pred;
+                sdiff += (double)d * d;
+                sobs += (double)obs * obs;
+            }
+            float r = sqrtf((float)sdiff) / (sqrtf((float)sobs) + eta);
+            float eps_l = first ? -1.f : eps;
+            if (cpi && cpi_mod > 0.f) {
+                float c = cpi[rk] < 0.f ? 0.f : (cpi[rk] > 1.f ? 1.f : cpi[rk]);
+                eps_l = eps_l * (1.f - cpi_mod * c);
+                if (eps_l < 1e-3f) eps_l = 1e-3f;
+            }
+            float g = gate_mode == 1 ? 1.0f / (1.0f + expf(-((r - eps_l) / Tp)))
+                                     : (r > eps_l ? 1.f : 0.f);
+            gate[rk] = first ? 1.f : g;
+            resid[rk] = r;
+            innov[rk] = init ? r : 0.f;
+            for (int64_t hh = 0; hh < H; ++hh) {
+                float acc = 0.f;
+                for (int64_t n = 0; n < N; ++n) {
+                    int64_t i = hh * N + n;
+                    cf P = cf_mul(dA[i], h[i]);
+                    cf xh = cf_add(P, cf_scale(cf_mul(dBb[i], Bp[n]), up[hh]));
+                    cf hu = cf_add(P, cf_scale(cf_mul(dBb[i], (cf){Bl[2 * n], Bl[2 * n + 1]}), ul[hh]));
+                    cf hc = cf_add(cf_scale(hu, g), cf_scale(xh, 1.f - g));
+                    h[i] = first ? hc : cf_add(cf_scale(hu, g), cf_scale(h[i], 1.f - g));
+                    acc += Cl[2 * n] * hc.re - Cl[2 * n + 1] * hc.im;
+                }
+                y[rk * H + hh] = acc + D[hh] * ul[hh];
+                up[hh] = first ? ul[hh] : g * ul[hh] + (1.f - g) * up[hh];
+            }
+            for (int64_t n = 0; n < N; ++n) {
+                cf b = {Bl[2 * n], Bl[2 * n + 1]}, c = {Cl[2 * n], Cl[2 * n + 1]};
+                Bp[n] = first ? b : cf_add(cf_scale(b, g), cf_scale(Bp[n], 1.f - g));
+                Cp[n] = first ? c : cf_add(cf_scale(c, g), cf_scale(Cp[n], 1.f - g));
+            }
+            tp = first ? tl : g * tl + (1.f - g) * tp;
+            init = 1;
+        }
+        t_out[bi] = tp;
+        init_out[bi] = (uint8_t)init;
+        free(dA); free(dBb);
+    }
+    return 0;
+}
+
+/* ---------------------------------------------------------------------------
  * Backward of GatedEACSCellFunction (eacs_cell_train.py:117-175): the VJP of
  * _step_functional (eacs_cell_train.py:15-66) chained in reverse over L,
  * derived by hand and evaluated in double.  Hard gates are pinned to the

@@ -47,6 +47,7 @@ def lib():
         L.eacs_oracle_cell_commits.argtypes = ([_P] * 9 + [_F] * 6 + [_I, _I, _F, _F]
                                                + [_P] * 8 + [_I64] * 4)
         L.eacs_oracle_query_readout.argtypes = [_P] * 12 + [_I64] * 5 + [_F, _F]
+        L.eacs_oracle_stream_chunk.argtypes = [_P] * 27 + [_F] * 7 + [_I, _F] + [_I64] * 4
         L.eacs_oracle_set_threads.argtypes = [_I]
         L.eacs_oracle_version.restype = ctypes.c_char_p
         _lib = L
@@ -258,3 +259,38 @@ def query_readout(lam, log_dt, D, ch, ct, cu, cB, cC, frame_t, t_query, idx=None
                                     _ptr(cB), _ptr(cC), _ptr(frame_t), _ptr(t_query), _ptr(idx),
                                     _ptr(y), B, L, Q, H, N, dt_min, dt_max)
     return y
+
+
+def stream_chunk(lam, log_dt, D, mean, var, u, Bc, Cc, t, valid, cpi, state, eps, eta,
+                 var_eps=1e-5, dt_init=1.0, dt_min=1e-3, dt_max=1e3, cpi_mod=0.0,
+                 gate_mode=0, T=0.1):
+    """K streaming steps of one branch with explicit state
+    (cst_ssm/modules/streaming.py:45-85).  state = (h (B,H,N), t (B), u (B,H),
+    B (B,N), C (B,N), initialized (B)).  Returns (y, gate, resid, innov, state')."""
+    lam = _c(lam, np.complex64)
+    log_dt = _c(log_dt, np.float32)
+    D = _c(D, np.float32)
+    mean = _c(mean, np.float32)
+    var = _c(var, np.float32)
+    u = _c(u, np.float32)
+    Bc = _c(Bc, np.complex64)
+    Cc = _c(Cc, np.complex64)
+    t = _c(t, np.float32)
+    valid = None if valid is None else _c(valid, np.uint8)
+    cpi = None if cpi is None else _c(cpi, np.float32)
+    h0, t0, u0, B0, C0, i0 = state
+    h0, t0, u0 = _c(h0, np.complex64), _c(t0, np.float32), _c(u0, np.float32)
+    B0, C0, i0 = _c(B0, np.complex64), _c(C0, np.complex64), _c(i0, np.uint8)
+    B, K, H = u.shape
+    N = lam.shape[1]
+    h1, t1, u1 = np.empty_like(h0), np.empty_like(t0), np.empty_like(u0)
+    B1, C1, i1 = np.empty_like(B0), np.empty_like(C0), np.empty_like(i0)
+    y = np.empty((B, K, H), np.float32)
+    g, r, n = (np.empty((B, K), np.float32) for _ in range(3))
+    lib().eacs_oracle_stream_chunk(_ptr(lam), _ptr(log_dt), _ptr(D), _ptr(mean), _ptr(var), _ptr(u),
+                                   _ptr(Bc), _ptr(Cc), _ptr(t), _ptr(valid), _ptr(cpi), _ptr(h0),
+                                   _ptr(t0), _ptr(u0), _ptr(B0), _ptr(C0), _ptr(i0), _ptr(h1),
+                                   _ptr(t1), _ptr(u1), _ptr(B1), _ptr(C1), _ptr(i1), _ptr(y),
+                                   _ptr(g), _ptr(r), _ptr(n), eps, eta, var_eps, dt_init, dt_min,
+                                   dt_max, cpi_mod, int(gate_mode), T, B, K, H, N)
+    return y, g, r, n, (h1, t1, u1, B1, C1, i1)

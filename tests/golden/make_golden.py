@@ -16,6 +16,7 @@ Reference functions exercised (paths inside the CST-SSM project):
   ops/eacs_cell_train.py:81-199  GatedEACSCellFunction forward/backward
   modules/eacs.py:386-439      run_with_commits (per-frame commits)
   modules/continuous_query.py:12-61  segment_index / readout_from_commits
+  modules/streaming.py:45-85   temporal_step (explicit branch state)
 
     python tests/golden/make_golden.py --groups query   # rewrite one group only
 """
@@ -347,20 +348,101 @@ def query_cases():
     return out
 
 
+def stream_cases():
+    """temporal_step (streaming.py:45-85) on a one-branch MultiScaleEACS with
+    proj_out = identity and out_norm removed, so each step's output is
+    x + y_core on valid rows; the per-step projections are recomputed with
+    the same calls temporal_step makes."""
+    from torch import nn
+    from cst_ssm.modules.multiscale import MultiScaleEACS
+    from cst_ssm.modules.streaming import initial_states, temporal_step
+    from cst_ssm.ops.spectral_init import BranchSpec
+    out = {}
+    specs = {
+        # name: (H, N, B, K, seed, init_eps, cpi_modulation, soft gate (train, no STE), T)
+        "stream_hard": (24, 8, 3, 14, 30, 0.6, 0.0, False, 0.1),
+        "stream_cpi": (16, 16, 2, 12, 31, 0.6, 0.5, False, 0.1),
+        "stream_soft": (12, 5, 2, 10, 32, 0.6, 0.0, True, 0.3),
+    }
+    for name, (H, N, B, K, seed, e0, m, soft, T) in specs.items():
+        torch.manual_seed(seed)
+        temporal = MultiScaleEACS(H, branches=[BranchSpec("s", N, 0.5, 4.0)],
+                                  gate_kwargs=dict(init_eps=e0, eps_max=3.0, cpi_modulation=m,
+                                                   use_ste=not soft, temperature=T))
+        br = temporal.branches[0]
+        with torch.no_grad():
+            br.log_dt_scale.normal_(0.0, 0.2)
+            br.D.normal_(0.0, 1.0)
+            br.obs_norm.running_mean.normal_(0.0, 0.1)
+            br.obs_norm.running_var.uniform_(0.5, 1.5)
+            br.proj_out.weight.copy_(torch.eye(H))
+            br.proj_out.bias.zero_()
+        temporal.out_norm = nn.Identity()
+        temporal.train(soft)
+        x = torch.randn(B, K, H)
+        for k in range(1, K):
+            if k % 4 == 2:  # repeated frames: small residuals, skipped steps
+                x[:, k] = x[:, k - 1]
+        t = timestamps_exp(torch.Generator().manual_seed(seed + 1), B, K)
+        t[:, 5] = t[:, 4]
+        valid = torch.ones(B, K, dtype=torch.bool)
+        valid[1, :3] = False   # row 1 starts late: its first valid step commits
+        valid[0, 6] = False
+        valid[-1, K - 2] = False
+        cpi = torch.rand(B, K) * 1.4 - 0.2 if m > 0 else None
+        states = initial_states(temporal, B, "cpu")
+        mid = K // 2
+        ys, gs, rs, ns, us, Bs, Cs, st_mid = [], [], [], [], [], [], [], None
+        with torch.no_grad():
+            for k in range(K):
+                xk = x[:, k]
+                u_k, B_k, C_k = br._project(br.norm(xk))
+                us.append(u_k); Bs.append(B_k); Cs.append(C_k)
+                y, g, r, n, w, states = temporal_step(temporal, xk, t[:, k], states, valid[:, k],
+                                                      None if cpi is None else cpi[:, k])
+                ys.append(torch.where(valid[:, k, None], y - xk, torch.zeros_like(y)))
+                gs.append(g[:, 0]); rs.append(r[:, 0]); ns.append(n[:, 0])
+                if k == mid - 1:
+                    st_mid = states[0]
+        st = states[0]
+        eps = float(br.gate.eps.detach())
+        rr = torch.stack(rs, 1)
+        print(f"{name}: eps {eps:.4f}, gate mean {float(torch.stack(gs, 1).mean()):.3f}, "
+              f"min|r-eps| {float((rr[torch.stack(gs, 1) < 2] - eps).abs().min()):.2e}")
+        d = dict(lam=_np(br.lam()), log_dt=_np(br.log_dt_scale), D=_np(br.D),
+                 mean=_np(br.obs_norm.running_mean), var=_np(br.obs_norm.running_var),
+                 u=_np(torch.stack(us, 1)), Bc=_np(torch.stack(Bs, 1)), Cc=_np(torch.stack(Cs, 1)),
+                 t=_np(t), valid=valid.numpy().astype(np.uint8),
+                 scalars=np.array([eps, br.gate.norm_eta, br.obs_norm.eps, br.dt_init, 1e-3,
+                                   br.dt_max, m, T, 1.0 if soft else 0.0, mid], np.float64),
+                 y=_np(torch.stack(ys, 1)), gate=_np(torch.stack(gs, 1)), resid=_np(rr),
+                 innov=_np(torch.stack(ns, 1)),
+                 h=_np(st.h), st_t=_np(st.t), st_u=_np(st.u), st_B=_np(st.B), st_C=_np(st.C),
+                 st_init=st.initialized.numpy().astype(np.uint8),
+                 mid_h=_np(st_mid.h), mid_t=_np(st_mid.t), mid_u=_np(st_mid.u),
+                 mid_B=_np(st_mid.B), mid_C=_np(st_mid.C),
+                 mid_init=st_mid.initialized.numpy().astype(np.uint8))
+        if cpi is not None:
+            d["cpi"] = _np(cpi)
+        out[name] = d
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--groups", default="scan,ssm,cell,train,query",
+    ap.add_argument("--groups", default="scan,ssm,cell,train,query,stream",
                     help="comma-separated groups to (re)write")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     gen = torch.Generator().manual_seed(1234)
     makers = {"scan": lambda: scan_cases(gen), "ssm": lambda: ssm_cases(gen),
-              "cell": cell_cases, "train": train_cases, "query": query_cases}
+              "cell": cell_cases, "train": train_cases, "query": query_cases,
+              "stream": stream_cases}
     want = args.groups.split(",")
     groups = {}
-    for name in ("scan", "ssm", "cell", "train", "query"):  # fixed order: gen is shared
+    for name in ("scan", "ssm", "cell", "train", "query", "stream"):  # fixed order: gen is shared
         cases = makers[name]()
         if name in want:
             groups[name] = cases

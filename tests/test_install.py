@@ -129,3 +129,29 @@ def test_query_dispatch_keeps_reference_on_cpu_and_with_grad(ref_pkg):
     assert commits["h"].shape == (2, 10, 8, 4) and y.shape == (2, 5, 8)
     assert torch.allclose(y, y2)
     assert torch.equal(cq.segment_index(t, tq), torch.arange(5).expand(2, 5))
+
+
+def test_streaming_dispatch_keeps_reference_on_cpu(ref_pkg):
+    import eacs_b200
+    from cst_ssm.modules.multiscale import MultiScaleEACS
+    from cst_ssm.ops.spectral_init import BranchSpec
+
+    st_mod = importlib.import_module("cst_ssm.modules.streaming")
+    saved = st_mod.temporal_step
+    try:
+        patched = eacs_b200.install("cst_ssm", streaming=True)
+        assert "streaming.temporal_step" in patched
+        assert st_mod.temporal_step.__wrapped__ is saved
+        torch.manual_seed(0)
+        temporal = MultiScaleEACS(8, branches=[BranchSpec("s", 4, 0.5, 4.0)]).eval()
+        states = st_mod.initial_states(temporal, 2, "cpu")
+        x = torch.randn(2, 8)
+        with torch.no_grad():
+            y, g, r, n, w, new = st_mod.temporal_step(temporal, x, torch.zeros(2), states,
+                                                      torch.ones(2, dtype=torch.bool))
+        assert y.shape == (2, 8) and bool(new[0].initialized.all())
+    finally:
+        st_mod.temporal_step = saved
+        ap = sys.modules.get("cst_ssm.models.adaptive_path")
+        if ap is not None and hasattr(ap.temporal_step, "__wrapped__"):
+            ap.temporal_step = ap.temporal_step.__wrapped__

@@ -105,3 +105,48 @@ def test_commits_and_query_readout(name):
     yf = oracle.query_readout(d["lam"], d["log_dt"], d["D"], d["ch"], d["ct"], d["cu"], d["cB"],
                               d["cC"], d["t"], d["t"], idx=idx, dt_min=dt_min, dt_max=dt_max)
     assert relerr(yf, d["yf"]) < 1e-5
+
+
+STREAM = cases("stream")
+
+
+def stream_args(d):
+    eps, eta, var_eps, dt_init, dt_min, dt_max, m, T, soft, mid = [float(v) for v in d["scalars"]]
+    return dict(eps=eps, eta=eta, var_eps=var_eps, dt_init=dt_init, dt_min=dt_min, dt_max=dt_max,
+                cpi_mod=m, gate_mode=int(soft), T=T), int(mid)
+
+
+def zero_state(d):
+    B, K, H = d["u"].shape
+    N = d["lam"].shape[1]
+    return (np.zeros((B, H, N), np.complex64), np.zeros(B, np.float32), np.zeros((B, H), np.float32),
+            np.zeros((B, N), np.complex64), np.zeros((B, N), np.complex64), np.zeros(B, np.uint8))
+
+
+@pytest.mark.parametrize("name", sorted(STREAM))
+def test_stream_chunk(name):
+    """temporal_step (streaming.py:45-85): the whole sequence as one chunk and
+    as two chunks through the intermediate state."""
+    d = STREAM[name]
+    kw, mid = stream_args(d)
+    cpi = d.get("cpi")
+    ins = (d["lam"], d["log_dt"], d["D"], d["mean"], d["var"])
+    y, g, r, n, st = oracle.stream_chunk(*ins, d["u"], d["Bc"], d["Cc"], d["t"], d["valid"], cpi,
+                                         zero_state(d), **kw)
+    assert relerr(y, d["y"]) < 1e-5
+    assert relerr(g, d["gate"]) < 1e-5
+    assert relerr(r, d["resid"]) < 1e-5
+    assert relerr(n, d["innov"]) < 1e-5
+    for got, key in zip(st, ("h", "st_t", "st_u", "st_B", "st_C", "st_init")):
+        assert relerr(got, d[key]) < 1e-5, key
+    # two chunks: [0, mid) then [mid, K) from the state after step mid-1
+    sl = lambda a, lo, hi: None if a is None else a[:, lo:hi]
+    _, _, _, _, st1 = oracle.stream_chunk(*ins, *(sl(d[k], 0, mid) for k in ("u", "Bc", "Cc", "t", "valid")),
+                                          sl(cpi, 0, mid), zero_state(d), **kw)
+    for got, key in zip(st1, ("mid_h", "mid_t", "mid_u", "mid_B", "mid_C", "mid_init")):
+        assert relerr(got, d[key]) < 1e-5, key
+    K = d["u"].shape[1]
+    y2, _, _, _, st2 = oracle.stream_chunk(*ins, *(sl(d[k], mid, K) for k in ("u", "Bc", "Cc", "t", "valid")),
+                                           sl(cpi, mid, K), st1, **kw)
+    assert relerr(y2, d["y"][:, mid:]) < 1e-5
+    assert relerr(st2[0], d["h"]) < 1e-5
