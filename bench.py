@@ -67,6 +67,9 @@ def parse():
                     help="budget of the CPU baseline sample (rank 0, N=1)")
     ap.add_argument("--profile", action="store_true",
                     help="device-timed section only (no e2e, no CPU sample): for ncu captures")
+    ap.add_argument("--eps", type=float, default=None,
+                    help="gate threshold override for the cell workload (e.g. ~1.01 skips about "
+                    "half the frames of the N(0,1) features and exercises the repair path)")
     ap.add_argument("--shape", default=None,
                     help="B,L,H,N override for --workload ssm_train (e.g. a small case for ncu)")
     ap.add_argument("--workload", choices=["cell", "scan", "ssm", "ssm_train", "train", "multiscale"],
@@ -251,6 +254,8 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     d, eps = make_inputs(0, torch.device("cpu")) if not torch.cuda.is_available() else \
         make_inputs(0, torch.device("cuda", 0))
+    if args.eps is not None:
+        eps = float(args.eps)
     host = oracle_sample_inputs(d)
     cores = cpu_cores()
     budget = 90.0 / max(1, args.steps + args.warmup)
@@ -291,6 +296,8 @@ def run_ours(args):
                                 device_id=dev)
 
     d, eps = make_inputs(rank, dev)
+    if args.eps is not None:
+        eps = float(args.eps)
     y = torch.empty(B, L, H, device=dev)
     gate = torch.empty(B, L, device=dev)
     resid = torch.empty(B, L, device=dev)
@@ -425,7 +432,8 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,1) fp16 features through a seed-0 EACSLayer init)",
-            "config": dict(CONFIG, update_rate=update_rate),
+            "config": dict(CONFIG, update_rate=update_rate,
+                           **({} if args.eps is None else {"eps_override": eps})),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
                          "kernel": "cell_chain<SPEC> (speculative all-commit gated chain)",

@@ -41,7 +41,7 @@ constexpr int kMinBlocks = 768 / kThreads;    // keep 24 warps per SM resident
 constexpr int kT = 32;                         // steps per staged chunk
 constexpr int kRepair = 1024;  // repair kernel CTA
 
-enum Mode { SPEC = 0, UNGATED = 1, REPLAY = 2 };
+enum Mode { SPEC = 0, UNGATED = 1, REPLAY = 2, SPEC_COMMITS = 3 };  // SPEC_COMMITS: SPEC + commit_h
 
 struct Args {
     const float2* lam;
@@ -135,7 +135,8 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
     constexpr int NP = LANES * NPT;
     constexpr int NW = kThreads / 32;
     constexpr int U = EACS_CHAIN_U;
-    constexpr int NV = MODE == SPEC ? 2 * U : U;  // readout sums per group
+    constexpr bool kSpec = MODE == SPEC || MODE == SPEC_COMMITS;  // speculative gated pass
+    constexpr int NV = kSpec ? 2 * U : U;  // readout sums per group
     using Shape = BflyShape<NV, LANES>;
     static_assert(kT % U == 0, "chunk must hold whole step groups");
     static_assert(kT % kSsmCk == 0 && kSsmCk % U == 0, "checkpoints fall on step-group starts");
@@ -251,12 +252,12 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                         hs[j] = hn;
                     // commits: under the all-commit assumption h_pi after step l is h_l;
                     // rows that skip get their steps from l* on rewritten by the repair
-                    if (MODE == SPEC && a.commit_h != nullptr && nv[j] && i < steps)
+                    if (MODE == SPEC_COMMITS && nv[j] && i < steps)
                         a.commit_h[((rowLH + l0 + i) * H + h) * N + n] = hn;
                     if (MODE != REPLAY) {
                         const float2 Cl = sC[i][n];
                         yp += cre_mul(Cl, hs[j]);
-                        if (MODE == SPEC) {
+                        if (kSpec) {
                             const float2 qp = cmul(dB, Bp[j]);
                             const float2 xh = make_float2(fmaf(qp.x, u_prev, P.x), fmaf(qp.y, u_prev, P.y));
                             yhp += cre_mul(Cp[j], xh);
@@ -266,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                     }
                 }
                 vals[uu] = yp;
-                if (MODE == SPEC) vals[U + uu] = yhp;
+                if (kSpec) vals[U + uu] = yhp;
                 if (act) {
                     u_prev = ul;
                     t_prev = tl;
@@ -283,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                 const int i = i0 + (orig % U);
                 if (orig < U) {  // output readout of step i
                     if (writer && hv && i < steps) sy[i][hl] = vals[k] + Dh * su[i][hl];
-                } else if (MODE == SPEC && writer && hv && i < steps) {  // prediction of step i
+                } else if (kSpec && writer && hv && i < steps) {  // prediction of step i
                     const float ul = su[i][hl];
                     const float obs = (ul - mu) * rsd;
                     const float pred = (vals[k] - mu) * rsd;
@@ -292,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                     r2[k] = obs * obs;
                 }
             }
-            if (MODE == SPEC) {
+            if (kSpec) {
                 // sum over the channel groups of the warp (lanes with equal ln hold the same step)
 #pragma unroll
                 for (int o = LANES; o < 32; o <<= 1) {
@@ -318,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                 const int i = idx / HT, k = idx % HT;
                 if (h0 + k < H) a.y[(rowLH + l0 + i) * H + h0 + k] = sy[i][k];
             }
-            if (MODE == SPEC) {
+            if (kSpec) {
                 for (int i = tid; i < steps; i += kThreads) {
                     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
@@ -911,7 +912,9 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
 
     cudaError_t e;
     if (c.gate_mode == 0) {
-        if ((e = chain_dispatch<SPEC>(a, c.u_dtype, stream)) != cudaSuccess) return cuda_check(e, fn);
+        e = commits ? chain_dispatch<SPEC_COMMITS>(a, c.u_dtype, stream)
+                    : chain_dispatch<SPEC>(a, c.u_dtype, stream);
+        if (e != cudaSuccess) return cuda_check(e, fn);
         cell_resid<<<dim3((a.L + 255) / 256, a.B), 256, 0, stream>>>(a);
         note_launch();
         if ((e = cudaGetLastError()) != cudaSuccess) return cuda_check(e, fn);

@@ -48,7 +48,10 @@ def stream_chunk(lam, log_dt_scale, D, mean, var, u, Bc, Cc, t, valid, cpi, stat
             and h0.shape == (B, H, N), "stream_chunk: shape mismatch")
     if u.dtype not in _lib.DTYPE_CODES:
         u = u.float()
+    # every converted copy stays bound to a name until the launch is enqueued:
+    # a temporary freed earlier could hand its memory to the next conversion
     u_c = u.contiguous()
+    B_c, C_c, t_c = _c64(Bc), _c64(Cc), _f32(t)
     valid_c = None if valid is None else valid.to(torch.uint8).contiguous()
     cpi_c = None if cpi is None else _f32(cpi)
     ins = [_c64(lam), _f32(log_dt_scale), _f32(D), _f32(mean), _f32(var)]
@@ -59,7 +62,7 @@ def stream_chunk(lam, log_dt_scale, D, mean, var, u, Bc, Cc, t, valid, cpi, stat
     with torch.cuda.device(dev):
         _lib.check(_lib.lib().eacs_stream_chunk(
             *[x.data_ptr() for x in ins], u_c.data_ptr(), _lib.DTYPE_CODES[u_c.dtype],
-            _c64(Bc).data_ptr(), _c64(Cc).data_ptr(), _f32(t).data_ptr(), _lib.ptr(valid_c),
+            B_c.data_ptr(), C_c.data_ptr(), t_c.data_ptr(), _lib.ptr(valid_c),
             _lib.ptr(cpi_c), *[x.data_ptr() for x in st_in], *[x.data_ptr() for x in st_out],
             y.data_ptr(), g.data_ptr(), r.data_ptr(), n.data_ptr(), float(eps), float(eta),
             float(var_eps), float(dt_init), float(dt_min), float(dt_max), float(cpi_modulation),
