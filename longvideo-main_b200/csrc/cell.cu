@@ -623,6 +623,276 @@ __global__ void __launch_bounds__(kRepair) cell_repair(Args a) {
 }
 
 // ---------------------------------------------------------------------------
+// 5' (cluster): the exact sequential gated cell from l*, one thread-block
+// cluster of CL CTAs per row.  CTA c owns channels [c*HC, (c+1)*HC); thread
+// (hl, ln) owns chains n = ln + LANES*j (j < NPT) and keeps their committed
+// state, B_pi, C_pi and its channel's u_pi in registers.  Per step: one ZOH
+// per chain (shared by the prediction and the update), the prediction's
+// residual sums reduced over the row through distributed shared memory --
+// every warp sends its two partial sums to every CTA with st.async, counted
+// on that CTA's mbarrier (double-buffered slots, bounded wait) -- then the
+// gate, the update and the readout.  Every CTA sums the slots in the same
+// order, so all of them take the same gate decision.
+// ---------------------------------------------------------------------------
+constexpr int kRcMaxThreads = 512;
+constexpr int kRcMaxCL = 16;
+
+__device__ __forceinline__ void rc_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <int LANES, int NPT, typename UT>
+__global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int CL, int HC) {
+    __shared__ uint64_t rbar[2];
+    __shared__ float2 slots[2][kRcMaxCL * (kRcMaxThreads / 32)];
+    const int b = blockIdx.y;
+    const int crank = blockIdx.x;  // the cluster spans the CL CTAs of a row
+    const int L = a.L, H = a.H, N = a.N;
+    const int4 rowv = a.row[b];
+    const int lstar = rowv.x;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int NW = blockDim.x >> 5;
+    const int ln = tid % LANES, hl = tid / LANES;
+    const int h = crank * HC + hl;
+    const bool hv = hl < HC && h < H;
+    if (tid == 0) {
+        mbar_init(&rbar[0], 1);
+        mbar_init(&rbar[1], 1);
+        fence_mbar_init();
+    }
+    rc_cluster_sync();  // barriers initialised everywhere before any remote store
+    if (lstar >= L) {   // row verified by the speculative pass (uniform over the cluster)
+        rc_cluster_sync();
+        return;
+    }
+    const UT* u = static_cast<const UT*>(a.u);
+    const size_t rowLH = static_cast<size_t>(b) * L;
+    const int lp = lstar > 0 ? lstar - 1 : 0;
+
+    float2 lam[NPT], ilam[NPT], hs[NPT], Bp[NPT], Cp[NPT];
+    bool nv[NPT];
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) {
+        const int n = ln + LANES * j;
+        nv[j] = hv && n < N;
+        const size_t o = static_cast<size_t>(hv ? h : 0) * N + (n < N ? n : 0);
+        lam[j] = nv[j] ? a.lam[o] : make_float2(-1.f, 0.f);
+        ilam[j] = crecip(lam[j]);
+        hs[j] = nv[j] ? a.hpi[static_cast<size_t>(b) * H * N + o] : make_float2(0.f, 0.f);
+        // every step before l* committed: the predecessor is step l* - 1 (or step 0's inputs)
+        Bp[j] = (n < N) ? a.Bc[(rowLH + lp) * N + n] : make_float2(0.f, 0.f);
+        Cp[j] = (n < N) ? a.Cc[(rowLH + lp) * N + n] : make_float2(0.f, 0.f);
+    }
+    const float scale = hv ? expf(a.log_dt[h]) : 1.f;
+    const float rsd = hv ? 1.0f / sqrtf(a.var[h] + a.var_eps) : 1.f;
+    const float mu = hv ? a.mean[h] : 0.f;
+    const float Dh = hv ? a.D[h] : 0.f;
+    float u_pi = hv ? to_f32(u[(rowLH + lp) * H + h]) : 0.f;
+    float t_pi = lstar > 0 ? a.t[rowLH + lp] : a.t[rowLH] - a.dt_init;
+    float spike = __int_as_float(rowv.y);
+    float prev_r = __int_as_float(rowv.z);
+    const bool soft = a.gate_mode == 1;
+    const int nslot = CL * NW;
+    uint32_t rslot[2] = {0u, 0u}, rbarr[2] = {0u, 0u};
+    if (lane < CL) {  // lane c sends to CTA c
+        rslot[0] = mapa_u32(&slots[0][crank * NW + wid], lane);
+        rslot[1] = mapa_u32(&slots[1][crank * NW + wid], lane);
+        rbarr[0] = mapa_u32(&rbar[0], lane);
+        rbarr[1] = mapa_u32(&rbar[1], lane);
+    }
+    bool failed = false;
+
+    // next step's inputs, loaded one step ahead
+    float t_nx = a.t[rowLH + lstar];
+    float u_nx = hv ? to_f32(u[(rowLH + lstar) * H + h]) : 0.f;
+    float2 B_nx[NPT], C_nx[NPT];
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) {
+        const int n = ln + LANES * j;
+        B_nx[j] = nv[j] ? a.Bc[(rowLH + lstar) * N + n] : make_float2(0.f, 0.f);
+        C_nx[j] = nv[j] ? a.Cc[(rowLH + lstar) * N + n] : make_float2(0.f, 0.f);
+    }
+
+    for (int l = lstar; l < L; ++l) {
+        const float tl = t_nx, ul = u_nx;
+        float2 Bl[NPT], Cl[NPT];
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            Bl[j] = B_nx[j];
+            Cl[j] = C_nx[j];
+        }
+        if (l + 1 < L) {
+            t_nx = a.t[rowLH + l + 1];
+            u_nx = hv ? to_f32(u[(rowLH + l + 1) * H + h]) : 0.f;
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                const int n = ln + LANES * j;
+                B_nx[j] = nv[j] ? a.Bc[(rowLH + l + 1) * N + n] : make_float2(0.f, 0.f);
+                C_nx[j] = nv[j] ? a.Cc[(rowLH + l + 1) * N + n] : make_float2(0.f, 0.f);
+            }
+        }
+        const float dte = eff_dt(fmaxf(tl - t_pi, 0.f), scale, a.dt_min, a.dt_max);
+        float2 P[NPT], dB[NPT], xh[NPT];
+        float yhp = 0.f;
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            float2 dA;
+            zoh(lam[j], ilam[j], dte, dA, dB[j]);
+            P[j] = cmul(dA, hs[j]);
+            const float2 q = cmul(dB[j], Bp[j]);
+            xh[j] = make_float2(fmaf(q.x, u_pi, P[j].x), fmaf(q.y, u_pi, P[j].y));
+            yhp += cre_mul(Cp[j], xh[j]);
+        }
+#pragma unroll
+        for (int o = LANES / 2; o > 0; o >>= 1) yhp += __shfl_xor_sync(0xffffffffu, yhp, o);
+        float d2 = 0.f, o2 = 0.f;
+        if (hv && ln == 0) {
+            const float obs = (ul - mu) * rsd;
+            const float dd = obs - (yhp - mu) * rsd;
+            d2 = dd * dd;
+            o2 = obs * obs;
+        }
+        d2 = warp_sum(d2);
+        o2 = warp_sum(o2);
+        // row sums through the cluster
+        const int k = l - lstar;
+        const int par = k & 1;
+        const uint32_t phase = (k >> 1) & 1;
+        if (!failed) {
+            if (tid == 0) mbar_expect_tx(&rbar[par], static_cast<uint32_t>(nslot) * 8u);
+            if (lane < CL) {
+                st_async_f32(rslot[par], d2, rbarr[par]);
+                st_async_f32(rslot[par] + 4u, o2, rbarr[par]);
+            }
+            if (!mbar_wait_cluster(&rbar[par], phase)) failed = true;
+        }
+        float s1 = 0.f, s2 = 0.f;
+        for (int q = lane; q < nslot; q += 32) {
+            const float2 v = slots[par][q];
+            s1 += v.x;
+            s2 += v.y;
+        }
+        s1 = warp_sum(s1);
+        s2 = warp_sum(s2);
+        const float num = sqrtf(s1), nobs = sqrtf(s2);
+        const float r = num / (nobs + a.eta);
+        float g;
+        if (soft) {
+            g = 1.0f / (1.0f + expf(-((r - a.eps) / a.Tp)));
+        } else {
+            float eps_l = a.eps;
+            if (a.robust && spike >= static_cast<float>(a.robust_k)) eps_l = a.eps_lo;
+            g = r > eps_l ? 1.f : 0.f;
+        }
+        if (a.robust) {
+            if (l > 0) spike = (r > prev_r * a.spike_ratio) ? spike + 1.f : 0.f;
+            prev_r = r;
+        }
+        if (crank == 0 && tid == 0) {
+            a.gate[rowLH + l] = g;
+            a.resid[rowLH + l] = r;
+            if (a.stats) a.stats[rowLH + l] = make_float2(num, nobs);
+        }
+        // update, readout, commit
+        float yp = 0.f;
+        const bool fire = soft || g > 0.5f;
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            float2 hc = xh[j];
+            if (fire) {
+                const float2 qc = cmul(dB[j], Bl[j]);
+                const float2 hu = make_float2(fmaf(qc.x, ul, P[j].x), fmaf(qc.y, ul, P[j].y));
+                if (soft) {
+                    const float2 gu = cscale(hu, g);
+                    hc = cadd(gu, cscale(xh[j], 1.f - g));
+                    hs[j] = cadd(gu, cscale(hs[j], 1.f - g));
+                } else {
+                    hc = hu;
+                    hs[j] = hu;
+                }
+            }
+            yp += cre_mul(Cl[j], hc);
+            if (a.commit_h != nullptr && nv[j])
+                a.commit_h[((rowLH + l) * H + h) * N + ln + LANES * j] = hs[j];
+        }
+#pragma unroll
+        for (int o = LANES / 2; o > 0; o >>= 1) yp += __shfl_xor_sync(0xffffffffu, yp, o);
+        if (hv && ln == 0) a.y[(rowLH + l) * H + h] = yp + Dh * ul;
+        if (soft) {
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                Bp[j] = cadd(cscale(Bl[j], g), cscale(Bp[j], 1.f - g));
+                Cp[j] = cadd(cscale(Cl[j], g), cscale(Cp[j], 1.f - g));
+            }
+            u_pi = g * ul + (1.f - g) * u_pi;
+            t_pi = g * tl + (1.f - g) * t_pi;
+        } else if (fire) {
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                Bp[j] = Bl[j];
+                Cp[j] = Cl[j];
+            }
+            u_pi = ul;
+            t_pi = tl;
+        }
+    }
+    rc_cluster_sync();  // no CTA leaves while a peer may still write its slots
+}
+
+// Cluster shape of the repair pass for (H, N): LANES x NPT chains per
+// channel and CL CTAs per row with at most kRcMaxThreads threads each; 0 when
+// the shape does not fit (the one-CTA repair pass handles it).
+struct RcShape {
+    int lanes, npt, cl, hc, threads;
+};
+RcShape rc_shape(int H, int N) {
+    RcShape r{0, 0, 0, 0, 0};
+    if (N <= 4) { r.lanes = 4; r.npt = 1; }
+    else if (N <= 8) { r.lanes = 4; r.npt = 2; }
+    else if (N <= 16) { r.lanes = 4; r.npt = 4; }
+    else if (N <= 32) { r.lanes = 8; r.npt = 4; }
+    else if (N <= 64) { r.lanes = 16; r.npt = 4; }
+    else return r;
+    for (int cl = 8; cl <= kRcMaxCL; cl *= 2) {  // 8 CTAs per row keeps a full row set co-resident
+        const int hc = (H + cl - 1) / cl;
+        const int threads = ((hc * r.lanes + 31) / 32) * 32;
+        if (threads <= kRcMaxThreads) {
+            r.cl = cl;
+            r.hc = hc;
+            r.threads = threads;
+            return r;
+        }
+    }
+    r.cl = 0;
+    return r;
+}
+
+template <int LANES, int NPT, typename UT>
+cudaError_t launch_repair_cluster(const Args& a, const RcShape& rs, cudaStream_t s) {
+    auto kern = cell_repair_cluster<LANES, NPT, UT>;
+    cudaError_t e;
+    if (rs.cl > 8) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rs.cl, a.B);
+    cfg.blockDim = dim3(rs.threads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = rs.cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, a, rs.cl, rs.hc);
+    note_launch();
+    return e;
+}
+
+// ---------------------------------------------------------------------------
 // 6 (commits): per row, the last committed step c(l) <= l as a max-scan of
 // (g_l > 0.5 ? l : -1), and t_pi after each step; then u_pi, B_pi, C_pi are
 // the inputs at max(c(l), 0) (the initial state holds step 0's u, B, C and
@@ -773,6 +1043,14 @@ cudaError_t chain_dispatch(const Args& a, int dtype, cudaStream_t s) {
 
 template <typename UT>
 cudaError_t repair_by_n(const Args& a, cudaStream_t s) {
+    const RcShape rs = rc_shape(a.H, a.N);
+    if (rs.cl > 0) {
+        if (rs.lanes == 4 && rs.npt == 1) return launch_repair_cluster<4, 1, UT>(a, rs, s);
+        if (rs.lanes == 4 && rs.npt == 2) return launch_repair_cluster<4, 2, UT>(a, rs, s);
+        if (rs.lanes == 4) return launch_repair_cluster<4, 4, UT>(a, rs, s);
+        if (rs.lanes == 8) return launch_repair_cluster<8, 4, UT>(a, rs, s);
+        return launch_repair_cluster<16, 4, UT>(a, rs, s);
+    }
     int lanes, npt;
     lanes_for(a.N, &lanes, &npt);
     while (npt > 1 && lanes < 32) {  // the repair pass keeps one chain per lane
