@@ -172,7 +172,7 @@ __device__ __forceinline__ void cluster_sync_all() {
 // [c*HC, (c+1)*HC); thread (hl, ln) owns chains n = ln + LANES*j.
 // ---------------------------------------------------------------------------
 template <int LANES, int NPT, typename UT>
-__global__ void train_bwd(TArgs a) {
+__global__ void __launch_bounds__(512) train_bwd(TArgs a) {
     constexpr int NP = LANES * NPT;
     extern __shared__ __align__(16) unsigned char smem[];
     const int T = blockDim.x;
@@ -605,7 +605,19 @@ __global__ void train_post_params(TArgs a) {
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
+#ifndef EACS_TRAIN_NPT
+#define EACS_TRAIN_NPT 4
+#endif
 int lanes_train(int N, int* lanes, int* npt) {
+    if (EACS_TRAIN_NPT == 4 && N > 8) {
+        // four chains a thread: half the threads per channel, so a row fits
+        // in a cluster of 8 CTAs and a batch of rows runs in one wave
+        if (N <= 16) { *lanes = 4; *npt = 4; }
+        else if (N <= 32) { *lanes = 8; *npt = 4; }
+        else if (N <= 64) { *lanes = 16; *npt = 4; }
+        else return 0;
+        return 1;
+    }
     if (N <= 8) { *lanes = 4; *npt = 2; }
     else if (N <= 16) { *lanes = 8; *npt = 2; }
     else if (N <= 32) { *lanes = 16; *npt = 2; }
@@ -675,14 +687,26 @@ TWs tws(int64_t B, int64_t L, int64_t H, int64_t N, int CL, int kK) {
     return w;
 }
 
+// The checkpoint pass is an independent chain per (h, n): it keeps two
+// chains a thread (the most threads per row) whatever the backward's layout.
+template <typename UT>
+cudaError_t launch_ckpt(TArgs& a, cudaStream_t s) {
+    const int N = a.N;
+    const int lanes = N <= 8 ? 4 : N <= 16 ? 8 : N <= 32 ? 16 : 32;
+    const dim3 grid((a.H + kCkThreads / lanes - 1) / (kCkThreads / lanes), a.B);
+    if (lanes == 4) train_ckpt<4, 2, UT><<<grid, kCkThreads, 0, s>>>(a);
+    else if (lanes == 8) train_ckpt<8, 2, UT><<<grid, kCkThreads, 0, s>>>(a);
+    else if (lanes == 16) train_ckpt<16, 2, UT><<<grid, kCkThreads, 0, s>>>(a);
+    else train_ckpt<32, 2, UT><<<grid, kCkThreads, 0, s>>>(a);
+    note_launch();
+    return cudaGetLastError();
+}
+
 template <int LANES, int NPT, typename UT>
 cudaError_t launch_train(TArgs& a, int T, cudaStream_t s) {
     constexpr int NP = LANES * NPT;
     {
-        dim3 grid((a.H + kCkThreads / LANES - 1) / (kCkThreads / LANES), a.B);
-        train_ckpt<LANES, NPT, UT><<<grid, kCkThreads, 0, s>>>(a);
-        note_launch();
-        cudaError_t e = cudaGetLastError();
+        cudaError_t e = launch_ckpt<UT>(a, s);
         if (e != cudaSuccess) return e;
     }
     const size_t smem = smem_bytes(T, NPT, NP, a.HC, a.K);
@@ -724,6 +748,13 @@ template <typename UT>
 cudaError_t train_by_n(TArgs& a, int T, cudaStream_t s) {
     int lanes, npt;
     lanes_train(a.N, &lanes, &npt);
+#if EACS_TRAIN_NPT == 4
+    if (npt == 4) {
+        if (lanes == 4) return launch_train<4, 4, UT>(a, T, s);
+        if (lanes == 8) return launch_train<8, 4, UT>(a, T, s);
+        return launch_train<16, 4, UT>(a, T, s);
+    }
+#endif
     if (lanes == 4) return launch_train<4, 2, UT>(a, T, s);
     if (lanes == 8) return launch_train<8, 2, UT>(a, T, s);
     if (lanes == 16) return launch_train<16, 2, UT>(a, T, s);
