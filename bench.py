@@ -45,6 +45,9 @@ UPDATES = B * L * H * N
 # Minimal (algorithmic) bytes of one call: read u (fp16), Bc, Cc (complex64),
 # t (fp32); write y (fp32), gate, resid (fp32).
 ALG_BYTES = B * L * H * 2 + 2 * B * L * N * 8 + B * L * 4 + B * L * H * 4 + 2 * B * L * 4
+# Frames per chunk of the host-buffer (end-to-end) call: the copies of one
+# chunk overlap the cell of the next.
+E2E_CHUNK = 512
 # Issue slots per state update of cell_chain<SPEC> at this workload: ncu
 # smsp__inst_executed.sum x 32 / updates = 1,051,860,480 x 32 / 402,653,184.
 INSTR_PER_UPDATE = 83.6
@@ -351,7 +354,7 @@ def run_ours(args):
     value = job_rate(args.steps, total_s, world)
 
     # ---- end to end through the public API, host buffers ------------------
-    from eacs_b200.ops.eacs_gated_scan import eacs_cell_forward
+    from eacs_b200.ops.eacs_gated_scan import eacs_cell_forward_host
     pin = {k: d[k].cpu().pin_memory() for k in ("u", "Bc", "Cc", "t")}
     out_host = [torch.empty(B, L, H).pin_memory(), torch.empty(B, L).pin_memory(),
                 torch.empty(B, L).pin_memory()]
@@ -359,13 +362,10 @@ def run_ours(args):
     d2h = sum(v.numel() * v.element_size() for v in out_host)
 
     def e2e_step():
-        dd = {k: v.to(dev, non_blocking=True) for k, v in pin.items()}
-        yy, gg, rr = eacs_cell_forward(d["lam"], d["log_dt"], dd["u"], dd["Bc"], dd["Cc"], dd["t"],
-                                       d["D"], d["mean"], d["var"], eps, ETA, VAR_EPS, DT_INIT,
-                                       DT_MIN, DT_MAX)
-        out_host[0].copy_(yy, non_blocking=True)
-        out_host[1].copy_(gg, non_blocking=True)
-        out_host[2].copy_(rr, non_blocking=True)
+        # the host-buffer entry point: time chunks' copies overlap the cell
+        eacs_cell_forward_host(d["lam"], d["log_dt"], pin["u"], pin["Bc"], pin["Cc"], pin["t"],
+                               d["D"], d["mean"], d["var"], eps, ETA, VAR_EPS, DT_INIT, DT_MIN,
+                               DT_MAX, chunk=E2E_CHUNK, out=out_host)
 
     e2e_steps = 0 if args.profile else max(3, min(args.steps, 30))
     for _ in range(3 if e2e_steps else 0):

@@ -280,6 +280,38 @@ EACS_API int eacs_stream_chunk(const void* lam, const float* log_dt, const float
                                int gate_mode, float temperature,
                                int64_t B, int64_t K, int64_t H, int64_t N, void* stream);
 
+/* Device workspace bytes eacs_cell_fwd_host needs (0 if unsupported). */
+EACS_API size_t eacs_cell_fwd_host_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N,
+                                                  int64_t chunk);
+
+/* eacs_cell_fwd (hard gate) with the sequences and outputs in HOST memory:
+ * u (B,L,H) of u_dtype, Bc/Cc (B,L,N) complex64, t (B,L) float32 in, y
+ * (B,L,H), gate, resid (B,L) float32 out -- pinned (cudaHostAlloc /
+ * cudaHostRegister) for the copies to overlap; pageable memory works but
+ * copies synchronously.  Parameters (lam, log_dt, D, mean, var) and the
+ * workspace are device pointers.  The frames are processed in chunks of
+ * `chunk` frames (rounded up to a multiple of 32; <= 0 picks 512): the
+ * copy-in of one chunk and the copy-out of another overlap the cell of a
+ * third, each row resuming from the state the previous chunk left, on two
+ * copy streams the library owns for the device and on `stream`, which
+ * completes when the outputs are in host memory.  Results equal one
+ * eacs_cell_fwd over the whole sequence.  Same semantics and gate options as
+ * eacs_cell_fwd; shapes whose repair pass cannot resume rows (more than 16
+ * CTAs of 512 threads per row) return EACS_ERR_UNSUPPORTED.  Calls on one
+ * device are enqueued one at a time.  No reference counterpart: it is the
+ * host-buffer form of eacs_cell_fwd for callers whose features are in host
+ * memory (long videos streamed from a feature cache). */
+EACS_API int eacs_cell_fwd_host(const void* lam, const float* log_dt, const float* D,
+                                const float* mean, const float* var,
+                                const void* u, int u_dtype, const void* Bc, const void* Cc,
+                                const float* t, float eps, float eta, float var_eps,
+                                float dt_init, float dt_min, float dt_max,
+                                int robust, int robust_k, float spike_ratio, float eps_factor,
+                                float* y, float* gate, float* resid,
+                                void* workspace, size_t workspace_bytes,
+                                int64_t B, int64_t L, int64_t H, int64_t N, int64_t chunk,
+                                void* stream);
+
 /* Bytes of the library-owned scratch array behind eacs_cell_fwd_noalloc. */
 #define EACS_NOALLOC_SCRATCH_BYTES (32u << 20)
 

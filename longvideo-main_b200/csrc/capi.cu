@@ -231,6 +231,24 @@ int eacs_stream_chunk(const void* lam, const float* log_dt, const float* D, cons
     return eacs::stream_chunk(c, static_cast<cudaStream_t>(stream));
 }
 
+size_t eacs_cell_fwd_host_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N, int64_t chunk) {
+    return eacs::cell_host_workspace_size(B, L, H, N, chunk);
+}
+
+int eacs_cell_fwd_host(const void* lam, const float* log_dt, const float* D, const float* mean,
+                       const float* var, const void* u, int u_dtype, const void* Bc, const void* Cc,
+                       const float* t, float eps, float eta, float var_eps, float dt_init,
+                       float dt_min, float dt_max, int robust, int robust_k, float spike_ratio,
+                       float eps_factor, float* y, float* gate, float* resid, void* workspace,
+                       size_t workspace_bytes, int64_t B, int64_t L, int64_t H, int64_t N,
+                       int64_t chunk, void* stream) {
+    eacs::CellHostCall c{lam,   log_dt, D,       mean,    var,    u,           u_dtype,
+                         Bc,    Cc,     t,       eps,     eta,    var_eps,     dt_init,
+                         dt_min, dt_max, robust, robust_k, spike_ratio, eps_factor, y,
+                         gate,  resid,  workspace, workspace_bytes, B, L, H, N, chunk};
+    return eacs::cell_fwd_host(c, static_cast<cudaStream_t>(stream));
+}
+
 int eacs_cell_fwd_noalloc(const void* lam, const float* log_dt, const void* u, int u_dtype,
                           const void* Bc, const void* Cc, const float* t, const float* D,
                           const float* mean, const float* var, float eps, float eta, float var_eps,

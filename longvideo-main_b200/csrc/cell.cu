@@ -74,6 +74,18 @@ struct Args {
     float2* commit_B;  // (B,L,N)
     float2* commit_C;
     int* cidx;         // [B][L] last committed step <= l (-1: the initial state)
+    // optional row state carried between time chunks (gated modes): the
+    // committed state before this call's first step and after its last one
+    const float2* cin_h;   // (B,H,N)
+    const float* cin_u;    // (B,H)
+    const float2* cin_B;   // (B,N)
+    const float2* cin_C;
+    const float4* cin_row; // (B) t_pi, spike count, r of the previous step, -
+    float2* cout_h;
+    float* cout_u;
+    float2* cout_B;
+    float2* cout_C;
+    float4* cout_row;
     int B, L, H, N, ntiles, nK;
 };
 
@@ -177,6 +189,11 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
         hs[j] = make_float2(0.f, 0.f);
         Bp[j] = nv[j] ? a.Bc[rowLH * N + n] : make_float2(0.f, 0.f);
         Cp[j] = nv[j] ? a.Cc[rowLH * N + n] : make_float2(0.f, 0.f);
+        if (MODE != UNGATED && a.cin_h != nullptr && nv[j]) {  // resumed row
+            hs[j] = a.cin_h[(static_cast<size_t>(b) * H + h) * N + n];
+            Bp[j] = a.cin_B[static_cast<size_t>(b) * N + n];
+            Cp[j] = a.cin_C[static_cast<size_t>(b) * N + n];
+        }
     }
     const float scale = hv ? expf(a.log_dt[h]) : 1.f;
     // 1/sqrt(var + var_eps): the residual standardises with a multiply
@@ -187,6 +204,10 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
     float u_prev = hv ? to_f32(u[rowLH * H + h]) : 0.f;
     const float t0 = a.t[rowLH];
     float t_prev = t0 - a.dt_init;
+    if (MODE != UNGATED && a.cin_h != nullptr) {
+        if (hv) u_prev = a.cin_u[static_cast<size_t>(b) * H + h];
+        t_prev = a.cin_row[b].x;
+    }
     float dt0 = 0.f;  // ungated: dt_0 = dt_1 (continuous_ssm.py:45-48)
     if (MODE == UNGATED && L > 1) dt0 = fmaxf(a.t[rowLH + 1] - t0, 0.f);
     const int held = Shape::held_index(ln);
@@ -337,6 +358,20 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
         for (int j = 0; j < NPT; ++j)
             if (nv[j]) a.hpi[(static_cast<size_t>(b) * H + h) * N + ln + LANES * j] = hs[j];
     }
+    if (kSpec && a.cout_h != nullptr) {
+        // state after the last step if every step committed (the repair pass
+        // rewrites it for rows that skip); the caller keeps L a multiple of U
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            if (nv[j]) a.cout_h[(static_cast<size_t>(b) * H + h) * N + n] = hs[j];
+            if (tile == 0 && hl == 0 && n < N) {
+                a.cout_B[static_cast<size_t>(b) * N + n] = Bp[j];
+                a.cout_C[static_cast<size_t>(b) * N + n] = Cp[j];
+            }
+        }
+        if (hv && ln == 0) a.cout_u[static_cast<size_t>(b) * H + h] = u_prev;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -372,8 +407,12 @@ __global__ void __launch_bounds__(1024) cell_gates(Args a) {
     const int tid = threadIdx.x;
     const int lane = tid & 31, wid = tid >> 5;
     const size_t rb = static_cast<size_t>(b) * a.L;
-    int carry_R = 0;       // R_{l0-1}
-    float carry_r = 0.f;   // r_{l0-1}
+    // R_{l0-1} (last step that was not a spike; the spike count after step
+    // l is l - R_l) and r_{l0-1}; a resumed row starts from its carried count
+    const bool resumed = a.cin_row != nullptr;
+    const float4 cin = resumed ? a.cin_row[b] : make_float4(0.f, 0.f, 0.f, 0.f);
+    int carry_R = resumed ? -1 - static_cast<int>(cin.y) : -1;
+    float carry_r = cin.z;
     int lstar = a.L;
     int4 rowv = make_int4(a.L, 0, 0, 0);
     for (int l0 = 0; l0 < a.L; l0 += 1024) {
@@ -386,7 +425,7 @@ __global__ void __launch_bounds__(1024) cell_gates(Args a) {
         if (lane == 31) sbound[wid] = r;
         __syncthreads();
         if (lane == 0) rprev = (wid == 0) ? carry_r : sbound[wid - 1];
-        const bool f = valid && l >= 1 && (r > rprev * a.spike_ratio);
+        const bool f = valid && (l >= 1 || resumed) && (r > rprev * a.spike_ratio);
         // inclusive max-scan of key = f ? -1 : l  (R_l), with the tile carry
         int key = f ? -1 : (valid ? l : -1);
         int x = key;
@@ -412,7 +451,7 @@ __global__ void __launch_bounds__(1024) cell_gates(Args a) {
         int excl = __shfl_up_sync(0xffffffffu, incl, 1);       // R_{l-1}
         if (lane == 0) excl = max(pre_w, carry_R);
         if (wid == 0 && lane == 0) excl = carry_R;
-        const float spike_prev = (l == 0) ? 0.f : static_cast<float>((l - 1) - excl);
+        const float spike_prev = static_cast<float>((l - 1) - excl);
         float eps_l = a.eps;
         if (a.robust && spike_prev >= static_cast<float>(a.robust_k)) eps_l = a.eps_lo;
         const bool g = r > eps_l;
@@ -441,7 +480,13 @@ __global__ void __launch_bounds__(1024) cell_gates(Args a) {
         carry_R = slast_R;
         __syncthreads();
     }
-    if (lstar == a.L && tid == 0) a.row[b] = rowv;
+    if (lstar == a.L && tid == 0) {
+        a.row[b] = rowv;
+        if (a.cout_row != nullptr) {  // every step committed: t_pi is the last step's time
+            a.cout_row[b] = make_float4(a.t[rb + a.L - 1], static_cast<float>((a.L - 1) - carry_R),
+                                        carry_r, 0.f);
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -668,6 +713,7 @@ __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int
     const UT* u = static_cast<const UT*>(a.u);
     const size_t rowLH = static_cast<size_t>(b) * L;
     const int lp = lstar > 0 ? lstar - 1 : 0;
+    const bool resumed = a.cin_row != nullptr;
 
     float2 lam[NPT], ilam[NPT], hs[NPT], Bp[NPT], Cp[NPT];
     bool nv[NPT];
@@ -679,9 +725,14 @@ __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int
         lam[j] = nv[j] ? a.lam[o] : make_float2(-1.f, 0.f);
         ilam[j] = crecip(lam[j]);
         hs[j] = nv[j] ? a.hpi[static_cast<size_t>(b) * H * N + o] : make_float2(0.f, 0.f);
-        // every step before l* committed: the predecessor is step l* - 1 (or step 0's inputs)
+        // every step before l* committed: the predecessor is step l* - 1, or at
+        // l* = 0 the carried state of a resumed row (else step 0's inputs)
         Bp[j] = (n < N) ? a.Bc[(rowLH + lp) * N + n] : make_float2(0.f, 0.f);
         Cp[j] = (n < N) ? a.Cc[(rowLH + lp) * N + n] : make_float2(0.f, 0.f);
+        if (lstar == 0 && resumed && n < N) {
+            Bp[j] = a.cin_B[static_cast<size_t>(b) * N + n];
+            Cp[j] = a.cin_C[static_cast<size_t>(b) * N + n];
+        }
     }
     const float scale = hv ? expf(a.log_dt[h]) : 1.f;
     const float rsd = hv ? 1.0f / sqrtf(a.var[h] + a.var_eps) : 1.f;
@@ -689,6 +740,10 @@ __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int
     const float Dh = hv ? a.D[h] : 0.f;
     float u_pi = hv ? to_f32(u[(rowLH + lp) * H + h]) : 0.f;
     float t_pi = lstar > 0 ? a.t[rowLH + lp] : a.t[rowLH] - a.dt_init;
+    if (lstar == 0 && resumed) {
+        if (hv) u_pi = a.cin_u[static_cast<size_t>(b) * H + h];
+        t_pi = a.cin_row[b].x;
+    }
     float spike = __int_as_float(rowv.y);
     float prev_r = __int_as_float(rowv.z);
     const bool soft = a.gate_mode == 1;
@@ -764,7 +819,7 @@ __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int
                 st_async_f32(rslot[par], d2, rbarr[par]);
                 st_async_f32(rslot[par] + 4u, o2, rbarr[par]);
             }
-            if (!mbar_wait_cluster(&rbar[par], phase)) failed = true;
+            if (!mbar_wait_row(&rbar[par], phase)) failed = true;
         }
         float s1 = 0.f, s2 = 0.f;
         for (int q = lane; q < nslot; q += 32) {
@@ -785,7 +840,9 @@ __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int
             g = r > eps_l ? 1.f : 0.f;
         }
         if (a.robust) {
-            if (l > 0) spike = (r > prev_r * a.spike_ratio) ? spike + 1.f : 0.f;
+            if (l > 0 || resumed) spike = (r > prev_r * a.spike_ratio) ? spike + 1.f : 0.f;
+            prev_r = r;
+        } else {
             prev_r = r;
         }
         if (crank == 0 && tid == 0) {
@@ -835,6 +892,19 @@ __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int
             u_pi = ul;
             t_pi = tl;
         }
+    }
+    if (a.cout_h != nullptr) {  // the row's state after its last step
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            if (nv[j]) a.cout_h[(static_cast<size_t>(b) * H + h) * N + n] = hs[j];
+            if (crank == 0 && hl == 0 && n < N) {
+                a.cout_B[static_cast<size_t>(b) * N + n] = Bp[j];
+                a.cout_C[static_cast<size_t>(b) * N + n] = Cp[j];
+            }
+        }
+        if (hv && ln == 0) a.cout_u[static_cast<size_t>(b) * H + h] = u_pi;
+        if (crank == 0 && tid == 0) a.cout_row[b] = make_float4(t_pi, spike, prev_r, 0.f);
     }
     rc_cluster_sync();  // no CTA leaves while a peer may still write its slots
 }
@@ -1115,6 +1185,11 @@ size_t cell_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
     return ws_layout(B, L, H, N).total;
 }
 
+bool cell_resumable(int64_t H, int64_t N) {
+    return H > 0 && N > 0 && N <= 64 && H <= (1LL << 24) &&
+           rc_shape(static_cast<int>(H), static_cast<int>(N)).cl > 0;
+}
+
 size_t cell_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
     if (B <= 0 || L <= 0 || H <= 0 || N <= 0 || N > 64) return 0;
     return ws_layout(B, L, H, N).total_commits;
@@ -1138,6 +1213,11 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
         return fail(EACS_ERR_INVALID, "%s: null commit output", fn);
     if (commits && c.gate_mode != 0)
         return fail(EACS_ERR_INVALID, "%s: commits are recorded for the hard gate only", fn);
+    const bool carry = c.cin_h != nullptr || c.cout_h != nullptr;
+    if (carry && !cell_resumable(c.H, c.N))
+        return fail(EACS_ERR_UNSUPPORTED, "%s: resuming rows needs the cluster repair shape", fn);
+    if (c.cout_h != nullptr && (c.L % 4) != 0)
+        return fail(EACS_ERR_INVALID, "%s: a chunk with a carried-out state needs L %% 4 == 0", fn);
     const WsLayout w = ws_layout(c.B, c.L, c.H, c.N);
     const size_t need = commits ? w.total_commits : w.total;
     if (!c.workspace || c.workspace_bytes < need)
@@ -1182,6 +1262,16 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
         a.commit_C = static_cast<float2*>(c.commit_C);
         a.cidx = reinterpret_cast<int*>(ws + w.cidx);
     }
+    a.cin_h = static_cast<const float2*>(c.cin_h);
+    a.cin_u = c.cin_u;
+    a.cin_B = static_cast<const float2*>(c.cin_B);
+    a.cin_C = static_cast<const float2*>(c.cin_C);
+    a.cin_row = static_cast<const float4*>(c.cin_row);
+    a.cout_h = static_cast<float2*>(c.cout_h);
+    a.cout_u = c.cout_u;
+    a.cout_B = static_cast<float2*>(c.cout_B);
+    a.cout_C = static_cast<float2*>(c.cout_C);
+    a.cout_row = static_cast<float4*>(c.cout_row);
     a.B = static_cast<int>(c.B);
     a.L = static_cast<int>(c.L);
     a.H = static_cast<int>(c.H);

@@ -239,6 +239,36 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t phase)
     return false;
 }
 
+// The same bounded wait by polling with mbarrier.test_wait, which never
+// suspends the thread (try_wait may suspend it for a system-dependent time).
+__device__ __forceinline__ bool mbar_poll_cluster(uint64_t* bar, uint32_t phase) {
+    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(phase)
+            : "memory");
+        if (ok) return true;
+    }
+    set_status(EACS_ERR_TIMEOUT);
+    return false;
+}
+
+// Wait used by the cluster reductions of the repair and training passes.
+#ifndef EACS_MBAR_POLL
+#define EACS_MBAR_POLL 0
+#endif
+__device__ __forceinline__ bool mbar_wait_row(uint64_t* bar, uint32_t phase) {
+#if EACS_MBAR_POLL
+    return mbar_poll_cluster(bar, phase);
+#else
+    return mbar_wait_cluster(bar, phase);
+#endif
+}
+
 // Address of `local` in the shared memory of CTA `cta` of this cluster.
 __device__ __forceinline__ uint32_t mapa_u32(const void* local, int cta) {
     uint32_t ra;

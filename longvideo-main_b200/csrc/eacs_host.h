@@ -60,9 +60,49 @@ struct CellCall {
     float* commit_u = nullptr; // (B,L,H)
     void* commit_B = nullptr;  // (B,L,N) complex64
     void* commit_C = nullptr;
+    // optional row state carried between time chunks (hard gate or soft gate,
+    // cluster repair shapes): in = state before step 0 (nullptr: the initial
+    // state), out = state after step L-1 (L a multiple of 4)
+    const void* cin_h = nullptr;  // (B,H,N) complex64
+    const float* cin_u = nullptr; // (B,H)
+    const void* cin_B = nullptr;  // (B,N) complex64
+    const void* cin_C = nullptr;
+    const void* cin_row = nullptr;  // (B) float4: t_pi, spike, r_prev, -
+    void* cout_h = nullptr;
+    float* cout_u = nullptr;
+    void* cout_B = nullptr;
+    void* cout_C = nullptr;
+    void* cout_row = nullptr;
 };
 size_t cell_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
 size_t cell_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+// true when the repair pass for (H, N) can resume rows from a carried state
+bool cell_resumable(int64_t H, int64_t N);
+
+// pipeline.cu: gated cell over host buffers, time chunks pipelined with the copies
+struct CellHostCall {
+    const void* lam;  // parameters: device pointers
+    const float* log_dt;
+    const float* D;
+    const float* mean;
+    const float* var;
+    const void* u;    // sequences and outputs: host pointers (pinned for overlap)
+    int u_dtype;
+    const void* Bc;
+    const void* Cc;
+    const float* t;
+    float eps, eta, var_eps, dt_init, dt_min, dt_max;
+    int robust, robust_k;
+    float spike_ratio, eps_factor;
+    float* y;
+    float* gate;
+    float* resid;
+    void* workspace;  // device
+    size_t workspace_bytes;
+    int64_t B, L, H, N, chunk;
+};
+size_t cell_host_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N, int64_t chunk);
+int cell_fwd_host(const CellHostCall& c, cudaStream_t stream);
 int cell_fwd(const CellCall& c, cudaStream_t stream);
 int cell_fwd_noalloc(const CellCall& c, cudaStream_t stream);
 // ckpt == nullptr: inference; otherwise also writes the state before every

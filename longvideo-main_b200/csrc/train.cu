@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(512) train_bwd(TArgs a) {
                 const uint32_t phase = (nred >> 1) & 1;
                 if (tid == 0) mbar_expect_tx(&rbar[par], static_cast<uint32_t>(nslot) * 4u);
                 if (lane < CL) st_async_f32(rslot[par], gl, rbarr[par]);
-                if (!mbar_wait_cluster(&rbar[par], phase)) failed = true;
+                if (!mbar_wait_row(&rbar[par], phase)) failed = true;
                 const float* sl = slots + par * 16 * 32;
                 float tot = 0.f;
                 for (int q = lane; q < nslot; q += 32) tot += sl[q];

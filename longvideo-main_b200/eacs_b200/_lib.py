@@ -50,6 +50,9 @@ SIGNATURES = {
                                _I64, _I64, _I64, _I64, _P]),
     "eacs_query_index": (_I, [_P, _P, _P, _I64, _I64, _I64, _P]),
     "eacs_query_readout": (_I, [_P] * 11 + [_I64] * 5 + [_F, _F, _P]),
+    "eacs_cell_fwd_host_workspace_size": (_SZ, [_I64] * 5),
+    "eacs_cell_fwd_host": (_I, [_P] * 6 + [_I] + [_P] * 3 + [_F] * 6 + [_I, _I, _F, _F]
+                           + [_P] * 4 + [_SZ] + [_I64] * 5 + [_P]),
     "eacs_stream_chunk": (_I, [_P] * 6 + [_I] + [_P] * 21 + [_F] * 7 + [_I, _F]
                           + [_I64] * 4 + [_P]),
     "eacs_ssm_bwd_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),

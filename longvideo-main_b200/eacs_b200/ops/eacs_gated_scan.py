@@ -99,6 +99,67 @@ def eacs_cell_forward(lam: Tensor, log_dt_scale: Tensor, u: Tensor, Bc: Tensor,
     return y, gates, resid
 
 
+def _host_tensor(name, x, dtype):
+    require(isinstance(x, Tensor) and not x.is_cuda, f"eacs_cell_forward_host: {name} must be a host tensor")
+    x = x if x.dtype == dtype else x.to(dtype)
+    return x.contiguous()
+
+
+@torch.no_grad()
+def eacs_cell_forward_host(lam: Tensor, log_dt_scale: Tensor, u: Tensor, Bc: Tensor, Cc: Tensor,
+                           t: Tensor, D: Tensor, mean: Tensor, var: Tensor, eps: float,
+                           eta: float, var_eps: float = 1e-5, dt_init: float = 1.0,
+                           dt_min: float = 1e-3, dt_max: float = 1e3, robust=None,
+                           chunk: int = 512, out=None):
+    """eacs_cell_forward (hard gate) with u, Bc, Cc, t and the outputs in host
+    memory: the time chunks' copies overlap the cell of neighbouring chunks
+    (eacs_cell_fwd_host).  Parameters stay on the device.  Host inputs should
+    be pinned (Tensor.pin_memory()); `out` = (y, gates, resid) pinned host
+    tensors to write into, else they are allocated pinned.  Returns them;
+    they are complete once the current stream has synchronised."""
+    dev = cuda_tensors("eacs_cell_forward_host", lam, log_dt_scale, D, mean, var)
+    require(u.dim() == 3 and lam.dim() == 2 and lam.size(0) == u.size(2), "u:(B,L,H), lam:(H,N)")
+    B, L, H = u.shape
+    N = lam.shape[1]
+    require(Bc.shape == (B, L, N) and Cc.shape == (B, L, N) and t.shape == (B, L),
+            "Bc, Cc: (B,L,N), t: (B,L)")
+    u_h = u.contiguous() if u.dtype in _lib.DTYPE_CODES else u.float().contiguous()
+    require(not u_h.is_cuda, "eacs_cell_forward_host: u must be a host tensor")
+    B_h = _host_tensor("Bc", Bc, torch.complex64)
+    C_h = _host_tensor("Cc", Cc, torch.complex64)
+    t_h = _host_tensor("t", t, torch.float32)
+    params = (lam.to(torch.complex64).contiguous(), log_dt_scale.float().contiguous(),
+              D.float().contiguous(), mean.float().contiguous(), var.float().contiguous())
+    if out is None:
+        out = (torch.empty(B, L, H, dtype=torch.float32, pin_memory=True),
+               torch.empty(B, L, dtype=torch.float32, pin_memory=True),
+               torch.empty(B, L, dtype=torch.float32, pin_memory=True))
+    y, gates, resid = out
+    require(y.shape == (B, L, H) and gates.shape == (B, L) and resid.shape == (B, L)
+            and not y.is_cuda and y.dtype == torch.float32 and y.is_contiguous(),
+            "eacs_cell_forward_host: out = (y (B,L,H), gates, resid (B,L)) float32 host tensors")
+    if y.numel() == 0:
+        return y, gates, resid
+    rb, rk, rr, rf = _robust_tuple(robust)
+    L_ = _lib.lib()
+    nbytes = int(L_.eacs_cell_fwd_host_workspace_size(B, L, H, N, int(chunk)))
+    require(nbytes > 0, f"eacs_cell_fwd_host: unsupported sizes B={B} L={L} H={H} N={N}")
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(L_.eacs_cell_fwd_host(
+            *[p.data_ptr() for p in params], u_h.data_ptr(), _lib.DTYPE_CODES[u_h.dtype],
+            B_h.data_ptr(), C_h.data_ptr(), t_h.data_ptr(), float(eps), float(eta),
+            float(var_eps), float(dt_init), float(dt_min), float(dt_max), rb, rk, rr, rf,
+            y.data_ptr(), gates.data_ptr(), resid.data_ptr(), ws.data_ptr(), ws.numel(),
+            B, L, H, N, int(chunk), _lib.stream_ptr(dev)), "eacs_cell_fwd_host")
+    # Lifetimes: the workspace and converted parameters are device memory of
+    # this stream, which the call leaves waiting for all its copies; converted
+    # host inputs are pageable, whose copies are staged before the call
+    # returns; the caller's own pinned tensors must stay alive until the
+    # stream has synchronised, as with any asynchronous copy.
+    return y, gates, resid
+
+
 class _CellExt:
     """Object with the reference extension's method (eacs_cell_cuda.cu:170-175)."""
 
