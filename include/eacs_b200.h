@@ -312,6 +312,33 @@ EACS_API int eacs_cell_fwd_host(const void* lam, const float* log_dt, const floa
                                 int64_t B, int64_t L, int64_t H, int64_t N, int64_t chunk,
                                 void* stream);
 
+/* ---- feature cache (host side; no device memory is touched except by
+ * eacs_fc_upload's copy) ----
+ * One video's features <vid>.npy (C-order little-endian float16 or float32,
+ * shape (L, P, d) or (L, d)) and timestamps <vid>.ts.npy (L float32 or
+ * float64), the layout the reference writes (data_pipeline/src/npz_to_npy.py)
+ * and memory-maps (cst_ssm/data/dataset.py:58-67, numpy.load mmap_mode="r").
+ * The feature file is mapped read-only; frames are copied out of the mapping
+ * with several threads.  Functions return EACS_OK or an error code with the
+ * message in eacs_last_error(). */
+typedef struct eacs_fc eacs_fc;
+
+/* Open `npy_path` and its "<stem>.ts.npy"; *out receives the handle. */
+EACS_API int eacs_fc_open(const char* npy_path, eacs_fc** out);
+/* Frames L, patches P (1 for (L, d) files), width d, EACS_DTYPE_F16/F32. */
+EACS_API int eacs_fc_info(const eacs_fc* fc, int64_t* L, int64_t* P, int64_t* d, int* dtype);
+/* The L timestamps as float32 into host memory `out`. */
+EACS_API int eacs_fc_timestamps(const eacs_fc* fc, float* out);
+/* Frames [l0, l0+n) (n*P*d elements of the file's dtype) into host `dst`. */
+EACS_API int eacs_fc_read(const eacs_fc* fc, int64_t l0, int64_t n, void* dst);
+/* eacs_fc_read into host `staging` (pinned, staging_bytes >= n*P*d*size),
+ * then an asynchronous copy to device `dst_device` on `stream`; `staging`
+ * must stay untouched until that copy has completed. */
+EACS_API int eacs_fc_upload(const eacs_fc* fc, int64_t l0, int64_t n, void* staging,
+                            size_t staging_bytes, void* dst_device, void* stream);
+/* Unmap and free the handle (NULL is a no-op). */
+EACS_API void eacs_fc_close(eacs_fc* fc);
+
 /* Bytes of the library-owned scratch array behind eacs_cell_fwd_noalloc. */
 #define EACS_NOALLOC_SCRATCH_BYTES (32u << 20)
 

@@ -50,6 +50,13 @@ SIGNATURES = {
                                _I64, _I64, _I64, _I64, _P]),
     "eacs_query_index": (_I, [_P, _P, _P, _I64, _I64, _I64, _P]),
     "eacs_query_readout": (_I, [_P] * 11 + [_I64] * 5 + [_F, _F, _P]),
+    "eacs_fc_open": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
+    "eacs_fc_info": (_I, [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I64), ctypes.POINTER(_I64),
+                          ctypes.POINTER(_I)]),
+    "eacs_fc_timestamps": (_I, [_P, _P]),
+    "eacs_fc_read": (_I, [_P, _I64, _I64, _P]),
+    "eacs_fc_upload": (_I, [_P, _I64, _I64, _P, _SZ, _P, _P]),
+    "eacs_fc_close": (None, [_P]),
     "eacs_cell_fwd_host_workspace_size": (_SZ, [_I64] * 5),
     "eacs_cell_fwd_host": (_I, [_P] * 6 + [_I] + [_P] * 3 + [_F] * 6 + [_I, _I, _F, _F]
                            + [_P] * 4 + [_SZ] + [_I64] * 5 + [_P]),
