@@ -312,6 +312,21 @@ EACS_API int eacs_cell_fwd_host(const void* lam, const float* log_dt, const floa
                                 int64_t B, int64_t L, int64_t H, int64_t N, int64_t chunk,
                                 void* stream);
 
+/* MultiScaleEACS branch epilogue in one pass (cst_ssm/modules/multiscale.py:
+ * 176-179): per row, w = softmax(x W^T + b) over the S branches, then
+ * y = LayerNorm(x + sum_s w_s delta_s) * ln_weight + ln_bias.
+ * x, y and the S branch outputs delta[s] (proj_out outputs): (rows, d) of
+ * `dtype` (float32, float16 or bfloat16), 16-byte aligned, d a multiple of 8
+ * (4 for float32) and at most 2048 (1024 for float32); `deltas` is a HOST
+ * array of S device pointers, S <= 8.  fusion_weight (S, d) and
+ * fusion_bias (S) float32 (bias may be NULL); ln_weight / ln_bias (d)
+ * float32 or NULL (1 / 0); weights (rows, S) float32 output or NULL.
+ * Computes in float32 with one rounding to `dtype` at the end. */
+EACS_API int eacs_branch_fuse(const void* x, const void* const* deltas, int S, int dtype,
+                              const float* fusion_weight, const float* fusion_bias,
+                              const float* ln_weight, const float* ln_bias, float ln_eps,
+                              void* y, float* weights, int64_t rows, int64_t d, void* stream);
+
 /* ---- feature cache (host side; no device memory is touched except by
  * eacs_fc_upload's copy) ----
  * One video's features <vid>.npy (C-order little-endian float16 or float32,

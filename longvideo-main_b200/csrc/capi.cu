@@ -249,6 +249,30 @@ int eacs_cell_fwd_host(const void* lam, const float* log_dt, const float* D, con
     return eacs::cell_fwd_host(c, static_cast<cudaStream_t>(stream));
 }
 
+int eacs_branch_fuse(const void* x, const void* const* deltas, int S, int dtype,
+                     const float* fusion_weight, const float* fusion_bias, const float* ln_weight,
+                     const float* ln_bias, float ln_eps, void* y, float* weights, int64_t rows,
+                     int64_t d, void* stream) {
+    if (S <= 0 || S > 8 || !deltas)
+        return eacs::fail(EACS_ERR_INVALID, "eacs_branch_fuse: S=%d outside 1..8 or no branch outputs", S);
+    if (d <= 0 || d > (1 << 20)) return eacs::fail(EACS_ERR_INVALID, "eacs_branch_fuse: d=%lld", (long long)d);
+    eacs::FuseCall c{};
+    c.x = x;
+    for (int s = 0; s < S; ++s) c.delta[s] = deltas[s];
+    c.S = S;
+    c.dtype = dtype;
+    c.wf = fusion_weight;
+    c.bf = fusion_bias;
+    c.gamma = ln_weight;
+    c.beta = ln_bias;
+    c.ln_eps = ln_eps;
+    c.y = y;
+    c.w = weights;
+    c.rows = rows;
+    c.d = static_cast<int>(d);
+    return eacs::branch_fuse(c, static_cast<cudaStream_t>(stream));
+}
+
 int eacs_cell_fwd_noalloc(const void* lam, const float* log_dt, const void* u, int u_dtype,
                           const void* Bc, const void* Cc, const float* t, const float* D,
                           const float* mean, const float* var, float eps, float eta, float var_eps,

@@ -161,6 +161,24 @@ struct StreamCall {
 };
 int stream_chunk(const StreamCall& c, cudaStream_t stream);
 
+// fuse.cu: MultiScaleEACS branch epilogue
+struct FuseCall {
+    const void* x;
+    const void* delta[8];
+    int S;
+    int dtype;
+    const float* wf;
+    const float* bf;
+    const float* gamma;
+    const float* beta;
+    float ln_eps;
+    void* y;
+    float* w;
+    int64_t rows;
+    int d;
+};
+int branch_fuse(const FuseCall& c, cudaStream_t stream);
+
 // train.cu
 struct TrainBwdCall {
     const void* lam;

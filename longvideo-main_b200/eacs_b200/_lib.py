@@ -50,6 +50,7 @@ SIGNATURES = {
                                _I64, _I64, _I64, _I64, _P]),
     "eacs_query_index": (_I, [_P, _P, _P, _I64, _I64, _I64, _P]),
     "eacs_query_readout": (_I, [_P] * 11 + [_I64] * 5 + [_F, _F, _P]),
+    "eacs_branch_fuse": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _F, _P, _P, _I64, _I64, _P]),
     "eacs_fc_open": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
     "eacs_fc_info": (_I, [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I64), ctypes.POINTER(_I64),
                           ctypes.POINTER(_I)]),

@@ -14,7 +14,7 @@ import importlib
 
 def install(package: str = "cst_ssm", fuse_ungated: bool = False,
             layer_dispatch: bool = False, queries: bool = False,
-            streaming: bool = False) -> dict:
+            streaming: bool = False, multiscale: bool = False) -> dict:
     """Patch `package` (already importable) and return what was replaced.
 
     fuse_ungated: also bind ContinuousSSMLayer.forward to the fused ungated
@@ -29,7 +29,10 @@ def install(package: str = "cst_ssm", fuse_ungated: bool = False,
     reference's own code runs otherwise.
     streaming: also route temporal_step (modules/streaming.py, and the name
     models/adaptive_path.py imported from it) through the streaming step
-    kernel under the same rule."""
+    kernel under the same rule.
+    multiscale: also route MultiScaleEACS.forward's epilogue (fusion softmax,
+    blend, LayerNorm) through the one-pass branch-fuse kernel, under the same
+    rule."""
     from .ops import eacs_gated_scan as ours_cell
     from .ops import scan_cuda as ours_scan
 
@@ -83,6 +86,14 @@ def install(package: str = "cst_ssm", fuse_ungated: bool = False,
             if not hasattr(current, "__wrapped__"):
                 mod.temporal_step = ours_s.make_temporal_step(current)
             patched[f"{mod_name.split('.')[-1]}.temporal_step"] = mod.temporal_step
+    if multiscale:
+        from .ops import multiscale as ours_ms
+
+        ref_ms = importlib.import_module(f"{package}.modules.multiscale")
+        current = ref_ms.MultiScaleEACS.forward
+        if not hasattr(current, "__wrapped__"):
+            ref_ms.MultiScaleEACS.forward = ours_ms.make_forward(current)
+        patched["multiscale.MultiScaleEACS.forward"] = ref_ms.MultiScaleEACS.forward
     if layer_dispatch:
         from .ops import eacs_layer as ours_layer
 

@@ -155,3 +155,24 @@ def test_streaming_dispatch_keeps_reference_on_cpu(ref_pkg):
         ap = sys.modules.get("cst_ssm.models.adaptive_path")
         if ap is not None and hasattr(ap.temporal_step, "__wrapped__"):
             ap.temporal_step = ap.temporal_step.__wrapped__
+
+
+def test_multiscale_dispatch_keeps_reference_on_cpu(ref_pkg):
+    import eacs_b200
+    from cst_ssm.modules.multiscale import MultiScaleEACS
+    from cst_ssm.ops.spectral_init import BranchSpec
+
+    ms_mod = importlib.import_module("cst_ssm.modules.multiscale")
+    saved = ms_mod.MultiScaleEACS.forward
+    try:
+        patched = eacs_b200.install("cst_ssm", multiscale=True)
+        assert ms_mod.MultiScaleEACS.forward.__wrapped__ is saved
+        assert "multiscale.MultiScaleEACS.forward" in patched
+        torch.manual_seed(0)
+        temporal = MultiScaleEACS(8, branches=[BranchSpec("a", 4, 0.5, 4.0),
+                                               BranchSpec("b", 4, 4.0, 32.0)]).eval()
+        with torch.no_grad():
+            out = temporal(torch.randn(2, 6, 8), torch.cumsum(torch.full((2, 6), 0.25), 1))
+        assert out.y.shape == (2, 6, 8) and out.fusion_weights.shape == (2, 6, 2)
+    finally:
+        ms_mod.MultiScaleEACS.forward = saved
