@@ -34,7 +34,7 @@ namespace {
 #define EACS_CHAIN_THREADS 128
 #endif
 #ifndef EACS_CHAIN_U
-#define EACS_CHAIN_U 4
+#define EACS_CHAIN_U 8
 #endif
 constexpr int kThreads = EACS_CHAIN_THREADS;  // chain kernel CTA
 constexpr int kMinBlocks = 768 / kThreads;    // keep 24 warps per SM resident

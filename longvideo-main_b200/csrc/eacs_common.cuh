@@ -77,10 +77,10 @@ __device__ __forceinline__ void expm1_exp(float a, float& em1, float& ea) {
 }
 
 // sin b, cos b and 2 sin^2(b/2) = 1 - cos b.  Cody & Waite reduction
-// b = 2 pi k + r with a three-part float split of 2 pi applied by FMA
-// (|r| <= pi; each FMA rounds once, so r keeps an absolute error near
-// ulp(pi) and stays relatively exact when small while |k| < ~1e4, and
-// absolutely within ~1e-7 up to |b| ~ 1e6), then with h = r/2:
+// b = 2 pi k + r with a two-part float split of 2 pi applied by FMA
+// (|r| <= pi; each FMA rounds once; the dropped third part of 2 pi,
+// 6.9e-15, adds 6.9e-15 |k| to r, under 1e-7 of |r| unless |r| < 7e-8 |k|),
+// then with h = r/2:
 // s = sin h from its Taylor series to h^11 (truncation below 6e-8 on
 // |h| <= pi/2, relative near 0) and c = cos h from the hardware cosine
 // (absolute error about 2^-21 on [-pi, pi]); finally sin b = 2 s c,
@@ -89,9 +89,8 @@ __device__ __forceinline__ void expm1_exp(float a, float& em1, float& ea) {
 // Branch-free, so unrolled steps and chains interleave.
 __device__ __forceinline__ void trig_half(float b, float& sb, float& cb, float& vb) {
     const float k = rintf(b * 0.159154943f);  // 1/(2 pi)
-    float r = fmaf(-k, 6.28318548e+00f, b);    // 2 pi = hi + mid + lo
+    float r = fmaf(-k, 6.28318548e+00f, b);    // 2 pi = hi + mid
     r = fmaf(-k, -1.74845553e-07f, r);
-    r = fmaf(-k, -6.86049804e-15f, r);
     const float h = 0.5f * r;
     const float h2 = h * h;
     // sin h = h + h^3 (-1/3! + h^2 (1/5! + h^2 (-1/7! + h^2 (1/9! - h^2/11!))))
