@@ -152,11 +152,14 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
     using Shape = BflyShape<NV, LANES>;
     static_assert(kT % U == 0, "chunk must hold whole step groups");
     static_assert(kT % kSsmCk == 0 && kSsmCk % U == 0, "checkpoints fall on step-group starts");
-    __shared__ float2 sB[kT][NP];
-    __shared__ float2 sC[kT][NP];
-    __shared__ float su[kT][HT];
+    // chunk inputs, double-buffered: chunk c+1 is copied in (cp.async) while
+    // chunk c runs
+    constexpr int NBUF = NP <= 32 ? 2 : 1;  // N > 32: one buffer (48 KB of static shared memory)
+    __shared__ float2 sB[NBUF][kT][NP];
+    __shared__ float2 sC[NBUF][kT][NP];
+    __shared__ __align__(16) UT su[NBUF][kT][HT];
+    __shared__ float st[NBUF][kT];
     __shared__ float sy[kT][HT];
-    __shared__ float st[kT];
     __shared__ float2 sred[kT][NW];
 
     const int tid = threadIdx.x;
@@ -213,23 +216,57 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
     const int held = Shape::held_index(ln);
     const bool writer = (ln & Shape::kPlainMask) == 0;
 
-    for (int l0 = 0; l0 < lstop; l0 += kT) {
-        const int steps = min(kT, lstop - l0);
-        __syncthreads();
-        // padded chains (n >= N) read zeros: with lam = -1 and B = C = 0
-        // their state stays 0 and they add exact zeros, without a branch
-        for (int idx = tid; idx < steps * NP; idx += kThreads) {
+    // Stage chunk [c0, c0 + kT) into buffer `buf`.  Padded chains (n >= N)
+    // and channels past H read zeros: with lam = -1 and B = C = 0 their
+    // state stays 0 and they add exact zeros, without a branch.  The
+    // asynchronous form copies u in 4-byte units (pairs of 16-bit values),
+    // so it needs H even for half / bfloat16 u.
+    constexpr int PAIR = sizeof(UT) == 4 ? 1 : 2;
+    const bool async_ok = NBUF == 2 && (PAIR == 1 || (H % 2) == 0) && (reinterpret_cast<uintptr_t>(u) & 3u) == 0 &&
+                          ((reinterpret_cast<uintptr_t>(a.Bc) | reinterpret_cast<uintptr_t>(a.Cc)) & 7u) == 0 &&
+                          (reinterpret_cast<uintptr_t>(a.t) & 3u) == 0;
+    auto stage = [&](int c0, int buf, bool async) {
+        const int sn = min(kT, lstop - c0);
+        for (int idx = tid; idx < sn * NP; idx += kThreads) {
             const int i = idx / NP, n = idx % NP;  // NP, HT are powers of two
-            const size_t o = (rowLH + l0 + i) * N + n;
-            sB[i][n] = n < N ? a.Bc[o] : make_float2(0.f, 0.f);
-            sC[i][n] = n < N ? a.Cc[o] : make_float2(0.f, 0.f);
+            const size_t o = (rowLH + c0 + i) * N + n;
+            if (async) {
+                cp_async8(&sB[buf][i][n], n < N ? a.Bc + o : a.Bc, n < N);
+                cp_async8(&sC[buf][i][n], n < N ? a.Cc + o : a.Cc, n < N);
+            } else {
+                sB[buf][i][n] = n < N ? a.Bc[o] : make_float2(0.f, 0.f);
+                sC[buf][i][n] = n < N ? a.Cc[o] : make_float2(0.f, 0.f);
+            }
         }
-        for (int idx = tid; idx < steps * HT; idx += kThreads) {
-            const int i = idx / HT, k = idx % HT;
-            su[i][k] = (h0 + k < H) ? to_f32(u[(rowLH + l0 + i) * H + h0 + k]) : 0.f;
+        if (async) {
+            for (int idx = tid; idx < sn * (HT / PAIR); idx += kThreads) {
+                const int i = idx / (HT / PAIR), k = (idx % (HT / PAIR)) * PAIR;
+                const bool ok = h0 + k < H;  // a pair is both in or both past H (H, h0 even)
+                cp_async4(&su[buf][i][k], ok ? u + (rowLH + c0 + i) * H + h0 + k : u, ok);
+            }
+            for (int i = tid; i < sn; i += kThreads) cp_async4(&st[buf][i], a.t + rowLH + c0 + i, true);
+            cp_async_commit();
+        } else {
+            for (int idx = tid; idx < sn * HT; idx += kThreads) {
+                const int i = idx / HT, k = idx % HT;
+                su[buf][i][k] = (h0 + k < H) ? u[(rowLH + c0 + i) * H + h0 + k] : static_cast<UT>(0.f);
+            }
+            for (int i = tid; i < sn; i += kThreads) st[buf][i] = a.t[rowLH + c0 + i];
         }
-        for (int i = tid; i < steps; i += kThreads) st[i] = a.t[rowLH + l0 + i];
-        __syncthreads();
+    };
+    if (async_ok && lstop > 0) stage(0, 0, true);
+
+    for (int l0 = 0, chunk = 0; l0 < lstop; l0 += kT, ++chunk) {
+        const int steps = min(kT, lstop - l0);
+        const int buf = chunk & (NBUF - 1);
+        if (async_ok) cp_async_wait_all();  // this thread's copies of chunk `chunk`
+        __syncthreads();                    // everyone's, and the previous chunk is done
+        if (!async_ok) {
+            stage(l0, buf, false);
+            __syncthreads();
+        } else if (l0 + kT < lstop) {
+            stage(l0 + kT, (buf ^ 1) & (NBUF - 1), true);
+        }
 
         for (int i0 = 0; i0 < steps; i0 += U) {
             if (MODE == UNGATED && a.ck != nullptr && ((l0 + i0) % kSsmCk) == 0) {
@@ -247,8 +284,8 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                 // whose final state is kept; elsewhere they compute values that
                 // are never stored (each butterfly sum stays within its step).
                 const bool act = MODE == REPLAY ? i < steps : true;
-                const float tl = act ? st[i] : t_prev;
-                const float ul = act ? su[i][hl] : 0.f;
+                const float tl = act ? st[buf][i] : t_prev;
+                const float ul = act ? to_f32(su[buf][i][hl]) : 0.f;
                 float delta;
                 if (MODE == UNGATED)
                     delta = (l0 + i == 0) ? dt0 : fmaxf(tl - t_prev, 0.f);
@@ -263,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                     const int n = ln + LANES * j;
                     float2 dA, dB;
                     zoh(lam[j], ilam[j], dte, dA, dB);
-                    const float2 Bl = sB[i][n];
+                    const float2 Bl = sB[buf][i][n];
                     const float2 P = cmul(dA, hs[j]);
                     const float2 qc = cmul(dB, Bl);
                     const float2 hn = make_float2(fmaf(qc.x, ul, P.x), fmaf(qc.y, ul, P.y));
@@ -276,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                     if (MODE == SPEC_COMMITS && nv[j] && i < steps)
                         a.commit_h[((rowLH + l0 + i) * H + h) * N + n] = hn;
                     if (MODE != REPLAY) {
-                        const float2 Cl = sC[i][n];
+                        const float2 Cl = sC[buf][i][n];
                         yp += cre_mul(Cl, hs[j]);
                         if (kSpec) {
                             const float2 qp = cmul(dB, Bp[j]);
@@ -304,9 +341,9 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                 const int orig = held + k;
                 const int i = i0 + (orig % U);
                 if (orig < U) {  // output readout of step i
-                    if (writer && hv && i < steps) sy[i][hl] = vals[k] + Dh * su[i][hl];
+                    if (writer && hv && i < steps) sy[i][hl] = vals[k] + Dh * to_f32(su[buf][i][hl]);
                 } else if (kSpec && writer && hv && i < steps) {  // prediction of step i
-                    const float ul = su[i][hl];
+                    const float ul = to_f32(su[buf][i][hl]);
                     const float obs = (ul - mu) * rsd;
                     const float pred = (vals[k] - mu) * rsd;
                     const float d = obs - pred;
@@ -1216,8 +1253,9 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
     const bool carry = c.cin_h != nullptr || c.cout_h != nullptr;
     if (carry && !cell_resumable(c.H, c.N))
         return fail(EACS_ERR_UNSUPPORTED, "%s: resuming rows needs the cluster repair shape", fn);
-    if (c.cout_h != nullptr && (c.L % 4) != 0)
-        return fail(EACS_ERR_INVALID, "%s: a chunk with a carried-out state needs L %% 4 == 0", fn);
+    if (c.cout_h != nullptr && (c.L % EACS_CHAIN_U) != 0)
+        return fail(EACS_ERR_INVALID, "%s: a chunk with a carried-out state needs L %% %d == 0", fn,
+                    EACS_CHAIN_U);
     const WsLayout w = ws_layout(c.B, c.L, c.H, c.N);
     const size_t need = commits ? w.total_commits : w.total;
     if (!c.workspace || c.workspace_bytes < need)

@@ -283,6 +283,21 @@ __device__ __forceinline__ void st_async_f32(uint32_t raddr, float v, uint32_t r
                  : "memory");
 }
 
+// Asynchronous global -> shared copies of 4 or 8 bytes (cp.async); with
+// `valid` false nothing is read and the destination is zero-filled.
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+                 "r"(valid ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+                 "r"(valid ? 8 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // 3-D tiled TMA load global -> shared, completion counted on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_t* bar, int x, int y, int z) {
     asm volatile(
