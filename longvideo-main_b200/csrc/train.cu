@@ -89,13 +89,26 @@ __device__ __forceinline__ float group_sum(float v) {
 
 // ---------------------------------------------------------------------------
 // Gated forward with known gates, writing checkpoints.  Thread layout as the
-// chain kernel: (hl, ln) owns chains n = ln + LANES*j of channel h.
+// chain kernel: (hl, ln) owns chains n = ln + LANES*j of channel h.  Inputs
+// (gate, t, u, B, C) are staged in shared memory 32 steps at a time,
+// double-buffered: the next chunk is copied in with cp.async while the
+// current one runs.
 // ---------------------------------------------------------------------------
+constexpr int kCkT = 32;  // steps per staged chunk (a multiple of every checkpoint interval)
+
 template <int LANES, int NPT, typename UT>
 __global__ void __launch_bounds__(kCkThreads) train_ckpt(TArgs a) {
     constexpr int HT = kCkThreads / LANES;
+    constexpr int NP = LANES * NPT;
+    constexpr int NBUF = NP <= 32 ? 2 : 1;
+    constexpr int PAIR = sizeof(UT) == 4 ? 1 : 2;
+    __shared__ float2 sB[NBUF][kCkT][NP];
+    __shared__ float2 sC[NBUF][kCkT][NP];
+    __shared__ __align__(16) UT su[NBUF][kCkT][HT];
+    __shared__ float st[NBUF][kCkT];
+    __shared__ float sg[NBUF][kCkT];
     const int tid = threadIdx.x, ln = tid % LANES, hl = tid / LANES;
-    const int b = blockIdx.y, h = blockIdx.x * HT + hl;
+    const int b = blockIdx.y, h0 = blockIdx.x * HT, h = h0 + hl;
     const bool hv = h < a.H;
     const int L = a.L, H = a.H, N = a.N;
     const UT* u = static_cast<const UT*>(a.u);
@@ -116,47 +129,100 @@ __global__ void __launch_bounds__(kCkThreads) train_ckpt(TArgs a) {
     float u_pi = hv ? to_f32(u[rowL * H + h]) : 0.f;
     float t_pi = a.t[rowL] - a.dt_init;
     const bool row_writer = blockIdx.x == 0 && tid == 0;
-    for (int l = 0; l < L; ++l) {
-        if (l % a.K == 0) {
-            const int k = l / a.K;
+    const bool async_ok = NBUF == 2 && (PAIR == 1 || (H % 2) == 0) &&
+                          (reinterpret_cast<uintptr_t>(u) & 3u) == 0 &&
+                          ((reinterpret_cast<uintptr_t>(a.Bc) | reinterpret_cast<uintptr_t>(a.Cc)) & 7u) == 0 &&
+                          ((reinterpret_cast<uintptr_t>(a.t) | reinterpret_cast<uintptr_t>(a.gates)) & 3u) == 0;
+    auto stage = [&](int c0, int buf, bool async) {
+        const int sn = min(kCkT, L - c0);
+        for (int idx = tid; idx < sn * NP; idx += kCkThreads) {
+            const int i = idx / NP, n = idx % NP;
+            const size_t o = (rowL + c0 + i) * N + n;
+            if (async) {
+                cp_async8(&sB[buf][i][n], n < N ? a.Bc + o : a.Bc, n < N);
+                cp_async8(&sC[buf][i][n], n < N ? a.Cc + o : a.Cc, n < N);
+            } else {
+                sB[buf][i][n] = n < N ? a.Bc[o] : make_float2(0.f, 0.f);
+                sC[buf][i][n] = n < N ? a.Cc[o] : make_float2(0.f, 0.f);
+            }
+        }
+        if (async) {
+            for (int idx = tid; idx < sn * (HT / PAIR); idx += kCkThreads) {
+                const int i = idx / (HT / PAIR), k = (idx % (HT / PAIR)) * PAIR;
+                const bool ok = h0 + k < H;
+                cp_async4(&su[buf][i][k], ok ? u + (rowL + c0 + i) * H + h0 + k : u, ok);
+            }
+            for (int i = tid; i < sn; i += kCkThreads) {
+                cp_async4(&st[buf][i], a.t + rowL + c0 + i, true);
+                cp_async4(&sg[buf][i], a.gates + rowL + c0 + i, true);
+            }
+            cp_async_commit();
+        } else {
+            for (int idx = tid; idx < sn * HT; idx += kCkThreads) {
+                const int i = idx / HT, k = idx % HT;
+                su[buf][i][k] = (h0 + k < H) ? u[(rowL + c0 + i) * H + h0 + k] : static_cast<UT>(0.f);
+            }
+            for (int i = tid; i < sn; i += kCkThreads) {
+                st[buf][i] = a.t[rowL + c0 + i];
+                sg[buf][i] = a.gates[rowL + c0 + i];
+            }
+        }
+    };
+    if (async_ok) stage(0, 0, true);
+    for (int l0 = 0, chunk = 0; l0 < L; l0 += kCkT, ++chunk) {
+        const int steps = min(kCkT, L - l0);
+        const int buf = chunk & (NBUF - 1);
+        if (async_ok) cp_async_wait_all();
+        __syncthreads();
+        if (!async_ok) {
+            stage(l0, buf, false);
+            __syncthreads();
+        } else if (l0 + kCkT < L) {
+            stage(l0 + kCkT, (buf ^ 1) & (NBUF - 1), true);
+        }
+        for (int i = 0; i < steps; ++i) {
+            const int l = l0 + i;
+            if (l % a.K == 0) {
+                const int k = l / a.K;
 #pragma unroll
-            for (int j = 0; j < NPT; ++j)
-                if (nv[j]) a.ck_h[((static_cast<size_t>(b) * a.nK + k) * H + h) * N + ln + LANES * j] = hs[j];
-            if (hv && ln == 0) a.ck_u[(static_cast<size_t>(b) * a.nK + k) * H + h] = u_pi;
-            if (row_writer) a.ck_row[static_cast<size_t>(b) * a.nK + k] = make_float4(t_pi, 0.f, 0.f, 0.f);
-            if (blockIdx.x == 0 && hl == 0) {
+                for (int j = 0; j < NPT; ++j)
+                    if (nv[j]) a.ck_h[((static_cast<size_t>(b) * a.nK + k) * H + h) * N + ln + LANES * j] = hs[j];
+                if (hv && ln == 0) a.ck_u[(static_cast<size_t>(b) * a.nK + k) * H + h] = u_pi;
+                if (row_writer) a.ck_row[static_cast<size_t>(b) * a.nK + k] = make_float4(t_pi, 0.f, 0.f, 0.f);
+                if (blockIdx.x == 0 && hl == 0) {
 #pragma unroll
-                for (int j = 0; j < NPT; ++j) {
-                    const int n = ln + LANES * j;
-                    if (n < N) {
-                        const size_t o = ((static_cast<size_t>(b) * a.nK + k) * 2) * N + n;
-                        a.ck_bc[o] = Bp[j];
-                        a.ck_bc[o + N] = Cp[j];
+                    for (int j = 0; j < NPT; ++j) {
+                        const int n = ln + LANES * j;
+                        if (n < N) {
+                            const size_t o = ((static_cast<size_t>(b) * a.nK + k) * 2) * N + n;
+                            a.ck_bc[o] = Bp[j];
+                            a.ck_bc[o + N] = Cp[j];
+                        }
                     }
                 }
             }
-        }
-        const float g = a.gates[rowL + l];
-        const float tl = a.t[rowL + l];
-        const float ul = hv ? to_f32(u[(rowL + l) * H + h]) : 0.f;
-        const float dte = eff_dt(fmaxf(tl - t_pi, 0.f), scale, a.dt_min, a.dt_max);
+            const float g = sg[buf][i];
+            const float tl = st[buf][i];
+            const float ul = to_f32(su[buf][i][hl]);
+            const float dte = eff_dt(fmaxf(tl - t_pi, 0.f), scale, a.dt_min, a.dt_max);
 #pragma unroll
-        for (int j = 0; j < NPT; ++j) {
-            const int n = ln + LANES * j;
-            const float2 Bl = nv[j] ? a.Bc[(rowL + l) * N + n] : make_float2(0.f, 0.f);
-            const float2 Cl = nv[j] ? a.Cc[(rowL + l) * N + n] : make_float2(0.f, 0.f);
-            float2 dA, dB;
-            zoh(lam[j], ilam[j], dte, dA, dB);
-            const float2 hf = cmul(dA, hs[j]);
-            const float2 ql = cmul(dB, Bl);
-            const float2 hu = make_float2(fmaf(ql.x, ul, hf.x), fmaf(ql.y, ul, hf.y));
-            const float2 gu = cscale(hu, g);
-            hs[j] = cadd(gu, cscale(hs[j], 1.f - g));
-            Bp[j] = cadd(cscale(Bl, g), cscale(Bp[j], 1.f - g));
-            Cp[j] = cadd(cscale(Cl, g), cscale(Cp[j], 1.f - g));
+            for (int j = 0; j < NPT; ++j) {
+                const int n = ln + LANES * j;
+                const float2 Bl = sB[buf][i][n];
+                const float2 Cl = sC[buf][i][n];
+                float2 dA, dB;
+                zoh(lam[j], ilam[j], dte, dA, dB);
+                const float2 hf = cmul(dA, hs[j]);
+                const float2 ql = cmul(dB, Bl);
+                const float2 hu = make_float2(fmaf(ql.x, ul, hf.x), fmaf(ql.y, ul, hf.y));
+                const float2 gu = cscale(hu, g);
+                hs[j] = cadd(gu, cscale(hs[j], 1.f - g));
+                Bp[j] = cadd(cscale(Bl, g), cscale(Bp[j], 1.f - g));
+                Cp[j] = cadd(cscale(Cl, g), cscale(Cp[j], 1.f - g));
+            }
+            u_pi = g * ul + (1.f - g) * u_pi;
+            t_pi = g * tl + (1.f - g) * t_pi;
         }
-        u_pi = g * ul + (1.f - g) * u_pi;
-        t_pi = g * tl + (1.f - g) * t_pi;
     }
 }
 
