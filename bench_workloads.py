@@ -275,9 +275,10 @@ def wl_ssm_train(args, dev, flush):
 
 
 def wl_train(args, dev, flush):
-    """Config 3: GatedEACSCellFunction forward + backward, B=8 L=8192 H=768 N=16, bf16 u."""
+    """Config 3: GatedEACSCellFunction forward + backward, B=8 L=8192 H=768 N=16, bf16 u
+    (--shape B,L,H,N gives a small case for ncu)."""
     from eacs_b200.ops.eacs_cell_train import fused_gated_scan
-    B, L, H, N = 8, 8192, 768, 16
+    B, L, H, N = (8, 8192, 768, 16) if getattr(args, "shape", None) is None else (int(v) for v in args.shape.split(","))
     g = torch.Generator().manual_seed(9)
     d = cell_inputs(g, B, L, H, N, (0.5, 4.0), dev, torch.bfloat16)
     gy = torch.randn(B, L, H, generator=g).to(dev)

@@ -26,6 +26,7 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "eacs_common.cuh"
 #include "eacs_host.h"
@@ -35,7 +36,10 @@ namespace cg = cooperative_groups;
 namespace eacs {
 namespace {
 
-constexpr int kKMax = 16;       // steps per checkpoint / recompute chunk (at most)
+#ifndef EACS_TRAIN_KMAX
+#define EACS_TRAIN_KMAX 16
+#endif
+constexpr int kKMax = EACS_TRAIN_KMAX;  // steps per checkpoint / recompute chunk (at most)
 constexpr int kCkThreads = 128; // checkpoint kernel CTA
 
 struct TArgs {
@@ -246,9 +250,9 @@ __global__ void __launch_bounds__(512) train_bwd(TArgs a) {
     const int HC = a.HC;
     const int kK = a.K;
     // shared layout (see smem_bytes)
-    float2* sh = reinterpret_cast<float2*>(smem);                 // [kK][T][NPT] h_pi
-    float2* sdA = sh + kK * T * NPT;                              // [kK][T][NPT] dA
-    float2* sdB = sdA + kK * T * NPT;                             // [kK][T][NPT] dB_bar
+    float2* sh = reinterpret_cast<float2*>(smem);                 // [kK][NPT][T] h_pi
+    float2* sdA = sh + kK * T * NPT;                              // [kK][NPT][T] dA
+    float2* sdB = sdA + kK * T * NPT;                             // [kK][NPT][T] dB_bar
     float2* sBpi = sdB + kK * T * NPT;                            // [kK][NP]
     float2* sCpi = sBpi + kK * NP;
     float2* sBl = sCpi + kK * NP;
@@ -367,8 +371,12 @@ __global__ void __launch_bounds__(512) train_bwd(TArgs a) {
         float u_pi = hv ? a.ck_u[(static_cast<size_t>(b) * a.nK + k) * H + h] : 0.f;
         float t_pi = a.ck_row[static_cast<size_t>(b) * a.nK + k].x;
         __syncthreads();
-        for (int i = 0; i < steps; ++i) {
-            const float g = sgt[i], tl = stl[i];
+        // one step; with G1 the gate is a hard 1 and the (1 - g) terms, which
+        // are exactly zero then, are left out
+        auto forward_step = [&](auto gm, const int i) {
+            constexpr bool G1 = decltype(gm)::value;
+            const float g = G1 ? 1.f : sgt[i];
+            const float tl = stl[i];
             const float ul = hv ? sul[i * HC + hl] : 0.f;
             if (hv && ln == 0) supi[i * HC + hl] = u_pi;
             if (tid == 0) stpi[i] = t_pi;
@@ -376,7 +384,7 @@ __global__ void __launch_bounds__(512) train_bwd(TArgs a) {
 #pragma unroll
             for (int j = 0; j < NPT; ++j) {
                 const int n = ln + LANES * j;
-                const size_t so = (static_cast<size_t>(i) * T + tid) * NPT + j;
+                const size_t so = (static_cast<size_t>(i) * NPT + j) * T + tid;
                 sh[so] = hs[j];
                 const float2 Bl = sBl[i * NP + n];
                 float2 dA, dB;
@@ -386,7 +394,7 @@ __global__ void __launch_bounds__(512) train_bwd(TArgs a) {
                 const float2 hf = cmul(dA, hs[j]);
                 const float2 ql = cmul(dB, Bl);
                 const float2 hu = make_float2(fmaf(ql.x, ul, hf.x), fmaf(ql.y, ul, hf.y));
-                hs[j] = cadd(cscale(hu, g), cscale(hs[j], 1.f - g));
+                hs[j] = G1 ? hu : cadd(cscale(hu, g), cscale(hs[j], 1.f - g));
             }
             if (row_owner) {  // warp 0 only: row-level B_pi, C_pi before each step
 #pragma unroll
@@ -395,19 +403,25 @@ __global__ void __launch_bounds__(512) train_bwd(TArgs a) {
                     sBpi[i * NP + n] = Bp[j];
                     sCpi[i * NP + n] = Cp[j];
                     const float2 Bl = sBl[i * NP + n], Cl = sCl[i * NP + n];
-                    Bp[j] = cadd(cscale(Bl, g), cscale(Bp[j], 1.f - g));
-                    Cp[j] = cadd(cscale(Cl, g), cscale(Cp[j], 1.f - g));
+                    Bp[j] = G1 ? Bl : cadd(cscale(Bl, g), cscale(Bp[j], 1.f - g));
+                    Cp[j] = G1 ? Cl : cadd(cscale(Cl, g), cscale(Cp[j], 1.f - g));
                 }
             }
-            u_pi = g * ul + (1.f - g) * u_pi;
-            t_pi = g * tl + (1.f - g) * t_pi;
+            u_pi = G1 ? ul : g * ul + (1.f - g) * u_pi;
+            t_pi = G1 ? tl : g * tl + (1.f - g) * t_pi;
+        };
+        for (int i = 0; i < steps; ++i) {
+            if (sgt[i] == 1.f) forward_step(std::true_type{}, i);
+            else forward_step(std::false_type{}, i);
         }
         __syncthreads();
 
         // ---- reverse over the chunk ----
-        for (int i = steps - 1; i >= 0; --i) {
+        auto reverse_step = [&](auto gm, const int i) {
+            constexpr bool G1 = decltype(gm)::value;
             const int l = l0 + i;
-            const float g = sgt[i], tl = stl[i], tpi = stpi[i];
+            const float g = G1 ? 1.f : sgt[i];
+            const float tl = stl[i], tpi = stpi[i];
             const float ul = hv ? sul[i * HC + hl] : 0.f;
             const float upi = hv ? supi[i * HC + hl] : 0.f;
             const float yb = hv ? sgy[i * HC + hl] : 0.f;
@@ -422,7 +436,7 @@ __global__ void __launch_bounds__(512) train_bwd(TArgs a) {
 #pragma unroll
             for (int j = 0; j < NPT; ++j) {
                 const int n = ln + LANES * j;
-                const size_t so = (static_cast<size_t>(i) * T + tid) * NPT + j;
+                const size_t so = (static_cast<size_t>(i) * NPT + j) * T + tid;
                 hp[j] = sh[so];
                 dA[j] = sdA[so];
                 dB[j] = sdB[so];
@@ -476,17 +490,22 @@ __global__ void __launch_bounds__(512) train_bwd(TArgs a) {
             const float pbar = -dbar - numtbar * dv * rw.z;
             const float yhbar = pbar * rsd;
             float s_u_pi = 0.f, s_u_l = 0.f, s_dte = 0.f;
+            float part[4 * NPT];  // (dBc.re, dBc.im, dCc.re, dCc.im) x chain, summed over channels below
 #pragma unroll
             for (int j = 0; j < NPT; ++j) {
                 const int n = ln + LANES * j;
                 const float2 Cl = sCl[i * NP + n], Bl = sBl[i * NP + n];
                 const float2 Bpi = sBpi[i * NP + n], Cpi = sCpi[i * NP + n];
                 const float2 ahc = make_float2(yb * Cl.x, -yb * Cl.y);
-                const float2 hc = cadd(cscale(hu[j], g), cscale(xh[j], 1.f - g));
                 // x_hat and h_upd adjoints
-                const float2 axh = make_float2((1.f - g) * ahc.x + yhbar * Cpi.x,
-                                               (1.f - g) * ahc.y - yhbar * Cpi.y);
-                const float2 ahu = make_float2(g * (ahc.x + ah[j].x), g * (ahc.y + ah[j].y));
+                float2 axh, ahu;
+                if constexpr (G1) {
+                    axh = make_float2(yhbar * Cpi.x, -yhbar * Cpi.y);
+                    ahu = cadd(ahc, ah[j]);
+                } else {
+                    axh = make_float2((1.f - g) * ahc.x + yhbar * Cpi.x, (1.f - g) * ahc.y - yhbar * Cpi.y);
+                    ahu = make_float2(g * (ahc.x + ah[j].x), g * (ahc.y + ah[j].y));
+                }
                 const float2 ahf = cadd(axh, ahu);
                 s_u_pi += axh.x * qp[j].x + axh.y * qp[j].y;
                 s_u_l += ahu.x * ql[j].x + ahu.y * ql[j].y;
@@ -494,37 +513,48 @@ __global__ void __launch_bounds__(512) train_bwd(TArgs a) {
                 const float2 adB = cadd(cmul(aqp, make_float2(Bpi.x, -Bpi.y)),
                                         cmul(aql, make_float2(Bl.x, -Bl.y)));
                 const float2 cdB = make_float2(dB[j].x, -dB[j].y);
-                const float2 outB = cadd(cscale(vB[j], g), cmul(cdB, aql));
-                vB[j] = cadd(cscale(vB[j], 1.f - g), cmul(cdB, aqp));
-                const float2 outC = cadd(cscale(vC[j], g), make_float2(yb * hc.x, -yb * hc.y));
-                vC[j] = cadd(cscale(vC[j], 1.f - g), make_float2(yhbar * xh[j].x, -yhbar * xh[j].y));
+                float2 outB, outC;
+                if constexpr (G1) {
+                    outB = cadd(vB[j], cmul(cdB, aql));
+                    vB[j] = cmul(cdB, aqp);
+                    outC = cadd(vC[j], make_float2(yb * hu[j].x, -yb * hu[j].y));
+                } else {
+                    const float2 hc = cadd(cscale(hu[j], g), cscale(xh[j], 1.f - g));
+                    outB = cadd(cscale(vB[j], g), cmul(cdB, aql));
+                    vB[j] = cadd(cscale(vB[j], 1.f - g), cmul(cdB, aqp));
+                    outC = cadd(cscale(vC[j], g), make_float2(yb * hc.x, -yb * hc.y));
+                }
+                const float2 vCn = make_float2(yhbar * xh[j].x, -yhbar * xh[j].y);
+                vC[j] = G1 ? vCn : cadd(cscale(vC[j], 1.f - g), vCn);
                 // state adjoint for the previous step
                 const float2 cdA = make_float2(dA[j].x, -dA[j].y);
                 const float2 adA = cmul(make_float2(hp[j].x, -hp[j].y), ahf);
-                ah[j] = cadd(cscale(ah[j], 1.f - g), cmul(cdA, ahf));
-                // dB_bar = E * ilam with E = expm1(z) = dB_bar * lam
-                const float2 E = cmul(dB[j], lam[j]);
+                ah[j] = G1 ? cmul(cdA, ahf) : cadd(cscale(ah[j], 1.f - g), cmul(cdA, ahf));
+                // dB_bar = expm1(z) / lam: the adjoint of expm1(z) is adB conj(1/lam)
+                // and lam's share through 1/lam is -adB conj(dB_bar / lam)
                 const float2 aE = cmul(adB, make_float2(ilam[j].x, -ilam[j].y));
-                const float2 ail = cmul(adB, make_float2(E.x, -E.y));
-                const float2 il2 = cmul(ilam[j], ilam[j]);
-                float2 alm = cmul(make_float2(-il2.x, il2.y), ail);  // -conj(ilam^2) ail
+                const float2 P = cmul(ilam[j], dB[j]);
+                float2 alm = cmul(make_float2(-adB.x, -adB.y), make_float2(P.x, -P.y));
                 const float2 az = cmul(cdA, cadd(adA, aE));
                 alm = cadd(alm, cscale(az, dte));
                 s_dte += az.x * lam[j].x + az.y * lam[j].y;
                 if (nv[j]) glam[j] = cadd(glam[j], alm);
-                // per-(step, n) partials over this warp's channel groups
-                float2 ob = nv[j] ? outB : make_float2(0.f, 0.f);
-                float2 oc = nv[j] ? outC : make_float2(0.f, 0.f);
+                part[j] = nv[j] ? outB.x : 0.f;
+                part[NPT + j] = nv[j] ? outB.y : 0.f;
+                part[2 * NPT + j] = nv[j] ? outC.x : 0.f;
+                part[3 * NPT + j] = nv[j] ? outC.y : 0.f;
+            }
+            // per-(step, n) partials over this warp's channel groups: a
+            // transposed butterfly leaves each lane kRem of the 4*NPT sums
+            using FS = FoldShape<4 * NPT, 16, LANES>;
+            Fold<4 * NPT, 16, LANES>::run(part, lane);
+            if (FS::writer(lane)) {
+                const int q0 = FS::held(lane);
 #pragma unroll
-                for (int o = LANES; o < 32; o <<= 1) {
-                    ob.x += __shfl_xor_sync(0xffffffffu, ob.x, o);
-                    ob.y += __shfl_xor_sync(0xffffffffu, ob.y, o);
-                    oc.x += __shfl_xor_sync(0xffffffffu, oc.x, o);
-                    oc.y += __shfl_xor_sync(0xffffffffu, oc.y, o);
-                }
-                if (lane < LANES) {
-                    soB[(i * NW + wid) * NP + n] = ob;
-                    soC[(i * NW + wid) * NP + n] = oc;
+                for (int r = 0; r < FS::kRem; ++r) {
+                    const int q = q0 + r, c = q / NPT, n = ln + LANES * (q % NPT);
+                    float* dst = reinterpret_cast<float*>(c < 2 ? soB : soC);
+                    dst[((i * NW + wid) * NP + n) * 2 + (c & 1)] = part[r];
                 }
             }
             s_u_pi = group_sum<LANES>(s_u_pi);
@@ -532,19 +562,23 @@ __global__ void __launch_bounds__(512) train_bwd(TArgs a) {
             s_dte = group_sum<LANES>(s_dte);
             float out_t = 0.f;
             if (hv) {
-                const float dub = yb * Dh + obar * rsd + g * vu + s_u_l;
-                vu = (1.f - g) * vu + s_u_pi;
+                const float dub = yb * Dh + obar * rsd + (G1 ? vu : g * vu) + s_u_l;
+                vu = G1 ? s_u_pi : (1.f - g) * vu + s_u_pi;
                 const float drb = mdt * s_dte;
                 const float dlt = drb * scale;  // this channel's share of delta_bar
                 glog += drb * delta * scale;
                 gD += yb * ul;
-                out_t = g * vt + mdel * dlt;
-                vt = (1.f - g) * vt - mdel * dlt;
+                out_t = (G1 ? vt : g * vt) + mdel * dlt;
+                vt = G1 ? -mdel * dlt : (1.f - g) * vt - mdel * dlt;
                 if (ln == 0) a.du[(rowL + l) * H + h] = dub;
             }
             float ot = (ln == 0) ? out_t : 0.f;
             ot = warp_sum(ot);
             if (lane == 0) sot[i * NW + wid] = ot;
+        };
+        for (int i = steps - 1; i >= 0; --i) {
+            if (sgt[i] == 1.f) reverse_step(std::true_type{}, i);
+            else reverse_step(std::false_type{}, i);
         }
         // ---- chunk end: per-CTA partials of dBc, dCc, dt ----
         __syncthreads();
