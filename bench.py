@@ -75,10 +75,13 @@ def parse():
                     "half the frames of the N(0,1) features and exercises the repair path)")
     ap.add_argument("--shape", default=None,
                     help="B,L,H,N override for --workload ssm_train or train (e.g. a small case for ncu)")
-    ap.add_argument("--workload", choices=["cell", "scan", "ssm", "ssm_train", "train", "multiscale"],
+    ap.add_argument("--workload", choices=["cell", "scan", "ssm", "ssm_train", "train", "multiscale",
+                                           "longvideo"],
                     default="cell", help="cell (default) is the headline; the others are the "
-                    "materialised scan, the fused ungated SSM, the training step and the "
-                    "three-branch multiscale cell")
+                    "materialised scan, the fused ungated SSM, the training step, the "
+                    "three-branch multiscale cell and the long-video cell (B=64, H=2048, N=32)")
+    ap.add_argument("--L", type=int, default=None, choices=[16384, 32768, 65536],
+                    help="frames per video for --workload longvideo (default 16384)")
     return ap.parse_args()
 
 

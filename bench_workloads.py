@@ -1,5 +1,6 @@
-"""Secondary bench.py workloads (one GPU): the materialised scan, the fused
-ungated SSM, the training step and the three-branch multiscale cell.
+"""Secondary bench.py workloads: the materialised scan, the fused ungated
+SSM, the training step and the three-branch multiscale cell (one GPU), and
+the long-video gated cell (one or more GPUs, videos split over the ranks).
 
 Each prints one JSON line like bench.py's headline (state updates/s, the
 dominant kernel's HBM roofline) and, where the reference's own CUDA kernels
@@ -377,7 +378,125 @@ def wl_multiscale(args, dev, flush):
          note="input projections (LayerNorm, proj_u/B/C) are outside the timed step")
 
 
+def longvideo_inputs(rows, L, dev, seed, H=2048, N=32):
+    """Config 4 inputs for `rows` videos, drawn on the device from one seeded
+    generator: fp16 u ~ N(0,1); B, C complex with N(0,1)/sqrt(N) parts;
+    t = cumsum(dt), dt ~ Exp(mean 0.5 s) clipped to [1/30, 2] s; lambda with
+    tau log-uniform on [0.5, 64] s and Im = pi*n; D ~ N(0,1)."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    s = 1.0 / math.sqrt(N)
+
+    def cplx(*shape):
+        return torch.complex(torch.randn(*shape, device=dev, generator=g) * s,
+                             torch.randn(*shape, device=dev, generator=g) * s)
+
+    log_tau = torch.empty(H, N, device=dev).uniform_(math.log(0.5), math.log(64.0), generator=g)
+    im = (math.pi * torch.arange(N, dtype=torch.float32, device=dev)).expand(H, N)
+    dt = torch.empty(rows, L, device=dev).exponential_(1.0 / 0.5, generator=g).clamp_(1 / 30, 2.0)
+    return dict(lam=torch.complex(-torch.exp(-log_tau), im.contiguous()),
+                log_dt=torch.zeros(H, device=dev),
+                u=torch.randn(rows, L, H, device=dev, dtype=torch.float16, generator=g),
+                Bc=cplx(rows, L, N), Cc=cplx(rows, L, N), t=torch.cumsum(dt, 1),
+                D=torch.randn(H, device=dev, generator=g), mean=torch.zeros(H, device=dev),
+                var=torch.ones(H, device=dev))
+
+
+def wl_longvideo(args):
+    """Config 4: long-video gated cell, B=64 videos, H=2048, N=32, fp16 u,
+    eps=0.12, L from --L (16384, 32768 or 65536).  The 64 videos are split
+    over the ranks (strong scaling, no collective on the data path); time is
+    device-measured, max over ranks."""
+    import datetime
+    import torch.distributed as dist
+    from bench import ClockSampler, max_over_ranks
+    from eacs_b200 import _lib
+    from eacs_b200.ops.eacs_gated_scan import cell_forward_into, workspace_bytes
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    Bt, H, N = 64, 2048, 32
+    L = args.L or 16384
+    if Bt % world:
+        raise SystemExit(f"longvideo: {Bt} videos do not split over {world} ranks")
+    rows = Bt // world
+    d = longvideo_inputs(rows, L, dev, 4000 + rank, H, N)
+    eps = 0.12 if args.eps is None else float(args.eps)
+    y = torch.empty(rows, L, H, device=dev)
+    gate = torch.empty(rows, L, device=dev)
+    resid = torch.empty(rows, L, device=dev)
+    ws = torch.empty(workspace_bytes(rows, L, H, N), dtype=torch.uint8, device=dev)
+
+    def op():
+        cell_forward_into(d["lam"], d["log_dt"], d["u"], d["Bc"], d["Cc"], d["t"], d["D"], d["mean"],
+                          d["var"], eps, 1e-6, 1e-5, 1.0, 1e-3, 1e3, None, "hard", 0.1, y, gate, resid, ws)
+
+    steps = max(1, min(args.steps, 10))
+    warmup = max(3, min(args.warmup, 5))
+    sampler = ClockSampler(local)
+    sampler.start()
+    for _ in range(warmup):
+        op()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    rate = float(gate.mean())
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in ev + kev:
+        a.record()
+        b.record()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.load = True
+    launches0 = _lib.kernel_launches()
+    for k in range(steps):
+        ev[k][0].record()
+        _lib.set_kernel_events(*kev[k])
+        op()
+        _lib.set_kernel_events(None, None)
+        ev[k][1].record()
+    torch.cuda.synchronize()
+    sampler.load = False
+    launches = _lib.kernel_launches() - launches0
+    sampler.stop()
+    total_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev), dev, world)
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    assert _lib.device_status() == 0
+    upd_rank = rows * L * H * N
+    upd_job = Bt * L * H * N
+    # algorithmic bytes of one launch: u fp16, Bc, Cc, t in; y fp32, gate, resid out
+    alg = rows * L * (H * 2 + 2 * N * 8 + 4 + H * 4 + 8)
+    peak, src = peak_hbm()
+    achieved = alg / (kern_ms / 1e3) / 1e9
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "EACS gated cell long-video Gstate-updates/s", "value": upd_job / (total_ms / 1e3 / steps) / 1e9,
+            "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": total_ms / steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded on the device)",
+            "config": {"workload": "long-video gated cell (event gate + ZOH predict/update), videos split "
+                       "over ranks", "B": Bt, "L": L, "H": H, "N": N, "u_dtype": "fp16", "eps": eps,
+                       "update_rate": rate, "videos_per_rank": rows,
+                       "l2": "inputs larger than L2 (no flush needed)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_source": src,
+                         "kernel": "cell_chain<SPEC> (rank 0)", "kernel_ms": kern_ms,
+                         "alg_bytes_per_launch": alg,
+                         "kernel_gupdates_per_s": upd_rank / (kern_ms / 1e3) / 1e9},
+            "gpu_launches": launches, "clocks": sampler.summary()}), flush=True)
+    return 0
+
+
 def run_workload(args):
+    if args.workload == "longvideo":
+        return wl_longvideo(args)
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
