@@ -552,12 +552,17 @@ __global__ void __launch_bounds__(kRepair) cell_repair(Args a) {
     float2* hpi = a.hpi + static_cast<size_t>(b) * H * N;
     float* upi = a.upi + static_cast<size_t>(b) * H;
 
+    // every step before l* committed: the predecessor is step l* - 1, or at
+    // l* = 0 the carried state of a resumed row (else step 0's inputs)
+    const bool resumed = a.cin_row != nullptr;
+    const bool from_carry = lstar == 0 && resumed;
     for (int n = tid; n < N; n += kRepair) {
-        sBpi[n] = a.Bc[(rowLH + lp) * N + n];
-        sCpi[n] = a.Cc[(rowLH + lp) * N + n];
+        sBpi[n] = from_carry ? a.cin_B[static_cast<size_t>(b) * N + n] : a.Bc[(rowLH + lp) * N + n];
+        sCpi[n] = from_carry ? a.cin_C[static_cast<size_t>(b) * N + n] : a.Cc[(rowLH + lp) * N + n];
     }
-    for (int hh = tid; hh < H; hh += kRepair) upi[hh] = to_f32(u[(rowLH + lp) * H + hh]);
-    float t_pi = lstar > 0 ? a.t[rowLH + lp] : a.t[rowLH] - a.dt_init;
+    for (int hh = tid; hh < H; hh += kRepair)
+        upi[hh] = from_carry ? a.cin_u[static_cast<size_t>(b) * H + hh] : to_f32(u[(rowLH + lp) * H + hh]);
+    float t_pi = lstar > 0 ? a.t[rowLH + lp] : (resumed ? a.cin_row[b].x : a.t[rowLH] - a.dt_init);
     float spike = __int_as_float(rowv.y);
     float prev_r = __int_as_float(rowv.z);
     __syncthreads();
@@ -621,10 +626,8 @@ __global__ void __launch_bounds__(kRepair) cell_repair(Args a) {
                 if (a.robust && spike >= static_cast<float>(a.robust_k)) eps_l = a.eps_lo;
                 g = r > eps_l ? 1.f : 0.f;
             }
-            if (a.robust) {
-                if (l > 0) spike = (r > prev_r * a.spike_ratio) ? spike + 1.f : 0.f;
-                prev_r = r;
-            }
+            if (a.robust && (l > 0 || resumed)) spike = (r > prev_r * a.spike_ratio) ? spike + 1.f : 0.f;
+            prev_r = r;
             a.gate[rowLH + l] = g;
             a.resid[rowLH + l] = r;
             sg = g;
@@ -701,6 +704,15 @@ __global__ void __launch_bounds__(kRepair) cell_repair(Args a) {
             t_pi = tl;
         }
         __syncthreads();
+    }
+    if (a.cout_h != nullptr) {  // the row's state after its last step
+        for (int i = tid; i < H * N; i += kRepair) a.cout_h[static_cast<size_t>(b) * H * N + i] = hpi[i];
+        for (int hh = tid; hh < H; hh += kRepair) a.cout_u[static_cast<size_t>(b) * H + hh] = upi[hh];
+        for (int n = tid; n < N; n += kRepair) {
+            a.cout_B[static_cast<size_t>(b) * N + n] = sBpi[n];
+            a.cout_C[static_cast<size_t>(b) * N + n] = sCpi[n];
+        }
+        if (tid == 0) a.cout_row[b] = make_float4(t_pi, spike, prev_r, 0.f);
     }
 }
 
@@ -1223,8 +1235,8 @@ size_t cell_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
 }
 
 bool cell_resumable(int64_t H, int64_t N) {
-    return H > 0 && N > 0 && N <= 64 && H <= (1LL << 24) &&
-           rc_shape(static_cast<int>(H), static_cast<int>(N)).cl > 0;
+    // both repair passes (cluster and one-CTA) take and return a carried state
+    return H > 0 && N > 0 && N <= 64 && H <= (1LL << 24);
 }
 
 size_t cell_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
@@ -1252,7 +1264,8 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
         return fail(EACS_ERR_INVALID, "%s: commits are recorded for the hard gate only", fn);
     const bool carry = c.cin_h != nullptr || c.cout_h != nullptr;
     if (carry && !cell_resumable(c.H, c.N))
-        return fail(EACS_ERR_UNSUPPORTED, "%s: resuming rows needs the cluster repair shape", fn);
+        return fail(EACS_ERR_UNSUPPORTED, "%s: H=%lld N=%lld rows cannot be resumed", fn, (long long)c.H,
+                    (long long)c.N);
     if (c.cout_h != nullptr && (c.L % EACS_CHAIN_U) != 0)
         return fail(EACS_ERR_INVALID, "%s: a chunk with a carried-out state needs L %% %d == 0", fn,
                     EACS_CHAIN_U);

@@ -81,17 +81,24 @@ def test_host_pipeline_with_skips(rate, robust, u_dtype):
     assert 0.0 < host[1].mean() < 1.0
 
 
-def test_host_pipeline_pageable_and_unsupported():
+def test_host_pipeline_pageable():
     d = cell_inputs(2, 70, 32, 8, seed=9)
     host = _run_host(d, 0.12, 32, pinned=False)
     dev = _run_dev(d, 0.12)
     for a, b in zip(host, dev):
         assert np.array_equal(a, b)
-    # a row that needs more than 16 CTAs of 512 threads cannot be resumed
-    z = torch.zeros(1, 4, 2048)
-    with pytest.raises(RuntimeError, match="resumable"):
-        eacs_cell_forward_host(torch.zeros(2048, 32, dtype=torch.complex64, device=DEV),
-                               torch.zeros(2048, device=DEV), z,
-                               torch.zeros(1, 4, 32, dtype=torch.complex64),
-                               torch.zeros(1, 4, 32, dtype=torch.complex64), torch.zeros(1, 4),
-                               *(torch.zeros(2048, device=DEV) for _ in range(3)), 0.1, 1e-6)
+
+
+def test_host_pipeline_wide_rows_with_skips():
+    """H=2048, N=32 rows (too wide for the cluster repair pass): the one-CTA
+    repair pass resumes them from the carried state at every chunk."""
+    from test_gpu_kernels import _calibrated_eps
+    d = cell_inputs(2, 64, 2048, 32, seed=21, tau=(0.5, 64.0))
+    eps = _calibrated_eps(d, 0.5)
+    host = _run_host(d, eps, 16)
+    ref = oracle.cell_fwd(**d, eps=eps, eta=1e-6)
+    dev = _run_dev(d, eps)
+    assert np.array_equal(host[1], ref[1]) and np.array_equal(dev[1], ref[1])
+    assert relerr(host[0], ref[0]) < 1e-4 and relerr(host[2], ref[2]) < 1e-4
+    assert relerr(host[0], dev[0]) < 1e-5 and relerr(host[2], dev[2]) < 1e-5
+    assert 0.0 < host[1].mean() < 1.0
