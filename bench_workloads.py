@@ -420,6 +420,8 @@ def wl_longvideo(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     Bt, H, N = 64, 2048, 32
     L = args.L or 16384
+    if getattr(args, "shape", None):  # a small case of the same kernel (for ncu)
+        Bt, L, H, N = (int(v) for v in args.shape.split(","))
     if Bt % world:
         raise SystemExit(f"longvideo: {Bt} videos do not split over {world} ranks")
     rows = Bt // world
