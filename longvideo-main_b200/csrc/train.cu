@@ -469,7 +469,8 @@ __global__ void __launch_bounds__(512) train_bwd(TArgs a) {
                 const int par = nred & 1;
                 const uint32_t phase = (nred >> 1) & 1;
                 if (tid == 0) mbar_expect_tx(&rbar[par], static_cast<uint32_t>(nslot) * 4u);
-                if (lane < CL) st_async_f32(rslot[par], gl, rbarr[par]);
+                if (lane < CL)  // addresses by select: a dynamic index would use local memory
+                    st_async_f32(par ? rslot[1] : rslot[0], gl, par ? rbarr[1] : rbarr[0]);
                 if (!mbar_wait_row(&rbar[par], phase)) failed = true;
                 const float* sl = slots + par * 16 * 32;
                 float tot = 0.f;
