@@ -319,7 +319,7 @@ def wl_multiscale(args, dev, flush):
     """Config 2: three gated branches (tau bands [0.5,4], [4,32], [32,256] s), each with its
     proj_out, and MultiScaleEACS's epilogue (fusion softmax, blend, LayerNorm) in one kernel."""
     from eacs_b200.ops.eacs_gated_scan import cell_forward_into, workspace_bytes
-    from eacs_b200.ops.multiscale import branch_fuse
+    from eacs_b200.ops.multiscale import branch_fuse, run_branches
     B, L, H, N = 4, 16384, 1024, 16
     g = torch.Generator().manual_seed(10)
     bands = [(0.5, 4.0), (4.0, 32.0), (32.0, 256.0)]
@@ -333,14 +333,16 @@ def wl_multiscale(args, dev, flush):
     ys = [torch.empty(B, L, H, device=dev) for _ in bands]
     gts = [torch.empty(B, L, device=dev) for _ in bands]
     rss = [torch.empty(B, L, device=dev) for _ in bands]
-    ws = torch.empty(workspace_bytes(B, L, H, N), dtype=torch.uint8, device=dev)
+    wss = [torch.empty(workspace_bytes(B, L, H, N), dtype=torch.uint8, device=dev) for _ in bands]
     dt_max = [max(1e3, 10 * tb[1]) for tb in bands]
 
-    def cells():
-        for i, d in enumerate(br):
-            cell_forward_into(d["lam"], d["log_dt"], d["u"], d["Bc"], d["Cc"], d["t"], d["D"],
-                              d["mean"], d["var"], 0.12, 1e-6, 1e-5, 1.0, 1e-3, dt_max[i], None, "hard",
-                              0.1, ys[i], gts[i], rss[i], ws)
+    def cell(i, d):
+        cell_forward_into(d["lam"], d["log_dt"], d["u"], d["Bc"], d["Cc"], d["t"], d["D"],
+                          d["mean"], d["var"], 0.12, 1e-6, 1e-5, 1.0, 1e-3, dt_max[i], None, "hard",
+                          0.1, ys[i], gts[i], rss[i], wss[i])
+
+    def cells():  # side by side on the branch streams, as multiscale_forward runs them
+        run_branches(br, dev, cell)
 
     @torch.no_grad()
     def deltas():
@@ -354,9 +356,11 @@ def wl_multiscale(args, dev, flush):
             return norm(x + fused)
 
     @torch.no_grad()
-    def step():
-        cells()
-        return branch_fuse(x, deltas(), fusion, norm)
+    def step():  # each branch's cell and proj_out on its stream (an EACSLayer forward each), then the epilogue
+        def branch(i, d):
+            cell(i, d)
+            return proj_out[i](ys[i].to(torch.bfloat16))
+        return branch_fuse(x, run_branches(br, dev, branch), fusion, norm)
 
     n = max(3, args.steps // 5)
     st, _ = timed(step, n, 2, flush, False)

@@ -5,7 +5,8 @@ w = softmax(fusion(x)) and y = out_norm(x + sum_s w_s delta_s) in one kernel
 (eacs_branch_fuse) instead of a GEMM, softmax, stack, einsum, add and
 LayerNorm over (B, L, d) tensors.  `multiscale_forward` is
 MultiScaleEACS.forward with that epilogue (the branches run as the reference
-calls them; with install() their cells are the B200 kernels).  Inference
+calls them, side by side on their own streams; with install() their cells are
+the B200 kernels).  Inference
 path; install(..., multiscale=True) keeps the reference's forward where
 gradients are needed.
 """
@@ -55,11 +56,46 @@ def branch_fuse(x: Tensor, deltas, fusion, out_norm):
     return y, w
 
 
+_STREAMS: dict = {}
+
+
+def branch_streams(dev: torch.device, n: int):
+    """n side streams of `dev`, created once and reused."""
+    key = (dev.index, n)
+    if key not in _STREAMS:
+        _STREAMS[key] = [torch.cuda.Stream(dev) for _ in range(n)]
+    return _STREAMS[key]
+
+
+def run_branches(branches, dev: torch.device, fn):
+    """fn(i, branch) for every branch, each on its own stream, joined back to
+    the current stream.  One branch's gated cell (B rows x H/16 channel tiles)
+    fills a fraction of the SMs; side by side the branches share them.
+    Tensors the calls return are marked as used by the current stream."""
+    cur = torch.cuda.current_stream(dev)
+    outs = []
+    for i, (br, s) in enumerate(zip(branches, branch_streams(dev, len(branches)))):
+        s.wait_stream(cur)
+        with torch.cuda.stream(s):
+            outs.append(fn(i, br))
+    for s in branch_streams(dev, len(branches)):
+        cur.wait_stream(s)
+    for o in outs:
+        for v in (vars(o).values() if hasattr(o, "__dict__") else o if isinstance(o, (tuple, list)) else (o,)):
+            if isinstance(v, Tensor) and v.is_cuda:
+                v.record_stream(cur)
+    return outs
+
+
 @torch.no_grad()
 def multiscale_forward(temporal, x: Tensor, timestamps: Tensor, frame_mask=None, cpi=None):
-    """MultiScaleEACS.forward (multiscale.py:162-193) with the fused epilogue."""
+    """MultiScaleEACS.forward (multiscale.py:162-193) with the fused epilogue;
+    the branches run side by side on their own streams."""
     if temporal._merge_ok(x):
         outs = temporal._merged_branches(x, timestamps, cpi, frame_mask)
+    elif x.is_cuda:
+        outs = run_branches(list(temporal.branches), x.device,
+                            lambda i, br: br(x, timestamps, cpi=cpi, frame_mask=frame_mask))
     else:
         outs = [br(x, timestamps, cpi=cpi, frame_mask=frame_mask) for br in temporal.branches]
     y, w = branch_fuse(x, [o.y for o in outs], temporal.fusion, temporal.out_norm)
