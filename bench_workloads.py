@@ -1,6 +1,7 @@
 """Secondary bench.py workloads: the materialised scan, the fused ungated
-SSM, the training step and the three-branch multiscale cell (one GPU), and
-the long-video gated cell (one or more GPUs, videos split over the ranks).
+SSM and the three-branch multiscale cell (one GPU), the training step (one
+or more GPUs, gradients all-reduced) and the long-video gated cell (one or
+more GPUs, videos split over the ranks).
 
 Each prints one JSON line like bench.py's headline (state updates/s, the
 dominant kernel's HBM roofline) and, where the reference's own CUDA kernels
@@ -275,12 +276,26 @@ def wl_ssm_train(args, dev, flush):
          gpu_launches=launches, **extra)
 
 
-def wl_train(args, dev, flush):
+def wl_train(args):
     """Config 3: GatedEACSCellFunction forward + backward, B=8 L=8192 H=768 N=16, bf16 u
-    (--shape B,L,H,N gives a small case for ncu)."""
-    from eacs_b200.ops.eacs_cell_train import fused_gated_scan
+    (--shape B,L,H,N gives a small case for ncu).  Under torchrun every rank
+    trains its own B videos (weak scaling) and the cell's parameter gradients
+    (lambda, log_dt, D, eps) are summed over the ranks with one NCCL
+    all-reduce per step, as DDP does; time is device-measured, max over ranks."""
+    import datetime
+    import torch.distributed as dist
+    from bench import max_over_ranks
+    from eacs_b200.ops.eacs_cell_train import _train_bwd, _train_fwd, fused_gated_scan
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     B, L, H, N = (8, 8192, 768, 16) if getattr(args, "shape", None) is None else (int(v) for v in args.shape.split(","))
-    g = torch.Generator().manual_seed(9)
+    g = torch.Generator().manual_seed(9 + rank)
     d = cell_inputs(g, B, L, H, N, (0.5, 4.0), dev, torch.bfloat16)
     gy = torch.randn(B, L, H, generator=g).to(dev)
     leaves = {k: d[k].clone().requires_grad_(True) for k in ("u", "Bc", "Cc", "lam", "log_dt", "D")}
@@ -290,29 +305,59 @@ def wl_train(args, dev, flush):
         y, gs, rs = fused_gated_scan(leaves["u"], leaves["Bc"], leaves["Cc"], d["t"], leaves["lam"],
                                      leaves["log_dt"], leaves["D"], eps, d["mean"], d["var"], 0.1, 1e-6)
         torch.autograd.backward([y], [gy])
+        if world > 1:  # DDP: one bucket with the cell parameters' gradients, summed over the ranks
+            grads = [torch.view_as_real(leaves["lam"].grad).reshape(-1), leaves["log_dt"].grad.reshape(-1),
+                     leaves["D"].grad.reshape(-1), eps.grad.reshape(-1)]
+            flat = torch.cat(grads)
+            dist.all_reduce(flat)
+            o = 0
+            for t in grads:
+                t.copy_(flat[o:o + t.numel()])
+                o += t.numel()
 
-    nsteps = max(3, args.steps // 10)
-    st, _ = timed(step, nsteps, 2, flush, False)
+    nsteps, warmup = max(3, args.steps // 10), 3
+    for _ in range(warmup):
+        step()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(nsteps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for k in range(nsteps):
+        flush.zero_()
+        ev[k][0].record()
+        step()
+        ev[k][1].record()
+    torch.cuda.synchronize()
+    st = [a.elapsed_time(b) for a, b in ev]
+    total_ms = max_over_ranks(sum(st), dev, world)
     # the backward kernel on its own (autograd runs it on its own thread, where
     # the library's per-thread timing events are not set)
-    from eacs_b200.ops.eacs_cell_train import _train_bwd, _train_fwd
     det = {k: v.detach() for k, v in leaves.items()}
     _, gs_, rs_, stats_, prep = _train_fwd(det["u"], det["Bc"], det["Cc"], d["t"], det["lam"],
                                            det["log_dt"], det["D"], 0.12, d["mean"], d["var"], 0.1,
                                            1e-6, 1e-5, 1.0, "ste", 1e3)
     _, kt = timed(lambda: _train_bwd(prep, gs_, rs_, stats_, 0.12, 0.1, 1e-6, 1e-5, 1.0, 1e3, gy,
-                                     None, None, None), nsteps, 2, flush, True)
+                                     None, None, None), nsteps, warmup, flush, True)
     upd = B * L * H * N
-    rate = float(fused_gated_scan(leaves["u"], leaves["Bc"], leaves["Cc"], d["t"], leaves["lam"],
-                                  leaves["log_dt"], leaves["D"], eps, d["mean"], d["var"], 0.1,
-                                  1e-6)[1].mean())
-    line("EACS gated cell training fwd+bwd Gstate-updates/s", upd / (statistics.median(st) / 1e3) / 1e9,
-         len(st), 2, statistics.median(st),
-         {"workload": "GatedEACSCellFunction fwd+bwd (STE, T=0.1)", "B": B, "L": L, "H": H, "N": N,
-          "u_dtype": "bf16", "update_rate": rate, "l2": "flushed between steps"},
-         backward_kernel_ms=statistics.median(kt),
-         backward_kernel_Gstate_updates_per_s=upd / (statistics.median(kt) / 1e3) / 1e9,
-         note="backward_kernel_ms is the cluster backward kernel (train_bwd) alone")
+    with torch.no_grad():
+        rate = float(gs_.mean())
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "EACS gated cell training fwd+bwd Gstate-updates/s",
+            "value": world * nsteps * upd / (total_ms / 1e3) / 1e9, "unit": UNIT, "n_gpus": world,
+            "steps": nsteps, "warmup": warmup, "ms_per_step": total_ms / nsteps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "GatedEACSCellFunction fwd+bwd (STE, T=0.1)"
+                                   + ("; DDP all-reduce of the cell parameters' gradients" if world > 1 else ""),
+                       "B_per_rank": B, "L": L, "H": H, "N": N, "u_dtype": "bf16", "update_rate": rate,
+                       "l2": "flushed between steps"},
+            "backward_kernel_ms": statistics.median(kt),
+            "backward_kernel_Gstate_updates_per_s": upd / (statistics.median(kt) / 1e3) / 1e9,
+            "note": "backward_kernel_ms is the cluster backward kernel (train_bwd) alone, rank 0"}), flush=True)
+    return 0
 
 
 def wl_multiscale(args, dev, flush):
@@ -478,6 +523,11 @@ def wl_longvideo(args):
     alg = rows * L * (H * 2 + 2 * N * 8 + 4 + H * 4 + 8)
     peak, src = peak_hbm()
     achieved = alg / (kern_ms / 1e3) / 1e9
+    # issue slots per update of cell_chain<SPEC> at H=2048, N=32 (ncu smsp__inst_executed.sum x 32
+    # / updates on the 8 x 4096 case: 5,394,518,016 x 32 / 2,147,483,648); the kernel is issue-bound
+    instr = 80.4 if (H, N) == (2048, 32) else None
+    n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
+    issue_peak = n_sm * 4 * 32 * (sampler.summary().get("sm_mhz") or 1965.0) * 1e6
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -495,7 +545,13 @@ def wl_longvideo(args):
                          "frac": achieved / peak, "traffic": None, "peak_source": src,
                          "kernel": "cell_chain<SPEC> (rank 0)", "kernel_ms": kern_ms,
                          "alg_bytes_per_launch": alg,
-                         "kernel_gupdates_per_s": upd_rank / (kern_ms / 1e3) / 1e9},
+                         "kernel_gupdates_per_s": upd_rank / (kern_ms / 1e3) / 1e9,
+                         "issue": None if instr is None else {
+                             "achieved_Tinstr_s": upd_rank / (kern_ms / 1e3) * instr / 1e12,
+                             "peak_Tinstr_s": issue_peak / 1e12,
+                             "frac": upd_rank / (kern_ms / 1e3) * instr / issue_peak,
+                             "instr_per_update": instr,
+                             "peak_basis": f"{n_sm} SMs x 128 lanes x median SM clock"}},
             "gpu_launches": launches, "clocks": sampler.summary()}), flush=True)
     return 0
 
@@ -503,10 +559,14 @@ def wl_longvideo(args):
 def run_workload(args):
     if args.workload == "longvideo":
         return wl_longvideo(args)
+    if args.workload == "train":
+        return wl_train(args)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit(f"--workload {args.workload} runs on one GPU")
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    {"scan": wl_scan, "ssm": wl_ssm, "ssm_train": wl_ssm_train, "train": wl_train,
+    {"scan": wl_scan, "ssm": wl_ssm, "ssm_train": wl_ssm_train,
      "multiscale": wl_multiscale}[args.workload](
         args, dev, flush)
     from eacs_b200 import _lib
