@@ -735,10 +735,22 @@ __device__ __forceinline__ void rc_cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+constexpr int kRcT = 32;  // steps per staged input chunk of the cluster repair pass
+
+// Dynamic shared memory of cell_repair_cluster: two input buffers of kRcT
+// steps, each B_l and C_l (NP complex), t_l and the CTA's HC channels of u_l.
+template <typename UT>
+__host__ __device__ constexpr size_t rc_buf_bytes(int NP, int HC) {
+    return ((static_cast<size_t>(kRcT) * NP * 2 * sizeof(float2) + kRcT * sizeof(float) +
+             static_cast<size_t>(kRcT) * ((HC + 1) & ~1) * sizeof(UT)) + 15) & ~static_cast<size_t>(15);
+}
+
 template <int LANES, int NPT, typename UT>
 __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int CL, int HC) {
+    constexpr int NP = LANES * NPT;
     __shared__ uint64_t rbar[2];
     __shared__ float2 slots[2][kRcMaxCL * (kRcMaxThreads / 32)];
+    extern __shared__ __align__(16) unsigned char rc_smem[];
     const int b = blockIdx.y;
     const int crank = blockIdx.x;  // the cluster spans the CL CTAs of a row
     const int L = a.L, H = a.H, N = a.N;
@@ -806,34 +818,72 @@ __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int
     }
     bool failed = false;
 
-    // next step's inputs, loaded one step ahead
-    float t_nx = a.t[rowLH + lstar];
-    float u_nx = hv ? to_f32(u[(rowLH + lstar) * H + h]) : 0.f;
-    float2 B_nx[NPT], C_nx[NPT];
+    // Inputs of kRcT steps at a time in shared memory, the next chunk copied
+    // in with cp.async while this one runs (zero-filled past N and H).
+    const int HC2 = (HC + 1) & ~1;
+    const size_t buf_bytes = rc_buf_bytes<UT>(NP, HC);
+    auto sBl = [&](int buf, int i) { return reinterpret_cast<float2*>(rc_smem + buf * buf_bytes) + i * NP; };
+    auto sCl = [&](int buf, int i) { return reinterpret_cast<float2*>(rc_smem + buf * buf_bytes) + (kRcT + i) * NP; };
+    auto stl = [&](int buf) { return reinterpret_cast<float*>(rc_smem + buf * buf_bytes + 2 * kRcT * NP * sizeof(float2)); };
+    auto sul = [&](int buf, int i) {
+        return reinterpret_cast<UT*>(rc_smem + buf * buf_bytes + 2 * kRcT * NP * sizeof(float2) + kRcT * sizeof(float)) +
+               i * HC2;
+    };
+    const int h0 = crank * HC;
+    constexpr bool kPair = sizeof(UT) == 2;
+    // 4-byte copies: u in pairs of channels when it is 2 bytes wide
+    const bool async_ok = (reinterpret_cast<uintptr_t>(u) & 3u) == 0 && (!kPair || ((H | h0) & 1) == 0) &&
+                          ((reinterpret_cast<uintptr_t>(a.Bc) | reinterpret_cast<uintptr_t>(a.Cc)) & 7u) == 0 &&
+                          (reinterpret_cast<uintptr_t>(a.t) & 3u) == 0;
+    auto stage = [&](int c0, int buf) {
+        const int sn = min(kRcT, L - c0);
+        for (int idx = tid; idx < sn * NP; idx += blockDim.x) {
+            const int i = idx / NP, n = idx % NP;
+            const size_t o = (rowLH + c0 + i) * N + n;
+            if (async_ok) {
+                cp_async8(sBl(buf, i) + n, n < N ? a.Bc + o : a.Bc, n < N);
+                cp_async8(sCl(buf, i) + n, n < N ? a.Cc + o : a.Cc, n < N);
+            } else {
+                sBl(buf, i)[n] = n < N ? a.Bc[o] : make_float2(0.f, 0.f);
+                sCl(buf, i)[n] = n < N ? a.Cc[o] : make_float2(0.f, 0.f);
+            }
+        }
+        constexpr int P = kPair ? 2 : 1;
+        for (int idx = tid; idx < sn * (HC2 / P); idx += blockDim.x) {
+            const int i = idx / (HC2 / P), c = (idx % (HC2 / P)) * P;
+            const bool ok = h0 + c < H && c < HC;
+            const UT* src = u + (rowLH + c0 + i) * H + h0 + c;
+            if (async_ok) {
+                cp_async4(sul(buf, i) + c, ok ? src : u, ok);
+            } else {
 #pragma unroll
-    for (int j = 0; j < NPT; ++j) {
-        const int n = ln + LANES * j;
-        B_nx[j] = nv[j] ? a.Bc[(rowLH + lstar) * N + n] : make_float2(0.f, 0.f);
-        C_nx[j] = nv[j] ? a.Cc[(rowLH + lstar) * N + n] : make_float2(0.f, 0.f);
-    }
+                for (int e = 0; e < P; ++e)
+                    sul(buf, i)[c + e] = (h0 + c + e < H && c + e < HC) ? src[e] : static_cast<UT>(0.f);
+            }
+        }
+        for (int i = tid; i < sn; i += blockDim.x) {
+            if (async_ok) cp_async4(stl(buf) + i, a.t + rowLH + c0 + i, true);
+            else stl(buf)[i] = a.t[rowLH + c0 + i];
+        }
+        if (async_ok) cp_async_commit();
+    };
+    stage(lstar, 0);
 
-    for (int l = lstar; l < L; ++l) {
-        const float tl = t_nx, ul = u_nx;
+    for (int c0 = lstar, chunk = 0; c0 < L; c0 += kRcT, ++chunk) {
+    const int buf = chunk & 1;
+    const int csteps = min(kRcT, L - c0);
+    if (async_ok) cp_async_wait_all();
+    __syncthreads();  // chunk c0 staged; every thread is done with the other buffer
+    if (c0 + kRcT < L) stage(c0 + kRcT, buf ^ 1);
+    for (int i = 0; i < csteps; ++i) {
+        const int l = c0 + i;
+        const float tl = stl(buf)[i];
+        const float ul = hv ? to_f32(sul(buf, i)[hl]) : 0.f;
         float2 Bl[NPT], Cl[NPT];
 #pragma unroll
         for (int j = 0; j < NPT; ++j) {
-            Bl[j] = B_nx[j];
-            Cl[j] = C_nx[j];
-        }
-        if (l + 1 < L) {
-            t_nx = a.t[rowLH + l + 1];
-            u_nx = hv ? to_f32(u[(rowLH + l + 1) * H + h]) : 0.f;
-#pragma unroll
-            for (int j = 0; j < NPT; ++j) {
-                const int n = ln + LANES * j;
-                B_nx[j] = nv[j] ? a.Bc[(rowLH + l + 1) * N + n] : make_float2(0.f, 0.f);
-                C_nx[j] = nv[j] ? a.Cc[(rowLH + l + 1) * N + n] : make_float2(0.f, 0.f);
-            }
+            Bl[j] = sBl(buf, i)[ln + LANES * j];
+            Cl[j] = sCl(buf, i)[ln + LANES * j];
         }
         const float dte = eff_dt(fmaxf(tl - t_pi, 0.f), scale, a.dt_min, a.dt_max);
         float2 P[NPT], dB[NPT], xh[NPT];
@@ -942,6 +992,7 @@ __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int
             t_pi = tl;
         }
     }
+    }
     if (a.cout_h != nullptr) {  // the row's state after its last step
 #pragma unroll
         for (int j = 0; j < NPT; ++j) {
@@ -994,10 +1045,13 @@ cudaError_t launch_repair_cluster(const Args& a, const RcShape& rs, cudaStream_t
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
     }
+    const size_t smem = 2 * rc_buf_bytes<UT>(LANES * NPT, rs.hc);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(rs.cl, a.B);
     cfg.blockDim = dim3(rs.threads);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
