@@ -915,8 +915,10 @@ __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int
         if (!failed) {
             if (tid == 0) mbar_expect_tx(&rbar[par], static_cast<uint32_t>(nslot) * 8u);
             if (lane < CL) {
-                st_async_f32(rslot[par], d2, rbarr[par]);
-                st_async_f32(rslot[par] + 4u, o2, rbarr[par]);
+                // addresses by select: a dynamic index would keep the arrays in local memory
+                const uint32_t rs = par ? rslot[1] : rslot[0], rb = par ? rbarr[1] : rbarr[0];
+                st_async_f32(rs, d2, rb);
+                st_async_f32(rs + 4u, o2, rb);
             }
             if (!mbar_wait_row(&rbar[par], phase)) failed = true;
         }
