@@ -6,7 +6,7 @@ more GPUs, videos split over the ranks).
 Each prints one JSON line like bench.py's headline (state updates/s, the
 dominant kernel's HBM roofline) and, where the reference's own CUDA kernels
 were built into oracle/_ref (oracle/build_ref.py), times them on the same
-tensors for comparison.  Inputs are seeded synthetic data with the BASELINE
+tensors for comparison.  Inputs are seeded synthetic data with the reference
 config shapes; L2 is flushed between timed steps.
 """
 from __future__ import annotations
@@ -103,7 +103,7 @@ def line(metric, value, steps, warmup, ms, config, **extra):
 
 # ----------------------------------------------------------------------------
 def wl_scan(args, dev, flush):
-    """scan_fwd / scan_bwd on one branch of config 2 at L=4096 (24 / 40 B per update)."""
+    """scan_fwd / scan_bwd on one multiscale branch (B=4 H=1024 N=16) at L=4096 (24 / 40 B per update)."""
     from eacs_b200.ops.scan_cuda import EXT
     B, L, H, N = 4, 4096, 1024, 16
     g = torch.Generator().manual_seed(7)
@@ -143,7 +143,7 @@ def wl_scan(args, dev, flush):
 
 
 def wl_ssm(args, dev, flush):
-    """Fused ungated continuous SSM forward, one branch of config 2 (bf16 u)."""
+    """Fused ungated continuous SSM forward, one multiscale branch (B=4 L=16384 H=1024 N=16, bf16 u)."""
     from eacs_b200.ops.continuous_ssm import ssm_forward
     B, L, H, N = 4, 16384, 1024, 16
     g = torch.Generator().manual_seed(8)
@@ -200,8 +200,8 @@ def ref_ssm_core(lam, log_dt, t, Bc, Cc, u, D, ext):
 
 
 def wl_ssm_train(args, dev, flush):
-    """Fused ungated SSM core, forward + backward (SSMCoreFunction), one branch of
-    config 2 (B=4 L=16384 H=1024 N=16, bf16 u); beside it, at B=1 L=4096 (where
+    """Fused ungated SSM core, forward + backward (SSMCoreFunction), at
+    the multiscale branch shape (B=4 L=16384 H=1024 N=16, bf16 u); beside it, at B=1 L=4096 (where
     its materialised (B,L,H,N) tensors fit), the reference's autograd path over
     its own scan kernels and ours on the same tensors."""
     from eacs_b200 import _lib
@@ -277,7 +277,7 @@ def wl_ssm_train(args, dev, flush):
 
 
 def wl_train(args):
-    """Config 3: GatedEACSCellFunction forward + backward, B=8 L=8192 H=768 N=16, bf16 u
+    """Gated-cell training: GatedEACSCellFunction forward + backward, B=8 L=8192 H=768 N=16, bf16 u
     (--shape B,L,H,N gives a small case for ncu).  Under torchrun every rank
     trains its own B videos (weak scaling) and the cell's parameter gradients
     (lambda, log_dt, D, eps) are summed over the ranks with one NCCL
@@ -361,7 +361,7 @@ def wl_train(args):
 
 
 def wl_multiscale(args, dev, flush):
-    """Config 2: three gated branches (tau bands [0.5,4], [4,32], [32,256] s), each with its
+    """MultiScaleEACS, B=4 L=16384 H=1024 N=16: three gated branches (tau bands [0.5,4], [4,32], [32,256] s), each with its
     proj_out, and MultiScaleEACS's epilogue (fusion softmax, blend, LayerNorm) in one kernel."""
     from eacs_b200.ops.eacs_gated_scan import cell_forward_into, workspace_bytes
     from eacs_b200.ops.multiscale import branch_fuse, run_branches
@@ -428,7 +428,7 @@ def wl_multiscale(args, dev, flush):
 
 
 def longvideo_inputs(rows, L, dev, seed, H=2048, N=32):
-    """Config 4 inputs for `rows` videos, drawn on the device from one seeded
+    """Long-video inputs (H=2048, N=32) for `rows` videos, drawn on the device from one seeded
     generator: fp16 u ~ N(0,1); B, C complex with N(0,1)/sqrt(N) parts;
     t = cumsum(dt), dt ~ Exp(mean 0.5 s) clipped to [1/30, 2] s; lambda with
     tau log-uniform on [0.5, 64] s and Im = pi*n; D ~ N(0,1)."""
@@ -451,7 +451,7 @@ def longvideo_inputs(rows, L, dev, seed, H=2048, N=32):
 
 
 def wl_longvideo(args):
-    """Config 4: long-video gated cell, B=64 videos, H=2048, N=32, fp16 u,
+    """Long-video gated cell: B=64 videos, H=2048, N=32, fp16 u,
     eps=0.12, L from --L (16384, 32768 or 65536).  The 64 videos are split
     over the ranks (strong scaling, no collective on the data path); time is
     device-measured, max over ranks."""

@@ -87,7 +87,7 @@ def ssm_cases(gen):
     from cst_ssm.ops.spectral_init import BranchSpec, init_branch_lambda
     out = {}
     cases = {
-        # config 0: B=2, L=256, D=64 channels, N=16, tau log-uniform [0.5, 64] s.
+        # the CPU scan case: B=2, L=256, D=64 channels, N=16, tau log-uniform [0.5, 64] s.
         "ssm_c0": (2, 256, 64, 16, 0.5, 64.0, False),
         "ssm_odd": (3, 9, 7, 5, 0.1, 4.0, True),
         "ssm_l1": (2, 1, 4, 4, 0.5, 4.0, False),

@@ -1,7 +1,7 @@
 """Training path (GatedEACSCellFunction) against the reference's autograd
 (golden vectors) and the double-precision oracle backward.
 
-Tolerances (north_star): forward values 1e-4 relative, gradients 1e-3
+Tolerances: forward values 1e-4 relative, gradients 1e-3
 relative (max |x - ref| / max |ref| per gradient tensor).
 """
 import numpy as np
