@@ -181,7 +181,8 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
     const UT* u = static_cast<const UT*>(a.u);
     const size_t rowLH = static_cast<size_t>(b) * L;
 
-    float2 lam[NPT], ilam[NPT], hs[NPT], Bp[NPT], Cp[NPT];
+    // Wp: B_pi u_pi / lam, the input term of the prediction (gated passes)
+    float2 lam[NPT], ilam[NPT], hs[NPT], Bp[NPT], Cp[NPT], Wp[NPT];
     bool nv[NPT];
 #pragma unroll
     for (int j = 0; j < NPT; ++j) {
@@ -190,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
         lam[j] = nv[j] ? a.lam[static_cast<size_t>(h) * N + n] : make_float2(-1.f, 0.f);
         ilam[j] = crecip(lam[j]);
         hs[j] = make_float2(0.f, 0.f);
+        Wp[j] = make_float2(0.f, 0.f);
         Bp[j] = nv[j] ? a.Bc[rowLH * N + n] : make_float2(0.f, 0.f);
         Cp[j] = nv[j] ? a.Cc[rowLH * N + n] : make_float2(0.f, 0.f);
         if (MODE != UNGATED && a.cin_h != nullptr && nv[j]) {  // resumed row
@@ -210,6 +212,10 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
     if (MODE != UNGATED && a.cin_h != nullptr) {
         if (hv) u_prev = a.cin_u[static_cast<size_t>(b) * H + h];
         t_prev = a.cin_row[b].x;
+    }
+    if (kSpec) {
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) Wp[j] = cscale(cmul(Bp[j], ilam[j]), u_prev);
     }
     float dt0 = 0.f;  // ungated: dt_0 = dt_1 (continuous_ssm.py:45-48)
     if (MODE == UNGATED && L > 1) dt0 = fmaxf(a.t[rowLH + 1] - t0, 0.f);
@@ -298,12 +304,28 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
 #pragma unroll
                 for (int j = 0; j < NPT; ++j) {
                     const int n = ln + LANES * j;
-                    float2 dA, dB;
-                    zoh(lam[j], ilam[j], dte, dA, dB);
                     const float2 Bl = sB[buf][i][n];
-                    const float2 P = cmul(dA, hs[j]);
-                    const float2 qc = cmul(dB, Bl);
-                    const float2 hn = make_float2(fmaf(qc.x, ul, P.x), fmaf(qc.y, ul, P.y));
+                    float2 dA, P, hn, W;
+                    if (MODE == UNGATED) {
+                        float2 dB;
+                        zoh(lam[j], ilam[j], dte, dA, dB);
+                        P = cmul(dA, hs[j]);
+                        const float2 qc = cmul(dB, Bl);
+                        hn = make_float2(fmaf(qc.x, ul, P.x), fmaf(qc.y, ul, P.y));
+                    } else {
+                        // dB_bar B u = expm1(z) W with W = B u / lam; step l's W is also
+                        // the input term of step l+1's prediction (carried in Wp)
+                        float2 E;
+                        zoh_e(lam[j], dte, dA, E);
+                        P = cmul(dA, hs[j]);
+                        W = cscale(cmul(Bl, ilam[j]), ul);
+                        hn = cfma(E, W, P);
+                        if (kSpec) {
+                            const float2 xh = cfma(E, Wp[j], P);
+                            yhp += cre_mul(Cp[j], xh);
+                            Wp[j] = W;
+                        }
+                    }
                     if (MODE == REPLAY)
                         hs[j] = act ? hn : hs[j];
                     else
@@ -315,13 +337,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                     if (MODE != REPLAY) {
                         const float2 Cl = sC[buf][i][n];
                         yp += cre_mul(Cl, hs[j]);
-                        if (kSpec) {
-                            const float2 qp = cmul(dB, Bp[j]);
-                            const float2 xh = make_float2(fmaf(qp.x, u_prev, P.x), fmaf(qp.y, u_prev, P.y));
-                            yhp += cre_mul(Cp[j], xh);
-                            Bp[j] = Bl;
-                            Cp[j] = Cl;
-                        }
+                        if (kSpec) Cp[j] = Cl;
                     }
                 }
                 vals[uu] = yp;
@@ -402,8 +418,8 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
         for (int j = 0; j < NPT; ++j) {
             const int n = ln + LANES * j;
             if (nv[j]) a.cout_h[(static_cast<size_t>(b) * H + h) * N + n] = hs[j];
-            if (tile == 0 && hl == 0 && n < N) {
-                a.cout_B[static_cast<size_t>(b) * N + n] = Bp[j];
+            if (tile == 0 && hl == 0 && n < N) {  // B_pi, C_pi: the last step's
+                a.cout_B[static_cast<size_t>(b) * N + n] = a.Bc[(rowLH + L - 1) * N + n];
                 a.cout_C[static_cast<size_t>(b) * N + n] = Cp[j];
             }
         }

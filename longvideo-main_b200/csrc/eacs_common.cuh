@@ -61,14 +61,14 @@ __device__ __forceinline__ float ex2_approx(float x) {
 
 // e^a and e^a - 1.  e^a from the hardware base-2 exponential (about 2^-22
 // relative).  e^a - 1 from it when |a| >= 0.35, where the subtraction loses at
-// most a factor 2.3 of that, and below from the Taylor series of expm1 to a^8
-// (truncation below 3e-10 relative), which keeps small |a| -- the slow modes,
-// where dB_bar ~ dt -- relatively exact.
+// most a factor 2.4 of that (a = Re(lam) dt <= 0: 6e-7 relative at a = -0.35),
+// and below from the Taylor series of expm1 to a^6 (alternating for a < 0, so
+// the error is under the first dropped term, |a|^7/7! / |expm1(a)| < 4.3e-7
+// at a = -0.35 and shrinking fast below), which keeps small |a| -- the slow
+// modes, where dB_bar ~ dt -- relatively exact.
 __device__ __forceinline__ void expm1_exp(float a, float& em1, float& ea) {
     ea = ex2_approx(a * 1.44269504f);  // log2(e)
-    float p = fmaf(a, 2.48015873e-05f, 1.98412698e-04f);  // 1/8!, 1/7!
-    p = fmaf(a, p, 1.38888889e-03f);                      // 1/6!
-    p = fmaf(a, p, 8.33333333e-03f);                      // 1/5!
+    float p = fmaf(a, 1.38888889e-03f, 8.33333333e-03f);  // 1/6!, 1/5!
     p = fmaf(a, p, 4.16666667e-02f);                      // 1/4!
     p = fmaf(a, p, 1.66666667e-01f);                      // 1/3!
     p = fmaf(a, p, 0.5f);                                 // 1/2!
@@ -110,7 +110,9 @@ __device__ __forceinline__ void trig_half(float b, float& sb, float& cb, float& 
 //   z = lam * dt,  dA = e^z,  dB_bar = expm1(z) / lam
 // with expm1(z) = (expm1(a) cos b - 2 sin^2(b/2), e^a sin b), the branch-free
 // form of discretization.py:10-17.
-__device__ __forceinline__ void zoh(float2 lam, float2 ilam, float dte, float2& dA, float2& dBbar) {
+// zoh_e returns expm1(z) itself (E, with dB_bar = E / lam), for callers that
+// fold 1/lam into the input term.
+__device__ __forceinline__ void zoh_e(float2 lam, float dte, float2& dA, float2& E) {
     const float a = lam.x * dte;
     const float b = lam.y * dte;
     float em1, ea, sb, cb, vb;
@@ -118,7 +120,17 @@ __device__ __forceinline__ void zoh(float2 lam, float2 ilam, float dte, float2& 
     trig_half(b, sb, cb, vb);
     const float im = ea * sb;
     dA = make_float2(ea * cb, im);
-    dBbar = cmul(make_float2(fmaf(em1, cb, -vb), im), ilam);
+    E = make_float2(fmaf(em1, cb, -vb), im);
+}
+__device__ __forceinline__ void zoh(float2 lam, float2 ilam, float dte, float2& dA, float2& dBbar) {
+    float2 E;
+    zoh_e(lam, dte, dA, E);
+    dBbar = cmul(E, ilam);
+}
+
+// a * b + c for complex a, b, c (four FMAs)
+__device__ __forceinline__ float2 cfma(float2 a, float2 b, float2 c) {
+    return make_float2(fmaf(a.x, b.x, fmaf(-a.y, b.y, c.x)), fmaf(a.x, b.y, fmaf(a.y, b.x, c.y)));
 }
 
 // ----------------------------------------------------------------------------
