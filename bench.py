@@ -49,8 +49,8 @@ ALG_BYTES = B * L * H * 2 + 2 * B * L * N * 8 + B * L * 4 + B * L * H * 4 + 2 * 
 # chunk overlap the cell of the next.
 E2E_CHUNK = 512
 # Issue slots per state update of cell_chain<SPEC> at this workload: ncu
-# smsp__inst_executed.sum x 32 / updates = 1,033,884,288 x 32 / 402,653,184.
-INSTR_PER_UPDATE = 82.2
+# smsp__inst_executed.sum x 32 / updates = 978,102,912 x 32 / 402,653,184.
+INSTR_PER_UPDATE = 77.7
 CONFIG = {
     "workload": "gated EACS cell inference forward (event gate + ZOH predict/update + commit), "
                 "B=8 L=4096 H=768 N=16",
