@@ -524,8 +524,8 @@ def wl_longvideo(args):
     peak, src = peak_hbm()
     achieved = alg / (kern_ms / 1e3) / 1e9
     # issue slots per update of cell_chain<SPEC> at H=2048, N=32 (ncu smsp__inst_executed.sum x 32
-    # / updates on the 8 x 4096 case: 5,091,733,504 x 32 / 2,147,483,648); the kernel is issue-bound
-    instr = 75.9 if (H, N) == (2048, 32) else None
+    # / updates on the 8 x 4096 case: 4,691,663,872 x 32 / 2,147,483,648); the kernel is issue-bound
+    instr = 69.9 if (H, N) == (2048, 32) else None
     n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
     issue_peak = n_sm * 4 * 32 * (sampler.summary().get("sm_mhz") or 1965.0) * 1e6
     if world > 1:
