@@ -534,8 +534,7 @@ __global__ void __launch_bounds__(512) train_bwd(TArgs a) {
                 // dB_bar = expm1(z) / lam: the adjoint of expm1(z) is adB conj(1/lam)
                 // and lam's share through 1/lam is -adB conj(dB_bar / lam)
                 const float2 aE = cmul(adB, make_float2(ilam[j].x, -ilam[j].y));
-                const float2 P = cmul(ilam[j], dB[j]);
-                float2 alm = cmul(make_float2(-adB.x, -adB.y), make_float2(P.x, -P.y));
+                float2 alm = cmul(make_float2(-aE.x, -aE.y), cdB);  // -adB conj(ilam) conj(dB_bar)
                 const float2 az = cmul(cdA, cadd(adA, aE));
                 alm = cadd(alm, cscale(az, dte));
                 s_dte += az.x * lam[j].x + az.y * lam[j].y;
