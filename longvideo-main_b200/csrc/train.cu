@@ -133,6 +133,7 @@ __global__ void __launch_bounds__(kCkThreads) train_ckpt(TArgs a) {
     float u_pi = hv ? to_f32(u[rowL * H + h]) : 0.f;
     float t_pi = a.t[rowL] - a.dt_init;
     const bool row_writer = blockIdx.x == 0 && tid == 0;
+    const bool bc_writer = blockIdx.x == 0 && hl == 0;  // writes B_pi, C_pi into the checkpoints
     const bool async_ok = NBUF == 2 && (PAIR == 1 || (H % 2) == 0) &&
                           (reinterpret_cast<uintptr_t>(u) & 3u) == 0 &&
                           ((reinterpret_cast<uintptr_t>(a.Bc) | reinterpret_cast<uintptr_t>(a.Cc)) & 7u) == 0 &&
@@ -193,7 +194,7 @@ __global__ void __launch_bounds__(kCkThreads) train_ckpt(TArgs a) {
                     if (nv[j]) a.ck_h[((static_cast<size_t>(b) * a.nK + k) * H + h) * N + ln + LANES * j] = hs[j];
                 if (hv && ln == 0) a.ck_u[(static_cast<size_t>(b) * a.nK + k) * H + h] = u_pi;
                 if (row_writer) a.ck_row[static_cast<size_t>(b) * a.nK + k] = make_float4(t_pi, 0.f, 0.f, 0.f);
-                if (blockIdx.x == 0 && hl == 0) {
+                if (bc_writer) {
 #pragma unroll
                     for (int j = 0; j < NPT; ++j) {
                         const int n = ln + LANES * j;
@@ -205,27 +206,39 @@ __global__ void __launch_bounds__(kCkThreads) train_ckpt(TArgs a) {
                     }
                 }
             }
-            const float g = sg[buf][i];
-            const float tl = st[buf][i];
-            const float ul = to_f32(su[buf][i][hl]);
-            const float dte = eff_dt(fmaxf(tl - t_pi, 0.f), scale, a.dt_min, a.dt_max);
+            // one step; with G1 the gate is a hard 1 and the (1 - g) terms, which
+            // are exactly zero then, are left out.  B_pi and C_pi are row values
+            // that only the threads writing them into the checkpoints keep.
+            auto step = [&](auto gm) {
+                constexpr bool G1 = decltype(gm)::value;
+                const float g = G1 ? 1.f : sg[buf][i];
+                const float tl = st[buf][i];
+                const float ul = to_f32(su[buf][i][hl]);
+                const float dte = eff_dt(fmaxf(tl - t_pi, 0.f), scale, a.dt_min, a.dt_max);
 #pragma unroll
-            for (int j = 0; j < NPT; ++j) {
-                const int n = ln + LANES * j;
-                const float2 Bl = sB[buf][i][n];
-                const float2 Cl = sC[buf][i][n];
-                float2 dA, dB;
-                zoh(lam[j], ilam[j], dte, dA, dB);
-                const float2 hf = cmul(dA, hs[j]);
-                const float2 ql = cmul(dB, Bl);
-                const float2 hu = make_float2(fmaf(ql.x, ul, hf.x), fmaf(ql.y, ul, hf.y));
-                const float2 gu = cscale(hu, g);
-                hs[j] = cadd(gu, cscale(hs[j], 1.f - g));
-                Bp[j] = cadd(cscale(Bl, g), cscale(Bp[j], 1.f - g));
-                Cp[j] = cadd(cscale(Cl, g), cscale(Cp[j], 1.f - g));
-            }
-            u_pi = g * ul + (1.f - g) * u_pi;
-            t_pi = g * tl + (1.f - g) * t_pi;
+                for (int j = 0; j < NPT; ++j) {
+                    const float2 Bl = sB[buf][i][ln + LANES * j];
+                    float2 dA, dB;
+                    zoh(lam[j], ilam[j], dte, dA, dB);
+                    const float2 hf = cmul(dA, hs[j]);
+                    const float2 ql = cmul(dB, Bl);
+                    const float2 hu = make_float2(fmaf(ql.x, ul, hf.x), fmaf(ql.y, ul, hf.y));
+                    hs[j] = G1 ? hu : cadd(cscale(hu, g), cscale(hs[j], 1.f - g));
+                }
+                if (bc_writer) {
+#pragma unroll
+                    for (int j = 0; j < NPT; ++j) {
+                        const float2 Bl = sB[buf][i][ln + LANES * j];
+                        const float2 Cl = sC[buf][i][ln + LANES * j];
+                        Bp[j] = G1 ? Bl : cadd(cscale(Bl, g), cscale(Bp[j], 1.f - g));
+                        Cp[j] = G1 ? Cl : cadd(cscale(Cl, g), cscale(Cp[j], 1.f - g));
+                    }
+                }
+                u_pi = G1 ? ul : g * ul + (1.f - g) * u_pi;
+                t_pi = G1 ? tl : g * tl + (1.f - g) * t_pi;
+            };
+            if (sg[buf][i] == 1.f) step(std::true_type{});
+            else step(std::false_type{});
         }
     }
 }
