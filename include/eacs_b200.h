@@ -195,8 +195,9 @@ EACS_API size_t eacs_cell_train_bwd_workspace_size(int64_t B, int64_t L, int64_t
  * Outputs (overwritten, float32 / complex64): du (B,L,H), dBc, dCc (B,L,N),
  * dt (B,L), dlam (H,N), dlog_dt (H), dD (H), deps (1).  temperature is T of
  * sigmoid((r - eps)/max(T, 1e-4)).  Rows are handled by one thread-block
- * cluster of up to 16 CTAs of at most 512 threads (H*lanes <= 8192, lanes = 8
- * for N <= 16, 16 for N <= 32, 32 for N <= 64). */
+ * cluster of up to 16 CTAs of at most 512 threads (H*lanes <= 8192): four
+ * chains a thread for N > 8 (lanes = 4 for N <= 16, 8 for N <= 32, 16 for
+ * N <= 64), two for N <= 8 (lanes = 4). */
 EACS_API int eacs_cell_train_bwd(const void* lam, const float* log_dt, const void* u, int u_dtype,
                                  const void* Bc, const void* Cc, const float* t, const float* D,
                                  const float* mean, const float* var,
