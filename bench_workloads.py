@@ -103,9 +103,10 @@ def line(metric, value, steps, warmup, ms, config, **extra):
 
 # ----------------------------------------------------------------------------
 def wl_scan(args, dev, flush):
-    """scan_fwd / scan_bwd on one multiscale branch (B=4 H=1024 N=16) at L=4096 (24 / 40 B per update)."""
+    """scan_fwd / scan_bwd on one multiscale branch (B=4 H=1024 N=16) at L=4096 (24 / 40 B per update);
+    --shape B,L,H,N gives a small case for ncu."""
     from eacs_b200.ops.scan_cuda import EXT
-    B, L, H, N = 4, 4096, 1024, 16
+    B, L, H, N = (4, 4096, 1024, 16) if getattr(args, "shape", None) is None else (int(v) for v in args.shape.split(","))
     g = torch.Generator().manual_seed(7)
     mag = (0.69 + 0.3 * torch.rand(B, L, H, N, generator=g))
     ph = 6.283185 * torch.rand(B, L, H, N, generator=g)
