@@ -6,8 +6,9 @@
 // reference runs a GEMM, a softmax, a stack, an einsum, an add and a
 // LayerNorm, each a pass over (B, L, d) tensors; here one warp per row reads
 // x and the S deltas once, computes the S logits against the fusion weights
-// held in shared memory, the softmax, the blend and the LayerNorm (two-pass
-// mean / variance in registers, fp32 throughout) and writes y and w.
+// held in shared memory (with the LayerNorm weights, lane-interleaved), the
+// softmax, the blend and the LayerNorm (two-pass mean / variance in
+// registers, fp32 throughout) and writes y and w.
 // Rows are read as 16-byte vectors (8 bf16/fp16 or 4 fp32 elements a lane).
 #include <algorithm>
 
@@ -64,10 +65,30 @@ __device__ __forceinline__ void store_vec(T* p, const float* f) {
 template <typename T, int VPL>
 __global__ void __launch_bounds__(kFuseRows * 32) branch_fuse_k(FuseArgs a) {
     constexpr int E = Vec<T>::E;
-    extern __shared__ float sw[];  // (S, d)
+    constexpr int Q = E / 4;  // float4 per lane vector
+    // The S fusion weight rows, then the LayerNorm gamma and beta, each laid
+    // out as [k][q][lane] float4: lane l's elements (k*32 + l)*E + 4q .. +3
+    // sit at consecutive 16-byte slots across the lanes (no bank conflicts).
+    extern __shared__ float4 sw4[];
     const int d = a.d, S = a.S;
-    for (int i = threadIdx.x; i < S * d; i += blockDim.x) sw[i] = a.wf[i];
+    const int per = VPL * 32 * E;  // padded row length
+    float* swf = reinterpret_cast<float*>(sw4);
+    for (int i = threadIdx.x; i < (S + 2) * per; i += blockDim.x) {
+        const int s = i / per, col = i - s * per;
+        const int k = col / (32 * E), ln_ = (col / E) % 32, e = col % E;
+        float v = 0.f;
+        if (col < d) {
+            if (s < S) v = a.wf[static_cast<size_t>(s) * d + col];
+            else if (s == S) v = a.gamma ? a.gamma[col] : 1.f;
+            else v = a.beta ? a.beta[col] : 0.f;
+        }
+        swf[((((s * VPL + k) * Q + (e >> 2)) * 32 + ln_) << 2) + (e & 3)] = v;
+    }
     __syncthreads();
+    auto w4 = [&](int s, int k, int q, int l) { return sw4[((s * VPL + k) * Q + q) * 32 + l]; };
+    float bias[kMaxBranch];
+#pragma unroll
+    for (int s = 0; s < kMaxBranch; ++s) bias[s] = (s < S && a.bf) ? a.bf[s] : 0.f;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     // rows in a grid-stride loop, so each CTA loads the fusion weights once
     for (int64_t r = static_cast<int64_t>(blockIdx.x) * kFuseRows + wid; r < a.rows;
@@ -94,11 +115,16 @@ __global__ void __launch_bounds__(kFuseRows * 32) branch_fuse_k(FuseArgs a) {
 #pragma unroll
         for (int k = 0; k < VPL; ++k)
             if (in[k]) {
-                const float* wr = sw + s * d + (k * 32 + lane) * E;
 #pragma unroll
-                for (int e = 0; e < E; ++e) acc = fmaf(v[k][e], wr[e], acc);
+                for (int q = 0; q < Q; ++q) {
+                    const float4 w = w4(s, k, q, lane);
+                    acc = fmaf(v[k][4 * q], w.x, acc);
+                    acc = fmaf(v[k][4 * q + 1], w.y, acc);
+                    acc = fmaf(v[k][4 * q + 2], w.z, acc);
+                    acc = fmaf(v[k][4 * q + 3], w.w, acc);
+                }
             }
-        acc = warp_sum(acc) + (a.bf ? a.bf[s] : 0.f);
+        acc = warp_sum(acc) + bias[s];
         logit[s] = acc;
         mx = fmaxf(mx, acc);
     }
@@ -150,15 +176,20 @@ __global__ void __launch_bounds__(kFuseRows * 32) branch_fuse_k(FuseArgs a) {
             const int i0 = (k * 32 + lane) * E;
             float o[E];
 #pragma unroll
-            for (int e = 0; e < E; ++e) {
-                const float g = a.gamma ? a.gamma[i0 + e] : 1.f;
-                const float bb = a.beta ? a.beta[i0 + e] : 0.f;
-                o[e] = fmaf((v[k][e] - mean) * rstd, g, bb);
+            for (int q = 0; q < Q; ++q) {
+                const float4 g = w4(S, k, q, lane), bb = w4(S + 1, k, q, lane);
+                o[4 * q] = fmaf((v[k][4 * q] - mean) * rstd, g.x, bb.x);
+                o[4 * q + 1] = fmaf((v[k][4 * q + 1] - mean) * rstd, g.y, bb.y);
+                o[4 * q + 2] = fmaf((v[k][4 * q + 2] - mean) * rstd, g.z, bb.z);
+                o[4 * q + 3] = fmaf((v[k][4 * q + 3] - mean) * rstd, g.w, bb.w);
             }
             store_vec(yr + i0, o);
         }
     }
 }
+
+// the vectors per lane the launched instance uses (a power of two)
+int vpl_pad(int vpl) { return vpl <= 1 ? 1 : vpl <= 2 ? 2 : vpl <= 4 ? 4 : 8; }
 
 template <typename T>
 cudaError_t launch_fuse(const FuseArgs& a, cudaStream_t s) {
@@ -169,7 +200,7 @@ cudaError_t launch_fuse(const FuseArgs& a, cudaStream_t s) {
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
     const unsigned grid = static_cast<unsigned>(
         std::min<int64_t>((a.rows + kFuseRows - 1) / kFuseRows, static_cast<int64_t>(n_sm) * 8));
-    const size_t smem = sizeof(float) * a.S * a.d;
+    const size_t smem = sizeof(float) * (a.S + 2) * vpl_pad(vpl) * 32 * E;
     cudaError_t e;
 #define EACS_FUSE(V)                                                                                \
     do {                                                                                            \
@@ -196,7 +227,7 @@ int branch_fuse(const FuseCall& c, cudaStream_t stream) {
     if (c.dtype != EACS_DTYPE_F32 && c.dtype != EACS_DTYPE_F16 && c.dtype != EACS_DTYPE_BF16)
         return fail(EACS_ERR_INVALID, "%s: unknown dtype %d", fn, c.dtype);
     const int E = c.dtype == EACS_DTYPE_F32 ? 4 : 8;
-    if (c.d % E != 0 || c.d > 8 * 32 * E || static_cast<size_t>(c.S) * c.d * 4 > 200u * 1024u)
+    if (c.d % E != 0 || c.d > 8 * 32 * E)  // shared memory: (S + 2) x 256 E floats, at most 80 KiB
         return fail(EACS_ERR_UNSUPPORTED, "%s: d=%d must be a multiple of %d and at most %d", fn, c.d, E,
                     8 * 32 * E);
     if (c.rows == 0) return EACS_OK;
