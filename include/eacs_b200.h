@@ -211,6 +211,42 @@ EACS_API int eacs_cell_train_bwd(const void* lam, const float* log_dt, const voi
                                  void* workspace, size_t workspace_bytes,
                                  int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
 
+/* The training forward (eacs_cell_train_fwd's arguments and outputs) that
+ * also writes the checkpoints the training backward recomputes from -- the
+ * committed state before every K-th step, K chosen by the backward -- into
+ * `bwd_workspace` (eacs_cell_train_bwd_workspace_size bytes, kept unchanged
+ * until the matching eacs_cell_train_bwd_ckpt call).  The forward computes
+ * those states anyway, so the backward's own checkpoint pass (a second
+ * forward) is skipped.  Same reference function as eacs_cell_train_fwd
+ * (GatedEACSCellFunction.forward, cst_ssm/ops/eacs_cell_train.py:81-116);
+ * needs rows that one thread-block cluster holds (as the repair pass does)
+ * and returns EACS_ERR_UNSUPPORTED otherwise. */
+EACS_API int eacs_cell_train_fwd_ckpt(const void* lam, const float* log_dt, const void* u, int u_dtype,
+                                      const void* Bc, const void* Cc, const float* t, const float* D,
+                                      const float* mean, const float* var,
+                                      float eps, float eta, float var_eps, float dt_init,
+                                      float dt_min, float dt_max, int gate_mode, float temperature,
+                                      float* y, float* gate, float* resid, float* stats,
+                                      void* workspace, size_t workspace_bytes,
+                                      void* bwd_workspace, size_t bwd_workspace_bytes,
+                                      int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
+
+/* eacs_cell_train_bwd reading the checkpoints that eacs_cell_train_fwd_ckpt
+ * wrote into `workspace` for the same inputs and sizes (the backward of
+ * GatedEACSCellFunction, cst_ssm/ops/eacs_cell_train.py:117-175). */
+EACS_API int eacs_cell_train_bwd_ckpt(const void* lam, const float* log_dt, const void* u, int u_dtype,
+                                      const void* Bc, const void* Cc, const float* t, const float* D,
+                                      const float* mean, const float* var,
+                                      float eps, float eta, float var_eps, float dt_init,
+                                      float dt_min, float dt_max, float temperature,
+                                      const float* gate, const float* resid, const float* stats,
+                                      const float* gy, const float* ggs, const float* grs,
+                                      const float* gns,
+                                      float* du, void* dBc, void* dCc, float* dt, void* dlam,
+                                      float* dlog_dt, float* dD, float* deps,
+                                      void* workspace, size_t workspace_bytes,
+                                      int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
+
 /* Workspace bytes eacs_cell_commits needs (eacs_cell_fwd's plus one int per
  * (b, l)); 0 if the sizes are unsupported. */
 EACS_API size_t eacs_cell_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);

@@ -153,6 +153,43 @@ int eacs_cell_train_fwd(const void* lam, const float* log_dt, const void* u, int
     return eacs::cell_fwd(c, static_cast<cudaStream_t>(stream));
 }
 
+int eacs_cell_train_fwd_ckpt(const void* lam, const float* log_dt, const void* u, int u_dtype, const void* Bc,
+                             const void* Cc, const float* t, const float* D, const float* mean,
+                             const float* var, float eps, float eta, float var_eps, float dt_init,
+                             float dt_min, float dt_max, int gate_mode, float temperature, float* y,
+                             float* gate, float* resid, float* stats, void* workspace,
+                             size_t workspace_bytes, void* bwd_workspace, size_t bwd_workspace_bytes,
+                             int64_t B, int64_t L, int64_t H, int64_t N, void* stream) {
+    if (!stats) return eacs::fail(EACS_ERR_INVALID, "eacs_cell_train_fwd_ckpt: null stats");
+    eacs::CellCall c{lam,  log_dt, u,       u_dtype, Bc,     Cc,      t,      D,
+                     mean, var,    eps,     eta,     var_eps, dt_init, dt_min, dt_max,
+                     0,    3,      2.0f,    0.3f,    gate_mode, temperature, y, gate,
+                     resid, workspace, workspace_bytes, B, L, H, N};
+    c.stats = stats;
+    if (B == 0 || L == 0 || H == 0) return EACS_OK;
+    const int rc = eacs::train_ckpt_layout(B, L, H, N, bwd_workspace, bwd_workspace_bytes, &c);
+    if (rc) return rc;
+    return eacs::cell_fwd(c, static_cast<cudaStream_t>(stream));
+}
+
+int eacs_cell_train_bwd_ckpt(const void* lam, const float* log_dt, const void* u, int u_dtype, const void* Bc,
+                             const void* Cc, const float* t, const float* D, const float* mean,
+                             const float* var, float eps, float eta, float var_eps, float dt_init,
+                             float dt_min, float dt_max, float temperature, const float* gate,
+                             const float* resid, const float* stats, const float* gy, const float* ggs,
+                             const float* grs, const float* gns, float* du, void* dBc, void* dCc,
+                             float* dt, void* dlam, float* dlog_dt, float* dD, float* deps,
+                             void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t H,
+                             int64_t N, void* stream) {
+    eacs::TrainBwdCall c{lam,   log_dt, u,     u_dtype, Bc,      Cc,     t,      D,       mean,
+                         var,   eps,    eta,   var_eps, dt_init, dt_min, dt_max, temperature,
+                         gate,  resid,  stats, gy,      ggs,     grs,    gns,    du,      dBc,
+                         dCc,   dt,     dlam,  dlog_dt, dD,      deps,   workspace, workspace_bytes,
+                         B,     L,      H,     N};
+    c.have_ckpt = true;
+    return eacs::train_bwd(c, static_cast<cudaStream_t>(stream));
+}
+
 size_t eacs_cell_train_bwd_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
     return eacs::train_workspace_size(B, L, H, N);
 }

@@ -41,7 +41,8 @@ constexpr int kMinBlocks = 768 / kThreads;    // keep 24 warps per SM resident
 constexpr int kT = 32;                         // steps per staged chunk
 constexpr int kRepair = 1024;  // repair kernel CTA
 
-enum Mode { SPEC = 0, UNGATED = 1, REPLAY = 2, SPEC_COMMITS = 3 };  // SPEC_COMMITS: SPEC + commit_h
+// SPEC_COMMITS: SPEC + commit_h; SPEC_CKPT: SPEC + the training backward's checkpoints
+enum Mode { SPEC = 0, UNGATED = 1, REPLAY = 2, SPEC_COMMITS = 3, SPEC_CKPT = 4 };
 
 struct Args {
     const float2* lam;
@@ -86,8 +87,41 @@ struct Args {
     float2* cout_B;
     float2* cout_C;
     float4* cout_row;
+    // optional training checkpoints (hard or soft gate): the committed state
+    // before every gK-th step, in the training backward's layout
+    float2* gck_h;   // [B][gnK][H][N]
+    float* gck_u;    // [B][gnK][H]
+    float4* gck_row; // [B][gnK] (t_pi, -, -, -)
+    float2* gck_bc;  // [B][gnK][2][N] (B_pi, C_pi)
+    int gK, gnK;
     int B, L, H, N, ntiles, nK;
 };
+
+// Checkpoint k = l / gK of row b from a thread owning chains n = ln + LANES*j
+// of channel h: its states, its channel's u_pi; B_pi / C_pi and t_pi by the
+// threads the caller names (one per row for t_pi, one channel's for B, C).
+template <int LANES, int NPT>
+__device__ __forceinline__ void write_gck(const Args& a, int b, int k, int h, int ln, const bool (&nv)[NPT],
+                                          const float2 (&hs)[NPT], bool chan_writer, float u_pi, bool bc_writer,
+                                          const float2 (&Bp)[NPT], const float2 (&Cp)[NPT], bool row_writer,
+                                          float t_pi) {
+    const size_t rk = static_cast<size_t>(b) * a.gnK + k;
+#pragma unroll
+    for (int j = 0; j < NPT; ++j)
+        if (nv[j]) a.gck_h[(rk * a.H + h) * a.N + ln + LANES * j] = hs[j];
+    if (chan_writer) a.gck_u[rk * a.H + h] = u_pi;
+    if (bc_writer) {
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            if (n < a.N) {
+                a.gck_bc[rk * 2 * a.N + n] = Bp[j];
+                a.gck_bc[(rk * 2 + 1) * a.N + n] = Cp[j];
+            }
+        }
+    }
+    if (row_writer) a.gck_row[rk] = make_float4(t_pi, 0.f, 0.f, 0.f);
+}
 
 // ---------------------------------------------------------------------------
 // Transposed shuffle butterfly over the LANES lanes of a channel group.  A lane
@@ -147,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
     constexpr int NP = LANES * NPT;
     constexpr int NW = kThreads / 32;
     constexpr int U = EACS_CHAIN_U;
-    constexpr bool kSpec = MODE == SPEC || MODE == SPEC_COMMITS;  // speculative gated pass
+    constexpr bool kSpec = MODE == SPEC || MODE == SPEC_COMMITS || MODE == SPEC_CKPT;  // speculative gated pass
     constexpr int NV = kSpec ? 2 * U : U;  // readout sums per group
     using Shape = BflyShape<NV, LANES>;
     static_assert(kT % U == 0, "chunk must hold whole step groups");
@@ -298,6 +332,20 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                 else
                     delta = fmaxf(tl - t_prev, 0.f);
                 const float dte = eff_dt(delta, scale, a.dt_min, a.dt_max);
+                if (MODE == SPEC_CKPT && i < steps && (l0 + i) % a.gK == 0) {
+                    // the state before step l under the all-commit assumption (rows
+                    // that skip get theirs from l* on rewritten by the repair pass);
+                    // B_pi is step l-1's B (step 0's own before the first step)
+                    const int l = l0 + i;
+                    float2 Bq[NPT];
+#pragma unroll
+                    for (int j = 0; j < NPT; ++j) {
+                        const int n = ln + LANES * j;
+                        Bq[j] = n < N ? a.Bc[(rowLH + (l > 0 ? l - 1 : 0)) * N + n] : make_float2(0.f, 0.f);
+                    }
+                    write_gck<LANES, NPT>(a, b, l / a.gK, h, ln, nv, hs, hv && ln == 0, u_prev,
+                                          tile == 0 && hl == 0, Bq, Cp, tile == 0 && tid == 0, t_prev);
+                }
                 float yp = 0.f, yhp = 0.f;
                 // Branch-free: channels past H stage u = 0 and padded chains
                 // stage B = C = 0, so both keep a zero state and add zeros.
@@ -901,6 +949,9 @@ __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int
             Bl[j] = sBl(buf, i)[ln + LANES * j];
             Cl[j] = sCl(buf, i)[ln + LANES * j];
         }
+        if (a.gck_h != nullptr && l % a.gK == 0)  // training checkpoint: the committed state before step l
+            write_gck<LANES, NPT>(a, b, l / a.gK, h, ln, nv, hs, hv && ln == 0, u_pi, crank == 0 && hl == 0, Bp,
+                                  Cp, crank == 0 && tid == 0, t_pi);
         const float dte = eff_dt(fmaxf(tl - t_pi, 0.f), scale, a.dt_min, a.dt_max);
         float2 P[NPT], dB[NPT], xh[NPT];
         float yhp = 0.f;
@@ -1336,6 +1387,11 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
         return fail(EACS_ERR_INVALID, "%s: null commit output", fn);
     if (commits && c.gate_mode != 0)
         return fail(EACS_ERR_INVALID, "%s: commits are recorded for the hard gate only", fn);
+    const bool ckpt = c.ck_h != nullptr;
+    if (ckpt && (!c.ck_u || !c.ck_row || !c.ck_bc || c.ck_K <= 0 || c.ck_nK <= 0))
+        return fail(EACS_ERR_INVALID, "%s: incomplete checkpoint layout", fn);
+    if (ckpt && (commits || rc_shape(static_cast<int>(c.H), static_cast<int>(c.N)).cl == 0))
+        return fail(EACS_ERR_UNSUPPORTED, "%s: checkpoints need the cluster repair shape and no commits", fn);
     const bool carry = c.cin_h != nullptr || c.cout_h != nullptr;
     if (carry && !cell_resumable(c.H, c.N))
         return fail(EACS_ERR_UNSUPPORTED, "%s: H=%lld N=%lld rows cannot be resumed", fn, (long long)c.H,
@@ -1397,6 +1453,14 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
     a.cout_B = static_cast<float2*>(c.cout_B);
     a.cout_C = static_cast<float2*>(c.cout_C);
     a.cout_row = static_cast<float4*>(c.cout_row);
+    if (ckpt) {
+        a.gck_h = static_cast<float2*>(c.ck_h);
+        a.gck_u = c.ck_u;
+        a.gck_row = static_cast<float4*>(c.ck_row);
+        a.gck_bc = static_cast<float2*>(c.ck_bc);
+        a.gK = c.ck_K;
+        a.gnK = c.ck_nK;
+    }
     a.B = static_cast<int>(c.B);
     a.L = static_cast<int>(c.L);
     a.H = static_cast<int>(c.H);
@@ -1406,6 +1470,7 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
     cudaError_t e;
     if (c.gate_mode == 0) {
         e = commits ? chain_dispatch<SPEC_COMMITS>(a, c.u_dtype, stream)
+            : ckpt  ? chain_dispatch<SPEC_CKPT>(a, c.u_dtype, stream)
                     : chain_dispatch<SPEC>(a, c.u_dtype, stream);
         if (e != cudaSuccess) return cuda_check(e, fn);
         cell_resid<<<dim3((a.L + 255) / 256, a.B), 256, 0, stream>>>(a);

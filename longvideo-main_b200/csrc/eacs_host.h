@@ -73,6 +73,13 @@ struct CellCall {
     void* cout_B = nullptr;
     void* cout_C = nullptr;
     void* cout_row = nullptr;
+    // optional training checkpoints (train_ckpt_layout): the state before
+    // every ck_K-th step, as the training backward reads them
+    void* ck_h = nullptr;    // [B][nK][H][N] complex64
+    float* ck_u = nullptr;   // [B][nK][H]
+    void* ck_row = nullptr;  // [B][nK] float4 (t_pi, -, -, -)
+    void* ck_bc = nullptr;   // [B][nK][2][N] complex64 (B_pi, C_pi)
+    int ck_K = 0, ck_nK = 0;
 };
 size_t cell_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
 size_t cell_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
@@ -210,8 +217,13 @@ struct TrainBwdCall {
     void* workspace;
     size_t workspace_bytes;
     int64_t B, L, H, N;
+    bool have_ckpt = false;  // the workspace already holds the forward's checkpoints
 };
 size_t train_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+// Where the training backward's workspace keeps its checkpoints (fills c's
+// ck_* fields); an EACS status code.
+int train_ckpt_layout(int64_t B, int64_t L, int64_t H, int64_t N, void* workspace, size_t workspace_bytes,
+                      CellCall* c);
 
 // ssm_train.cu
 struct SsmBwdCall {

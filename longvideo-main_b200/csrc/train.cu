@@ -82,6 +82,7 @@ struct TArgs {
     float* peps;          // [B]
     int B, L, H, N, nK, CL, HC;
     int K;                // steps per checkpoint / recompute chunk
+    int have_ckpt;        // the forward already wrote the checkpoints
 };
 
 template <int LANES>
@@ -818,7 +819,7 @@ cudaError_t launch_ckpt(TArgs& a, cudaStream_t s) {
 template <int LANES, int NPT, typename UT>
 cudaError_t launch_train(TArgs& a, int T, cudaStream_t s) {
     constexpr int NP = LANES * NPT;
-    {
+    if (!a.have_ckpt) {
         cudaError_t e = launch_ckpt<UT>(a, s);
         if (e != cudaSuccess) return e;
     }
@@ -885,8 +886,32 @@ size_t train_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
     return tws(B, L, H, N, CL, K).total;
 }
 
+int train_ckpt_layout(int64_t B, int64_t L, int64_t H, int64_t N, void* workspace, size_t workspace_bytes,
+                      CellCall* c) {
+    const char* fn = "eacs_cell_train_fwd_ckpt";
+    int lanes, npt, CL, HC, T;
+    if (B <= 0 || L <= 0 || H <= 0 || N <= 0 || !lanes_train(static_cast<int>(N), &lanes, &npt) ||
+        !train_shape(H, lanes, &CL, &HC, &T))
+        return fail(EACS_ERR_UNSUPPORTED, "%s: no training backward for B=%lld L=%lld H=%lld N=%lld", fn,
+                    (long long)B, (long long)L, (long long)H, (long long)N);
+    const int K = chunk_len(T, npt, lanes * npt, HC);
+    if (K == 0) return fail(EACS_ERR_UNSUPPORTED, "%s: shared memory too small for H=%lld", fn, (long long)H);
+    const TWs w = tws(B, L, H, N, CL, K);
+    if (!workspace || workspace_bytes < w.total)
+        return fail(EACS_ERR_WORKSPACE, "%s: backward workspace of %zu bytes needed, %zu given", fn, w.total,
+                    workspace_bytes);
+    char* ws = static_cast<char*>(workspace);
+    c->ck_h = ws + w.ck_h;
+    c->ck_u = reinterpret_cast<float*>(ws + w.ck_u);
+    c->ck_row = ws + w.ck_row;
+    c->ck_bc = ws + w.ck_bc;
+    c->ck_K = K;
+    c->ck_nK = static_cast<int>((L + K - 1) / K);
+    return EACS_OK;
+}
+
 int train_bwd(const TrainBwdCall& c, cudaStream_t stream) {
-    const char* fn = "eacs_cell_train_bwd";
+    const char* fn = c.have_ckpt ? "eacs_cell_train_bwd_ckpt" : "eacs_cell_train_bwd";
     if (c.B < 0 || c.L < 0 || c.H < 0 || c.N < 0) return fail(EACS_ERR_INVALID, "%s: negative size", fn);
     if (c.B == 0 || c.L == 0 || c.H == 0) return EACS_OK;
     int lanes, npt, CL, HC, T;
@@ -960,6 +985,7 @@ int train_bwd(const TrainBwdCall& c, cudaStream_t stream) {
     a.nK = static_cast<int>((c.L + K - 1) / K);
     a.CL = CL;
     a.HC = HC;
+    a.have_ckpt = c.have_ckpt ? 1 : 0;
     cudaError_t e;
     if (c.u_dtype == EACS_DTYPE_F16) e = train_by_n<__half>(a, T, stream);
     else if (c.u_dtype == EACS_DTYPE_BF16) e = train_by_n<__nv_bfloat16>(a, T, stream);

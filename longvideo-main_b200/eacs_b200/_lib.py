@@ -80,6 +80,15 @@ SIGNATURES = {
                                  _P, _P, _P, _P, _P, _P, _P,
                                  _P, _P, _P, _P, _P, _P, _P, _P,
                                  _P, ctypes.c_size_t, _I64, _I64, _I64, _I64, _P]),
+    "eacs_cell_train_fwd_ckpt": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
+                                      _F, _F, _F, _F, _F, _F, _I, _F,
+                                      _P, _P, _P, _P, _P, ctypes.c_size_t, _P, ctypes.c_size_t,
+                                      _I64, _I64, _I64, _I64, _P]),
+    "eacs_cell_train_bwd_ckpt": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
+                                      _F, _F, _F, _F, _F, _F, _F,
+                                      _P, _P, _P, _P, _P, _P, _P,
+                                      _P, _P, _P, _P, _P, _P, _P, _P,
+                                      _P, ctypes.c_size_t, _I64, _I64, _I64, _I64, _P]),
     "eacs_cell_fwd_noalloc": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
                                    _F, _F, _F, _F, _F, _F, _I, _I, _F, _F, _I, _F,
                                    _P, _P, _P, _I64, _I64, _I64, _I64, _P]),

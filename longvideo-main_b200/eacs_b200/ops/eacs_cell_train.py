@@ -5,7 +5,9 @@ eta, var_eps, dt_init, gate_mode, use_kernel, dt_max)` and `fused_gated_scan`
 keep the reference signatures (eacs_cell_train.py:81-199).  The forward is the
 gated cell kernel (hard gate values for "ste", the soft gate for "soft"); the
 backward is the hand-derived VJP of the L-step scan (libeacs_b200.so,
-eacs_cell_train_bwd) -- no Python loop and no (L,B,H,N) state list.
+eacs_cell_train_bwd) -- no Python loop and no (L,B,H,N) state list.  The
+forward writes the checkpoints the backward recomputes from
+(eacs_cell_train_fwd_ckpt / eacs_cell_train_bwd_ckpt).
 `use_kernel` is accepted for signature compatibility; there is no other path.
 """
 from __future__ import annotations
@@ -19,7 +21,10 @@ from .eacs_gated_scan import prepare, workspace_bytes
 
 
 def _train_fwd(u, Bc, Cc, t, lam, log_dt, D, eps, mean, var, T, eta, var_eps, dt_init,
-               gate_mode, dt_max):
+               gate_mode, dt_max, bwd_ws=None):
+    """The gated forward for training.  With `bwd_ws` (a uint8 tensor of
+    eacs_cell_train_bwd_workspace_size bytes) it also writes the backward's
+    checkpoints there (eacs_cell_train_fwd_ckpt)."""
     dev, (lam_c, log_c, u_c, B_c, C_c, t_c, D_c, m_c, v_c) = prepare(
         lam, log_dt, u, Bc, Cc, t, D, mean, var)
     B, L, H = u_c.shape
@@ -30,18 +35,26 @@ def _train_fwd(u, Bc, Cc, t, lam, log_dt, D, eps, mean, var, T, eta, var_eps, dt
     stats = torch.empty(B, L, 2, dtype=torch.float32, device=dev)
     if ys.numel():
         ws = torch.empty(workspace_bytes(B, L, H, N), dtype=torch.uint8, device=dev)
-        with torch.cuda.device(dev):
-            _lib.check(_lib.lib().eacs_cell_train_fwd(
-                lam_c.data_ptr(), log_c.data_ptr(), u_c.data_ptr(), _lib.DTYPE_CODES[u_c.dtype],
+        args = (lam_c.data_ptr(), log_c.data_ptr(), u_c.data_ptr(), _lib.DTYPE_CODES[u_c.dtype],
                 B_c.data_ptr(), C_c.data_ptr(), t_c.data_ptr(), D_c.data_ptr(), m_c.data_ptr(),
                 v_c.data_ptr(), float(eps), float(eta), float(var_eps), float(dt_init), 1e-3,
                 float(dt_max), 1 if gate_mode == "soft" else 0, float(T),
-                ys.data_ptr(), gs.data_ptr(), rs.data_ptr(), stats.data_ptr(),
-                ws.data_ptr(), ws.numel(), B, L, H, N, _lib.stream_ptr(dev)), "eacs_cell_train_fwd")
+                ys.data_ptr(), gs.data_ptr(), rs.data_ptr(), stats.data_ptr(), ws.data_ptr(), ws.numel())
+        with torch.cuda.device(dev):
+            if bwd_ws is None:
+                _lib.check(_lib.lib().eacs_cell_train_fwd(*args, B, L, H, N, _lib.stream_ptr(dev)),
+                           "eacs_cell_train_fwd")
+            else:
+                _lib.check(_lib.lib().eacs_cell_train_fwd_ckpt(
+                    *args, bwd_ws.data_ptr(), bwd_ws.numel(), B, L, H, N, _lib.stream_ptr(dev)),
+                    "eacs_cell_train_fwd_ckpt")
     return ys, gs, rs, stats, (lam_c, log_c, u_c, B_c, C_c, t_c, D_c, m_c, v_c)
 
 
-def _train_bwd(prep, gs, rs, stats, eps, T, eta, var_eps, dt_init, dt_max, g_ys, g_gs, g_rs, g_ns):
+def _train_bwd(prep, gs, rs, stats, eps, T, eta, var_eps, dt_init, dt_max, g_ys, g_gs, g_rs, g_ns,
+               bwd_ws=None):
+    """The backward.  With `bwd_ws` holding the checkpoints a _train_fwd call
+    with the same tensors wrote, its checkpoint pass is skipped."""
     lam_c, log_c, u_c, B_c, C_c, t_c, D_c, m_c, v_c = prep
     dev = u_c.device
     B, L, H = u_c.shape
@@ -60,9 +73,11 @@ def _train_bwd(prep, gs, rs, stats, eps, T, eta, var_eps, dt_init, dt_max, g_ys,
     L_ = _lib.lib()
     nbytes = int(L_.eacs_cell_train_bwd_workspace_size(B, L, H, N))
     require(nbytes > 0, f"eacs_cell_train_bwd: unsupported sizes B={B} L={L} H={H} N={N}")
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev) if bwd_ws is None else bwd_ws
+    require(ws.numel() >= nbytes, "eacs_cell_train_bwd: checkpoint workspace too small")
+    entry = L_.eacs_cell_train_bwd if bwd_ws is None else L_.eacs_cell_train_bwd_ckpt
     with torch.cuda.device(dev):
-        _lib.check(L_.eacs_cell_train_bwd(
+        _lib.check(entry(
             lam_c.data_ptr(), log_c.data_ptr(), u_c.data_ptr(), _lib.DTYPE_CODES[u_c.dtype],
             B_c.data_ptr(), C_c.data_ptr(), t_c.data_ptr(), D_c.data_ptr(), m_c.data_ptr(),
             v_c.data_ptr(), float(eps), float(eta), float(var_eps), float(dt_init), 1e-3,
@@ -70,7 +85,7 @@ def _train_bwd(prep, gs, rs, stats, eps, T, eta, var_eps, dt_init, dt_max, g_ys,
             gy.data_ptr(), *[_lib.ptr(g) for g in opt],
             du.data_ptr(), dBc.data_ptr(), dCc.data_ptr(), dt.data_ptr(), dlam.data_ptr(),
             dlog.data_ptr(), dD.data_ptr(), deps.data_ptr(), ws.data_ptr(), ws.numel(),
-            B, L, H, N, _lib.stream_ptr(dev)), "eacs_cell_train_bwd")
+            B, L, H, N, _lib.stream_ptr(dev)), "eacs_cell_train_bwd" if bwd_ws is None else "eacs_cell_train_bwd_ckpt")
     return du, dBc, dCc, dt, dlam, dlog, dD, deps
 
 
@@ -81,8 +96,17 @@ class GatedEACSCellFunction(torch.autograd.Function):
         ctx.set_materialize_grads(False)
         cuda_tensors("GatedEACSCellFunction", u, Bc, Cc, t, lam, log_dt, D, mean, var)
         eps_v = float(eps)
+        # When gradients are wanted, the forward also writes the checkpoints the
+        # backward recomputes from (it computes those states anyway), into the
+        # backward's workspace, held until the backward.
+        bwd_ws = None
+        if any(ctx.needs_input_grad[:8]) and u.numel():
+            nbytes = int(_lib.lib().eacs_cell_train_bwd_workspace_size(*u.shape, lam.shape[1]))
+            if nbytes:
+                bwd_ws = torch.empty(nbytes, dtype=torch.uint8, device=u.device)
         ys, gs, rs, stats, prep = _train_fwd(u, Bc, Cc, t, lam, log_dt, D, eps_v, mean, var, T,
-                                             eta, var_eps, dt_init, gate_mode, dt_max)
+                                             eta, var_eps, dt_init, gate_mode, dt_max, bwd_ws)
+        ctx.bwd_ws = bwd_ws
         ctx.prep = prep
         ctx.save_for_backward(gs, rs, stats)
         ctx.hp = (eps_v, float(T), float(eta), float(var_eps), float(dt_init), float(dt_max))
@@ -97,7 +121,8 @@ class GatedEACSCellFunction(torch.autograd.Function):
         gs, rs, stats = ctx.saved_tensors
         eps_v, T, eta, var_eps, dt_init, dt_max = ctx.hp
         du, dBc, dCc, dt, dlam, dlog, dD, deps = _train_bwd(
-            ctx.prep, gs, rs, stats, eps_v, T, eta, var_eps, dt_init, dt_max, g_ys, g_gs, g_rs, g_ns)
+            ctx.prep, gs, rs, stats, eps_v, T, eta, var_eps, dt_init, dt_max, g_ys, g_gs, g_rs, g_ns,
+            ctx.bwd_ws)
         u_t, B_t, C_t, t_t, lam_t, log_t, D_t, eps_t, eps_shape = ctx.dtypes
         deps_out = None
         if eps_t is not None:

@@ -118,3 +118,39 @@ def test_fused_gated_scan_api_and_bf16_u():
                           d["mean"], d["var"], 0.12, 1e-6, 1e-5, 1.0, 1e3, 0.1, 0,
                           g.detach().cpu().numpy(), gy, None, np.ones(r.shape, np.float32), None)
     assert relerr(lam.grad.cpu().numpy(), ref[4]) < GRAD_TOL
+
+
+@pytest.mark.parametrize("B,L,H,N,rate,T,mode", [
+    (2, 70, 768, 16, None, 0.1, "ste"),   # every frame commits: checkpoints from the speculative pass
+    (2, 45, 64, 16, 0.5, 0.3, "ste"),     # skips: checkpoints from l* on from the repair pass
+    (2, 33, 40, 32, 0.5, 0.4, "soft"),    # soft gate: every checkpoint from the repair pass
+])
+def test_forward_checkpoints_match_backward_pass(B, L, H, N, rate, T, mode):
+    """The backward from the checkpoints the forward wrote
+    (eacs_cell_train_fwd_ckpt / _bwd_ckpt) against the backward that runs its
+    own checkpoint pass: the same gradients up to rounding (the two compute the
+    checkpointed states with differently ordered arithmetic)."""
+    from eacs_b200 import _lib
+    from eacs_b200.ops.eacs_cell_train import _train_bwd, _train_fwd
+    d = cell_inputs(B, L, H, N, seed=B + L + H + N)
+    eps = 0.12 if rate is None else _calibrated(d, rate)
+    dev = "cuda:0"
+    tt = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in d.items()}
+    rng = np.random.default_rng(7)
+    gy = torch.from_numpy(rng.standard_normal((B, L, H)).astype(np.float32)).to(dev)
+    grs = torch.from_numpy(rng.standard_normal((B, L)).astype(np.float32)).to(dev)
+    args = (tt["u"], tt["Bc"], tt["Cc"], tt["t"], tt["lam"], tt["log_dt"], tt["D"], eps, tt["mean"], tt["var"],
+            T, 1e-6, 1e-5, 1.0, mode, 1e3)
+    ws = torch.empty(int(_lib.lib().eacs_cell_train_bwd_workspace_size(B, L, H, N)), dtype=torch.uint8,
+                     device=dev)
+    outs = []
+    for bwd_ws in (None, ws):
+        _, gs, rs, stats, prep = _train_fwd(*args, bwd_ws)
+        outs.append((gs, _train_bwd(prep, gs, rs, stats, eps, T, 1e-6, 1e-5, 1.0, 1e3, gy, None, grs, None,
+                                    bwd_ws)))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0][0], outs[1][0])
+    if rate is not None:
+        assert 0.0 < float(outs[0][0].mean()) < 1.0
+    for k, a, b in zip(NAMES, outs[0][1], outs[1][1]):
+        assert relerr(b.cpu().numpy(), a.cpu().numpy()) < 1e-5, (k, relerr(b.cpu().numpy(), a.cpu().numpy()))
