@@ -93,7 +93,7 @@ struct Args {
     float* gck_u;    // [B][gnK][H]
     float4* gck_row; // [B][gnK] (t_pi, -, -, -)
     float2* gck_bc;  // [B][gnK][2][N] (B_pi, C_pi)
-    int gK, gnK;
+    int gK, gnK, gKlog;  // gK = 1 << gKlog
     int B, L, H, N, ntiles, nK;
 };
 
@@ -332,19 +332,11 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                 else
                     delta = fmaxf(tl - t_prev, 0.f);
                 const float dte = eff_dt(delta, scale, a.dt_min, a.dt_max);
-                if (MODE == SPEC_CKPT && i < steps && (l0 + i) % a.gK == 0) {
+                if (MODE == SPEC_CKPT && i < steps && ((l0 + i) & (a.gK - 1)) == 0) {
                     // the state before step l under the all-commit assumption (rows
-                    // that skip get theirs from l* on rewritten by the repair pass);
-                    // B_pi is step l-1's B (step 0's own before the first step)
-                    const int l = l0 + i;
-                    float2 Bq[NPT];
-#pragma unroll
-                    for (int j = 0; j < NPT; ++j) {
-                        const int n = ln + LANES * j;
-                        Bq[j] = n < N ? a.Bc[(rowLH + (l > 0 ? l - 1 : 0)) * N + n] : make_float2(0.f, 0.f);
-                    }
-                    write_gck<LANES, NPT>(a, b, l / a.gK, h, ln, nv, hs, hv && ln == 0, u_prev,
-                                          tile == 0 && hl == 0, Bq, Cp, tile == 0 && tid == 0, t_prev);
+                    // that skip get theirs from l* on rewritten by the repair pass)
+                    write_gck<LANES, NPT>(a, b, (l0 + i) >> a.gKlog, h, ln, nv, hs, hv && ln == 0, u_prev,
+                                          tile == 0 && hl == 0, Bp, Cp, tile == 0 && tid == 0, t_prev);
                 }
                 float yp = 0.f, yhp = 0.f;
                 // Branch-free: channels past H stage u = 0 and padded chains
@@ -372,6 +364,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                             const float2 xh = cfma(E, Wp[j], P);
                             yhp += cre_mul(Cp[j], xh);
                             Wp[j] = W;
+                            if (MODE == SPEC_CKPT) Bp[j] = Bl;  // B_pi for the checkpoints
                         }
                     }
                     if (MODE == REPLAY)
@@ -949,8 +942,8 @@ __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int
             Bl[j] = sBl(buf, i)[ln + LANES * j];
             Cl[j] = sCl(buf, i)[ln + LANES * j];
         }
-        if (a.gck_h != nullptr && l % a.gK == 0)  // training checkpoint: the committed state before step l
-            write_gck<LANES, NPT>(a, b, l / a.gK, h, ln, nv, hs, hv && ln == 0, u_pi, crank == 0 && hl == 0, Bp,
+        if (a.gck_h != nullptr && (l & (a.gK - 1)) == 0)  // training checkpoint: the committed state before step l
+            write_gck<LANES, NPT>(a, b, l >> a.gKlog, h, ln, nv, hs, hv && ln == 0, u_pi, crank == 0 && hl == 0, Bp,
                                   Cp, crank == 0 && tid == 0, t_pi);
         const float dte = eff_dt(fmaxf(tl - t_pi, 0.f), scale, a.dt_min, a.dt_max);
         float2 P[NPT], dB[NPT], xh[NPT];
@@ -1388,8 +1381,8 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
     if (commits && c.gate_mode != 0)
         return fail(EACS_ERR_INVALID, "%s: commits are recorded for the hard gate only", fn);
     const bool ckpt = c.ck_h != nullptr;
-    if (ckpt && (!c.ck_u || !c.ck_row || !c.ck_bc || c.ck_K <= 0 || c.ck_nK <= 0))
-        return fail(EACS_ERR_INVALID, "%s: incomplete checkpoint layout", fn);
+    if (ckpt && (!c.ck_u || !c.ck_row || !c.ck_bc || c.ck_K <= 0 || (c.ck_K & (c.ck_K - 1)) || c.ck_nK <= 0))
+        return fail(EACS_ERR_INVALID, "%s: incomplete checkpoint layout (K a power of two)", fn);
     if (ckpt && (commits || rc_shape(static_cast<int>(c.H), static_cast<int>(c.N)).cl == 0))
         return fail(EACS_ERR_UNSUPPORTED, "%s: checkpoints need the cluster repair shape and no commits", fn);
     const bool carry = c.cin_h != nullptr || c.cout_h != nullptr;
@@ -1460,6 +1453,8 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
         a.gck_bc = static_cast<float2*>(c.ck_bc);
         a.gK = c.ck_K;
         a.gnK = c.ck_nK;
+        a.gKlog = 0;
+        while ((1 << a.gKlog) < a.gK) ++a.gKlog;
     }
     a.B = static_cast<int>(c.B);
     a.L = static_cast<int>(c.L);

@@ -81,7 +81,7 @@ struct TArgs {
     float* pD;            // [B][H]
     float* peps;          // [B]
     int B, L, H, N, nK, CL, HC;
-    int K;                // steps per checkpoint / recompute chunk
+    int K, Klog;          // steps per checkpoint / recompute chunk (K = 1 << Klog)
     int have_ckpt;        // the forward already wrote the checkpoints
 };
 
@@ -188,8 +188,8 @@ __global__ void __launch_bounds__(kCkThreads) train_ckpt(TArgs a) {
         }
         for (int i = 0; i < steps; ++i) {
             const int l = l0 + i;
-            if (l % a.K == 0) {
-                const int k = l / a.K;
+            if ((l & (a.K - 1)) == 0) {  // K is a power of two
+                const int k = l >> a.Klog;
 #pragma unroll
                 for (int j = 0; j < NPT; ++j)
                     if (nv[j]) a.ck_h[((static_cast<size_t>(b) * a.nK + k) * H + h) * N + ln + LANES * j] = hs[j];
@@ -986,6 +986,8 @@ int train_bwd(const TrainBwdCall& c, cudaStream_t stream) {
     a.CL = CL;
     a.HC = HC;
     a.have_ckpt = c.have_ckpt ? 1 : 0;
+    a.Klog = 0;
+    while ((1 << a.Klog) < a.K) ++a.Klog;
     cudaError_t e;
     if (c.u_dtype == EACS_DTYPE_F16) e = train_by_n<__half>(a, T, stream);
     else if (c.u_dtype == EACS_DTYPE_BF16) e = train_by_n<__nv_bfloat16>(a, T, stream);
