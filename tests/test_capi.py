@@ -65,6 +65,21 @@ def test_cell_rejects_bad_dtype_and_gate_mode():
     assert rc == _lib.EACS_ERR_INVALID
 
 
+def test_train_fwd_ckpt_rejects_missing_backward_workspace_without_device():
+    """The checkpoint-writing training forward needs the backward's workspace;
+    it is checked before anything touches the device."""
+    L = _lib.lib()
+    p = 16  # any non-null pointer value; rejected before use
+    B, Ln, H, N = 2, 16, 8, 16
+    need = L.eacs_cell_train_bwd_workspace_size(B, Ln, H, N)
+    assert need > 0
+    for ws, nbytes in ((None, 0), (p, need - 1)):
+        rc = L.eacs_cell_train_fwd_ckpt(p, p, p, 0, p, p, p, p, p, p, 0.1, 1e-6, 1e-5, 1.0, 1e-3, 1e3, 0, 0.1,
+                                        p, p, p, p, p, 1 << 30, ws, nbytes, B, Ln, H, N, None)
+        assert rc == _lib.EACS_ERR_WORKSPACE
+        assert "backward workspace" in _lib.last_error()
+
+
 def test_empty_shapes_are_noops():
     L = _lib.lib()
     assert L.eacs_scan_fwd(None, None, None, 0, 5, 3, 2, None) == _lib.EACS_OK
