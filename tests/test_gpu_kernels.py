@@ -95,7 +95,7 @@ def test_ssm_golden(name):
     _status_ok()
 
 
-@pytest.mark.parametrize("B,L,H,N", [(2, 512, 96, 16), (1, 300, 40, 32), (2, 77, 19, 64),
+@pytest.mark.parametrize("B,L,H,N", [(2, 512, 96, 16), (1, 300, 40, 32), (2, 130, 24, 20), (2, 77, 19, 64),
                                      (3, 64, 33, 3), (1, 40, 128, 8)])
 @pytest.mark.parametrize("u_dtype", ["f32", "f16", "bf16"])
 def test_ssm_vs_oracle(B, L, H, N, u_dtype):
@@ -163,6 +163,8 @@ def _calibrated_eps(d, rate, robust=None, margin=2e-4):
     (2, 96, 768, 16, None, None),        # config-1 channel count, all commit
     (2, 64, 768, 16, 0.5, None),         # gate-exercising
     (3, 80, 100, 32, 0.3, None),
+    (2, 70, 50, 24, 0.5, None),          # 16 < N < 32: four chains a thread, padded chains
+    (1, 41, 36, 17, None, None),
     (2, 50, 70, 64, 0.7, None),
     (2, 60, 45, 5, 0.5, (3, 2.0, 0.3)),
     (2, 60, 64, 16, 0.5, (1, 1.05, 0.5)),
