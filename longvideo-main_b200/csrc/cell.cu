@@ -38,6 +38,11 @@ namespace {
 #endif
 constexpr int kThreads = EACS_CHAIN_THREADS;  // chain kernel CTA
 constexpr int kMinBlocks = 768 / kThreads;    // keep 24 warps per SM resident
+// Wide speculative pass: one CTA of 11 warps per SM.  Four-warp CTAs leave
+// SMs unevenly loaded when a launch is a little over two CTAs per SM (B=8,
+// H=768: 384 CTAs on 148 SMs, so 88 SMs run 12 warps and 60 run 8); with
+// 44-channel tiles the same rows are 144 CTAs, every SM runs at most 11 warps.
+constexpr int kWideThreads = 352;
 constexpr int kT = 32;                         // steps per staged chunk
 constexpr int kRepair = 1024;  // repair kernel CTA
 
@@ -95,6 +100,7 @@ struct Args {
     float2* gck_bc;  // [B][gnK][2][N] (B_pi, C_pi)
     int gK, gnK, gKlog;  // gK = 1 << gKlog
     int B, L, H, N, ntiles, nK;
+    int wide;  // SPEC: 44-channel tiles of kWideThreads threads (wide_tiles)
 };
 
 // Checkpoint k = l / gK of row b from a thread owning chains n = ln + LANES*j
@@ -175,11 +181,12 @@ struct BflyShape {
 // transposed butterfly, after which the per-channel residual work of the U
 // steps is spread over the group's lanes instead of repeated by every lane.
 // ---------------------------------------------------------------------------
-template <int LANES, int NPT, int MODE, typename UT>
-__global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks * 2 / 3)) cell_chain(Args a) {
-    constexpr int HT = kThreads / LANES;
+template <int LANES, int NPT, int MODE, typename UT, int CT = kThreads>
+__global__ void __launch_bounds__(CT, (CT != kThreads ? 1 : NPT == 1 ? kMinBlocks : kMinBlocks * 2 / 3))
+    cell_chain(Args a) {
+    constexpr int HT = CT / LANES;
     constexpr int NP = LANES * NPT;
-    constexpr int NW = kThreads / 32;
+    constexpr int NW = CT / 32;
     constexpr int U = EACS_CHAIN_U;
     constexpr bool kSpec = MODE == SPEC || MODE == SPEC_COMMITS || MODE == SPEC_CKPT;  // speculative gated pass
     constexpr int NV = kSpec ? 2 * U : U;  // readout sums per group
@@ -189,12 +196,14 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
     // chunk inputs, double-buffered: chunk c+1 is copied in (cp.async) while
     // chunk c runs
     constexpr int NBUF = NP <= 32 ? 2 : 1;  // N > 32: one buffer (48 KB of static shared memory)
-    __shared__ float2 sB[NBUF][kT][NP];
-    __shared__ float2 sC[NBUF][kT][NP];
+    // (B, C) of a step and chain side by side: one 16-byte load per chain
+    __shared__ float4 sBC[NBUF][kT][NP];
     __shared__ __align__(16) UT su[NBUF][kT][HT];
     __shared__ float st[NBUF][kT];
-    __shared__ float sy[kT][HT];
-    __shared__ float2 sred[kT][NW];
+    // readouts and residual partials of a chunk, written out after the next
+    // chunk's first barrier (one barrier per chunk), so double-buffered
+    __shared__ float sy[2][kT][HT];
+    __shared__ float2 sred[2][kT][NW];
 
     const int tid = threadIdx.x;
     const int ln = tid % LANES;
@@ -267,40 +276,61 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                           (reinterpret_cast<uintptr_t>(a.t) & 3u) == 0;
     auto stage = [&](int c0, int buf, bool async) {
         const int sn = min(kT, lstop - c0);
-        for (int idx = tid; idx < sn * NP; idx += kThreads) {
-            const int i = idx / NP, n = idx % NP;  // NP, HT are powers of two
+        for (int idx = tid; idx < sn * NP; idx += CT) {
+            const int i = idx / NP, n = idx % NP;  // NP is a power of two
             const size_t o = (rowLH + c0 + i) * N + n;
+            float2* d = reinterpret_cast<float2*>(&sBC[buf][i][n]);
             if (async) {
-                cp_async8(&sB[buf][i][n], n < N ? a.Bc + o : a.Bc, n < N);
-                cp_async8(&sC[buf][i][n], n < N ? a.Cc + o : a.Cc, n < N);
+                cp_async8(d, n < N ? a.Bc + o : a.Bc, n < N);
+                cp_async8(d + 1, n < N ? a.Cc + o : a.Cc, n < N);
             } else {
-                sB[buf][i][n] = n < N ? a.Bc[o] : make_float2(0.f, 0.f);
-                sC[buf][i][n] = n < N ? a.Cc[o] : make_float2(0.f, 0.f);
+                d[0] = n < N ? a.Bc[o] : make_float2(0.f, 0.f);
+                d[1] = n < N ? a.Cc[o] : make_float2(0.f, 0.f);
             }
         }
         if (async) {
-            for (int idx = tid; idx < sn * (HT / PAIR); idx += kThreads) {
+            for (int idx = tid; idx < sn * (HT / PAIR); idx += CT) {
                 const int i = idx / (HT / PAIR), k = (idx % (HT / PAIR)) * PAIR;
                 const bool ok = h0 + k < H;  // a pair is both in or both past H (H, h0 even)
                 cp_async4(&su[buf][i][k], ok ? u + (rowLH + c0 + i) * H + h0 + k : u, ok);
             }
-            for (int i = tid; i < sn; i += kThreads) cp_async4(&st[buf][i], a.t + rowLH + c0 + i, true);
+            for (int i = tid; i < sn; i += CT) cp_async4(&st[buf][i], a.t + rowLH + c0 + i, true);
             cp_async_commit();
         } else {
-            for (int idx = tid; idx < sn * HT; idx += kThreads) {
+            for (int idx = tid; idx < sn * HT; idx += CT) {
                 const int i = idx / HT, k = idx % HT;
                 su[buf][i][k] = (h0 + k < H) ? u[(rowLH + c0 + i) * H + h0 + k] : static_cast<UT>(0.f);
             }
-            for (int i = tid; i < sn; i += kThreads) st[buf][i] = a.t[rowLH + c0 + i];
+            for (int i = tid; i < sn; i += CT) st[buf][i] = a.t[rowLH + c0 + i];
         }
     };
     if (async_ok && lstop > 0) stage(0, 0, true);
+    // y and the residual partials of the chunk at f0 from slot fb
+    auto flush = [&](int f0, int fsteps, int fb) {
+        for (int idx = tid; idx < fsteps * HT; idx += CT) {
+            const int i = idx / HT, k = idx % HT;
+            if (h0 + k < H) a.y[(rowLH + f0 + i) * H + h0 + k] = sy[fb][i][k];
+        }
+        if (kSpec) {
+            for (int i = tid; i < fsteps; i += CT) {
+                float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+                for (int w = 0; w < NW; ++w) {
+                    s1 += sred[fb][i][w].x;
+                    s2 += sred[fb][i][w].y;
+                }
+                a.part[(static_cast<size_t>(b) * a.ntiles + tile) * L + f0 + i] = make_float2(s1, s2);
+            }
+        }
+    };
 
     for (int l0 = 0, chunk = 0; l0 < lstop; l0 += kT, ++chunk) {
         const int steps = min(kT, lstop - l0);
         const int buf = chunk & (NBUF - 1);
+        const int ob = chunk & 1;           // output slot of this chunk
         if (async_ok) cp_async_wait_all();  // this thread's copies of chunk `chunk`
         __syncthreads();                    // everyone's, and the previous chunk is done
+        if (MODE != REPLAY && chunk > 0) flush(l0 - kT, kT, ob ^ 1);
         if (!async_ok) {
             stage(l0, buf, false);
             __syncthreads();
@@ -344,7 +374,8 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
 #pragma unroll
                 for (int j = 0; j < NPT; ++j) {
                     const int n = ln + LANES * j;
-                    const float2 Bl = sB[buf][i][n];
+                    const float4 bc = sBC[buf][i][n];
+                    const float2 Bl = make_float2(bc.x, bc.y);
                     float2 dA, P, hn, W;
                     if (MODE == UNGATED) {
                         float2 dB;
@@ -376,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                     if (MODE == SPEC_COMMITS && nv[j] && i < steps)
                         a.commit_h[((rowLH + l0 + i) * H + h) * N + n] = hn;
                     if (MODE != REPLAY) {
-                        const float2 Cl = sC[buf][i][n];
+                        const float2 Cl = make_float2(bc.z, bc.w);
                         yp += cre_mul(Cl, hs[j]);
                         if (kSpec) Cp[j] = Cl;
                     }
@@ -398,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                 const int orig = held + k;
                 const int i = i0 + (orig % U);
                 if (orig < U) {  // output readout of step i
-                    if (writer && hv && i < steps) sy[i][hl] = vals[k] + Dh * to_f32(su[buf][i][hl]);
+                    if (writer && hv && i < steps) sy[ob][i][hl] = vals[k] + Dh * to_f32(su[buf][i][hl]);
                 } else if (kSpec && writer && hv && i < steps) {  // prediction of step i
                     const float ul = to_f32(su[buf][i][hl]);
                     const float obs = (ul - mu) * rsd;
@@ -423,29 +454,16 @@ __global__ void __launch_bounds__(kThreads, (NPT == 1 ? kMinBlocks : kMinBlocks 
                     for (int k = 0; k < Shape::kRem; ++k) {
                         const int orig = held + k;
                         const int i = i0 + (orig % U);
-                        if (orig >= U && i < steps) sred[i][tid >> 5] = make_float2(r1[k], r2[k]);
+                        if (orig >= U && i < steps) sred[ob][i][tid >> 5] = make_float2(r1[k], r2[k]);
                     }
                 }
             }
         }
-        if (MODE != REPLAY) {
-            __syncthreads();
-            for (int idx = tid; idx < steps * HT; idx += kThreads) {
-                const int i = idx / HT, k = idx % HT;
-                if (h0 + k < H) a.y[(rowLH + l0 + i) * H + h0 + k] = sy[i][k];
-            }
-            if (kSpec) {
-                for (int i = tid; i < steps; i += kThreads) {
-                    float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-                    for (int w = 0; w < NW; ++w) {
-                        s1 += sred[i][w].x;
-                        s2 += sred[i][w].y;
-                    }
-                    a.part[(static_cast<size_t>(b) * a.ntiles + tile) * L + l0 + i] = make_float2(s1, s2);
-                }
-            }
-        }
+    }
+    if (MODE != REPLAY && lstop > 0) {  // the last chunk
+        __syncthreads();
+        const int last = (lstop - 1) / kT;
+        flush(last * kT, lstop - last * kT, last & 1);
     }
     if (MODE == REPLAY) {
 #pragma unroll
@@ -1239,11 +1257,11 @@ int lanes_for(int N, int* lanes, int* npt) {
     return 1;
 }
 
-template <int LANES, int NPT, int MODE, typename UT>
+template <int LANES, int NPT, int MODE, typename UT, int CT = kThreads>
 cudaError_t launch_chain(const Args& a, cudaStream_t s) {
     dim3 grid(a.ntiles, a.B);
     if (MODE != REPLAY) mark_start(s);
-    cell_chain<LANES, NPT, MODE, UT><<<grid, kThreads, 0, s>>>(a);
+    cell_chain<LANES, NPT, MODE, UT, CT><<<grid, CT, 0, s>>>(a);
     if (MODE != REPLAY) mark_stop(s);
     note_launch();
     return cudaGetLastError();
@@ -1253,6 +1271,9 @@ template <int MODE, typename UT>
 cudaError_t chain_by_n(const Args& a, cudaStream_t s) {
     int lanes, npt;
     lanes_for(a.N, &lanes, &npt);
+    if constexpr (MODE == SPEC) {
+        if (a.wide && lanes == 8 && npt == 2) return launch_chain<8, 2, MODE, UT, kWideThreads>(a, s);
+    }
 #if EACS_CHAIN_NPT == 4
     if (lanes == 4) return launch_chain<4, 4, MODE, UT>(a, s);
     if (lanes == 8) return launch_chain<8, 4, MODE, UT>(a, s);
@@ -1314,6 +1335,35 @@ int tiles_for(int H, int N) {
     lanes_for(N, &lanes, &npt);
     const int HT = kThreads / lanes;
     return (H + HT - 1) / HT;
+}
+
+int sm_count() {
+    static int cache[64];  // per device; a repeated query writes the same value
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+// Tiles of the wide speculative pass, or 0 where the four-warp layout is as
+// good: the wide one runs when its B x tiles CTAs fit one per SM and the
+// four-warp CTAs would put three or more on some SM (12+ warps against 11).
+// Its tiles never outnumber tiles_for's, so the workspace sized by that holds
+// its partial sums.
+int wide_tiles(int B, int H, int N) {
+    int lanes, npt;
+    lanes_for(N, &lanes, &npt);
+    if (lanes != 8 || npt != 2) return 0;
+    const int sms = sm_count();
+    if (sms <= 0) return 0;
+    const int64_t nt = (H + kWideThreads / 8 - 1) / (kWideThreads / 8);
+    const int64_t narrow = static_cast<int64_t>(B) * tiles_for(H, N);
+    if (static_cast<int64_t>(B) * nt > sms || narrow <= 2LL * sms) return 0;
+    return static_cast<int>(nt);
 }
 
 size_t align_up(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -1464,6 +1514,13 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
 
     cudaError_t e;
     if (c.gate_mode == 0) {
+        if (!commits && !ckpt) {
+            const int wt = wide_tiles(a.B, a.H, a.N);
+            if (wt > 0) {
+                a.wide = 1;
+                a.ntiles = wt;  // partial sums per row for cell_resid
+            }
+        }
         e = commits ? chain_dispatch<SPEC_COMMITS>(a, c.u_dtype, stream)
             : ckpt  ? chain_dispatch<SPEC_CKPT>(a, c.u_dtype, stream)
                     : chain_dispatch<SPEC>(a, c.u_dtype, stream);
@@ -1479,6 +1536,8 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
         if ((e = cudaMemsetAsync(a.row, 0, static_cast<size_t>(a.B) * sizeof(int4), stream)) != cudaSuccess)
             return cuda_check(e, fn);
     }
+    a.wide = 0;  // the replay pass covers the channels in four-warp tiles
+    a.ntiles = tiles_for(a.H, a.N);
     if ((e = chain_dispatch<REPLAY>(a, c.u_dtype, stream)) != cudaSuccess) return cuda_check(e, fn);
     if ((e = repair_dispatch(a, c.u_dtype, stream)) != cudaSuccess) return cuda_check(e, fn);
     if (commits) {

@@ -76,22 +76,25 @@ __device__ __forceinline__ void expm1_exp(float a, float& em1, float& ea) {
     em1 = fabsf(a) < 0.35f ? p : ea - 1.0f;
 }
 
-// sin b, cos b and 2 sin^2(b/2) = 1 - cos b.  Cody & Waite reduction
-// b = 2 pi k + r with a two-part float split of 2 pi applied by FMA
-// (|r| <= pi; each FMA rounds once; the dropped third part of 2 pi,
-// 6.9e-15, adds 6.9e-15 |k| to r, under 1e-7 of |r| unless |r| < 7e-8 |k|),
-// then with h = r/2:
+// sin b, cos b and 2 sin^2(b/2) = 1 - cos b from the half angle bh = b/2.
+// Cody & Waite reduction bh = pi k + h with a two-part float split of pi
+// applied by FMA (|h| <= pi/2; each FMA rounds once; the dropped third part
+// of pi, 3.4e-15, adds 3.4e-15 |k| to h, under 1e-7 of |h| unless
+// |h| < 3.4e-8 |k|); the constants are the exact halves of a split of 2 pi,
+// so h is bit for bit half of the full-angle remainder b - 2 pi k.  Then:
 // s = sin h from its Taylor series to h^11 (truncation below 6e-8 on
 // |h| <= pi/2, relative near 0) and c = cos h from the hardware cosine
 // (absolute error about 2^-21 on [-pi, pi]); finally sin b = 2 s c,
 // 2 sin^2(b/2) = 2 s^2, cos b = 1 - 2 s^2.  Every error term is proportional
 // to s, so expm1(z) built from these keeps its relative accuracy as |z| -> 0.
 // Branch-free, so unrolled steps and chains interleave.
-__device__ __forceinline__ void trig_half(float b, float& sb, float& cb, float& vb) {
-    const float k = rintf(b * 0.159154943f);  // 1/(2 pi)
-    float r = fmaf(-k, 6.28318548e+00f, b);    // 2 pi = hi + mid
-    r = fmaf(-k, -1.74845553e-07f, r);
-    const float h = 0.5f * r;
+__device__ __forceinline__ void trig_half(float bh, float& sb, float& cb, float& vb) {
+    constexpr float kInvPi = 2.0f * 0.159154943f;    // 2 / (2 pi)
+    constexpr float kPiHi = 0.5f * 6.28318548e+00f;  // (2 pi = hi + mid) / 2
+    constexpr float kPiMid = 0.5f * -1.74845553e-07f;
+    const float k = rintf(bh * kInvPi);
+    float h = fmaf(-k, kPiHi, bh);
+    h = fmaf(-k, kPiMid, h);
     const float h2 = h * h;
     // sin h = h + h^3 (-1/3! + h^2 (1/5! + h^2 (-1/7! + h^2 (1/9! - h^2/11!))))
     float ps = fmaf(h2, -2.50521084e-08f, 2.75573192e-06f);
@@ -114,10 +117,12 @@ __device__ __forceinline__ void trig_half(float b, float& sb, float& cb, float& 
 // fold 1/lam into the input term.
 __device__ __forceinline__ void zoh_e(float2 lam, float dte, float2& dA, float2& E) {
     const float a = lam.x * dte;
-    const float b = lam.y * dte;
+    // b/2 = (Im(lam)/2) dt, exactly half of Im(lam) dt; callers that keep lam
+    // in registers across steps compute Im(lam)/2 once
+    const float bh = (0.5f * lam.y) * dte;
     float em1, ea, sb, cb, vb;
     expm1_exp(a, em1, ea);
-    trig_half(b, sb, cb, vb);
+    trig_half(bh, sb, cb, vb);
     const float im = ea * sb;
     dA = make_float2(ea * cb, im);
     E = make_float2(fmaf(em1, cb, -vb), im);

@@ -180,6 +180,29 @@ def test_cell_vs_oracle(B, L, H, N, rate, robust):
     _status_ok()
 
 
+@pytest.mark.parametrize("B,L,H,N,rate,robust,u_dtype", [
+    (8, 48, 768, 16, None, None, torch.float16),         # config-1 rows: 18 tiles of 44 channels, last 20
+    (8, 40, 768, 16, 0.5, None, torch.float16),          # skips: replay and repair after the wide pass
+    (16, 40, 384, 16, 0.6, None, torch.float32),         # last tile 32 channels
+    (6, 40, 975, 16, 0.5, None, torch.float16),          # odd H: synchronous staging
+    (8, 40, 768, 12, 0.5, (3, 2.0, 0.3), torch.bfloat16),  # padded chains, robust_guard
+])
+def test_cell_wide_tiles(B, L, H, N, rate, robust, u_dtype):
+    """Row counts whose four-warp tiles put three or more CTAs on an SM run the
+    speculative pass as one 11-warp CTA per SM (44-channel tiles, B x tiles <=
+    SM count); results are the oracle's like every other layout."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    if sms == 148:
+        assert B * -(-H // 44) <= sms < B * -(-H // 16) / 2, "shape does not select the wide layout"
+    d = cell_inputs(B, L, H, N, seed=B + L + H + N)
+    d["u"] = _t(d["u"]).to(u_dtype).float().cpu().numpy()
+    eps = 0.12 if rate is None else _calibrated_eps(d, rate, robust)
+    ref = oracle.cell_fwd(**d, eps=eps, eta=1e-6, robust=robust)
+    got = _cell(d, u_dtype=u_dtype, eps=eps, eta=1e-6, robust=robust)
+    assert_cell_match(got, ref, eps, robust)
+    _status_ok()
+
+
 @pytest.mark.parametrize("u_dtype", [torch.float16, torch.bfloat16])
 def test_cell_half_inputs(u_dtype):
     d = cell_inputs(2, 70, 96, 16, seed=5)
