@@ -347,6 +347,24 @@ __global__ void __launch_bounds__(CT, (CT != kThreads ? 1 : NPT == 1 ? kMinBlock
                     if (nv[j]) a.ck[ko * N + ln + LANES * j] = hs[j];
             }
             float vals[NV];
+            // With one lane per step of a group (LANES == U), lane ln of each
+            // channel group forms the effective step of step i0 + ln (it
+            // depends on the row's times and the channel's scale only) and the
+            // group's lanes read it by shuffle, instead of every lane forming
+            // all U of them.
+            constexpr bool kLaneDt = LANES == U && MODE != REPLAY;
+            float dte_own = 0.f;
+            if constexpr (kLaneDt) {
+                const int i = i0 + ln;
+                const float tl = st[buf][i];
+                const float tp = ln == 0 ? t_prev : st[buf][i - 1];
+                float delta;
+                if (MODE == UNGATED)
+                    delta = (l0 + i == 0) ? dt0 : fmaxf(tl - tp, 0.f);
+                else
+                    delta = fmaxf(tl - tp, 0.f);
+                dte_own = eff_dt(delta, scale, a.dt_min, a.dt_max);
+            }
 #pragma unroll
             for (int uu = 0; uu < U; ++uu) {
                 const int i = i0 + uu;
@@ -354,19 +372,25 @@ __global__ void __launch_bounds__(CT, (CT != kThreads ? 1 : NPT == 1 ? kMinBlock
                 // whose final state is kept; elsewhere they compute values that
                 // are never stored (each butterfly sum stays within its step).
                 const bool act = MODE == REPLAY ? i < steps : true;
-                const float tl = act ? st[buf][i] : t_prev;
                 const float ul = act ? to_f32(su[buf][i][hl]) : 0.f;
-                float delta;
-                if (MODE == UNGATED)
-                    delta = (l0 + i == 0) ? dt0 : fmaxf(tl - t_prev, 0.f);
-                else
-                    delta = fmaxf(tl - t_prev, 0.f);
-                const float dte = eff_dt(delta, scale, a.dt_min, a.dt_max);
+                float dte, tl = 0.f;
+                if constexpr (kLaneDt) {
+                    dte = __shfl_sync(0xffffffffu, dte_own, (tid & 31 & ~(LANES - 1)) | uu);
+                } else {
+                    tl = act ? st[buf][i] : t_prev;
+                    float delta;
+                    if (MODE == UNGATED)
+                        delta = (l0 + i == 0) ? dt0 : fmaxf(tl - t_prev, 0.f);
+                    else
+                        delta = fmaxf(tl - t_prev, 0.f);
+                    dte = eff_dt(delta, scale, a.dt_min, a.dt_max);
+                }
                 if (MODE == SPEC_CKPT && i < steps && ((l0 + i) & (a.gK - 1)) == 0) {
                     // the state before step l under the all-commit assumption (rows
                     // that skip get theirs from l* on rewritten by the repair pass)
+                    const float t_pi = (kLaneDt && uu > 0) ? st[buf][i - 1] : t_prev;
                     write_gck<LANES, NPT>(a, b, (l0 + i) >> a.gKlog, h, ln, nv, hs, hv && ln == 0, u_prev,
-                                          tile == 0 && hl == 0, Bp, Cp, tile == 0 && tid == 0, t_prev);
+                                          tile == 0 && hl == 0, Bp, Cp, tile == 0 && tid == 0, t_pi);
                 }
                 float yp = 0.f, yhp = 0.f;
                 // Branch-free: channels past H stage u = 0 and padded chains
@@ -416,9 +440,10 @@ __global__ void __launch_bounds__(CT, (CT != kThreads ? 1 : NPT == 1 ? kMinBlock
                 if (kSpec) vals[U + uu] = yhp;
                 if (act) {
                     u_prev = ul;
-                    t_prev = tl;
+                    if constexpr (!kLaneDt) t_prev = tl;
                 }
             }
+            if constexpr (kLaneDt) t_prev = st[buf][i0 + U - 1];
             if (MODE == REPLAY) continue;
             Bfly<NV, LANES / 2>::run(vals, ln);
             float r1[Shape::kRem], r2[Shape::kRem];

@@ -59,15 +59,19 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
-// e^a and e^a - 1.  e^a from the hardware base-2 exponential (about 2^-22
-// relative).  e^a - 1 from it when |a| >= 0.35, where the subtraction loses at
+// e^a, 2 e^a and e^a - 1.  2 e^a = 2^(a log2(e) + 1) from the hardware
+// base-2 exponential (about 2^-22 relative; for a <= 0 the argument's
+// rounding adds at most 2^-25 absolute, 2.1e-8 relative to the result), so
+// the factor 2 costs no multiply, and e^a as its exact half.  e^a - 1 from it
+// when |a| >= 0.35, where the subtraction loses at
 // most a factor 2.4 of that (a = Re(lam) dt <= 0: 6e-7 relative at a = -0.35),
 // and below from the Taylor series of expm1 to a^6 (alternating for a < 0, so
 // the error is under the first dropped term, |a|^7/7! / |expm1(a)| < 4.3e-7
 // at a = -0.35 and shrinking fast below), which keeps small |a| -- the slow
 // modes, where dB_bar ~ dt -- relatively exact.
-__device__ __forceinline__ void expm1_exp(float a, float& em1, float& ea) {
-    ea = ex2_approx(a * 1.44269504f);  // log2(e)
+__device__ __forceinline__ void expm1_exp(float a, float& em1, float& ea, float& ea2) {
+    ea2 = ex2_approx(fmaf(a, 1.44269504f, 1.0f));  // log2(e)
+    ea = 0.5f * ea2;
     float p = fmaf(a, 1.38888889e-03f, 8.33333333e-03f);  // 1/6!, 1/5!
     p = fmaf(a, p, 4.16666667e-02f);                      // 1/4!
     p = fmaf(a, p, 1.66666667e-01f);                      // 1/3!
@@ -76,7 +80,8 @@ __device__ __forceinline__ void expm1_exp(float a, float& em1, float& ea) {
     em1 = fabsf(a) < 0.35f ? p : ea - 1.0f;
 }
 
-// sin b, cos b and 2 sin^2(b/2) = 1 - cos b from the half angle bh = b/2.
+// s = sin h and c = cos h of the reduced half angle h = b/2 - pi k (both
+// carry the sign (-1)^k, which cancels in s c and s^2).
 // Cody & Waite reduction bh = pi k + h with a two-part float split of pi
 // applied by FMA (|h| <= pi/2; each FMA rounds once; the dropped third part
 // of pi, 3.4e-15, adds 3.4e-15 |k| to h, under 1e-7 of |h| unless
@@ -84,11 +89,11 @@ __device__ __forceinline__ void expm1_exp(float a, float& em1, float& ea) {
 // so h is bit for bit half of the full-angle remainder b - 2 pi k.  Then:
 // s = sin h from its Taylor series to h^11 (truncation below 6e-8 on
 // |h| <= pi/2, relative near 0) and c = cos h from the hardware cosine
-// (absolute error about 2^-21 on [-pi, pi]); finally sin b = 2 s c,
-// 2 sin^2(b/2) = 2 s^2, cos b = 1 - 2 s^2.  Every error term is proportional
-// to s, so expm1(z) built from these keeps its relative accuracy as |z| -> 0.
-// Branch-free, so unrolled steps and chains interleave.
-__device__ __forceinline__ void trig_half(float bh, float& sb, float& cb, float& vb) {
+// (absolute error about 2^-21 on [-pi, pi]).  The caller forms sin b = 2 s c,
+// 1 - cos b = 2 s^2; every error term is proportional to s, so expm1(z) built
+// from these keeps its relative accuracy as |z| -> 0.  Branch-free, so
+// unrolled steps and chains interleave.
+__device__ __forceinline__ void trig_half(float bh, float& s, float& c) {
     constexpr float kInvPi = 2.0f * 0.159154943f;    // 2 / (2 pi)
     constexpr float kPiHi = 0.5f * 6.28318548e+00f;  // (2 pi = hi + mid) / 2
     constexpr float kPiMid = 0.5f * -1.74845553e-07f;
@@ -101,18 +106,16 @@ __device__ __forceinline__ void trig_half(float bh, float& sb, float& cb, float&
     ps = fmaf(h2, ps, -1.98412698e-04f);
     ps = fmaf(h2, ps, 8.33333333e-03f);
     ps = fmaf(h2, ps, -1.66666667e-01f);
-    const float s = fmaf(h * h2, ps, h);
-    const float c = __cosf(h);
-    const float s2 = s + s;
-    sb = s2 * c;
-    vb = s2 * s;
-    cb = 1.0f - vb;
+    s = fmaf(h * h2, ps, h);
+    c = __cosf(h);
 }
 
 // Zero-order-hold kernels of one chain (discretization.py:20-36):
 //   z = lam * dt,  dA = e^z,  dB_bar = expm1(z) / lam
 // with expm1(z) = (expm1(a) cos b - 2 sin^2(b/2), e^a sin b), the branch-free
-// form of discretization.py:10-17.
+// form of discretization.py:10-17, here as (expm1(a) - 2 e^a s^2, 2 e^a s c)
+// and e^z = (e^a - 2 e^a s^2, 2 e^a s c) with s, c the half-angle sine and
+// cosine (cos b = 1 - 2 s^2, sin b = 2 s c).
 // zoh_e returns expm1(z) itself (E, with dB_bar = E / lam), for callers that
 // fold 1/lam into the input term.
 __device__ __forceinline__ void zoh_e(float2 lam, float dte, float2& dA, float2& E) {
@@ -120,12 +123,13 @@ __device__ __forceinline__ void zoh_e(float2 lam, float dte, float2& dA, float2&
     // b/2 = (Im(lam)/2) dt, exactly half of Im(lam) dt; callers that keep lam
     // in registers across steps compute Im(lam)/2 once
     const float bh = (0.5f * lam.y) * dte;
-    float em1, ea, sb, cb, vb;
-    expm1_exp(a, em1, ea);
-    trig_half(bh, sb, cb, vb);
-    const float im = ea * sb;
-    dA = make_float2(ea * cb, im);
-    E = make_float2(fmaf(em1, cb, -vb), im);
+    float em1, ea, ea2, s, c;
+    expm1_exp(a, em1, ea, ea2);
+    trig_half(bh, s, c);
+    const float t = s * s;
+    const float im = (ea2 * s) * c;
+    dA = make_float2(fmaf(-ea2, t, ea), im);
+    E = make_float2(fmaf(-ea2, t, em1), im);
 }
 __device__ __forceinline__ void zoh(float2 lam, float2 ilam, float dte, float2& dA, float2& dBbar) {
     float2 E;
