@@ -50,8 +50,8 @@ ALG_BYTES = B * L * H * 2 + 2 * B * L * N * 8 + B * L * 4 + B * L * H * 4 + 2 * 
 E2E_CHUNK = 512
 # Issue slots per state update of cell_chain<SPEC> at this workload (one
 # 352-thread CTA per SM): ncu smsp__inst_executed.sum x 32 / updates
-# = 958,370,648 x 32 / 402,653,184.
-INSTR_PER_UPDATE = 76.2
+# = 927,565,016 x 32 / 402,653,184.
+INSTR_PER_UPDATE = 73.7
 CONFIG = {
     "workload": "gated EACS cell inference forward (event gate + ZOH predict/update + commit), "
                 "B=8 L=4096 H=768 N=16",
