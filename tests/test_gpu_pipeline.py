@@ -51,7 +51,8 @@ def _run_dev(d, eps, robust=None, u_dtype=torch.float32):
 
 
 @pytest.mark.parametrize("B,L,H,N,chunk", [(3, 300, 96, 16, 64), (2, 256, 768, 16, 32),
-                                           (2, 100, 40, 32, 512), (4, 97, 24, 5, 32)])
+                                           (2, 100, 40, 32, 512), (4, 97, 24, 5, 32),
+                                           (8, 256, 768, 16, 64)])  # 8 rows of 768: wide speculative pass
 def test_host_pipeline_all_commit_bit_exact(B, L, H, N, chunk):
     d = cell_inputs(B, L, H, N, seed=B * L + H)
     host = _run_host(d, 0.12, chunk)
@@ -96,6 +97,23 @@ def test_host_pipeline_wide_rows_with_skips():
     d = cell_inputs(2, 64, 2048, 32, seed=21, tau=(0.5, 64.0))
     eps = _calibrated_eps(d, 0.5)
     host = _run_host(d, eps, 16)
+    ref = oracle.cell_fwd(**d, eps=eps, eta=1e-6)
+    dev = _run_dev(d, eps)
+    assert np.array_equal(host[1], ref[1]) and np.array_equal(dev[1], ref[1])
+    assert relerr(host[0], ref[0]) < 1e-4 and relerr(host[2], ref[2]) < 1e-4
+    assert relerr(host[0], dev[0]) < 1e-5 and relerr(host[2], dev[2]) < 1e-5
+    assert 0.0 < host[1].mean() < 1.0
+
+
+def test_host_pipeline_one_cta_per_sm_with_skips():
+    """8 rows of 768 channels (the speculative pass in one 11-warp CTA per SM)
+    with skips: every chunk resumes from the carried state the wide pass or the
+    repair pass left."""
+    from test_gpu_kernels import _calibrated_eps
+    B, L, H, N = 8, 96, 768, 16
+    d = cell_inputs(B, L, H, N, seed=77)
+    eps = _calibrated_eps(d, 0.5)
+    host = _run_host(d, eps, 32)
     ref = oracle.cell_fwd(**d, eps=eps, eta=1e-6)
     dev = _run_dev(d, eps)
     assert np.array_equal(host[1], ref[1]) and np.array_equal(dev[1], ref[1])
