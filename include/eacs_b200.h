@@ -166,6 +166,27 @@ EACS_API int eacs_cell_fwd(const void* lam, const float* log_dt, const void* u, 
                   void* workspace, size_t workspace_bytes,
                   int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
 
+/* eacs_cell_fwd for a caller that runs cells_side_by_side cells of this
+ * shape at the same time on separate streams, this one included (the
+ * branches of MultiScaleEACS, modules/multiscale.py:162-179, which the
+ * reference runs one after another).  Same arguments, workspace and
+ * results as eacs_cell_fwd (outputs equal to its tolerance: the layout
+ * changes the order of the residual and readout sums); the count only picks
+ * the layout of the speculative pass, so that the cells' CTAs together fit
+ * the GPU in one wave.  cells_side_by_side < 1 is EACS_ERR_INVALID; 1 is
+ * eacs_cell_fwd. */
+EACS_API int eacs_cell_fwd_side_by_side(const void* lam, const float* log_dt, const void* u,
+                  int u_dtype, const void* Bc, const void* Cc, const float* t, const float* D,
+                  const float* mean, const float* var,
+                  float eps, float eta, float var_eps, float dt_init,
+                  float dt_min, float dt_max,
+                  int robust, int robust_k, float spike_ratio, float eps_factor,
+                  int gate_mode, float temperature,
+                  float* y, float* gate, float* resid,
+                  void* workspace, size_t workspace_bytes,
+                  int64_t B, int64_t L, int64_t H, int64_t N, int cells_side_by_side,
+                  void* stream);
+
 /* Training forward of the gated cell: eacs_cell_fwd plus, in `stats`
  * (B,L,2) float32, the two norms of each step's residual
  * (||obs - pred||, ||obs||) that the backward needs.  gate_mode 0 gives the

@@ -137,6 +137,24 @@ int eacs_cell_fwd(const void* lam, const float* log_dt, const void* u, int u_dty
     return eacs::cell_fwd(c, static_cast<cudaStream_t>(stream));
 }
 
+int eacs_cell_fwd_side_by_side(const void* lam, const float* log_dt, const void* u, int u_dtype,
+                               const void* Bc, const void* Cc, const float* t, const float* D,
+                               const float* mean, const float* var, float eps, float eta,
+                               float var_eps, float dt_init, float dt_min, float dt_max, int robust,
+                               int robust_k, float spike_ratio, float eps_factor, int gate_mode,
+                               float temperature, float* y, float* gate, float* resid,
+                               void* workspace, size_t workspace_bytes, int64_t B, int64_t L,
+                               int64_t H, int64_t N, int cells_side_by_side, void* stream) {
+    if (cells_side_by_side < 1)
+        return eacs::fail(EACS_ERR_INVALID, "eacs_cell_fwd_side_by_side: cells_side_by_side must be >= 1");
+    eacs::CellCall c{lam,  log_dt, u,       u_dtype, Bc,     Cc,          t,           D,
+                     mean, var,    eps,     eta,     var_eps, dt_init,    dt_min,      dt_max,
+                     robust, robust_k, spike_ratio, eps_factor, gate_mode, temperature, y, gate,
+                     resid, workspace, workspace_bytes, B, L, H, N};
+    c.side_by_side = cells_side_by_side;
+    return eacs::cell_fwd(c, static_cast<cudaStream_t>(stream));
+}
+
 int eacs_cell_train_fwd(const void* lam, const float* log_dt, const void* u, int u_dtype, const void* Bc,
                         const void* Cc, const float* t, const float* D, const float* mean,
                         const float* var, float eps, float eta, float var_eps, float dt_init,

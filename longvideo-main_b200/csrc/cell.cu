@@ -100,7 +100,8 @@ struct Args {
     float2* gck_bc;  // [B][gnK][2][N] (B_pi, C_pi)
     int gK, gnK, gKlog;  // gK = 1 << gKlog
     int B, L, H, N, ntiles, nK;
-    int wide;  // SPEC: 44-channel tiles of kWideThreads threads (wide_tiles)
+    int wide;     // SPEC: 44-channel tiles of kWideThreads threads (wide_tiles)
+    int chains4;  // SPEC: four chains a thread, 32-channel tiles (side_by_side_tiles)
 };
 
 // Checkpoint k = l / gK of row b from a thread owning chains n = ln + LANES*j
@@ -1298,6 +1299,7 @@ cudaError_t chain_by_n(const Args& a, cudaStream_t s) {
     lanes_for(a.N, &lanes, &npt);
     if constexpr (MODE == SPEC) {
         if (a.wide && lanes == 8 && npt == 2) return launch_chain<8, 2, MODE, UT, kWideThreads>(a, s);
+        if (a.chains4 && lanes == 8 && npt == 2) return launch_chain<4, 4, MODE, UT>(a, s);
     }
 #if EACS_CHAIN_NPT == 4
     if (lanes == 4) return launch_chain<4, 4, MODE, UT>(a, s);
@@ -1389,6 +1391,26 @@ int wide_tiles(int B, int H, int N) {
     const int64_t narrow = static_cast<int64_t>(B) * tiles_for(H, N);
     if (static_cast<int64_t>(B) * nt > sms || narrow <= 2LL * sms) return 0;
     return static_cast<int>(nt);
+}
+
+// Tiles of the four-chains-a-thread speculative pass for k cells of this
+// shape run side by side, or 0: it runs when the k cells' four-warp CTAs of
+// two chains a thread are more than the SMs hold at once (four each at 128
+// registers), so a thin second wave would follow, and the four-chain CTAs
+// (half as many) fit in one.  A lone cell keeps its own layout: halving its
+// CTAs would leave SMs idle.
+int side_by_side_tiles(int k, int B, int H, int N) {
+    int lanes, npt;
+    lanes_for(N, &lanes, &npt);
+    if (k <= 1 || lanes != 8 || npt != 2) return 0;
+    const int sms = sm_count();
+    if (sms <= 0) return 0;
+    const int64_t t4 = (H + kThreads / 4 - 1) / (kThreads / 4);
+    const int64_t cap = 4LL * sms;
+    const int64_t two = static_cast<int64_t>(k) * B * tiles_for(H, N);
+    const int64_t four = static_cast<int64_t>(k) * B * t4;
+    if (two <= cap || four > cap) return 0;
+    return static_cast<int>(t4);
 }
 
 size_t align_up(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -1540,8 +1562,12 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
     cudaError_t e;
     if (c.gate_mode == 0) {
         if (!commits && !ckpt) {
-            const int wt = wide_tiles(a.B, a.H, a.N);
-            if (wt > 0) {
+            const int st4 = side_by_side_tiles(c.side_by_side, a.B, a.H, a.N);
+            const int wt = c.side_by_side > 1 ? 0 : wide_tiles(a.B, a.H, a.N);
+            if (st4 > 0) {
+                a.chains4 = 1;
+                a.ntiles = st4;
+            } else if (wt > 0) {
                 a.wide = 1;
                 a.ntiles = wt;  // partial sums per row for cell_resid
             }
@@ -1562,6 +1588,7 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
             return cuda_check(e, fn);
     }
     a.wide = 0;  // the replay pass covers the channels in four-warp tiles
+    a.chains4 = 0;
     a.ntiles = tiles_for(a.H, a.N);
     if ((e = chain_dispatch<REPLAY>(a, c.u_dtype, stream)) != cudaSuccess) return cuda_check(e, fn);
     if ((e = repair_dispatch(a, c.u_dtype, stream)) != cudaSuccess) return cuda_check(e, fn);

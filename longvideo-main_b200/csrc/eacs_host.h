@@ -80,6 +80,9 @@ struct CellCall {
     void* ck_row = nullptr;  // [B][nK] float4 (t_pi, -, -, -)
     void* ck_bc = nullptr;   // [B][nK][2][N] complex64 (B_pi, C_pi)
     int ck_K = 0, ck_nK = 0;
+    // cells of this shape the caller runs at the same time on other streams
+    // (this one included); it picks the speculative pass's layout
+    int side_by_side = 1;
 };
 size_t cell_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
 size_t cell_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);

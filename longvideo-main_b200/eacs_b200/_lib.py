@@ -71,6 +71,10 @@ SIGNATURES = {
     "eacs_cell_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
                            _F, _F, _F, _F, _F, _F, _I, _I, _F, _F, _I, _F,
                            _P, _P, _P, _P, ctypes.c_size_t, _I64, _I64, _I64, _I64, _P]),
+    "eacs_cell_fwd_side_by_side": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
+                                        _F, _F, _F, _F, _F, _F, _I, _I, _F, _F, _I, _F,
+                                        _P, _P, _P, _P, ctypes.c_size_t, _I64, _I64, _I64, _I64,
+                                        _I, _P]),
     "eacs_cell_train_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
                                  _F, _F, _F, _F, _F, _F, _I, _F,
                                  _P, _P, _P, _P, _P, ctypes.c_size_t, _I64, _I64, _I64, _I64, _P]),

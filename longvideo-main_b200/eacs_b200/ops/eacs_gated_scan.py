@@ -12,6 +12,9 @@ reference casts it to float32 first; the values are the same).  y is float32.
 """
 from __future__ import annotations
 
+import contextlib
+import contextvars
+
 import torch
 from torch import Tensor
 
@@ -33,6 +36,23 @@ def workspace_bytes(B: int, L: int, H: int, N: int) -> int:
     return int(_lib.lib().eacs_cell_fwd_workspace_size(B, L, H, N))
 
 
+# Cells the caller is launching side by side on separate streams (the
+# branches of a MultiScaleEACS forward); set by side_by_side().
+_SIDE_BY_SIDE = contextvars.ContextVar("eacs_cells_side_by_side", default=1)
+
+
+@contextlib.contextmanager
+def side_by_side(n: int):
+    """Cells launched inside this block run n at a time on separate streams:
+    eacs_cell_forward then lays out the speculative pass so that the n cells
+    together fit the GPU in one wave (eacs_cell_fwd_side_by_side)."""
+    tok = _SIDE_BY_SIDE.set(max(1, int(n)))
+    try:
+        yield
+    finally:
+        _SIDE_BY_SIDE.reset(tok)
+
+
 def cell_forward_into(lam, log_dt_scale, u, Bc, Cc, t, D, mean, var, eps, eta, var_eps,
                       dt_init, dt_min, dt_max, robust, gate_mode, temperature,
                       y, gates, resid, workspace):
@@ -40,15 +60,20 @@ def cell_forward_into(lam, log_dt_scale, u, Bc, Cc, t, D, mean, var, eps, eta, v
     B, L, H = u.shape
     N = lam.shape[1]
     rb, rk, rr, rf = _robust_tuple(robust)
-    _lib.check(_lib.lib().eacs_cell_fwd(
-        lam.data_ptr(), log_dt_scale.data_ptr(), u.data_ptr(), _lib.DTYPE_CODES[u.dtype],
-        Bc.data_ptr(), Cc.data_ptr(), t.data_ptr(), D.data_ptr(), mean.data_ptr(), var.data_ptr(),
-        float(eps), float(eta), float(var_eps), float(dt_init), float(dt_min), float(dt_max),
-        rb, rk, rr, rf, 1 if gate_mode == "soft" else 0, float(temperature),
-        y.data_ptr(), gates.data_ptr(), resid.data_ptr(),
-        workspace.data_ptr() if workspace is not None else None,
-        workspace.numel() if workspace is not None else 0,
-        B, L, H, N, _lib.stream_ptr(u.device)), "eacs_cell_fwd")
+    args = (lam.data_ptr(), log_dt_scale.data_ptr(), u.data_ptr(), _lib.DTYPE_CODES[u.dtype],
+            Bc.data_ptr(), Cc.data_ptr(), t.data_ptr(), D.data_ptr(), mean.data_ptr(), var.data_ptr(),
+            float(eps), float(eta), float(var_eps), float(dt_init), float(dt_min), float(dt_max),
+            rb, rk, rr, rf, 1 if gate_mode == "soft" else 0, float(temperature),
+            y.data_ptr(), gates.data_ptr(), resid.data_ptr(),
+            workspace.data_ptr() if workspace is not None else None,
+            workspace.numel() if workspace is not None else 0,
+            B, L, H, N)
+    k = _SIDE_BY_SIDE.get()
+    if k > 1:
+        _lib.check(_lib.lib().eacs_cell_fwd_side_by_side(*args, k, _lib.stream_ptr(u.device)),
+                   "eacs_cell_fwd_side_by_side")
+    else:
+        _lib.check(_lib.lib().eacs_cell_fwd(*args, _lib.stream_ptr(u.device)), "eacs_cell_fwd")
 
 
 def prepare(lam, log_dt_scale, u, Bc, Cc, t, D, mean, var):

@@ -20,6 +20,7 @@ from torch import Tensor
 
 from .. import _lib
 from ._check import cuda_tensors, require
+from .eacs_gated_scan import side_by_side
 
 
 def fuse_supported(x: Tensor, n_branch: int) -> bool:
@@ -70,14 +71,16 @@ def branch_streams(dev: torch.device, n: int):
 def run_branches(branches, dev: torch.device, fn):
     """fn(i, branch) for every branch, each on its own stream, joined back to
     the current stream.  One branch's gated cell (B rows x H/16 channel tiles)
-    fills a fraction of the SMs; side by side the branches share them.
+    fills a fraction of the SMs; side by side the branches share them, and
+    the cells launched here are told how many run at once (side_by_side).
     Tensors the calls return are marked as used by the current stream."""
     cur = torch.cuda.current_stream(dev)
     outs = []
-    for i, (br, s) in enumerate(zip(branches, branch_streams(dev, len(branches)))):
-        s.wait_stream(cur)
-        with torch.cuda.stream(s):
-            outs.append(fn(i, br))
+    with side_by_side(len(branches)):
+        for i, (br, s) in enumerate(zip(branches, branch_streams(dev, len(branches)))):
+            s.wait_stream(cur)
+            with torch.cuda.stream(s):
+                outs.append(fn(i, br))
     for s in branch_streams(dev, len(branches)):
         cur.wait_stream(s)
     for o in outs:

@@ -233,3 +233,41 @@ def test_cell_repeatable_and_decreasing_time():
     for o in outs[1:]:
         for x, y in zip(outs[0], o):
             assert np.array_equal(x, y)
+
+
+def test_cells_side_by_side():
+    """Three cells of B=4, H=1024, N=16 launched side by side on their own
+    streams (MultiScaleEACS's branches at config 2's width) are told so and
+    run the speculative pass with four chains a thread, so their CTAs fit the
+    GPU in one wave.  Each matches the oracle like a lone call, with and
+    without skips, and a count below 1 is rejected."""
+    from eacs_b200.ops.eacs_gated_scan import side_by_side
+    from eacs_b200.ops.multiscale import run_branches
+    B, L, H, N = 4, 48, 1024, 16
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    if sms == 148:
+        assert 3 * B * (H // 16) > 4 * sms >= 3 * B * (H // 32), "shape does not select the layout"
+    ds = [cell_inputs(B, L, H, N, seed=300 + k) for k in range(3)]
+    epss = [0.12, _calibrated_eps(ds[1], 0.5), 0.12]
+    refs = [oracle.cell_fwd(**d, eps=e, eta=1e-6) for d, e in zip(ds, epss)]
+    outs = run_branches(list(range(3)), torch.device(DEV),
+                        lambda i, _: eacs_cell_forward(
+                            _t(ds[i]["lam"]), _t(ds[i]["log_dt"]), _t(ds[i]["u"]), _t(ds[i]["Bc"]),
+                            _t(ds[i]["Cc"]), _t(ds[i]["t"]), _t(ds[i]["D"]), _t(ds[i]["mean"]),
+                            _t(ds[i]["var"]), eps=epss[i], eta=1e-6))
+    torch.cuda.synchronize()
+    for o, ref, d, e in zip(outs, refs, ds, epss):
+        got = tuple(x.cpu().numpy() for x in o)
+        assert_cell_match(got, ref, e, None)
+        alone = _cell(d, eps=e, eta=1e-6)
+        assert np.array_equal(got[1], alone[1])
+        assert relerr(got[0], alone[0]) < 1e-5 and relerr(got[2], alone[2]) < 1e-5
+    assert 0.0 < refs[1][1].mean() < 1.0
+    _status_ok()
+    with side_by_side(0):  # clamped to 1 on the Python side: a lone call
+        y = _cell(ds[0], eps=0.12, eta=1e-6)[0]
+    assert np.array_equal(y, _cell(ds[0], eps=0.12, eta=1e-6)[0])
+    args = ([None, None, None, 0] + [None] * 6 + [0.0] * 6 + [0, 3, 2.0, 0.3, 0, 0.1]
+            + [None] * 4 + [0, 1, 1, 1, 1, 0, None])
+    rc = _lib.lib().eacs_cell_fwd_side_by_side(*args)
+    assert rc != 0 and b"cells_side_by_side" in _lib.lib().eacs_last_error()
