@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(CT, (CT != kThreads ? 1 : NPT == 1 ? kMinBlock
             // depends on the row's times and the channel's scale only) and the
             // group's lanes read it by shuffle, instead of every lane forming
             // all U of them.
-            constexpr bool kLaneDt = LANES == U && MODE != REPLAY;
+            constexpr bool kLaneDt = LANES == U && NPT == 2 && MODE != REPLAY && MODE != SPEC_COMMITS;
             float dte_own = 0.f;
             if constexpr (kLaneDt) {
                 const int i = i0 + ln;
