@@ -93,6 +93,38 @@ def cell_inputs(g, B, L, H, N, tau, dev, u_dtype, mean_dt=0.25):
     return {k: v.to(dev) for k, v in d.items()}
 
 
+def train_inputs(rank, dev, B=8, L=8192, H=768, N=16):
+    """Gated-cell training inputs (tau band [0.5, 4] s, bf16 u, Exp(0.25 s)
+    frame gaps) and the upstream gradient dL/dy ~ N(0,1) for one rank."""
+    g = torch.Generator().manual_seed(9 + rank)
+    d = cell_inputs(g, B, L, H, N, (0.5, 4.0), dev, torch.bfloat16)
+    gy = torch.randn(B, L, H, generator=g).to(dev)
+    return d, gy
+
+
+MULTISCALE_SHAPE = (4, 16384, 1024, 16)
+MULTISCALE_BANDS = [(0.5, 4.0), (4.0, 32.0), (32.0, 256.0)]
+
+
+def multiscale_inputs(dev, B=None, L=None):
+    """MultiScaleEACS inputs: the layer input x (bf16) and one op-boundary set
+    per branch (tau bands [0.5,4], [4,32], [32,256] s, bf16 u); every branch
+    sees the same timestamps (one video).  B, L below the full shape take
+    the leading rows and frames of the same draw."""
+    B0, L0, H, N = MULTISCALE_SHAPE
+    g = torch.Generator().manual_seed(10)
+    x = torch.randn(B0, L0, H, generator=g).to(torch.bfloat16)
+    br = [cell_inputs(g, B0, L0, H, N, tb, "cpu", torch.bfloat16) for tb in MULTISCALE_BANDS]
+    for d in br:
+        d["t"] = br[0]["t"]
+    B, L = B or B0, L or L0
+
+    def cut(k, v):
+        return v[:B, :L].contiguous() if k in ("u", "Bc", "Cc", "t") else v
+    br = [{k: cut(k, v).to(dev) for k, v in d.items()} for d in br]
+    return x[:B, :L].contiguous().to(dev), br
+
+
 def line(metric, value, steps, warmup, ms, config, **extra):
     out = {"metric": metric, "value": value, "unit": UNIT, "n_gpus": 1, "steps": steps,
            "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -296,9 +328,7 @@ def wl_train(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     B, L, H, N = (8, 8192, 768, 16) if getattr(args, "shape", None) is None else (int(v) for v in args.shape.split(","))
-    g = torch.Generator().manual_seed(9 + rank)
-    d = cell_inputs(g, B, L, H, N, (0.5, 4.0), dev, torch.bfloat16)
-    gy = torch.randn(B, L, H, generator=g).to(dev)
+    d, gy = train_inputs(rank, dev, B, L, H, N)
     leaves = {k: d[k].clone().requires_grad_(True) for k in ("u", "Bc", "Cc", "lam", "log_dt", "D")}
     eps = torch.tensor(0.12, device=dev, requires_grad=True)
 
@@ -366,13 +396,9 @@ def wl_multiscale(args, dev, flush):
     proj_out, and MultiScaleEACS's epilogue (fusion softmax, blend, LayerNorm) in one kernel."""
     from eacs_b200.ops.eacs_gated_scan import cell_forward_into, workspace_bytes
     from eacs_b200.ops.multiscale import branch_fuse, run_branches
-    B, L, H, N = 4, 16384, 1024, 16
-    g = torch.Generator().manual_seed(10)
-    bands = [(0.5, 4.0), (4.0, 32.0), (32.0, 256.0)]
-    x = torch.randn(B, L, H, generator=g).to(torch.bfloat16).to(dev)
-    br = [cell_inputs(g, B, L, H, N, tb, dev, torch.bfloat16) for tb in bands]
-    for d in br:  # one video: every branch sees the same timestamps
-        d["t"] = br[0]["t"]
+    B, L, H, N = MULTISCALE_SHAPE
+    bands = MULTISCALE_BANDS
+    x, br = multiscale_inputs(dev)
     fusion = torch.nn.Linear(H, 3).to(dev)
     norm = torch.nn.LayerNorm(H).to(dev)
     proj_out = [torch.nn.Linear(H, H).to(dev, torch.bfloat16) for _ in bands]

@@ -7,7 +7,9 @@ toolchain the reference's JIT loader uses) and an explicit sm_100a target.
 Outputs go to oracle/_ref/ only (git-ignored; they travel to the GPU machine
 with the working tree).  bench.py times them beside this project's kernels.
 
-    python oracle/build_ref.py [--reference /root/reference]
+    python oracle/build_ref.py [--reference <checkout>]
+
+The checkout defaults to CST_SSM_REFERENCE, else `reference` beside the repository.
 """
 from __future__ import annotations
 
@@ -20,7 +22,8 @@ OUT = os.path.join(HERE, "_ref")
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get(
+        "CST_SSM_REFERENCE", os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")))
     args = ap.parse_args()
     from torch.utils.cpp_extension import load
     csrc = os.path.join(args.reference, "cst_ssm", "ops", "csrc")

@@ -335,7 +335,7 @@ static void cell_row(const float* lam, const float* log_dt, const float* u,
                      float spike_ratio, float eps_factor, int gate_mode, float T,
                      int train_exp, float* y, float* gate, float* resid,
                      float* ch, float* ct, float* cu, float* cB, float* cC,
-                     int64_t L, int64_t H, int64_t N) {
+                     int64_t L, int64_t H, int64_t N, int nthr) {
     cf* hpi = (cf*)calloc((size_t)(H * N), sizeof(cf));
     cf* dA = (cf*)malloc(sizeof(cf) * (size_t)(H * N));
     cf* dBb = (cf*)malloc(sizeof(cf) * (size_t)(H * N));
@@ -344,6 +344,8 @@ static void cell_row(const float* lam, const float* log_dt, const float* u,
     float* upi = (float*)malloc(sizeof(float) * (size_t)H);
     float* scale = (float*)malloc(sizeof(float) * (size_t)H);
     float* sd = (float*)malloc(sizeof(float) * (size_t)H);
+    float* dsq = (float*)malloc(sizeof(float) * (size_t)H);
+    float* osq = (float*)malloc(sizeof(float) * (size_t)H);
     cf* Bpi = (cf*)malloc(sizeof(cf) * (size_t)N);
     cf* Cpi = (cf*)malloc(sizeof(cf) * (size_t)N);
     for (int64_t i = 0; i < H * N; ++i) {
@@ -363,11 +365,20 @@ static void cell_row(const float* lam, const float* log_dt, const float* u,
     float spike = 0.f, prev_r = 0.f;
     float eps_lo = eps * eps_factor;
     float Tp = T > 1e-4f ? T : 1e-4f;
+    float delta = 0.f, g = 0.f;
+    /* With nthr > 1 one row's channels are split over threads inside every
+     * step (long rows of few videos); the residual's sums are still taken
+     * over h in order, in double, so the result does not depend on nthr. */
+#pragma omp parallel num_threads(nthr) if (nthr > 1)
     for (int64_t l = 0; l < L; ++l) {
-        float tl = t[l];
-        float delta = tl - tpi;
-        if (delta < 0.f) delta = 0.f;
-        double sdiff = 0.0, sobs = 0.0;
+        const float* Bl = Bc + l * N * 2;
+        const float* Cl = Cc + l * N * 2;
+#pragma omp single
+        {
+            delta = t[l] - tpi;
+            if (delta < 0.f) delta = 0.f;
+        }
+#pragma omp for schedule(static)
         for (int64_t hh = 0; hh < H; ++hh) {
             float dte = eff_dt(delta, scale[hh], dt_min, dt_max);
             float yhat = 0.f;
@@ -396,19 +407,29 @@ static void cell_row(const float* lam, const float* log_dt, const float* u,
             float obs = (ul - mean[hh]) / sd[hh];
             float pred = (yhat - mean[hh]) / sd[hh];
             float d = obs - pred;
-            sdiff += (double)d * d;
-            sobs += (double)obs * obs;
+            dsq[hh] = d;
+            osq[hh] = obs;
         }
-        float r = sqrtf((float)sdiff) / (sqrtf((float)sobs) + eta);
-        float eps_l = eps;
-        if (robust) eps_l = (spike >= (float)robust_k) ? eps_lo : eps;
-        float g;
-        if (gate_mode == 1) g = 1.0f / (1.0f + expf(-((r - eps_l) / Tp)));
-        else g = (r > eps_l) ? 1.0f : 0.0f;
-        gate[l] = g;
-        resid[l] = r;
-        const float* Bl = Bc + l * N * 2;
-        const float* Cl = Cc + l * N * 2;
+#pragma omp single
+        {
+            double sdiff = 0.0, sobs = 0.0;
+            for (int64_t hh = 0; hh < H; ++hh) {
+                sdiff += (double)dsq[hh] * dsq[hh];
+                sobs += (double)osq[hh] * osq[hh];
+            }
+            float r = sqrtf((float)sdiff) / (sqrtf((float)sobs) + eta);
+            float eps_l = eps;
+            if (robust) eps_l = (spike >= (float)robust_k) ? eps_lo : eps;
+            if (gate_mode == 1) g = 1.0f / (1.0f + expf(-((r - eps_l) / Tp)));
+            else g = (r > eps_l) ? 1.0f : 0.0f;
+            gate[l] = g;
+            resid[l] = r;
+            if (robust) {
+                if (l > 0) spike = (r > prev_r * spike_ratio) ? spike + 1.0f : 0.0f;
+                prev_r = r;
+            }
+        }
+#pragma omp for schedule(static)
         for (int64_t hh = 0; hh < H; ++hh) {
             float ul = u[l * H + hh];
             float acc = 0.f;
@@ -433,47 +454,62 @@ static void cell_row(const float* lam, const float* log_dt, const float* u,
                 acc += Cl[2 * n] * hcur.re - Cl[2 * n + 1] * hcur.im;
             }
             y[l * H + hh] = acc + D[hh] * ul;
-        }
-        if (gate_mode == 1) {
-            for (int64_t hh = 0; hh < H; ++hh) upi[hh] = g * u[l * H + hh] + (1.0f - g) * upi[hh];
-            for (int64_t n = 0; n < N; ++n) {
-                Bpi[n].re = g * Bl[2 * n] + (1.0f - g) * Bpi[n].re;
-                Bpi[n].im = g * Bl[2 * n + 1] + (1.0f - g) * Bpi[n].im;
-                Cpi[n].re = g * Cl[2 * n] + (1.0f - g) * Cpi[n].re;
-                Cpi[n].im = g * Cl[2 * n + 1] + (1.0f - g) * Cpi[n].im;
-            }
-            tpi = g * tl + (1.0f - g) * tpi;
-        } else if (g > 0.5f) {
-            for (int64_t hh = 0; hh < H; ++hh) upi[hh] = u[l * H + hh];
-            for (int64_t n = 0; n < N; ++n) {
-                Bpi[n] = (cf){Bl[2 * n], Bl[2 * n + 1]};
-                Cpi[n] = (cf){Cl[2 * n], Cl[2 * n + 1]};
-            }
-            tpi = tl;
-        }
-        if (ch) {
-            /* commits after step l (eacs.py:386-402): the committed state */
-            for (int64_t i = 0; i < H * N; ++i) {
-                ch[(l * H * N + i) * 2] = hpi[i].re;
-                ch[(l * H * N + i) * 2 + 1] = hpi[i].im;
-            }
-            ct[l] = tpi;
-            for (int64_t hh = 0; hh < H; ++hh) cu[l * H + hh] = upi[hh];
-            for (int64_t n = 0; n < N; ++n) {
-                cB[(l * N + n) * 2] = Bpi[n].re;
-                cB[(l * N + n) * 2 + 1] = Bpi[n].im;
-                cC[(l * N + n) * 2] = Cpi[n].re;
-                cC[(l * N + n) * 2 + 1] = Cpi[n].im;
+            if (gate_mode == 1) upi[hh] = g * ul + (1.0f - g) * upi[hh];
+            else if (g > 0.5f) upi[hh] = ul;
+            if (ch) {
+                /* commits after step l (eacs.py:386-402): the committed state */
+                for (int64_t n = 0; n < N; ++n) {
+                    int64_t i = hh * N + n;
+                    ch[(l * H * N + i) * 2] = hpi[i].re;
+                    ch[(l * H * N + i) * 2 + 1] = hpi[i].im;
+                }
+                cu[l * H + hh] = upi[hh];
             }
         }
-        if (robust) {
-            if (l > 0) spike = (r > prev_r * spike_ratio) ? spike + 1.0f : 0.0f;
-            prev_r = r;
+#pragma omp single
+        {
+            if (gate_mode == 1) {
+                for (int64_t n = 0; n < N; ++n) {
+                    Bpi[n].re = g * Bl[2 * n] + (1.0f - g) * Bpi[n].re;
+                    Bpi[n].im = g * Bl[2 * n + 1] + (1.0f - g) * Bpi[n].im;
+                    Cpi[n].re = g * Cl[2 * n] + (1.0f - g) * Cpi[n].re;
+                    Cpi[n].im = g * Cl[2 * n + 1] + (1.0f - g) * Cpi[n].im;
+                }
+                tpi = g * t[l] + (1.0f - g) * tpi;
+            } else if (g > 0.5f) {
+                for (int64_t n = 0; n < N; ++n) {
+                    Bpi[n] = (cf){Bl[2 * n], Bl[2 * n + 1]};
+                    Cpi[n] = (cf){Cl[2 * n], Cl[2 * n + 1]};
+                }
+                tpi = t[l];
+            }
+            if (ch) {
+                ct[l] = tpi;
+                for (int64_t n = 0; n < N; ++n) {
+                    cB[(l * N + n) * 2] = Bpi[n].re;
+                    cB[(l * N + n) * 2 + 1] = Bpi[n].im;
+                    cC[(l * N + n) * 2] = Cpi[n].re;
+                    cC[(l * N + n) * 2 + 1] = Cpi[n].im;
+                }
+            }
         }
     }
     free(hpi); free(dA); free(dBb); free(xh); free(ilam); free(upi);
-    free(scale); free(sd); free(Bpi); free(Cpi);
+    free(scale); free(sd); free(dsq); free(osq); free(Bpi); free(Cpi);
 }
+
+/* Rows in parallel when there are at least as many rows as threads; otherwise
+ * one row after another, each split over all threads. */
+#define CELL_ROWS(CALL)                                                            \
+    do {                                                                           \
+        int nt_ = nthreads();                                                      \
+        if (B >= nt_ || nt_ <= 1) {                                                \
+            _Pragma("omp parallel for num_threads(nt_) schedule(dynamic, 1)")      \
+            for (int64_t bi = 0; bi < B; ++bi) { int rt_ = 1; CALL; }              \
+        } else {                                                                   \
+            for (int64_t bi = 0; bi < B; ++bi) { int rt_ = nt_; CALL; }            \
+        }                                                                          \
+    } while (0)
 
 int eacs_oracle_cell_fwd(const float* lam, const float* log_dt, const float* u,
                          const float* Bc, const float* Cc, const float* t,
@@ -483,13 +519,11 @@ int eacs_oracle_cell_fwd(const float* lam, const float* log_dt, const float* u,
                          float spike_ratio, float eps_factor, int gate_mode, float T,
                          int train_exp, float* y, float* gate, float* resid,
                          int64_t B, int64_t L, int64_t H, int64_t N) {
-#pragma omp parallel for num_threads(nthreads()) schedule(dynamic, 1)
-    for (int64_t bi = 0; bi < B; ++bi)
-        cell_row(lam, log_dt, u + bi * L * H, Bc + bi * L * N * 2, Cc + bi * L * N * 2,
-                 t + bi * L, D, mean, var, eps, eta, var_eps, dt_init, dt_min, dt_max,
-                 robust, robust_k, spike_ratio, eps_factor, gate_mode, T, train_exp,
-                 y + bi * L * H, gate + bi * L, resid + bi * L, NULL, NULL, NULL, NULL, NULL,
-                 L, H, N);
+    CELL_ROWS(cell_row(lam, log_dt, u + bi * L * H, Bc + bi * L * N * 2, Cc + bi * L * N * 2,
+                       t + bi * L, D, mean, var, eps, eta, var_eps, dt_init, dt_min, dt_max,
+                       robust, robust_k, spike_ratio, eps_factor, gate_mode, T, train_exp,
+                       y + bi * L * H, gate + bi * L, resid + bi * L, NULL, NULL, NULL, NULL,
+                       NULL, L, H, N, rt_));
     return 0;
 }
 
@@ -508,14 +542,12 @@ int eacs_oracle_cell_commits(const float* lam, const float* log_dt, const float*
                              float* y, float* gate, float* resid,
                              float* ch, float* ct, float* cu, float* cB, float* cC,
                              int64_t B, int64_t L, int64_t H, int64_t N) {
-#pragma omp parallel for num_threads(nthreads()) schedule(dynamic, 1)
-    for (int64_t bi = 0; bi < B; ++bi)
-        cell_row(lam, log_dt, u + bi * L * H, Bc + bi * L * N * 2, Cc + bi * L * N * 2,
-                 t + bi * L, D, mean, var, eps, eta, var_eps, dt_init, dt_min, dt_max,
-                 robust, robust_k, spike_ratio, eps_factor, 0, 0.1f, 0,
-                 y + bi * L * H, gate + bi * L, resid + bi * L,
-                 ch + bi * L * H * N * 2, ct + bi * L, cu + bi * L * H,
-                 cB + bi * L * N * 2, cC + bi * L * N * 2, L, H, N);
+    CELL_ROWS(cell_row(lam, log_dt, u + bi * L * H, Bc + bi * L * N * 2, Cc + bi * L * N * 2,
+                       t + bi * L, D, mean, var, eps, eta, var_eps, dt_init, dt_min, dt_max,
+                       robust, robust_k, spike_ratio, eps_factor, 0, 0.1f, 0,
+                       y + bi * L * H, gate + bi * L, resid + bi * L,
+                       ch + bi * L * H * N * 2, ct + bi * L, cu + bi * L * H,
+                       cB + bi * L * N * 2, cC + bi * L * N * 2, L, H, N, rt_));
     return 0;
 }
 

@@ -40,3 +40,22 @@ def decisive(resid, eps, robust, margin=1e-5):
     if robust is not None:
         gap = np.minimum(gap, np.abs(resid - np.float32(eps) * np.float32(robust[2])))
     return gap > margin
+
+
+def assert_cell_match(got, ref, eps, robust, tol=1e-4):
+    """Gate masks bit-exact and outputs within tol, row by row up to the first
+    step whose residual is within 1e-5 of its threshold (after it the
+    trajectories may legitimately part).  Returns the steps compared."""
+    y, g, r = got
+    y_ref, g_ref, r_ref = ref
+    dec = decisive(r_ref, eps, robust)
+    compared = 0
+    for bi in range(g_ref.shape[0]):
+        bad = np.where(~dec[bi])[0]
+        stop = int(bad[0]) if bad.size else g_ref.shape[1]
+        assert np.array_equal(g[bi, :stop], g_ref[bi, :stop]), f"row {bi}: gates differ"
+        assert relerr(r[bi, :stop], r_ref[bi, :stop]) < tol, f"row {bi}: resid"
+        assert relerr(y[bi, :stop], y_ref[bi, :stop]) < tol, f"row {bi}: y"
+        compared += stop
+    assert compared >= 0.9 * g_ref.size
+    return compared

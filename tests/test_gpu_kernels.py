@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from golden_io import cases, cell_args, decisive, relerr
+from golden_io import assert_cell_match, cases, cell_args, decisive, relerr
 from inputs import cell_inputs, scan_inputs
 from oracle import oracle
 
@@ -113,24 +113,6 @@ def _cell(d, u_dtype=torch.float32, **kw):
                                 _t(d["Cc"]), _t(d["t"]), _t(d["D"]), _t(d["mean"]), _t(d["var"]),
                                 **kw)
     return y.cpu().numpy(), g.cpu().numpy(), r.cpu().numpy()
-
-
-def assert_cell_match(got, ref, eps, robust, tol=FWD_TOL):
-    """Gate masks bit-exact and outputs within tol, row by row up to the first
-    step whose residual is within 1e-5 of its threshold (after it the
-    trajectories may legitimately part)."""
-    y, g, r = got
-    y_ref, g_ref, r_ref = ref
-    dec = decisive(r_ref, eps, robust)
-    compared = 0
-    for bi in range(g_ref.shape[0]):
-        bad = np.where(~dec[bi])[0]
-        stop = int(bad[0]) if bad.size else g_ref.shape[1]
-        assert np.array_equal(g[bi, :stop], g_ref[bi, :stop]), f"row {bi}: gates differ"
-        assert relerr(r[bi, :stop], r_ref[bi, :stop]) < tol, f"row {bi}: resid"
-        assert relerr(y[bi, :stop], y_ref[bi, :stop]) < tol, f"row {bi}: y"
-        compared += stop
-    assert compared >= 0.9 * g_ref.size
 
 
 @pytest.mark.parametrize("name", sorted(cases("cell")))

@@ -1,0 +1,188 @@
+"""The reference's own layers on CUDA, unmodified, with and without install().
+
+Each test builds a reference module (cst_ssm, imported from the reference
+package: tests/ref_pkg.py) on the GPU and runs it twice on the same inputs:
+
+* reference only: its CUDA extensions are marked absent, so the reference
+  runs its own PyTorch code on the GPU (EACSLayer's step loop, MultiScaleEACS's
+  merged loop, ContinuousSSMLayer's associative scan, GatedEACSCellFunction's
+  Python forward and per-step autograd backward);
+* after eacs_b200.install(): the same module objects, now reaching this
+  library's kernels through the reference's own lazy imports.
+
+The installed run must launch this library's kernels (its launch counter
+grows: the reference's callers swallow extension errors and would otherwise
+fall back silently, modules/eacs.py:308-311) and match the reference-only run:
+forward outputs 1e-4 relative, gates bit-exact where the residual is more than
+1e-5 from its threshold, gradients 1e-3 relative.
+"""
+import copy
+
+import numpy as np
+import pytest
+import torch
+
+from golden_io import decisive, relerr
+from ref_pkg import import_reference, reference_only, reference_root, restore, snapshot
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(reference_root() is None, reason="reference package not present")]
+
+FWD_TOL = 1e-4
+GRAD_TOL = 1e-3
+DEV = "cuda:0"
+
+
+@pytest.fixture()
+def ref():
+    mods = import_reference()
+    if mods is None:
+        pytest.skip("reference not importable")
+    saved = snapshot(mods)
+    reference_only(mods)
+    yield mods
+    restore(saved)
+
+
+def _launches():
+    from eacs_b200 import _lib
+    return _lib.kernel_launches()
+
+
+def _install(**kw):
+    import eacs_b200
+    eacs_b200.install("cst_ssm", **kw)
+
+
+def _video(B, L, d, seed, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn(B, L, d, generator=g) * scale).to(DEV)
+    dt = 0.25 + 1.75 * torch.rand(B, L, generator=g)
+    dt[torch.rand(B, L, generator=g) < 0.1] = 0.25
+    return x, torch.cumsum(dt, 1).to(DEV)
+
+
+def _rows_match(y, y_ref, g, g_ref, r_ref, eps):
+    """Row by row up to the first step whose residual is within 1e-5 of eps."""
+    dec = decisive(r_ref, eps, None)
+    compared = 0
+    for b in range(g_ref.shape[0]):
+        bad = np.where(~dec[b])[0]
+        stop = int(bad[0]) if bad.size else g_ref.shape[1]
+        assert np.array_equal(g[b, :stop], g_ref[b, :stop]), f"row {b}: gates"
+        assert relerr(y[b, :stop], y_ref[b, :stop]) < FWD_TOL, f"row {b}: y"
+        compared += stop
+    assert compared >= 0.9 * g_ref.size
+
+
+@pytest.mark.parametrize("half_skip", [False, True])
+def test_eacs_layer_eval(ref, half_skip):
+    """EACSLayer.eval() at config 1's width (H=768, N=16, tau [0.1, 1] s).
+    With half_skip the gate's threshold is lifted (eps_anneal) to the median
+    residual, so about half the frames skip (the repair path)."""
+    from cst_ssm.modules.event_gate import EventGate
+    from cst_ssm.ops.spectral_init import BranchSpec
+    torch.manual_seed(0)
+    layer = ref["modules.eacs"].EACSLayer(768, BranchSpec("short", 16, 0.1, 1.0),
+                                          gate=EventGate(init_eps=0.12)).to(DEV).eval()
+    x, t = _video(2, 96, 768, 1)
+    with torch.no_grad():
+        if half_skip:
+            r = layer(x, t).residual
+            layer.gate.set_eps_anneal(float(r.median()) / float(layer.gate.eps))
+        n0 = _launches()
+        out_ref = layer(x, t)
+        assert _launches() == n0
+        _install()
+        out = layer(x, t)
+        assert _launches() > n0
+        eps = float(layer.gate.eps)
+    g, g_ref = out.gates.cpu().numpy(), out_ref.gates.cpu().numpy()
+    if half_skip:
+        assert 0.2 < g_ref.mean() < 0.8
+    _rows_match(out.y.cpu().numpy(), out_ref.y.cpu().numpy(), g, g_ref,
+                out_ref.residual.cpu().numpy(), eps)
+
+
+def test_multiscale_eval(ref):
+    """MultiScaleEACS with config 2's three branch bands (N=16 each), whose
+    reference path is the merged sequential loop over the branches."""
+    from cst_ssm.ops.spectral_init import BranchSpec
+    torch.manual_seed(0)
+    specs = [BranchSpec("short", 16, 0.5, 4.0), BranchSpec("mid", 16, 4.0, 32.0),
+             BranchSpec("long", 16, 32.0, 256.0)]
+    ms = ref["modules.multiscale"].MultiScaleEACS(256, branches=specs,
+                                                  gate_kwargs={"init_eps": 0.12}).to(DEV).eval()
+    x, t = _video(2, 80, 256, 2)
+    with torch.no_grad():
+        assert ms._merge_ok(x)
+        n0 = _launches()
+        out_ref = ms(x, t)
+        assert _launches() == n0
+        _install(multiscale=True)
+        out = ms(x, t)
+        assert _launches() > n0
+    assert relerr(out.y.cpu().numpy(), out_ref.y.cpu().numpy()) < FWD_TOL
+    assert relerr(out.fusion_weights.cpu().numpy(), out_ref.fusion_weights.cpu().numpy()) < FWD_TOL
+
+
+def test_continuous_ssm_layer_forward_backward(ref):
+    """ContinuousSSMLayer (config 0's shape: H=64, N=16): forward and every
+    parameter gradient, the reference's associative scan against the fused
+    ungated core."""
+    from cst_ssm.ops.spectral_init import BranchSpec
+    torch.manual_seed(0)
+    layer = ref["modules.continuous_ssm"].ContinuousSSMLayer(64, BranchSpec("b", 16, 0.5, 64.0)).to(DEV)
+    twin = copy.deepcopy(layer)
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(2, 256, 64, generator=g).to(DEV)
+    dt = torch.empty(2, 256).exponential_(4.0, generator=g).clamp(1 / 30, 2.0)
+    t = torch.cumsum(dt, 1).to(DEV)
+    gy = torch.randn(2, 256, 64, generator=g).to(DEV)
+    n0 = _launches()
+    y_ref = layer(x, t)
+    y_ref.backward(gy)
+    assert _launches() == n0
+    _install(fuse_ungated=True)
+    y = twin(x, t)
+    y.backward(gy)
+    assert _launches() > n0
+    assert relerr(y.detach().cpu().numpy(), y_ref.detach().cpu().numpy()) < FWD_TOL
+    for (name, p), p_ref in zip(twin.named_parameters(), layer.parameters()):
+        assert relerr(p.grad.cpu().numpy(), p_ref.grad.cpu().numpy()) < GRAD_TOL, name
+
+
+def test_eacs_layer_fused_train(ref):
+    """EACSLayer(fused_train=True) in training mode: the layer output, the
+    innovation loss and every parameter gradient, the reference's
+    GatedEACSCellFunction (Python forward, per-step autograd backward) against
+    this library's checkpointed backward kernels."""
+    from cst_ssm.modules.event_gate import EventGate
+    from cst_ssm.ops.spectral_init import BranchSpec
+    torch.manual_seed(0)
+    layer = ref["modules.eacs"].EACSLayer(128, BranchSpec("short", 16, 0.5, 4.0),
+                                          gate=EventGate(init_eps=0.12), fused_train=True).to(DEV).train()
+    twin = copy.deepcopy(layer)
+    x, t = _video(2, 48, 128, 4)
+    gy = torch.randn(x.shape, generator=torch.Generator().manual_seed(5)).to(DEV)
+
+    def run(m):
+        out = m(x, t)
+        loss = (out.y * gy).sum() + out.innovation.square().mean()
+        loss.backward()
+        return out
+
+    n0 = _launches()
+    out_ref = run(layer)
+    assert _launches() == n0
+    _install()
+    out = run(twin)
+    assert _launches() > n0
+    assert torch.equal(out.gates, out_ref.gates)
+    assert relerr(out.y.detach().cpu().numpy(), out_ref.y.detach().cpu().numpy()) < FWD_TOL
+    assert relerr(out.residual.detach().cpu().numpy(), out_ref.residual.detach().cpu().numpy()) < FWD_TOL
+    for (name, p), p_ref in zip(twin.named_parameters(), layer.parameters()):
+        if p_ref.grad is None:
+            assert p.grad is None or not p.grad.any(), name
+            continue
+        assert relerr(p.grad.cpu().numpy(), p_ref.grad.cpu().numpy()) < GRAD_TOL, name

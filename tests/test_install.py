@@ -1,58 +1,31 @@
-"""eacs_b200.install() against an unmodified reference checkout (CPU only).
+"""eacs_b200.install() against an unmodified reference package (CPU only).
 
-Runs only where the reference is importable: the checkout given by the
-CST_SSM_REFERENCE environment variable, default /root/reference.  Checks that
-every hook the reference's lazy loaders and dispatch go through is replaced,
-that the replaced layer paths keep the reference's CPU behaviour where the
-reference falls back (EACSLayer on CPU) and that the fused ungated layer
-refuses CPU tensors instead of silently running elsewhere.
+Runs only where the reference's Python package is importable (tests/ref_pkg.py:
+CST_SSM_REFERENCE or baseline/_ref).  Checks that every hook the reference's
+lazy loaders and dispatch go through is replaced, that the replaced layer
+paths keep the reference's CPU behaviour where the reference falls back
+(EACSLayer on CPU) and that the fused ungated layer refuses CPU tensors
+instead of silently running elsewhere.
 """
 import importlib
-import os
 import sys
 
 import pytest
 import torch
 
-REF = os.environ.get("CST_SSM_REFERENCE", "/root/reference")
-pytestmark = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "cst_ssm")),
-                                reason="reference checkout not present")
+from ref_pkg import import_reference, reference_root, restore, snapshot
+
+pytestmark = pytest.mark.skipif(reference_root() is None, reason="reference package not present")
 
 
 @pytest.fixture()
 def ref_pkg():
-    sys.path.insert(0, REF)
-    try:
-        mods = {n: importlib.import_module(f"cst_ssm.{n}") for n in
-                ("ops.scan_cuda", "ops.eacs_gated_scan", "ops.eacs_cell_train",
-                 "modules.continuous_ssm", "modules.eacs", "modules.continuous_query")}
-    except ImportError as e:
-        sys.path.remove(REF)
-        pytest.skip(f"reference not importable: {e}")
-    saved = {
-        "scan": (mods["ops.scan_cuda"]._EXT, mods["ops.scan_cuda"]._TRIED),
-        "cell": (mods["ops.eacs_gated_scan"]._EXT, mods["ops.eacs_gated_scan"]._TRIED),
-        "train": (mods["ops.eacs_cell_train"].GatedEACSCellFunction,
-                  mods["ops.eacs_cell_train"].fused_gated_scan),
-        "ssm_fwd": mods["modules.continuous_ssm"].ContinuousSSMLayer.forward,
-        "ok": mods["modules.eacs"].EACSLayer._cuda_fused_ok,
-        "fused": mods["modules.eacs"].EACSLayer._forward_fused,
-        "rwc": mods["modules.eacs"].EACSLayer.run_with_commits,
-        "rfc": mods["modules.continuous_query"].readout_from_commits,
-        "seg": mods["modules.continuous_query"].segment_index,
-    }
+    mods = import_reference()
+    if mods is None:
+        pytest.skip("reference not importable")
+    saved = snapshot(mods)
     yield mods
-    mods["ops.scan_cuda"]._EXT, mods["ops.scan_cuda"]._TRIED = saved["scan"]
-    mods["ops.eacs_gated_scan"]._EXT, mods["ops.eacs_gated_scan"]._TRIED = saved["cell"]
-    (mods["ops.eacs_cell_train"].GatedEACSCellFunction,
-     mods["ops.eacs_cell_train"].fused_gated_scan) = saved["train"]
-    mods["modules.continuous_ssm"].ContinuousSSMLayer.forward = saved["ssm_fwd"]
-    mods["modules.eacs"].EACSLayer._cuda_fused_ok = saved["ok"]
-    mods["modules.eacs"].EACSLayer._forward_fused = saved["fused"]
-    mods["modules.eacs"].EACSLayer.run_with_commits = saved["rwc"]
-    mods["modules.continuous_query"].readout_from_commits = saved["rfc"]
-    mods["modules.continuous_query"].segment_index = saved["seg"]
-    sys.path.remove(REF)
+    restore(saved)
 
 
 def test_install_replaces_every_hook(ref_pkg):
