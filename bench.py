@@ -85,6 +85,9 @@ def parse():
                     "three-branch multiscale cell and the long-video cell (B=64, H=2048, N=32)")
     ap.add_argument("--L", type=int, default=None, choices=[16384, 32768, 65536],
                     help="frames per video for --workload longvideo (default 16384)")
+    ap.add_argument("--global-batch", action="store_true",
+                    help="--workload train: the 8 videos are the global batch, split over the ranks "
+                    "(DDP with one video per rank on 8 GPUs, strong scaling) instead of 8 per rank")
     return ap.parse_args()
 
 
@@ -296,6 +299,42 @@ def cpu_model():
 
 
 # --------------------------------------------------------------------------
+# host placement: each rank's host buffers on the NUMA node of its GPU
+# --------------------------------------------------------------------------
+def _cpulist(text):
+    cpus = set()
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        lo, _, hi = part.partition("-")
+        cpus.update(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+def numa_bind(dev_index: int):
+    """Restrict this process to the CPUs of the NUMA node its GPU hangs off
+    (the node sysfs reports for the GPU's PCI function), so that the pinned
+    host buffers it then allocates and first touches sit in that node's
+    memory: the host-to-device and device-to-host copies of the end-to-end
+    leg then stay off the inter-socket link.  Returns the placement, or None
+    where the node is unknown or the affinity cannot be set."""
+    try:
+        pr = torch.cuda.get_device_properties(dev_index)
+        bdf = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        node = int(open(f"/sys/bus/pci/devices/{bdf}/numa_node").read())
+        if node < 0:
+            return None
+        cpus = _cpulist(open(f"/sys/devices/system/node/node{node}/cpulist").read())
+        cpus &= set(os.sched_getaffinity(0))
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return {"gpu_pci": bdf, "numa_node": node, "cpus": len(cpus)}
+    except (OSError, ValueError, AttributeError):
+        return None
+
+
+# --------------------------------------------------------------------------
 # multi-rank aggregation (weak scaling: every rank runs its own B videos)
 # --------------------------------------------------------------------------
 def max_over_ranks(ms: float, dev, world: int) -> float:
@@ -377,6 +416,7 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                                 device_id=dev)
 
+    placement = numa_bind(local) if world > 1 else None
     d, eps = make_inputs(rank, dev)
     if args.eps is not None:
         eps = float(args.eps)
@@ -516,7 +556,8 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,1) fp16 features through a seed-0 EACSLayer init)",
             "config": dict(CONFIG, update_rate=update_rate,
-                           **({} if args.eps is None else {"eps_override": eps})),
+                           **({} if args.eps is None else {"eps_override": eps}),
+                           **({} if world == 1 else {"host_numa_rank0": placement})),
             "roofline": {"bound": "issue", "achieved": issue_achieved / 1e12,
                          "peak": issue_peak / 1e12, "unit": "Tinstr/s",
                          "frac": issue_achieved / issue_peak, "traffic": traffic,

@@ -312,9 +312,11 @@ def wl_ssm_train(args, dev, flush):
 def wl_train(args):
     """Gated-cell training: GatedEACSCellFunction forward + backward, B=8 L=8192 H=768 N=16, bf16 u
     (--shape B,L,H,N gives a small case for ncu).  Under torchrun every rank
-    trains its own B videos (weak scaling) and the cell's parameter gradients
-    (lambda, log_dt, D, eps) are summed over the ranks with one NCCL
-    all-reduce per step, as DDP does; time is device-measured, max over ranks."""
+    trains its own B videos (weak scaling), or with --global-batch its share
+    of the 8 (strong scaling: one video per rank on 8 GPUs), and the cell's
+    parameter gradients (lambda, log_dt, D, eps) are summed over the ranks
+    with one NCCL all-reduce per step, as DDP does; time is device-measured,
+    max over ranks."""
     import datetime
     import torch.distributed as dist
     from bench import max_over_ranks
@@ -328,7 +330,18 @@ def wl_train(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     B, L, H, N = (8, 8192, 768, 16) if getattr(args, "shape", None) is None else (int(v) for v in args.shape.split(","))
-    d, gy = train_inputs(rank, dev, B, L, H, N)
+    split = bool(getattr(args, "global_batch", False))
+    if split:  # the global batch's rows of this rank, from the one-rank draw
+        if B % world:
+            raise SystemExit(f"train: {B} videos do not split over {world} ranks")
+        d, gy = train_inputs(0, "cpu", B, L, H, N)
+        per = B // world
+        rows = slice(rank * per, (rank + 1) * per)
+        d = {k: (v[rows].contiguous() if k in ("u", "Bc", "Cc", "t") else v).to(dev) for k, v in d.items()}
+        gy = gy[rows].contiguous().to(dev)
+        B = per
+    else:
+        d, gy = train_inputs(rank, dev, B, L, H, N)
     leaves = {k: d[k].clone().requires_grad_(True) for k in ("u", "Bc", "Cc", "lam", "log_dt", "D")}
     eps = torch.tensor(0.12, device=dev, requires_grad=True)
 
@@ -380,10 +393,11 @@ def wl_train(args):
             "metric": "EACS gated cell training fwd+bwd Gstate-updates/s",
             "value": world * nsteps * upd / (total_ms / 1e3) / 1e9, "unit": UNIT, "n_gpus": world,
             "steps": nsteps, "warmup": warmup, "ms_per_step": total_ms / nsteps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong" if split else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "GatedEACSCellFunction fwd+bwd (STE, T=0.1)"
                                    + ("; DDP all-reduce of the cell parameters' gradients" if world > 1 else ""),
-                       "B_per_rank": B, "L": L, "H": H, "N": N, "u_dtype": "bf16", "update_rate": rate,
+                       "B_per_rank": B, "global_batch": B * world, "L": L, "H": H, "N": N, "u_dtype": "bf16",
+                       "update_rate": rate,
                        "l2": "flushed between steps"},
             "backward_kernel_ms": statistics.median(kt),
             "backward_kernel_Gstate_updates_per_s": upd / (statistics.median(kt) / 1e3) / 1e9,

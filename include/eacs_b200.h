@@ -55,6 +55,14 @@ EACS_API const char* eacs_last_error(void);
  * wait).  *status receives EACS_OK when nothing was recorded. */
 EACS_API int eacs_device_status(int* status, void* stream);
 
+/* Failure-path check (no counterpart in the reference): one CTA waits, with
+ * the library's bounded waits (CTA scope and cluster scope) limited to
+ * `polls` polls (1..65536), on an mbarrier phase that nothing completes.
+ * Both waits expire, record EACS_ERR_TIMEOUT in the device status word and
+ * return, so the kernel ends and the context stays usable; a following
+ * eacs_device_status() reports EACS_ERR_TIMEOUT once. */
+EACS_API int eacs_wait_selftest(int polls, void* stream);
+
 /* Number of kernel launches this library has issued in this process (all
  * devices).  Lets a caller prove the native path ran. */
 EACS_API uint64_t eacs_kernel_launches(void);
@@ -426,6 +434,9 @@ EACS_API void eacs_fc_close(eacs_fc* fc);
  * device code is loaded and every GPU that loads it keeps it until exit.
  * The first call on each device looks up the array's device address (with
  * that device current); make that first call before any stream capture.
+ * The address is kept for the life of the process and belongs to the
+ * device's primary context: after cudaDeviceReset on that device it no
+ * longer names the array, so do not call this entry point after a reset.
  * Sizes whose scratch (eacs_cell_fwd_workspace_size) exceeds the array are
  * rejected with EACS_ERR_WORKSPACE.  All calls share the one array per device
  * and it keeps the last call's contents (every byte a call reads it writes

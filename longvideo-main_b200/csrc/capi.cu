@@ -68,6 +68,10 @@ int eacs_device_status(int* status, void* stream) {
     return EACS_OK;
 }
 
+int eacs_wait_selftest(int polls, void* stream) {
+    return eacs::wait_selftest(polls, static_cast<cudaStream_t>(stream));
+}
+
 int eacs_scan_fwd(const void* a, const void* b, void* h, int64_t B, int64_t L, int64_t H, int64_t N,
                   void* stream) {
     if (B < 0 || L < 0 || H < 0 || N < 0) return eacs::fail(EACS_ERR_INVALID, "eacs_scan_fwd: negative size");

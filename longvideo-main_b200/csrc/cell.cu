@@ -1648,6 +1648,31 @@ int ssm_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc
 
 cudaError_t cell_read_status(int* out, cudaStream_t stream) { return read_clear_status(out, stream); }
 
+// Failure-path check: an mbarrier (count 1) that nothing arrives at, waited on
+// with the bounded waits the repair and training passes use, at a small poll
+// limit.  Both waits give up, record EACS_ERR_TIMEOUT and return.
+__global__ void wait_selftest_k(uint32_t polls) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const bool a = mbar_wait(&bar, 0, polls);
+        const bool b = mbar_wait_row(&bar, 0, polls);
+        if (a || b) set_status(EACS_ERR_INVALID);  // a phase nothing completes cannot complete
+    }
+}
+
+int wait_selftest(int polls, cudaStream_t stream) {
+    if (polls < 1 || polls > 65536)
+        return fail(EACS_ERR_INVALID, "eacs_wait_selftest: polls %d outside 1..65536", polls);
+    wait_selftest_k<<<1, 32, 0, stream>>>(static_cast<uint32_t>(polls));
+    note_launch();
+    return cuda_check(cudaGetLastError(), "eacs_wait_selftest");
+}
+
 int zoh_kernels(const void* lam, const float* dt, void* dA, void* dBbar, int64_t M, int64_t H,
                 int64_t N, cudaStream_t stream) {
     const char* fn = "eacs_zoh_kernels";

@@ -234,8 +234,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
 // Bounded wait on an mbarrier phase.  Returns false (and records a timeout)
 // when the phase has not completed after `limit` polls.
 constexpr uint32_t kWaitLimit = 1u << 22;
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
-    for (uint32_t i = 0; i < kWaitLimit; ++i)
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_t limit = kWaitLimit) {
+    for (uint32_t i = 0; i < limit; ++i)
         if (mbar_try_wait(bar, phase)) return true;
     set_status(EACS_ERR_TIMEOUT);
     return false;
@@ -243,8 +243,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
 
 // Bounded wait on an mbarrier phase completed by other CTAs of the cluster
 // (acquire at cluster scope, so their st.async data is visible afterwards).
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t phase) {
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t phase, uint32_t limit = kWaitLimit) {
+    for (uint32_t i = 0; i < limit; ++i) {
         uint32_t ok;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
@@ -261,8 +261,8 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t phase)
 
 // The same bounded wait by polling with mbarrier.test_wait, which never
 // suspends the thread (try_wait may suspend it for a system-dependent time).
-__device__ __forceinline__ bool mbar_poll_cluster(uint64_t* bar, uint32_t phase) {
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+__device__ __forceinline__ bool mbar_poll_cluster(uint64_t* bar, uint32_t phase, uint32_t limit = kWaitLimit) {
+    for (uint32_t i = 0; i < limit; ++i) {
         uint32_t ok;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
@@ -281,11 +281,11 @@ __device__ __forceinline__ bool mbar_poll_cluster(uint64_t* bar, uint32_t phase)
 #ifndef EACS_MBAR_POLL
 #define EACS_MBAR_POLL 0
 #endif
-__device__ __forceinline__ bool mbar_wait_row(uint64_t* bar, uint32_t phase) {
+__device__ __forceinline__ bool mbar_wait_row(uint64_t* bar, uint32_t phase, uint32_t limit = kWaitLimit) {
 #if EACS_MBAR_POLL
-    return mbar_poll_cluster(bar, phase);
+    return mbar_poll_cluster(bar, phase, limit);
 #else
-    return mbar_wait_cluster(bar, phase);
+    return mbar_wait_cluster(bar, phase, limit);
 #endif
 }
 

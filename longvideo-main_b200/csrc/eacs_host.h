@@ -123,6 +123,7 @@ int ssm_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc
             size_t ckpt_bytes, cudaStream_t stream);
 size_t ssm_ckpt_size(int64_t B, int64_t L, int64_t H, int64_t N);
 cudaError_t cell_read_status(int* out, cudaStream_t stream);
+int wait_selftest(int polls, cudaStream_t stream);
 int zoh_kernels(const void* lam, const float* dt, void* dA, void* dBbar, int64_t M, int64_t H,
                 int64_t N, cudaStream_t stream);
 

@@ -72,7 +72,9 @@ int parse_npy(const unsigned char* p, size_t len, std::string* descr, bool* fort
     *descr = h.substr(q0 + 1, q1 - q0 - 1);
     v = value_after("'fortran_order'");
     if (v == std::string::npos) return fail(EACS_ERR_INVALID, "feature cache: %s: no fortran_order", what);
-    *fortran = h.compare(h.find_first_not_of(' ', v), 4, "True") == 0;
+    const size_t fv = h.find_first_not_of(' ', v);
+    if (fv == std::string::npos) return fail(EACS_ERR_INVALID, "feature cache: %s: bad fortran_order", what);
+    *fortran = h.compare(fv, 4, "True") == 0;
     v = value_after("'shape'");
     const size_t s0 = v == std::string::npos ? v : h.find('(', v);
     const size_t s1 = s0 == std::string::npos ? s0 : h.find(')', s0);
@@ -169,8 +171,16 @@ int eacs_fc_open(const char* path, eacs_fc** out) {
         fc->d = shape.back();
         fc->dtype = descr == "<f2" ? EACS_DTYPE_F16 : EACS_DTYPE_F32;
         fc->esz = descr == "<f2" ? 2 : 4;
-        const size_t need = fc->data_off + static_cast<size_t>(fc->L * fc->P * fc->d) * fc->esz;
-        if (need > fc->map_len) rc = fail(EACS_ERR_INVALID, "feature cache: %s is truncated", path);
+        // element count and byte size with overflow checks: a crafted header
+        // must not wrap the product past the truncation check
+        size_t elems = 0, bytes = 0, need = 0;
+        if (__builtin_mul_overflow(static_cast<size_t>(fc->L), static_cast<size_t>(fc->P), &elems) ||
+            __builtin_mul_overflow(elems, static_cast<size_t>(fc->d), &elems) ||
+            __builtin_mul_overflow(elems, static_cast<size_t>(fc->esz), &bytes) ||
+            __builtin_add_overflow(bytes, static_cast<size_t>(fc->data_off), &need))
+            rc = fail(EACS_ERR_INVALID, "feature cache: %s: shape too large", path);
+        else if (need > fc->map_len)
+            rc = fail(EACS_ERR_INVALID, "feature cache: %s is truncated", path);
     }
     // timestamps: <path minus .npy>.ts.npy
     if (!rc) {

@@ -36,6 +36,7 @@ SIGNATURES = {
     "eacs_last_error": (ctypes.c_char_p, []),
     "eacs_device_status": (_I, [ctypes.POINTER(_I), _P]),
     "eacs_kernel_launches": (ctypes.c_uint64, []),
+    "eacs_wait_selftest": (_I, [_I, _P]),
     "eacs_set_kernel_events": (_I, [_P, _P]),
     "eacs_scan_fwd": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "eacs_scan_bwd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),

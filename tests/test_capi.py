@@ -101,3 +101,10 @@ def test_python_ops_reject_cpu_tensors():
                           torch.zeros(1, 2, N, dtype=torch.complex64),
                           torch.zeros(1, 2, N, dtype=torch.complex64), torch.zeros(1, 2), z, z, z,
                           0.1, 1e-6)
+
+
+def test_wait_selftest_rejects_bad_poll_counts_without_device():
+    lib = _lib.lib()
+    for polls in (0, -1, 65537):
+        assert lib.eacs_wait_selftest(polls, None) == _lib.EACS_ERR_INVALID
+    assert "polls" in _lib.last_error()

@@ -59,6 +59,33 @@ def test_rejects_bad_files(tmp_path):
         FeatureCache(str(tmp_path / "junk.npy"))
 
 
+def _raw_npy(path, header: str, payload: bytes = b"\0" * 64):
+    """A .npy file (format 1.0) with the given header dict text, and a
+    matching timestamps file."""
+    h = header.encode("latin1")
+    h += b" " * ((-(10 + len(h) + 1)) % 64) + b"\n"
+    with open(path, "wb") as f:
+        f.write(b"\x93NUMPY\x01\x00" + len(h).to_bytes(2, "little") + h + payload)
+    np.save(path[:-4] + ".ts.npy", np.zeros(4, np.float32))
+
+
+def test_rejects_crafted_headers(tmp_path):
+    """Shapes whose byte size wraps 64 bits, and a header cut off after a
+    key, are rejected with an error (no read past the mapping, no abort)."""
+    big = str(tmp_path / "big.npy")
+    _raw_npy(big, "{'descr': '<f2', 'fortran_order': False, 'shape': (4, 4611686018427387904, 2), }")
+    with pytest.raises(RuntimeError, match="too large|truncated"):
+        FeatureCache(big)
+    wrap = str(tmp_path / "wrap.npy")
+    _raw_npy(wrap, "{'descr': '<f4', 'fortran_order': False, 'shape': (4, 1152921504606846976, 4), }")
+    with pytest.raises(RuntimeError, match="too large|truncated"):
+        FeatureCache(wrap)
+    cut = str(tmp_path / "cut.npy")
+    _raw_npy(cut, "{'descr': '<f2', 'fortran_order':" + " " * 40)
+    with pytest.raises(RuntimeError, match="fortran_order|shape"):
+        FeatureCache(cut)
+
+
 def test_writer_round_trip(tmp_path):
     feats = np.arange(2 * 3 * 4, dtype=np.float16).reshape(2, 3, 4)
     path = write_npy_pair(str(tmp_path / "w"), feats, np.array([0.0, 0.5]))

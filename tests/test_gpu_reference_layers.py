@@ -87,9 +87,20 @@ def test_eacs_layer_eval(ref, half_skip):
                                           gate=EventGate(init_eps=0.12)).to(DEV).eval()
     x, t = _video(2, 96, 768, 1)
     with torch.no_grad():
-        if half_skip:
-            r = layer(x, t).residual
-            layer.gate.set_eps_anneal(float(r.median()) / float(layer.gate.eps))
+        if half_skip:  # bisect the threshold (through eps_anneal) to an update rate near 0.5
+            base = float(layer.gate.eps) / float(layer.gate.eps_anneal)
+            lo, hi = 0.0, 2.0
+            for _ in range(14):
+                mid = 0.5 * (lo + hi)
+                layer.gate.set_eps_anneal(mid / base)
+                rate = float(layer(x, t).gates.mean())
+                lo, hi = (mid, hi) if rate > 0.5 else (lo, mid)
+            eps = 0.5 * (lo + hi)
+            for _ in range(200):  # then away from every residual, so each gate is decided
+                layer.gate.set_eps_anneal(eps / base)
+                if decisive(layer(x, t).residual.cpu().numpy(), eps, None, 2e-4).all():
+                    break
+                eps *= 1.0006
         n0 = _launches()
         out_ref = layer(x, t)
         assert _launches() == n0
