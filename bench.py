@@ -578,14 +578,15 @@ def run_ours(args):
         }
         if ref_cuda is not None:
             line["reference_cuda"] = ref_cuda
-        if not args.profile:
-            line["parity"] = parity_check(d, eps, (y, gate, resid), out_host if e2e_steps else None)
-        if world == 1 and not args.profile:
-            line["cpu_baseline"] = cpu_baseline(d, eps, args.cpu_seconds, y, line["parity"],
-                                                 args.eps is not None)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    # CPU work on rank 0 after the ranks have parted (no rank waits on it)
+    if line is not None and not args.profile:
+        line["parity"] = parity_check(d, eps, (y, gate, resid), out_host if e2e_steps else None)
+        if world == 1:
+            line["cpu_baseline"] = cpu_baseline(d, eps, args.cpu_seconds, y, line["parity"],
+                                                 args.eps is not None)
     if line is not None:
         print(json.dumps(line), flush=True)
     return 0

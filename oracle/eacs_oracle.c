@@ -498,17 +498,16 @@ static void cell_row(const float* lam, const float* log_dt, const float* u,
     free(scale); free(sd); free(dsq); free(osq); free(Bpi); free(Cpi);
 }
 
-/* Rows in parallel when there are at least as many rows as threads; otherwise
- * one row after another, each split over all threads. */
+/* Rows in parallel; when there are fewer rows than threads, each row is split
+ * over the threads left over (nested parallel regions: nt / B threads per row). */
 #define CELL_ROWS(CALL)                                                            \
     do {                                                                           \
         int nt_ = nthreads();                                                      \
-        if (B >= nt_ || nt_ <= 1) {                                                \
-            _Pragma("omp parallel for num_threads(nt_) schedule(dynamic, 1)")      \
-            for (int64_t bi = 0; bi < B; ++bi) { int rt_ = 1; CALL; }              \
-        } else {                                                                   \
-            for (int64_t bi = 0; bi < B; ++bi) { int rt_ = nt_; CALL; }            \
-        }                                                                          \
+        int outer_ = (int)(B < nt_ ? B : nt_);                                     \
+        int rt_ = B < nt_ ? nt_ / (int)(B > 0 ? B : 1) : 1;                        \
+        if (rt_ > 1) omp_set_max_active_levels(2);                                 \
+        _Pragma("omp parallel for num_threads(outer_) schedule(dynamic, 1)")       \
+        for (int64_t bi = 0; bi < B; ++bi) { CALL; }                               \
     } while (0)
 
 int eacs_oracle_cell_fwd(const float* lam, const float* log_dt, const float* u,

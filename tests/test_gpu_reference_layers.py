@@ -98,9 +98,9 @@ def test_eacs_layer_eval(ref, half_skip):
             eps = 0.5 * (lo + hi)
             for _ in range(200):  # then away from every residual, so each gate is decided
                 layer.gate.set_eps_anneal(eps / base)
-                if decisive(layer(x, t).residual.cpu().numpy(), eps, None, 2e-4).all():
+                if decisive(layer(x, t).residual.cpu().numpy(), eps, None, 2e-5).all():
                     break
-                eps *= 1.0006
+                eps *= 1.00002
         n0 = _launches()
         out_ref = layer(x, t)
         assert _launches() == n0
