@@ -55,6 +55,28 @@ EACS_API const char* eacs_last_error(void);
  * wait).  *status receives EACS_OK when nothing was recorded. */
 EACS_API int eacs_device_status(int* status, void* stream);
 
+/* LayerNorm and the three input projections of an EACS layer in one kernel
+ * on the tensor cores (tcgen05.mma, weights staged by TMA).  Replaces, for a
+ * float16 / bfloat16 autocast region, x = self.norm(x) then _project(x)
+ * (cst_ssm/modules/eacs.py:334 / :376 and :261-267): u = proj_u(x),
+ * Bc = complex(b[..., :N], b[..., N:]) with b = proj_B(x), Cc likewise.
+ * x (M, d) in x_dtype; gamma, beta (d) float32 (LayerNorm affine, eps ln_eps);
+ * weight (w_rows, d) in w_dtype (float16 or bfloat16: the GEMM type T) holds
+ * proj_u.weight (H rows), proj_B.weight (2N), proj_C.weight (2N), then zero
+ * rows up to w_rows, a multiple of 256; bias (H + 4N) float32 likewise.
+ * LayerNorm runs in float32 and is rounded to T; products accumulate in
+ * float32, the bias (rounded to T) is added and the sum rounded to T, as an
+ * autocast Linear does.  u (M, H) is written in u_dtype, Bc and Cc (M, N) as
+ * complex64 of the T-rounded values.  d must be a multiple of 8; x, weight,
+ * gamma and beta 16-byte aligned; workspace (8-byte aligned) of
+ * eacs_project_workspace_size(M) bytes, the caller's. */
+EACS_API int eacs_project(const void* x, int x_dtype, const float* gamma, const float* beta, float ln_eps,
+                          const void* weight, int w_dtype, int64_t w_rows, const float* bias, void* u,
+                          int u_dtype, void* Bc, void* Cc, void* workspace, size_t workspace_bytes,
+                          int64_t M, int64_t d, int64_t H, int64_t N, void* stream);
+/* Bytes of eacs_project's workspace for M rows (its LayerNorm statistics). */
+EACS_API size_t eacs_project_workspace_size(int64_t M);
+
 /* Failure-path check (no counterpart in the reference): one CTA waits, with
  * the library's bounded waits (CTA scope and cluster scope) limited to
  * `polls` polls (1..65536), on an mbarrier phase that nothing completes.

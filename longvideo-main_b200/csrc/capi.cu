@@ -68,6 +68,17 @@ int eacs_device_status(int* status, void* stream) {
     return EACS_OK;
 }
 
+size_t eacs_project_workspace_size(int64_t M) { return eacs::project_workspace_size(M); }
+
+int eacs_project(const void* x, int x_dtype, const float* gamma, const float* beta, float ln_eps,
+                 const void* weight, int w_dtype, int64_t w_rows, const float* bias, void* u, int u_dtype,
+                 void* Bc, void* Cc, void* workspace, size_t workspace_bytes, int64_t M, int64_t d, int64_t H,
+                 int64_t N, void* stream) {
+    eacs::ProjectCall c{x, x_dtype, gamma, beta, ln_eps, weight, w_dtype, w_rows, bias, u, u_dtype, Bc, Cc,
+                        M, d, H, N, workspace, workspace_bytes};
+    return eacs::project_fwd(c, static_cast<cudaStream_t>(stream));
+}
+
 int eacs_wait_selftest(int polls, void* stream) {
     return eacs::wait_selftest(polls, static_cast<cudaStream_t>(stream));
 }

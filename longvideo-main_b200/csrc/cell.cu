@@ -1115,13 +1115,21 @@ __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int
     rc_cluster_sync();  // no CTA leaves while a peer may still write its slots
 }
 
-// Cluster shape of the repair pass for (H, N): LANES x NPT chains per
-// channel and CL CTAs per row with at most kRcMaxThreads threads each; 0 when
-// the shape does not fit (the one-CTA repair pass handles it).
+// Cluster shape of the repair pass for (H, N) over B rows: LANES x NPT chains
+// per channel and CL CTAs per row with at most kRcMaxThreads threads each; 0
+// when the shape does not fit (the one-CTA repair pass handles it).  CL is
+// the smallest of 8, 10, .., EACS_RC_MAXCL that fits.  (A repair step is
+// bound by its dependent instruction chain and the cluster exchange, not by
+// the SM count: 12- and 16-CTA rows at config 1's shape measured no faster,
+// and with one CTA per SM slower, since fewer such clusters are resident.)
+#ifndef EACS_RC_MAXCL
+#define EACS_RC_MAXCL 16
+#endif
 struct RcShape {
     int lanes, npt, cl, hc, threads;
 };
-RcShape rc_shape(int H, int N) {
+RcShape rc_shape(int H, int N, int B) {
+    (void)B;
     RcShape r{0, 0, 0, 0, 0};
     if (N <= 4) { r.lanes = 4; r.npt = 1; }
     else if (N <= 8) { r.lanes = 4; r.npt = 2; }
@@ -1129,17 +1137,15 @@ RcShape rc_shape(int H, int N) {
     else if (N <= 32) { r.lanes = 8; r.npt = 4; }
     else if (N <= 64) { r.lanes = 16; r.npt = 4; }
     else return r;
-    for (int cl = 8; cl <= kRcMaxCL; cl *= 2) {  // 8 CTAs per row keeps a full row set co-resident
+    int best = 0;
+    for (int cl = 8; cl <= kRcMaxCL && cl <= EACS_RC_MAXCL && best == 0; cl += 2) {
         const int hc = (H + cl - 1) / cl;
-        const int threads = ((hc * r.lanes + 31) / 32) * 32;
-        if (threads <= kRcMaxThreads) {
-            r.cl = cl;
-            r.hc = hc;
-            r.threads = threads;
-            return r;
-        }
+        if (((hc * r.lanes + 31) / 32) * 32 <= kRcMaxThreads) best = cl;
     }
-    r.cl = 0;
+    if (best == 0) return r;
+    r.cl = best;
+    r.hc = (H + best - 1) / best;
+    r.threads = ((r.hc * r.lanes + 31) / 32) * 32;
     return r;
 }
 
@@ -1152,6 +1158,517 @@ cudaError_t launch_repair_cluster(const Args& a, const RcShape& rs, cudaStream_t
         if (e != cudaSuccess) return e;
     }
     const size_t smem = 2 * rc_buf_bytes<UT>(LANES * NPT, rs.hc);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rs.cl, a.B);
+    cfg.blockDim = dim3(rs.threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = rs.cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, a, rs.cl, rs.hc);
+    note_launch();
+    return e;
+}
+
+// ---------------------------------------------------------------------------
+// 5b: windowed speculative repair (hard gate, no commit or checkpoint
+// recording).  From l* on, a row's gates are decided a window of up to
+// kWinMax steps per cluster exchange instead of one step per exchange.  A
+// window runs under one hypothesis: every step commits (after a committed
+// step) or every step skips (after a skipped one).  Under "commit" the
+// committed state of step k is step k-1's update (a linear chain, as in the
+// speculative pass); under "skip" it stays the window's starting state, so
+// the window's predictions are independent of one another.  Every step
+// forms its prediction x_hat, its update h_upd = dA h_pi + E W_l and both
+// candidate outputs Re C_l x_hat and Re C_l h_upd; one exchange then gives
+// each CTA the residual sums of all the window's steps.  The gates are taken
+// in order and the window is accepted up to and including the first step
+// whose gate differs from the hypothesis: that step's prediction came from
+// the exact committed state, so it is exact whichever way its gate went.
+// The committed state then moves to the update of the last committed step
+// (each step's update is kept in shared memory for this), and the next
+// window runs under the hypothesis that the last accepted step's gate makes
+// true.  Window lengths follow the run lengths seen for each hypothesis.
+// ---------------------------------------------------------------------------
+constexpr int kWinMax = 8;
+
+template <typename UT>
+__host__ __device__ constexpr size_t win_smem_bytes(int NP, int NPT, int T, int HC) {
+    return 2 * rc_buf_bytes<UT>(NP, HC) +                                   // staged inputs
+           static_cast<size_t>(kWinMax + 1) * NPT * T * sizeof(float2) +     // updates (+ start state)
+           static_cast<size_t>(kWinMax) * HC * 2 * sizeof(float) +           // candidate outputs
+           static_cast<size_t>(kWinMax) * (T / 32) * sizeof(float2);         // warp residual sums
+}
+
+template <int LANES, int NPT, typename UT>
+__global__ void __launch_bounds__(kRcMaxThreads) cell_repair_window(Args a, int CL, int HC) {
+    constexpr int NP = LANES * NPT;
+    constexpr int V = 3 * kWinMax;  // per step: y_hat (prediction), y if skipped, y if committed
+    using Shape = BflyShape<V, LANES>;
+    __shared__ uint64_t rbar[2];
+    __shared__ float2 slots[2][kRcMaxCL][kWinMax];  // (sum d^2, sum obs^2) per source CTA and step
+    __shared__ float2 wslots[2][kRcMaxCL * (kRcMaxThreads / 32)];  // single steps: per source warp
+    extern __shared__ __align__(16) unsigned char rc_smem[];
+    const int b = blockIdx.y;
+    const int crank = blockIdx.x;
+    const int L = a.L, H = a.H, N = a.N;
+    const int4 rowv = a.row[b];
+    const int lstar = rowv.x;
+    const int tid = threadIdx.x;
+    const int T = blockDim.x, NW = T >> 5;
+    const int ln = tid % LANES, hl = tid / LANES;
+    const int h0 = crank * HC;
+    const int h = h0 + hl;
+    const bool hv = hl < HC && h < H;
+    if (tid == 0) {
+        mbar_init(&rbar[0], 1);
+        mbar_init(&rbar[1], 1);
+        fence_mbar_init();
+    }
+    rc_cluster_sync();  // barriers initialised everywhere before any remote store
+    if (lstar >= L) {
+        rc_cluster_sync();
+        return;
+    }
+    const UT* u = static_cast<const UT*>(a.u);
+    const size_t rowLH = static_cast<size_t>(b) * L;
+    const int lp = lstar > 0 ? lstar - 1 : 0;
+    const bool resumed = a.cin_row != nullptr;
+    const bool from_carry = lstar == 0 && resumed;
+
+    float2 lam[NPT], ilam[NPT], hs[NPT], Cp[NPT], Wc[NPT];
+    bool nv[NPT];
+    const float scale = hv ? expf(a.log_dt[h]) : 1.f;
+    const float rsd = hv ? 1.0f / sqrtf(a.var[h] + a.var_eps) : 1.f;
+    const float mu = hv ? a.mean[h] : 0.f;
+    // committed inputs (u_pi, B_pi, C_pi) of step lc, or with lc < 0 those the
+    // row held before l*: step l* - 1's, a resumed row's carried ones, or step 0's
+    auto committed_inputs = [&](int lc, float& upi, float2 (&Bq)[NPT], float2 (&Cq)[NPT]) {
+        const int ls = lc >= 0 ? lc : lp;
+        upi = hv ? to_f32(u[(rowLH + ls) * H + h]) : 0.f;
+        if (lc < 0 && from_carry && hv) upi = a.cin_u[static_cast<size_t>(b) * H + h];
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            Bq[j] = n < N ? a.Bc[(rowLH + ls) * N + n] : make_float2(0.f, 0.f);
+            Cq[j] = n < N ? a.Cc[(rowLH + ls) * N + n] : make_float2(0.f, 0.f);
+            if (lc < 0 && from_carry && n < N) {
+                Bq[j] = a.cin_B[static_cast<size_t>(b) * N + n];
+                Cq[j] = a.cin_C[static_cast<size_t>(b) * N + n];
+            }
+        }
+    };
+    float u_pi;
+    {
+        float2 Bq[NPT];
+        committed_inputs(-1, u_pi, Bq, Cp);
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            nv[j] = hv && n < N;
+            const size_t o = static_cast<size_t>(hv ? h : 0) * N + (n < N ? n : 0);
+            lam[j] = nv[j] ? a.lam[o] : make_float2(-1.f, 0.f);
+            ilam[j] = crecip(lam[j]);
+            hs[j] = nv[j] ? a.hpi[static_cast<size_t>(b) * H * N + o] : make_float2(0.f, 0.f);
+            Wc[j] = cscale(cmul(Bq[j], ilam[j]), u_pi);
+        }
+    }
+    float t_pi = lstar > 0 ? a.t[rowLH + lp] : a.t[rowLH] - a.dt_init;
+    if (from_carry) t_pi = a.cin_row[b].x;
+    float spike = __int_as_float(rowv.y);
+    float prev_r = __int_as_float(rowv.z);
+    int lc = -1;  // last committed step since l* (-1: none yet)
+
+    // shared memory: staged inputs (kRcT steps per buffer, two buffers), the
+    // window's updates [k][j][thread] and the start state, candidate outputs,
+    // per-warp residual sums
+    const int HC2 = (HC + 1) & ~1;
+    const size_t buf_bytes = rc_buf_bytes<UT>(NP, HC);
+    auto sBl = [&](int buf, int i) { return reinterpret_cast<float2*>(rc_smem + buf * buf_bytes) + i * NP; };
+    auto sCl = [&](int buf, int i) { return reinterpret_cast<float2*>(rc_smem + buf * buf_bytes) + (kRcT + i) * NP; };
+    auto stl = [&](int buf) { return reinterpret_cast<float*>(rc_smem + buf * buf_bytes + 2 * kRcT * NP * sizeof(float2)); };
+    auto sul = [&](int buf, int i) {
+        return reinterpret_cast<UT*>(rc_smem + buf * buf_bytes + 2 * kRcT * NP * sizeof(float2) + kRcT * sizeof(float)) +
+               i * HC2;
+    };
+    float2* hist = reinterpret_cast<float2*>(rc_smem + 2 * buf_bytes);
+    float* ycand = reinterpret_cast<float*>(hist + static_cast<size_t>(kWinMax + 1) * NPT * T);
+    float2* wsum = reinterpret_cast<float2*>(ycand + static_cast<size_t>(kWinMax) * HC * 2);
+
+    constexpr bool kPair = sizeof(UT) == 2;
+    const bool async_ok = (reinterpret_cast<uintptr_t>(u) & 3u) == 0 && (!kPair || ((H | h0) & 1) == 0) &&
+                          ((reinterpret_cast<uintptr_t>(a.Bc) | reinterpret_cast<uintptr_t>(a.Cc)) & 7u) == 0 &&
+                          (reinterpret_cast<uintptr_t>(a.t) & 3u) == 0;
+    // chunk c holds steps [l* + c kRcT, l* + (c+1) kRcT) in buffer c & 1
+    auto stage = [&](int c) {
+        const int c0 = lstar + c * kRcT, buf = c & 1;
+        const int sn = min(kRcT, L - c0);
+        for (int idx = tid; idx < sn * NP; idx += T) {
+            const int i = idx / NP, n = idx % NP;
+            const size_t o = (rowLH + c0 + i) * N + n;
+            if (async_ok) {
+                cp_async8(sBl(buf, i) + n, n < N ? a.Bc + o : a.Bc, n < N);
+                cp_async8(sCl(buf, i) + n, n < N ? a.Cc + o : a.Cc, n < N);
+            } else {
+                sBl(buf, i)[n] = n < N ? a.Bc[o] : make_float2(0.f, 0.f);
+                sCl(buf, i)[n] = n < N ? a.Cc[o] : make_float2(0.f, 0.f);
+            }
+        }
+        constexpr int P = kPair ? 2 : 1;
+        for (int idx = tid; idx < sn * (HC2 / P); idx += T) {
+            const int i = idx / (HC2 / P), c2 = (idx % (HC2 / P)) * P;
+            const bool ok = h0 + c2 < H && c2 < HC;
+            const UT* src = u + (rowLH + c0 + i) * H + h0 + c2;
+            if (async_ok) {
+                cp_async4(sul(buf, i) + c2, ok ? src : u, ok);
+            } else {
+#pragma unroll
+                for (int e = 0; e < P; ++e)
+                    sul(buf, i)[c2 + e] = (h0 + c2 + e < H && c2 + e < HC) ? src[e] : static_cast<UT>(0.f);
+            }
+        }
+        for (int i = tid; i < sn; i += T) {
+            if (async_ok) cp_async4(stl(buf) + i, a.t + rowLH + c0 + i, true);
+            else stl(buf)[i] = a.t[rowLH + c0 + i];
+        }
+        if (async_ok) cp_async_commit();
+    };
+    int issued = 0, ready = 0;  // chunks issued / known complete (uniform over the CTA)
+    const int nchunks = (L - lstar + kRcT - 1) / kRcT;
+
+    float run_est[2] = {2.f, 2.f};  // run lengths seen for "skip" (0) and "commit" (1)
+    int run = 0;                    // accepted steps of the current hypothesis so far
+    bool cr = false;                // l* skips: the first window assumes skips
+    int wlen = kWinMax;
+    bool failed = false;
+    for (int l0 = lstar, w = 0; l0 < L; ++w) {
+        const int Wn = min(wlen, L - l0);
+        const int r0 = l0 - lstar;
+        const int cA = r0 / kRcT, cB = (r0 + Wn - 1) / kRcT;
+        while (issued <= cB) stage(issued++);
+        if (ready <= cB) {
+            if (async_ok) cp_async_wait_all();
+            __syncthreads();
+            ready = issued;
+        }
+        if (cA == cB && issued == cB + 1 && issued < nchunks) stage(issued++);  // the next chunk
+
+        if (Wn == 1) {
+            // ---- one step (short runs): every warp sends its own partial sums
+            // straight to every CTA, and no shared-memory staging of results ----
+            const int buf = (r0 / kRcT) & 1, i = r0 % kRcT;
+            const float tl = stl(buf)[i];
+            const float ul = hv ? to_f32(sul(buf, i)[hl]) : 0.f;
+            const float dte = eff_dt(fmaxf(tl - t_pi, 0.f), scale, a.dt_min, a.dt_max);
+            float2 P[NPT], E[NPT], xh[NPT];
+            float yhp = 0.f;
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                float2 dA;
+                zoh_e(lam[j], dte, dA, E[j]);
+                P[j] = cmul(dA, hs[j]);
+                xh[j] = cfma(E[j], Wc[j], P[j]);
+                yhp += cre_mul(Cp[j], xh[j]);
+            }
+#pragma unroll
+            for (int o = LANES / 2; o > 0; o >>= 1) yhp += __shfl_xor_sync(0xffffffffu, yhp, o);
+            float d2 = 0.f, o2 = 0.f;
+            if (hv && ln == 0) {
+                const float obs = (ul - mu) * rsd;
+                const float dd = obs - (yhp - mu) * rsd;
+                d2 = dd * dd;
+                o2 = obs * obs;
+            }
+            d2 = warp_sum(d2);
+            o2 = warp_sum(o2);
+            const int par = w & 1;
+            const uint32_t phase = (w >> 1) & 1;
+            const int nslot = CL * NW;
+            if (!failed) {
+                if (tid == 0) mbar_expect_tx(&rbar[par], static_cast<uint32_t>(nslot) * 8u);
+                if ((tid & 31) < CL) {  // lane c sends to CTA c
+                    const uint32_t rs = mapa_u32(&wslots[par][crank * NW + (tid >> 5)], tid & 31);
+                    const uint32_t rb = mapa_u32(&rbar[par], tid & 31);
+                    st_async_f32(rs, d2, rb);
+                    st_async_f32(rs + 4u, o2, rb);
+                }
+                if (!mbar_wait_row(&rbar[par], phase)) failed = true;
+            }
+            float s1 = 0.f, s2 = 0.f;
+            for (int q = tid & 31; q < nslot; q += 32) {
+                const float2 v = wslots[par][q];
+                s1 += v.x;
+                s2 += v.y;
+            }
+            s1 = warp_sum(s1);
+            s2 = warp_sum(s2);
+            const float num = sqrtf(s1), nobs = sqrtf(s2);
+            const float r = num / (nobs + a.eta);
+            float eps_l = a.eps;
+            if (a.robust && spike >= static_cast<float>(a.robust_k)) eps_l = a.eps_lo;
+            const bool g = r > eps_l;
+            if (a.robust && (l0 > 0 || resumed)) spike = (r > prev_r * a.spike_ratio) ? spike + 1.f : 0.f;
+            prev_r = r;
+            if (crank == 0 && tid == 0) {
+                a.gate[rowLH + l0] = g ? 1.f : 0.f;
+                a.resid[rowLH + l0] = r;
+                if (a.stats) a.stats[rowLH + l0] = make_float2(num, nobs);
+            }
+            float yp = 0.f;
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                const float2 Cl = sCl(buf, i)[ln + LANES * j];
+                float2 hc = xh[j];
+                if (g) {
+                    const float2 Wk = cscale(cmul(sBl(buf, i)[ln + LANES * j], ilam[j]), ul);
+                    hc = cfma(E[j], Wk, P[j]);
+                    hs[j] = hc;
+                    Wc[j] = Wk;
+                    Cp[j] = Cl;
+                }
+                yp += cre_mul(Cl, hc);
+            }
+#pragma unroll
+            for (int o = LANES / 2; o > 0; o >>= 1) yp += __shfl_xor_sync(0xffffffffu, yp, o);
+            if (hv && ln == 0) a.y[(rowLH + l0) * H + h] = yp + a.D[h] * ul;
+            if (g) {
+                t_pi = tl;
+                u_pi = ul;
+                lc = l0;
+            }
+            const int hyp = cr ? 1 : 0;
+            if (g != cr) {
+                run_est[hyp] = 0.5f * run_est[hyp] + 0.5f * static_cast<float>(run);
+                run = 1;
+                cr = g;
+            } else {
+                ++run;
+            }
+            const float m = fmaxf(run_est[cr ? 1 : 0], static_cast<float>(run));
+            wlen = m < 5.f ? 1 : min(kWinMax, max(2, __float2int_rn(sqrtf(1.3f * m))));
+            ++l0;
+            continue;
+        }
+
+        // ---- the window under the hypothesis ----
+        if (cr) {
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) hist[(static_cast<size_t>(kWinMax) * NPT + j) * T + tid] = hs[j];
+        }
+        float vals[V];
+        float tp = t_pi;
+#pragma unroll
+        for (int k = 0; k < kWinMax; ++k) {
+            vals[k] = vals[kWinMax + k] = vals[2 * kWinMax + k] = 0.f;
+            if (k < Wn) {
+                const int r = r0 + k, buf = (r / kRcT) & 1, i = r % kRcT;
+                const float tl = stl(buf)[i];
+                const float ul = hv ? to_f32(sul(buf, i)[hl]) : 0.f;
+                const float dte = eff_dt(fmaxf(tl - tp, 0.f), scale, a.dt_min, a.dt_max);
+                float yh = 0.f, ys = 0.f, yc = 0.f;
+#pragma unroll
+                for (int j = 0; j < NPT; ++j) {
+                    const float2 Bl = sBl(buf, i)[ln + LANES * j];
+                    const float2 Cl = sCl(buf, i)[ln + LANES * j];
+                    float2 dA, E;
+                    zoh_e(lam[j], dte, dA, E);
+                    const float2 P = cmul(dA, hs[j]);
+                    const float2 xh = cfma(E, Wc[j], P);
+                    const float2 Wk = cscale(cmul(Bl, ilam[j]), ul);
+                    const float2 hk = cfma(E, Wk, P);
+                    yh += cre_mul(Cp[j], xh);
+                    ys += cre_mul(Cl, xh);
+                    yc += cre_mul(Cl, hk);
+                    hist[(static_cast<size_t>(k) * NPT + j) * T + tid] = hk;
+                    if (cr) {  // the next step's committed state is this step's update
+                        hs[j] = hk;
+                        Wc[j] = Wk;
+                        Cp[j] = Cl;
+                    }
+                }
+                if (cr) tp = tl;
+                vals[k] = yh;
+                vals[kWinMax + k] = ys;
+                vals[2 * kWinMax + k] = yc;
+            }
+        }
+        Bfly<V, LANES / 2>::run(vals, ln);
+        // residual terms of the predictions; candidate outputs to shared memory
+        float dd[Shape::kRem], oo[Shape::kRem];
+        const int held = Shape::held_index(ln);
+#pragma unroll
+        for (int q = 0; q < Shape::kRem; ++q) {
+            const int orig = held + q, k = orig % kWinMax, kind = orig / kWinMax;
+            dd[q] = 0.f;
+            oo[q] = 0.f;
+            if (hv && k < Wn) {
+                if (kind == 0) {
+                    const int r = r0 + k;
+                    const float ul = to_f32(sul((r / kRcT) & 1, r % kRcT)[hl]);
+                    const float obs = (ul - mu) * rsd;
+                    const float d = obs - (vals[q] - mu) * rsd;
+                    dd[q] = d * d;
+                    oo[q] = obs * obs;
+                } else if ((ln & Shape::kPlainMask) == 0) {
+                    ycand[(k * HC + hl) * 2 + (kind - 1)] = vals[q];
+                }
+            }
+        }
+#pragma unroll
+        for (int o = LANES; o < 32; o <<= 1) {
+#pragma unroll
+            for (int q = 0; q < Shape::kRem; ++q) {
+                dd[q] += __shfl_xor_sync(0xffffffffu, dd[q], o);
+                oo[q] += __shfl_xor_sync(0xffffffffu, oo[q], o);
+            }
+        }
+        if ((tid & 31) < LANES && (ln & Shape::kPlainMask) == 0) {
+#pragma unroll
+            for (int q = 0; q < Shape::kRem; ++q) {
+                const int orig = held + q;
+                if (orig < Wn) wsum[orig * NW + (tid >> 5)] = make_float2(dd[q], oo[q]);
+            }
+        }
+        __syncthreads();
+        // ---- one exchange: this CTA's sums of the window's steps to every CTA ----
+        const int par = w & 1;
+        const uint32_t phase = (w >> 1) & 1;
+        if (!failed) {
+            if (tid == 0) mbar_expect_tx(&rbar[par], static_cast<uint32_t>(CL * Wn) * 8u);
+            if (tid < Wn) {
+                float s1 = 0.f, s2 = 0.f;
+                for (int q = 0; q < NW; ++q) {
+                    const float2 v = wsum[tid * NW + q];
+                    s1 += v.x;
+                    s2 += v.y;
+                }
+                for (int c = 0; c < CL; ++c) {
+                    const uint32_t rs = mapa_u32(&slots[par][crank][tid], c), rb = mapa_u32(&rbar[par], c);
+                    st_async_f32(rs, s1, rb);
+                    st_async_f32(rs + 4u, s2, rb);
+                }
+            }
+            if (!mbar_wait_row(&rbar[par], phase)) failed = true;
+        }
+        // ---- gates in order, up to the first step against the hypothesis ----
+        int A = Wn;
+        unsigned gmask = 0u;
+        bool deviated = false;
+        for (int k = 0; k < Wn; ++k) {
+            float s1 = 0.f, s2 = 0.f;
+            for (int c = 0; c < CL; ++c) {
+                const float2 v = slots[par][c][k];
+                s1 += v.x;
+                s2 += v.y;
+            }
+            const float num = sqrtf(s1), nobs = sqrtf(s2);
+            const float r = num / (nobs + a.eta);
+            const int l = l0 + k;
+            float eps_l = a.eps;
+            if (a.robust && spike >= static_cast<float>(a.robust_k)) eps_l = a.eps_lo;
+            const bool g = r > eps_l;
+            if (a.robust && (l > 0 || resumed)) spike = (r > prev_r * a.spike_ratio) ? spike + 1.f : 0.f;
+            prev_r = r;
+            if (crank == 0 && tid == 0) {
+                a.gate[rowLH + l] = g ? 1.f : 0.f;
+                a.resid[rowLH + l] = r;
+                if (a.stats) a.stats[rowLH + l] = make_float2(num, nobs);
+            }
+            if (g) gmask |= 1u << k;
+            if (g != cr) {
+                A = k + 1;
+                deviated = true;
+                break;
+            }
+        }
+        // ---- outputs of the accepted steps ----
+        for (int idx = tid; idx < A * HC; idx += T) {
+            const int k = idx / HC, c = idx % HC;
+            const int hh = h0 + c;
+            if (hh < H) {
+                const int r = r0 + k;
+                const float ul = to_f32(sul((r / kRcT) & 1, r % kRcT)[c]);
+                a.y[(rowLH + l0 + k) * H + hh] = ycand[(k * HC + c) * 2 + ((gmask >> k) & 1u)] + a.D[hh] * ul;
+            }
+        }
+        // ---- the committed state after the window ----
+        const bool last_g = (gmask >> (A - 1)) & 1u;
+        const int kc = last_g ? A - 1 : (cr ? A - 2 : -1);
+        if (kc >= 0) {
+            const int r = r0 + kc, buf = (r / kRcT) & 1, i = r % kRcT;
+            t_pi = stl(buf)[i];
+            u_pi = hv ? to_f32(sul(buf, i)[hl]) : 0.f;
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                hs[j] = hist[(static_cast<size_t>(kc) * NPT + j) * T + tid];
+                Cp[j] = sCl(buf, i)[ln + LANES * j];
+                Wc[j] = cscale(cmul(sBl(buf, i)[ln + LANES * j], ilam[j]), u_pi);
+            }
+            lc = l0 + kc;
+        } else if (cr) {  // "commit" window whose first step skipped: back to its start state
+            float2 Bq[NPT];
+            committed_inputs(lc, u_pi, Bq, Cp);
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                hs[j] = hist[(static_cast<size_t>(kWinMax) * NPT + j) * T + tid];
+                Wc[j] = cscale(cmul(Bq[j], ilam[j]), u_pi);
+            }
+        }
+        // ---- next hypothesis and window length ----
+        const int hyp = cr ? 1 : 0;
+        if (deviated) {
+            run_est[hyp] = 0.5f * run_est[hyp] + 0.5f * static_cast<float>(run + A - 1);
+            run = 1;
+            cr = !cr;
+        } else {
+            run += A;
+        }
+        // Window length: a window of W steps costs about W steps of compute
+        // plus one exchange and accepts (1 - q^W) / (1 - q) steps on average
+        // when the hypothesis holds step to step with probability q = 1 - 1/m
+        // (m the mean run length); with the exchange worth ~0.7 step of
+        // compute (measured at config 1), W ~ sqrt(1.3 m) minimises the cost
+        // per accepted step, and below m = 5 single steps (the lean path) win.
+        const float m = fmaxf(run_est[cr ? 1 : 0], static_cast<float>(run));
+        wlen = m < 5.f ? 1 : min(kWinMax, max(2, __float2int_rn(sqrtf(1.3f * m))));
+        l0 += A;
+        __syncthreads();  // the window's shared memory is reused by the next one
+    }
+    if (a.cout_h != nullptr) {  // the row's state after its last step
+        float2 Bq[NPT], Cq[NPT];
+        float uq;
+        committed_inputs(lc, uq, Bq, Cq);
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            if (nv[j]) a.cout_h[(static_cast<size_t>(b) * H + h) * N + n] = hs[j];
+            if (crank == 0 && hl == 0 && n < N) {
+                a.cout_B[static_cast<size_t>(b) * N + n] = Bq[j];
+                a.cout_C[static_cast<size_t>(b) * N + n] = Cq[j];
+            }
+        }
+        if (hv && ln == 0) a.cout_u[static_cast<size_t>(b) * H + h] = u_pi;
+        if (crank == 0 && tid == 0) a.cout_row[b] = make_float4(t_pi, spike, prev_r, 0.f);
+    }
+    rc_cluster_sync();  // no CTA leaves while a peer may still write its slots
+}
+
+template <int LANES, int NPT, typename UT>
+cudaError_t launch_repair_window(const Args& a, const RcShape& rs, cudaStream_t s) {
+    auto kern = cell_repair_window<LANES, NPT, UT>;
+    cudaError_t e;
+    if (rs.cl > 8) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+    }
+    const size_t smem = win_smem_bytes<UT>(LANES * NPT, NPT, rs.threads, rs.hc);
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
@@ -1328,7 +1845,19 @@ cudaError_t chain_dispatch(const Args& a, int dtype, cudaStream_t s) {
 
 template <typename UT>
 cudaError_t repair_by_n(const Args& a, cudaStream_t s) {
-    const RcShape rs = rc_shape(a.H, a.N);
+    const RcShape rs = rc_shape(a.H, a.N, a.B);
+#ifndef EACS_REPAIR_WINDOW
+#define EACS_REPAIR_WINDOW 1
+#endif
+    if (EACS_REPAIR_WINDOW && rs.cl > 0 && rs.lanes <= 8 && a.gate_mode == 0 && a.commit_h == nullptr &&
+        a.gck_h == nullptr &&
+        win_smem_bytes<UT>(rs.lanes * rs.npt, rs.npt, rs.threads, rs.hc) <= 200u * 1024u) {
+        // hard gate without per-step recording: the windowed speculative repair
+        if (rs.lanes == 4 && rs.npt == 1) return launch_repair_window<4, 1, UT>(a, rs, s);
+        if (rs.lanes == 4 && rs.npt == 2) return launch_repair_window<4, 2, UT>(a, rs, s);
+        if (rs.lanes == 4) return launch_repair_window<4, 4, UT>(a, rs, s);
+        return launch_repair_window<8, 4, UT>(a, rs, s);
+    }
     if (rs.cl > 0) {
         if (rs.lanes == 4 && rs.npt == 1) return launch_repair_cluster<4, 1, UT>(a, rs, s);
         if (rs.lanes == 4 && rs.npt == 2) return launch_repair_cluster<4, 2, UT>(a, rs, s);
@@ -1480,7 +2009,7 @@ int cell_fwd(const CellCall& c, cudaStream_t stream) {
     const bool ckpt = c.ck_h != nullptr;
     if (ckpt && (!c.ck_u || !c.ck_row || !c.ck_bc || c.ck_K <= 0 || (c.ck_K & (c.ck_K - 1)) || c.ck_nK <= 0))
         return fail(EACS_ERR_INVALID, "%s: incomplete checkpoint layout (K a power of two)", fn);
-    if (ckpt && (commits || rc_shape(static_cast<int>(c.H), static_cast<int>(c.N)).cl == 0))
+    if (ckpt && (commits || rc_shape(static_cast<int>(c.H), static_cast<int>(c.N), static_cast<int>(c.B)).cl == 0))
         return fail(EACS_ERR_UNSUPPORTED, "%s: checkpoints need the cluster repair shape and no commits", fn);
     const bool carry = c.cin_h != nullptr || c.cout_h != nullptr;
     if (carry && !cell_resumable(c.H, c.N))

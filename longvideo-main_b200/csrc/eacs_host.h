@@ -124,6 +124,28 @@ int ssm_fwd(const void* lam, const float* log_dt, const float* t, const void* Bc
 size_t ssm_ckpt_size(int64_t B, int64_t L, int64_t H, int64_t N);
 cudaError_t cell_read_status(int* out, cudaStream_t stream);
 int wait_selftest(int polls, cudaStream_t stream);
+
+// LayerNorm + input projections (project.cu)
+struct ProjectCall {
+    const void* x;       // (M, d), x_dtype
+    int x_dtype;
+    const float* gamma;  // (d)
+    const float* beta;
+    float ln_eps;
+    const void* weight;  // (w_rows, d), w_dtype: [proj_u; proj_B; proj_C; zero rows]
+    int w_dtype;
+    int64_t w_rows;
+    const float* bias;   // (H + 4N)
+    void* u;             // (M, H), u_dtype
+    int u_dtype;
+    void* Bc;            // (M, N) complex64
+    void* Cc;
+    int64_t M, d, H, N;
+    void* workspace;     // project_workspace_size(M) bytes
+    size_t workspace_bytes;
+};
+size_t project_workspace_size(int64_t M);
+int project_fwd(const ProjectCall& c, cudaStream_t stream);
 int zoh_kernels(const void* lam, const float* dt, void* dA, void* dBbar, int64_t M, int64_t H,
                 int64_t N, cudaStream_t stream);
 

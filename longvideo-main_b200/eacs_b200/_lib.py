@@ -37,6 +37,9 @@ SIGNATURES = {
     "eacs_device_status": (_I, [ctypes.POINTER(_I), _P]),
     "eacs_kernel_launches": (ctypes.c_uint64, []),
     "eacs_wait_selftest": (_I, [_I, _P]),
+    "eacs_project": (_I, [_P, _I, _P, _P, _F, _P, _I, _I64, _P, _P, _I, _P, _P, _P, _SZ,
+                          _I64, _I64, _I64, _I64, _P]),
+    "eacs_project_workspace_size": (_SZ, [_I64]),
     "eacs_set_kernel_events": (_I, [_P, _P]),
     "eacs_scan_fwd": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "eacs_scan_bwd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),

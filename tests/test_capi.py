@@ -108,3 +108,18 @@ def test_wait_selftest_rejects_bad_poll_counts_without_device():
     for polls in (0, -1, 65537):
         assert lib.eacs_wait_selftest(polls, None) == _lib.EACS_ERR_INVALID
     assert "polls" in _lib.last_error()
+
+
+def test_project_rejects_bad_arguments_without_device():
+    from eacs_b200 import _lib
+    lib = _lib.lib()
+    p = 256
+    # d not a multiple of 8
+    assert lib.eacs_project(p, 1, p, p, 1e-5, p, 1, 256, p, p, 1, p, p, p, 80, 10, 12, 8, 4, None) == _lib.EACS_ERR_UNSUPPORTED
+    # too few weight rows
+    assert lib.eacs_project(p, 1, p, p, 1e-5, p, 1, 0, p, p, 1, p, p, p, 80, 10, 16, 8, 4, None) == _lib.EACS_ERR_INVALID
+    # float32 weight
+    assert lib.eacs_project(p, 1, p, p, 1e-5, p, 0, 256, p, p, 1, p, p, p, 80, 10, 16, 8, 4, None) == _lib.EACS_ERR_INVALID
+    # workspace too small (checked before any launch)
+    assert lib.eacs_project(p, 1, p, p, 1e-5, p, 1, 256, p, p, 1, p, p, p, 8, 10, 16, 8, 4, None) == _lib.EACS_ERR_WORKSPACE
+    assert lib.eacs_project_workspace_size(10) == 80
