@@ -79,7 +79,7 @@ def parse():
     ap.add_argument("--shape", default=None,
                     help="B,L,H,N override for --workload scan, ssm_train, train or longvideo (e.g. a small case for ncu)")
     ap.add_argument("--workload", choices=["cell", "scan", "ssm", "ssm_train", "train", "multiscale",
-                                           "longvideo"],
+                                           "longvideo", "project"],
                     default="cell", help="cell (default) is the headline; the others are the "
                     "materialised scan, the fused ungated SSM, the training step, the "
                     "three-branch multiscale cell and the long-video cell (B=64, H=2048, N=32)")

@@ -468,6 +468,57 @@ def wl_multiscale(args, dev, flush):
          note="input projections (LayerNorm, proj_u/B/C) are outside the timed step")
 
 
+def wl_project(args, dev, flush):
+    """EACS layer input projections inside a float16 autocast region:
+    LayerNorm -> proj_u / proj_B / proj_C (eacs.py:376, :261-267) for config 1's
+    rows and widths (8 x 4096 frames, d = H = 768, N = 16) and config 2's
+    (4 x 16384, d = H = 1024), as one tcgen05 kernel (eacs_project, with its
+    row-statistics pass) against the reference's autocast sequence on the same
+    tensors.  Roofline: tensor, algorithmic flops 2 M d (H + 4N) per launch
+    over the measured dense bf16 GEMM peak."""
+    from eacs_b200.ops.projection import project
+    peaks = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak, src = (json.load(open(peaks))["bf16_tflops"], "measured") if os.path.exists(peaks) else (1590.0, "fallback")
+    out = []
+    for (Bb, Ll, d, Hh, Nn) in ((8, 4096, 768, 768, 16), (4, 16384, 1024, 1024, 16)):
+        torch.manual_seed(0)
+        norm = torch.nn.LayerNorm(d).to(dev)
+        lins = [torch.nn.Linear(d, o).to(dev) for o in (Hh, 2 * Nn, 2 * Nn)]
+        x = torch.randn(Bb, Ll, d, generator=torch.Generator().manual_seed(1)).to(dev).half()
+
+        def ours():
+            project(x, norm, *lins, torch.float16)
+
+        @torch.no_grad()
+        def ref():
+            with torch.autocast("cuda", torch.float16):
+                xn = norm(x)
+                u = lins[0](xn).float()
+                b = lins[1](xn).float()
+                c = lins[2](xn).float()
+                return u, torch.complex(b[..., :Nn], b[..., Nn:]), torch.complex(c[..., :Nn], c[..., Nn:])
+        n = max(5, args.steps // 5)
+        st, kt = timed(ours, n, 3, flush, True)
+        rt, _ = timed(ref, n, 3, flush, False)
+        flops = 2 * Bb * Ll * d * (Hh + 4 * Nn)
+        kms = statistics.median(kt)
+        out.append({"rows": Bb * Ll, "d": d, "H": Hh, "N": Nn, "ms": statistics.median(st),
+                    "kernel_ms": kms, "reference_autocast_ms": statistics.median(rt),
+                    "roofline": {"bound": "tensor", "achieved": flops / (kms / 1e3) / 1e12, "peak": peak,
+                                 "unit": "TFLOP/s", "frac": flops / (kms / 1e3) / 1e12 / peak,
+                                 "peak_source": src, "alg_flops_per_launch": flops}})
+    first = out[0]
+    fl0 = first["roofline"]["alg_flops_per_launch"]
+    line("EACS layer input projections (LayerNorm + proj_u/B/C, fp16 autocast) TFLOP/s", fl0 / (first["ms"] / 1e3) / 1e12,
+         n, 3, first["ms"],
+         {"workload": "LayerNorm + proj_u/B/C as one tcgen05 kernel (plus its row-statistics pass), "
+                      "8 x 4096 rows, d = H = 768, N = 16", "cases": out, "l2": "flushed between steps"},
+         unit="TFLOP/s", dtype="f16 x f16 -> f32",
+         note="value: algorithmic flops / call time at config 1's rows and widths; cases[1] is config 2's widths; "
+              "kernel_ms is the GEMM kernel alone; reference_autocast_ms the reference's sequence on the same tensors")
+    return 0
+
+
 def longvideo_inputs(rows, L, dev, seed, H=2048, N=32):
     """Long-video inputs (H=2048, N=32) for `rows` videos, drawn on the device from one seeded
     generator: fp16 u ~ N(0,1); B, C complex with N(0,1)/sqrt(N) parts;
@@ -608,7 +659,7 @@ def run_workload(args):
     torch.cuda.set_device(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     {"scan": wl_scan, "ssm": wl_ssm, "ssm_train": wl_ssm_train,
-     "multiscale": wl_multiscale}[args.workload](
+     "multiscale": wl_multiscale, "project": wl_project}[args.workload](
         args, dev, flush)
     from eacs_b200 import _lib
     assert _lib.device_status() == 0

@@ -9,6 +9,11 @@ so `cuda_fused_ok` admits it and `forward_fused` passes the layer's
 (EventGate.residual of the detached target, eacs.py:104) has the values of the
 residual and is returned as such.
 
+Inside a float16 / bfloat16 autocast region, LayerNorm and the input
+projections (eacs.py:376, :261-267) run as one tcgen05 kernel
+(ops/projection.py) with autocast's rounding; outside one they run as the
+reference writes them (float32 Linear layers).
+
 install(..., layer_dispatch=True) binds both functions to the reference
 class as `_cuda_fused_ok` and `_forward_fused`.
 """
@@ -41,8 +46,14 @@ def forward_fused(layer, x: Tensor, timestamps: Tensor):
     from .eacs_gated_scan import eacs_cell_forward
 
     x_in = x
-    xn = layer.norm(x)
-    u, Bc, Cc = layer._project(xn)
+    T = torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else None
+    if T in (torch.float16, torch.bfloat16) and x.shape[-1] % 8 == 0:
+        # LayerNorm + _project as autocast runs them, in one tensor-core kernel
+        from .projection import project
+        u, Bc, Cc = project(x, layer.norm, layer.proj_u, layer.proj_B, layer.proj_C, T)
+    else:
+        xn = layer.norm(x)
+        u, Bc, Cc = layer._project(xn)
     robust = ((layer.robust_k, layer.robust_spike_ratio, layer.robust_eps_factor)
               if layer.robust_guard else None)
     ys, gates, resid = eacs_cell_forward(

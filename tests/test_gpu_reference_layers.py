@@ -115,6 +115,37 @@ def test_eacs_layer_eval(ref, half_skip):
                 out_ref.residual.cpu().numpy(), eps)
 
 
+@pytest.mark.parametrize("T", [torch.float16, torch.bfloat16])
+def test_eacs_layer_eval_autocast(ref, T):
+    """EACSLayer.eval() inside an autocast region: after install(layer_dispatch=True)
+    LayerNorm and the input projections run as the tensor-core kernel, the
+    cell and proj_out follow.  The reference runs its own autocast path.  Both
+    round the projections' outputs to T, in different summation orders, so
+    the layer output is compared to 2e-3 of its largest value (a few units in
+    the last place of float16 in the projected inputs) with identical gates."""
+    from cst_ssm.modules.event_gate import EventGate
+    from cst_ssm.ops.spectral_init import BranchSpec
+    torch.manual_seed(0)
+    layer = ref["modules.eacs"].EACSLayer(768, BranchSpec("short", 16, 0.1, 1.0),
+                                          gate=EventGate(init_eps=0.12)).to(DEV).eval()
+    x, t = _video(2, 96, 768, 7)
+    with torch.no_grad(), torch.autocast("cuda", T):
+        n0 = _launches()
+        out_ref = layer(x, t)
+        assert _launches() == n0
+        _install(layer_dispatch=True)
+        calls = dict(_lib_calls())
+        out = layer(x, t)
+        assert _launches() > n0 and _lib_calls().get("eacs_project", 0) > calls.get("eacs_project", 0)
+    assert torch.equal(out.gates, out_ref.gates)
+    assert relerr(out.y.float().cpu().numpy(), out_ref.y.float().cpu().numpy()) < 2e-3
+
+
+def _lib_calls():
+    from eacs_b200 import _lib
+    return _lib.calls
+
+
 def test_multiscale_eval(ref):
     """MultiScaleEACS with config 2's three branch bands (N=16 each), whose
     reference path is the merged sequential loop over the branches."""
