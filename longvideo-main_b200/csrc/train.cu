@@ -255,8 +255,8 @@ __device__ __forceinline__ void cluster_sync_all() {
 // Backward: one cluster of CL CTAs per row, CTA c owns channels
 // [c*HC, (c+1)*HC); thread (hl, ln) owns chains n = ln + LANES*j.
 // ---------------------------------------------------------------------------
-template <int LANES, int NPT, typename UT>
-__global__ void __launch_bounds__(512) train_bwd(TArgs a) {
+template <int LANES, int NPT, typename UT, int MAXT = 512>
+__global__ void __launch_bounds__(MAXT) train_bwd(TArgs a) {
     constexpr int NP = LANES * NPT;
     extern __shared__ __align__(16) unsigned char smem[];
     const int T = blockDim.x;
@@ -742,9 +742,17 @@ int lanes_train(int N, int* lanes, int* npt) {
 
 // Cluster size and channels per CTA: the smallest power-of-two cluster (up to
 // 16) whose CTAs hold at most 512 threads (train_bwd needs ~118 registers a
-// thread, so 512 threads is the most one SM can hold).
-bool train_shape(int64_t H, int lanes, int* CL, int* HC, int* T) {
-    for (int cl = 1; cl <= 16; cl *= 2) {
+// thread, so 512 threads is the most one SM can hold).  With at most
+// kFewRows rows (data-parallel training with one or a few videos per GPU) the
+// rows use 16-CTA clusters: the GPU has room for them, and a row's per-step
+// work is spread over twice the SMs.
+#ifndef EACS_TRAIN_FEW_ROWS
+#define EACS_TRAIN_FEW_ROWS 4
+#endif
+constexpr int kFewRows = EACS_TRAIN_FEW_ROWS;
+bool train_shape(int64_t H, int lanes, int64_t B, int* CL, int* HC, int* T) {
+    const int first = B <= kFewRows ? 16 : 1;
+    for (int cl = first; cl <= 16; cl *= 2) {
         const int64_t hc = (H + cl - 1) / cl;
         const int64_t t = ((hc * lanes + 31) / 32) * 32;
         if (t <= 512) {
@@ -824,7 +832,9 @@ cudaError_t launch_train(TArgs& a, int T, cudaStream_t s) {
         if (e != cudaSuccess) return e;
     }
     const size_t smem = smem_bytes(T, NPT, NP, a.HC, a.K);
-    auto kern = train_bwd<LANES, NPT, UT>;
+    // CTAs of at most 384 threads (config 3: 96 channels x 4 lanes) may use up to
+    // 168 registers a thread; the 512-thread bound (128) made the kernel spill
+    auto kern = T <= 384 ? train_bwd<LANES, NPT, UT, 384> : train_bwd<LANES, NPT, UT, 512>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     if (a.CL > 8) {
@@ -880,7 +890,7 @@ cudaError_t train_by_n(TArgs& a, int T, cudaStream_t s) {
 size_t train_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
     int lanes, npt, CL, HC, T;
     if (B <= 0 || L <= 0 || H <= 0 || N <= 0 || !lanes_train(static_cast<int>(N), &lanes, &npt)) return 0;
-    if (!train_shape(H, lanes, &CL, &HC, &T)) return 0;
+    if (!train_shape(H, lanes, B, &CL, &HC, &T)) return 0;
     const int K = chunk_len(T, npt, lanes * npt, HC);
     if (K == 0) return 0;
     return tws(B, L, H, N, CL, K).total;
@@ -891,7 +901,7 @@ int train_ckpt_layout(int64_t B, int64_t L, int64_t H, int64_t N, void* workspac
     const char* fn = "eacs_cell_train_fwd_ckpt";
     int lanes, npt, CL, HC, T;
     if (B <= 0 || L <= 0 || H <= 0 || N <= 0 || !lanes_train(static_cast<int>(N), &lanes, &npt) ||
-        !train_shape(H, lanes, &CL, &HC, &T))
+        !train_shape(H, lanes, B, &CL, &HC, &T))
         return fail(EACS_ERR_UNSUPPORTED, "%s: no training backward for B=%lld L=%lld H=%lld N=%lld", fn,
                     (long long)B, (long long)L, (long long)H, (long long)N);
     const int K = chunk_len(T, npt, lanes * npt, HC);
@@ -917,7 +927,7 @@ int train_bwd(const TrainBwdCall& c, cudaStream_t stream) {
     int lanes, npt, CL, HC, T;
     if (c.N <= 0 || !lanes_train(static_cast<int>(c.N), &lanes, &npt))
         return fail(EACS_ERR_UNSUPPORTED, "%s: N=%lld outside 1..64", fn, (long long)c.N);
-    if (!train_shape(c.H, lanes, &CL, &HC, &T))
+    if (!train_shape(c.H, lanes, c.B, &CL, &HC, &T))
         return fail(EACS_ERR_UNSUPPORTED, "%s: H=%lld needs more than 16 CTAs of 512 threads per row", fn,
                     (long long)c.H);
     if (c.B > 65535 || c.L > (1LL << 30)) return fail(EACS_ERR_UNSUPPORTED, "%s: B or L too large", fn);
