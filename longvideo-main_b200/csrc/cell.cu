@@ -846,8 +846,8 @@ __host__ __device__ constexpr size_t rc_buf_bytes(int NP, int HC) {
              static_cast<size_t>(kRcT) * ((HC + 1) & ~1) * sizeof(UT)) + 15) & ~static_cast<size_t>(15);
 }
 
-template <int LANES, int NPT, typename UT>
-__global__ void __launch_bounds__(kRcMaxThreads) cell_repair_cluster(Args a, int CL, int HC) {
+template <int LANES, int NPT, typename UT, int MAXT = kRcMaxThreads>
+__global__ void __launch_bounds__(MAXT) cell_repair_cluster(Args a, int CL, int HC) {
     constexpr int NP = LANES * NPT;
     __shared__ uint64_t rbar[2];
     __shared__ float2 slots[2][kRcMaxCL * (kRcMaxThreads / 32)];
@@ -1151,7 +1151,9 @@ RcShape rc_shape(int H, int N, int B) {
 
 template <int LANES, int NPT, typename UT>
 cudaError_t launch_repair_cluster(const Args& a, const RcShape& rs, cudaStream_t s) {
-    auto kern = cell_repair_cluster<LANES, NPT, UT>;
+    // CTAs of at most 384 threads (config 1: 96 channels x 4 lanes) may use up
+    // to 168 registers a thread instead of the 512-thread bound's 128
+    auto kern = rs.threads <= 384 ? cell_repair_cluster<LANES, NPT, UT, 384> : cell_repair_cluster<LANES, NPT, UT>;
     cudaError_t e;
     if (rs.cl > 8) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -1207,8 +1209,8 @@ __host__ __device__ constexpr size_t win_smem_bytes(int NP, int NPT, int T, int 
            static_cast<size_t>(kWinMax) * (T / 32) * sizeof(float2);         // warp residual sums
 }
 
-template <int LANES, int NPT, typename UT>
-__global__ void __launch_bounds__(kRcMaxThreads) cell_repair_window(Args a, int CL, int HC) {
+template <int LANES, int NPT, typename UT, int MAXT = kRcMaxThreads>
+__global__ void __launch_bounds__(MAXT) cell_repair_window(Args a, int CL, int HC) {
     constexpr int NP = LANES * NPT;
     constexpr int V = 3 * kWinMax;  // per step: y_hat (prediction), y if skipped, y if committed
     using Shape = BflyShape<V, LANES>;
@@ -1662,7 +1664,7 @@ __global__ void __launch_bounds__(kRcMaxThreads) cell_repair_window(Args a, int 
 
 template <int LANES, int NPT, typename UT>
 cudaError_t launch_repair_window(const Args& a, const RcShape& rs, cudaStream_t s) {
-    auto kern = cell_repair_window<LANES, NPT, UT>;
+    auto kern = rs.threads <= 384 ? cell_repair_window<LANES, NPT, UT, 384> : cell_repair_window<LANES, NPT, UT>;
     cudaError_t e;
     if (rs.cl > 8) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
