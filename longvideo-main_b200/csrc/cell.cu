@@ -1345,7 +1345,7 @@ __global__ void __launch_bounds__(MAXT) cell_repair_window(Args a, int CL, int H
     int issued = 0, ready = 0;  // chunks issued / known complete (uniform over the CTA)
     const int nchunks = (L - lstar + kRcT - 1) / kRcT;
 
-    float run_est[2] = {2.f, 2.f};  // run lengths seen for "skip" (0) and "commit" (1)
+    float run_skip = 2.f, run_commit = 2.f;  // run lengths seen for each hypothesis
     int run = 0;                    // accepted steps of the current hypothesis so far
     bool cr = false;                // l* skips: the first window assumes skips
     int wlen = kWinMax;
@@ -1445,15 +1445,15 @@ __global__ void __launch_bounds__(MAXT) cell_repair_window(Args a, int CL, int H
                 u_pi = ul;
                 lc = l0;
             }
-            const int hyp = cr ? 1 : 0;
             if (g != cr) {
-                run_est[hyp] = 0.5f * run_est[hyp] + 0.5f * static_cast<float>(run);
+                float& est = cr ? run_commit : run_skip;
+                est = 0.5f * est + 0.5f * static_cast<float>(run);
                 run = 1;
                 cr = g;
             } else {
                 ++run;
             }
-            const float m = fmaxf(run_est[cr ? 1 : 0], static_cast<float>(run));
+            const float m = fmaxf(cr ? run_commit : run_skip, static_cast<float>(run));
             wlen = m < 5.f ? 1 : min(kWinMax, max(2, __float2int_rn(sqrtf(1.3f * m))));
             ++l0;
             continue;
@@ -1624,9 +1624,9 @@ __global__ void __launch_bounds__(MAXT) cell_repair_window(Args a, int CL, int H
             }
         }
         // ---- next hypothesis and window length ----
-        const int hyp = cr ? 1 : 0;
         if (deviated) {
-            run_est[hyp] = 0.5f * run_est[hyp] + 0.5f * static_cast<float>(run + A - 1);
+            float& est = cr ? run_commit : run_skip;
+            est = 0.5f * est + 0.5f * static_cast<float>(run + A - 1);
             run = 1;
             cr = !cr;
         } else {
@@ -1638,7 +1638,7 @@ __global__ void __launch_bounds__(MAXT) cell_repair_window(Args a, int CL, int H
         // (m the mean run length); with the exchange worth ~0.7 step of
         // compute (measured at config 1), W ~ sqrt(1.3 m) minimises the cost
         // per accepted step, and below m = 5 single steps (the lean path) win.
-        const float m = fmaxf(run_est[cr ? 1 : 0], static_cast<float>(run));
+        const float m = fmaxf(cr ? run_commit : run_skip, static_cast<float>(run));
         wlen = m < 5.f ? 1 : min(kWinMax, max(2, __float2int_rn(sqrtf(1.3f * m))));
         l0 += A;
         __syncthreads();  // the window's shared memory is reused by the next one
