@@ -238,21 +238,28 @@ def reference_run(layer, cpu, L_s, threads):
     """The reference's scan_range (skip_compute inference path, as
     EACSLayer.forward runs it, eacs.py:276-285 and :340-349) over the first
     L_s frames of all B videos of the op-boundary tensors `cpu` (host
-    tensors).  Returns (updates/s, seconds, (ys, gates, resid))."""
+    tensors, or device tensors with the layer on that device).  Returns
+    (updates/s, seconds, (ys, gates, resid) as numpy)."""
     torch.set_num_threads(threads)
+    dev = cpu["u"].device
     u = cpu["u"][:, :L_s].float()
     Bc, Cc, t = cpu["Bc"][:, :L_s], cpu["Cc"][:, :L_s], cpu["t"][:, :L_s]
     lam = layer.lam().to(torch.complex64)
-    state = (torch.zeros(B, H, N, dtype=torch.complex64), t[:, 0] - layer.dt_init, u[:, 0], Bc[:, 0],
+    state = (torch.zeros(B, H, N, dtype=torch.complex64, device=dev), t[:, 0] - layer.dt_init, u[:, 0], Bc[:, 0],
              Cc[:, 0])
+    if dev.type == "cuda":
+        torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
     ys, gs, rs, _, _ = layer._scan_range(lam, state, u, Bc, Cc, t, 0, L_s)
+    if dev.type == "cuda":
+        torch.cuda.synchronize(dev)
     dt = time.perf_counter() - t0
-    return B * L_s * H * N / dt, dt, (ys.numpy(), gs.numpy(), rs.numpy())
+    return B * L_s * H * N / dt, dt, (ys.cpu().numpy(), gs.cpu().numpy(), rs.cpu().numpy())
 
 
 def reference_sample_len(layer, cpu, threads, seconds):
-    rate, _, _ = reference_run(layer, cpu, 8, threads)
+    reference_run(layer, cpu, 8, threads)  # first call: thread pool start-up
+    rate, _, _ = reference_run(layer, cpu, 64, threads)
     return int(max(2, min(L, seconds * rate / (B * H * N))))
 
 
@@ -578,6 +585,18 @@ def run_ours(args):
         }
         if ref_cuda is not None:
             line["reference_cuda"] = ref_cuda
+        layer = reference_layer() if (world == 1 and not args.profile and args.eps is None) else None
+        if layer is not None:  # the reference's PyTorch path on this GPU (its Python step loop)
+            layer = layer.to(dev)
+            reference_run(layer, d, 4, 1)  # warm-up
+            L_g = 256
+            rate_g, secs_g, (yg, _, _) = reference_run(layer, d, L_g, 1)
+            yd = y[:, :L_g].cpu().numpy()
+            line["reference_pytorch_gpu"] = {
+                "value": rate_g / 1e9, "unit": UNIT, "frames": L_g, "seconds": secs_g,
+                "y_rel_vs_this_build": float(np.abs(yd - yg).max() / np.abs(yg).max()),
+                "what": f"cst_ssm/modules/eacs.py scan_range (PyTorch step loop) on this GPU, first {L_g} of "
+                        f"{L} frames of all {B} videos"}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
