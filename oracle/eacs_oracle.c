@@ -606,6 +606,129 @@ int eacs_oracle_query_readout(const float* lam, const float* log_dt, const float
 }
 
 /* ---------------------------------------------------------------------------
+ * Adjoint of readout_from_commits (continuous_query.py:20-54) before the
+ * layer's proj_out: given gy (B,Q,H) = dLoss/dy, accumulate (in double, rows
+ * in order, queries in order) the adjoints of the commits the queries read,
+ *   x* = dA h_pi + dB_bar B_pi u_pi,  y = Re sum_n C_pi x* + D u_pi,
+ *   dA = e^z, dB_bar = expm1(z)/lam, z = lam dte,
+ *   dte = clamp(max(t_q - t_pi, 0) e^log_dt, dt_min, dt_max),
+ * into gcH (B,L,H,N) complex, gcT (B,L), gcU (B,L,H), gcB, gcC (B,L,N) complex
+ * (overwritten: zero where no query reads a frame), the query times' gtq
+ * (B,Q) (may be NULL) and the parameters' dlam (H,N) complex, dlog (H), dD (H).
+ * idx as for eacs_oracle_query_readout (NULL = segment_index of t_query).
+ * ------------------------------------------------------------------------- */
+int eacs_oracle_query_readout_bwd(const float* lam, const float* log_dt, const float* D,
+                                  const float* ch, const float* ct, const float* cu,
+                                  const float* cB, const float* cC, const float* frame_t,
+                                  const float* t_query, const int32_t* idx, const float* gy,
+                                  float* gcH, float* gcT, float* gcU, float* gcB, float* gcC,
+                                  float* gtq, float* dlam, float* dlog, float* dD,
+                                  int64_t B, int64_t L, int64_t Q, int64_t H, int64_t N,
+                                  float dt_min, float dt_max) {
+    const int64_t HN = H * N;
+    double* acc_lam = (double*)calloc((size_t)(B * HN * 2), sizeof(double));
+    double* acc_log = (double*)calloc((size_t)(B * H), sizeof(double));
+    double* acc_D = (double*)calloc((size_t)(B * H), sizeof(double));
+#pragma omp parallel for num_threads(nthreads()) schedule(dynamic, 1)
+    for (int64_t bi = 0; bi < B; ++bi) {
+        cd* aH = (cd*)calloc((size_t)(L * HN), sizeof(cd));
+        cd* aB = (cd*)calloc((size_t)(L * N), sizeof(cd));
+        cd* aC = (cd*)calloc((size_t)(L * N), sizeof(cd));
+        double* aU = (double*)calloc((size_t)(L * H), sizeof(double));
+        double* aT = (double*)calloc((size_t)L, sizeof(double));
+        double* alam = acc_lam + bi * HN * 2;
+        double* alog = acc_log + bi * H;
+        double* aD = acc_D + bi * H;
+        for (int64_t q = 0; q < Q; ++q) {
+            const float tq = t_query[bi * Q + q];
+            const int64_t k = idx ? idx[bi * Q + q] : segment_index(frame_t + bi * L, L, tq);
+            const int64_t row = bi * L + k;
+            const double draw = (double)tq - (double)ct[row];
+            const double delta = draw > 0 ? draw : 0;
+            double deltabar = 0;
+            for (int64_t hh = 0; hh < H; ++hh) {
+                const double sc = exp((double)log_dt[hh]);
+                const double dte_raw = delta * sc;
+                double dte = dte_raw < dt_min ? dt_min : dte_raw;
+                if (dte > dt_max) dte = dt_max;
+                const double upi = cu[row * H + hh];
+                const double gyv = gy[(bi * Q + q) * H + hh];
+                aD[hh] += gyv * upi;
+                aU[k * H + hh] += gyv * D[hh];
+                double dtebar = 0;
+                for (int64_t n = 0; n < N; ++n) {
+                    const int64_t i = hh * N + n;
+                    const cd lm = {lam[2 * i], lam[2 * i + 1]};
+                    const double d2 = lm.re * lm.re + lm.im * lm.im;
+                    const cd il = {lm.re / d2, -lm.im / d2};
+                    const double a = lm.re * dte, b = lm.im * dte, e = exp(a);
+                    const cd dA = {e * cos(b), e * sin(b)};
+                    const cd E = {expm1(a) * cos(b) - 2 * sin(0.5 * b) * sin(0.5 * b), e * sin(b)};
+                    const cd dB = cd_mul(E, il);
+                    const cd hp = cd_of(ch + ((row * H + hh) * N + n) * 2);
+                    const cd Bp = cd_of(cB + (row * N + n) * 2);
+                    const cd Cp = cd_of(cC + (row * N + n) * 2);
+                    const cd qv = cd_mul(dB, Bp);
+                    const cd xs = cd_add(cd_mul(dA, hp), cd_scale(qv, upi));
+                    const cd ax = cd_scale(cd_conj(Cp), gyv);
+                    aC[k * N + n] = cd_add(aC[k * N + n], cd_scale(cd_conj(xs), gyv));
+                    aH[k * HN + i] = cd_add(aH[k * HN + i], cd_mul(cd_conj(dA), ax));
+                    aU[k * H + hh] += cd_redot(ax, qv);
+                    const cd aq = cd_scale(ax, upi);
+                    aB[k * N + n] = cd_add(aB[k * N + n], cd_mul(cd_conj(dB), aq));
+                    const cd adB = cd_mul(aq, cd_conj(Bp));
+                    const cd adA = cd_mul(cd_conj(hp), ax);
+                    const cd aE = cd_mul(adB, cd_conj(il));
+                    const cd ail = cd_mul(adB, cd_conj(E));
+                    cd alm = cd_scale(cd_mul(cd_conj(cd_mul(il, il)), ail), -1.0);
+                    const cd az = cd_mul(cd_conj(dA), cd_add(adA, aE));
+                    alm = cd_add(alm, cd_scale(az, dte));
+                    dtebar += cd_redot(az, lm);
+                    alam[2 * i] += alm.re;
+                    alam[2 * i + 1] += alm.im;
+                }
+                const double m = (dte_raw >= dt_min && dte_raw <= (double)dt_max) ? 1.0 : 0.0;
+                const double drb = m * dtebar;
+                deltabar += drb * sc;
+                alog[hh] += drb * delta * sc;
+            }
+            const double mdel = draw >= 0 ? 1.0 : 0.0;
+            if (gtq) gtq[bi * Q + q] = (float)(mdel * deltabar);
+            aT[k] -= mdel * deltabar;
+        }
+        for (int64_t l = 0; l < L; ++l) {
+            const int64_t rl = bi * L + l;
+            gcT[rl] = (float)aT[l];
+            for (int64_t hh = 0; hh < H; ++hh) gcU[rl * H + hh] = (float)aU[l * H + hh];
+            for (int64_t i = 0; i < HN; ++i) {
+                gcH[(rl * HN + i) * 2] = (float)aH[l * HN + i].re;
+                gcH[(rl * HN + i) * 2 + 1] = (float)aH[l * HN + i].im;
+            }
+            for (int64_t n = 0; n < N; ++n) {
+                gcB[(rl * N + n) * 2] = (float)aB[l * N + n].re;
+                gcB[(rl * N + n) * 2 + 1] = (float)aB[l * N + n].im;
+                gcC[(rl * N + n) * 2] = (float)aC[l * N + n].re;
+                gcC[(rl * N + n) * 2 + 1] = (float)aC[l * N + n].im;
+            }
+        }
+        free(aH); free(aB); free(aC); free(aU); free(aT);
+    }
+    for (int64_t i = 0; i < HN * 2; ++i) {
+        double s = 0;
+        for (int64_t bi = 0; bi < B; ++bi) s += acc_lam[bi * HN * 2 + i];
+        dlam[i] = (float)s;
+    }
+    for (int64_t hh = 0; hh < H; ++hh) {
+        double s = 0, s2 = 0;
+        for (int64_t bi = 0; bi < B; ++bi) { s += acc_log[bi * H + hh]; s2 += acc_D[bi * H + hh]; }
+        dlog[hh] = (float)s;
+        dD[hh] = (float)s2;
+    }
+    free(acc_lam); free(acc_log); free(acc_D);
+    return 0;
+}
+
+/* ---------------------------------------------------------------------------
  * Streaming steps with explicit branch state (streaming.py:45-85 per branch,
  * over eacs_step eacs.py:78-142 and EventGate.forward event_gate.py:86-105).
  * Per row and step k (valid masks, first observation of a row commits with
@@ -736,14 +859,18 @@ typedef struct {
     cd *hpi, *Bpi, *Cpi;
 } dstate;
 
-int eacs_oracle_cell_bwd(const float* lam, const float* log_dt, const float* u,
+static int cell_bwd_impl(const float* lam, const float* log_dt, const float* u,
                          const float* Bc, const float* Cc, const float* t,
                          const float* D, const float* mean, const float* var,
                          float eps, float eta, float var_eps, float dt_init,
                          float dt_max, float T, int gate_mode, const float* gs,
                          const float* gy, const float* ggs, const float* grs,
-                         const float* gns, float* du, float* dBc, float* dCc,
+                         const float* gns, const float* gcH, const float* gcT,
+                         const float* gcU, const float* gcB, const float* gcC,
+                         float* du, float* dBc, float* dCc,
                          float* dt, float* dlam, float* dlog, float* dD, float* deps,
+                         float* y_out, float* g_out, float* r_out, float* ch_out,
+                         float* ct_out, float* cu_out, float* cB_out, float* cC_out,
                          int64_t B, int64_t L, int64_t H, int64_t N) {
     const double dt_min = 1e-3;
     const double Tp = T > 1e-4f ? (double)T : 1e-4;
@@ -838,7 +965,7 @@ int eacs_oracle_cell_bwd(const float* lam, const float* log_dt, const float* u,
             num = sqrt(sdiff); nobs = sqrt(sobs); den = nobs + eta;                   \
             r = num / den;                                                            \
             soft = 1.0 / (1.0 + exp(-((r - (double)eps) / Tp)));                      \
-            g = gate_mode == 1 ? soft : (double)gs[bi * L + l];                       \
+            g = gate_mode == 1 ? soft : gs ? (double)gs[bi * L + l] : (r > (double)eps ? 1.0 : 0.0); \
             for (int64_t hh = 0; hh < H; ++hh) {                                      \
                 double ul = ub[l * H + hh];                                           \
                 for (int64_t n = 0; n < N; ++n) {                                     \
@@ -862,7 +989,40 @@ int eacs_oracle_cell_bwd(const float* lam, const float* log_dt, const float* u,
         } while (0)
 
         double draw, delta, sdiff, sobs, num, nobs, den, r, soft, g;
-        for (int64_t l = 0; l < L; ++l) STEP_FWD(l, 1);
+        for (int64_t l = 0; l < L; ++l) {
+            STEP_FWD(l, 1);
+            /* optional forward outputs: y, gate, residual and the commits
+             * (the state after the step) */
+            const int64_t rl = bi * L + l;
+            if (y_out) {
+                for (int64_t hh = 0; hh < H; ++hh) {
+                    double acc = 0;
+                    for (int64_t n = 0; n < N; ++n) {
+                        cd c = cd_of(Cb + 2 * (l * N + n));
+                        acc += c.re * hcur[hh * N + n].re - c.im * hcur[hh * N + n].im;
+                    }
+                    y_out[rl * H + hh] = (float)(acc + (double)D[hh] * ub[l * H + hh]);
+                }
+            }
+            if (g_out) g_out[rl] = (float)g;
+            if (r_out) r_out[rl] = (float)r;
+            const dstate* S2 = &st[l + 1];
+            if (ch_out)
+                for (int64_t i = 0; i < HN; ++i) {
+                    ch_out[(rl * HN + i) * 2] = (float)S2->hpi[i].re;
+                    ch_out[(rl * HN + i) * 2 + 1] = (float)S2->hpi[i].im;
+                }
+            if (ct_out) ct_out[rl] = (float)S2->tpi;
+            if (cu_out)
+                for (int64_t hh = 0; hh < H; ++hh) cu_out[rl * H + hh] = (float)S2->upi[hh];
+            if (cB_out && cC_out)
+                for (int64_t n = 0; n < N; ++n) {
+                    cB_out[(rl * N + n) * 2] = (float)S2->Bpi[n].re;
+                    cB_out[(rl * N + n) * 2 + 1] = (float)S2->Bpi[n].im;
+                    cC_out[(rl * N + n) * 2] = (float)S2->Cpi[n].re;
+                    cC_out[(rl * N + n) * 2 + 1] = (float)S2->Cpi[n].im;
+                }
+        }
 
         /* Adjoints of the carried state (state after step l). */
         cd* ah = (cd*)calloc((size_t)HN, sizeof(cd));
@@ -889,6 +1049,23 @@ int eacs_oracle_cell_bwd(const float* lam, const float* log_dt, const float* u,
             STEP_FWD(l, 0);
             dstate* S = &st[l];
             double tl = tb[l];
+            /* upstream adjoints of the commits of step l (the state after it,
+             * eacs.py:386-401 returns it per frame) join the carried ones */
+            {
+                const int64_t rl = bi * L + l;
+                if (gcH)
+                    for (int64_t i = 0; i < HN; ++i) {
+                        ah[i].re += gcH[(rl * HN + i) * 2];
+                        ah[i].im += gcH[(rl * HN + i) * 2 + 1];
+                    }
+                if (gcT) at += gcT[rl];
+                if (gcU)
+                    for (int64_t hh = 0; hh < H; ++hh) au[hh] += gcU[rl * H + hh];
+                for (int64_t n = 0; n < N; ++n) {
+                    if (gcB) { aB[n].re += gcB[(rl * N + n) * 2]; aB[n].im += gcB[(rl * N + n) * 2 + 1]; }
+                    if (gcC) { aC[n].re += gcC[(rl * N + n) * 2]; aC[n].im += gcC[(rl * N + n) * 2 + 1]; }
+                }
+            }
             double gyl_any = gy != NULL;
             double gbar = ggs ? ggs[bi * L + l] : 0.0;
             double rbar = grs ? grs[bi * L + l] : 0.0;
@@ -1057,4 +1234,48 @@ int eacs_oracle_cell_bwd(const float* lam, const float* log_dt, const float* u,
     return 0;
 }
 
-const char* eacs_oracle_version(void) { return "eacs-oracle 1"; }
+int eacs_oracle_cell_bwd(const float* lam, const float* log_dt, const float* u,
+                         const float* Bc, const float* Cc, const float* t,
+                         const float* D, const float* mean, const float* var,
+                         float eps, float eta, float var_eps, float dt_init,
+                         float dt_max, float T, int gate_mode, const float* gs,
+                         const float* gy, const float* ggs, const float* grs,
+                         const float* gns, float* du, float* dBc, float* dCc,
+                         float* dt, float* dlam, float* dlog, float* dD, float* deps,
+                         int64_t B, int64_t L, int64_t H, int64_t N) {
+    return cell_bwd_impl(lam, log_dt, u, Bc, Cc, t, D, mean, var, eps, eta, var_eps, dt_init,
+                         dt_max, T, gate_mode, gs, gy, ggs, grs, gns, NULL, NULL, NULL, NULL,
+                         NULL, du, dBc, dCc, dt, dlam, dlog, dD, deps, NULL, NULL, NULL, NULL,
+                         NULL, NULL, NULL, NULL, B, L, H, N);
+}
+
+/* ---------------------------------------------------------------------------
+ * Training through per-frame commits: EACSLayer._commit_range (eacs.py:386-401)
+ * under autograd, i.e. the gated cell of eacs_step (eacs.py:78-142) with the
+ * training gate (STE hard forward for gate_mode 0, soft for 1;
+ * event_gate.py:84-105), which also returns the state after every step.
+ * Forward outputs (any may be NULL): y (B,L,H), gate, resid (B,L) and the
+ * commits h (B,L,H,N) complex, t (B,L), u (B,L,H), B, C (B,L,N) complex.
+ * Backward: the cell backward above with the upstream adjoints of the commits
+ * gcH, gcT, gcU, gcB, gcC (same shapes; any may be NULL = zero) added to the
+ * carried state adjoints at their step.  gy may be NULL.
+ * ------------------------------------------------------------------------- */
+int eacs_oracle_cell_bwd_commits(const float* lam, const float* log_dt, const float* u,
+                                 const float* Bc, const float* Cc, const float* t,
+                                 const float* D, const float* mean, const float* var,
+                                 float eps, float eta, float var_eps, float dt_init,
+                                 float dt_max, float T, int gate_mode, const float* gs,
+                                 const float* gy, const float* ggs, const float* grs,
+                                 const float* gcH, const float* gcT, const float* gcU,
+                                 const float* gcB, const float* gcC, float* du, float* dBc,
+                                 float* dCc, float* dt, float* dlam, float* dlog, float* dD,
+                                 float* deps, float* y_out, float* g_out, float* r_out,
+                                 float* ch_out, float* ct_out, float* cu_out, float* cB_out,
+                                 float* cC_out, int64_t B, int64_t L, int64_t H, int64_t N) {
+    return cell_bwd_impl(lam, log_dt, u, Bc, Cc, t, D, mean, var, eps, eta, var_eps, dt_init,
+                         dt_max, T, gate_mode, gs, gy, ggs, grs, NULL, gcH, gcT, gcU, gcB, gcC,
+                         du, dBc, dCc, dt, dlam, dlog, dD, deps, y_out, g_out, r_out, ch_out,
+                         ct_out, cu_out, cB_out, cC_out, B, L, H, N);
+}
+
+const char* eacs_oracle_version(void) { return "eacs-oracle 2"; }

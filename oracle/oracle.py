@@ -47,6 +47,9 @@ def lib():
         L.eacs_oracle_cell_commits.argtypes = ([_P] * 9 + [_F] * 6 + [_I, _I, _F, _F]
                                                + [_P] * 8 + [_I64] * 4)
         L.eacs_oracle_query_readout.argtypes = [_P] * 12 + [_I64] * 5 + [_F, _F]
+        L.eacs_oracle_cell_bwd_commits.argtypes = ([_P] * 9 + [_F] * 5 + [_F, _I] + [_P] * 4
+                                                   + [_P] * 5 + [_P] * 8 + [_P] * 8 + [_I64] * 4)
+        L.eacs_oracle_query_readout_bwd.argtypes = [_P] * 21 + [_I64] * 5 + [_F, _F]
         L.eacs_oracle_stream_chunk.argtypes = [_P] * 27 + [_F] * 7 + [_I, _F] + [_I64] * 4
         L.eacs_oracle_set_threads.argtypes = [_I]
         L.eacs_oracle_version.restype = ctypes.c_char_p
@@ -203,6 +206,85 @@ def cell_bwd(lam, log_dt, u, Bc, Cc, t, D, mean, var, eps, eta, var_eps, dt_init
                                _ptr(grs), _ptr(gns), _ptr(du), _ptr(dBc), _ptr(dCc), _ptr(dt),
                                _ptr(dlam), _ptr(dlog), _ptr(dD), _ptr(deps), B, L, H, N)
     return du, dBc, dCc, dt, dlam, dlog, dD, deps
+
+
+def cell_train_commits(lam, log_dt, u, Bc, Cc, t, D, mean, var, eps, eta, var_eps, dt_init,
+                       dt_max, T, gate_mode, gs=None, gy=None, ggs=None, grs=None, gc=None):
+    """Training through per-frame commits: EACSLayer._commit_range
+    (cst_ssm/modules/eacs.py:386-401) under autograd with the training gate
+    (gate_mode 0: STE, hard forward; 1: soft).
+
+    gs: forward gates to pin (None: decided here, r > eps); gc: upstream
+    adjoints of the commits, a dict with any of h, t, u, B, C.
+    Returns (forward, grads): forward = (y, gate, resid, h, t_pi, u_pi, B_pi,
+    C_pi), grads = (du, dBc, dCc, dt, dlam, dlog_dt, dD, deps).
+    """
+    lam = _c(lam, np.complex64)
+    u = _c(u, np.float32)
+    Bc = _c(Bc, np.complex64)
+    Cc = _c(Cc, np.complex64)
+    t = _c(t, np.float32)
+    log_dt = _c(log_dt, np.float32)
+    D = _c(D, np.float32)
+    mean = _c(mean, np.float32)
+    var = _c(var, np.float32)
+    B, L, H = u.shape
+    N = lam.shape[1]
+    gs = None if gs is None else _c(gs, np.float32)
+    opt = [None if g is None else _c(g, np.float32) for g in (gy, ggs, grs)]
+    gc = gc or {}
+    kinds = {"h": np.complex64, "t": np.float32, "u": np.float32, "B": np.complex64, "C": np.complex64}
+    gcs = [None if gc.get(k) is None else _c(gc[k], kinds[k]) for k in ("h", "t", "u", "B", "C")]
+    fwd = (np.empty((B, L, H), np.float32), np.empty((B, L), np.float32), np.empty((B, L), np.float32),
+           np.empty((B, L, H, N), np.complex64), np.empty((B, L), np.float32),
+           np.empty((B, L, H), np.float32), np.empty((B, L, N), np.complex64),
+           np.empty((B, L, N), np.complex64))
+    grads = (np.empty((B, L, H), np.float32), np.empty((B, L, N), np.complex64),
+             np.empty((B, L, N), np.complex64), np.empty((B, L), np.float32),
+             np.empty((H, N), np.complex64), np.empty((H,), np.float32), np.empty((H,), np.float32),
+             np.empty((1,), np.float32))
+    lib().eacs_oracle_cell_bwd_commits(
+        _ptr(lam), _ptr(log_dt), _ptr(u), _ptr(Bc), _ptr(Cc), _ptr(t), _ptr(D), _ptr(mean),
+        _ptr(var), eps, eta, var_eps, dt_init, dt_max, T, int(gate_mode), _ptr(gs),
+        *[_ptr(g) for g in opt], *[_ptr(g) for g in gcs], *[_ptr(g) for g in grads],
+        *[_ptr(f) for f in fwd], B, L, H, N)
+    return fwd, grads
+
+
+def query_readout_bwd(lam, log_dt, D, ch, ct, cu, cB, cC, frame_t, t_query, gy, idx=None,
+                      dt_min=1e-3, dt_max=1e3):
+    """Adjoint of readout_from_commits before proj_out
+    (cst_ssm/modules/continuous_query.py:20-54).
+
+    Returns (gc, gtq, dlam, dlog_dt, dD) with gc a dict h, t, u, B, C of the
+    commits' adjoints."""
+    lam = _c(lam, np.complex64)
+    log_dt = _c(log_dt, np.float32)
+    D = _c(D, np.float32)
+    ch = _c(ch, np.complex64)
+    ct = _c(ct, np.float32)
+    cu = _c(cu, np.float32)
+    cB = _c(cB, np.complex64)
+    cC = _c(cC, np.complex64)
+    frame_t = _c(frame_t, np.float32)
+    t_query = _c(t_query, np.float32)
+    gy = _c(gy, np.float32)
+    idx = None if idx is None else _c(idx, np.int32)
+    B, L, H, N = ch.shape
+    Q = t_query.shape[1]
+    gc = dict(h=np.empty((B, L, H, N), np.complex64), t=np.empty((B, L), np.float32),
+              u=np.empty((B, L, H), np.float32), B=np.empty((B, L, N), np.complex64),
+              C=np.empty((B, L, N), np.complex64))
+    gtq = np.empty((B, Q), np.float32)
+    dlam = np.empty((H, N), np.complex64)
+    dlog = np.empty((H,), np.float32)
+    dD = np.empty((H,), np.float32)
+    lib().eacs_oracle_query_readout_bwd(
+        _ptr(lam), _ptr(log_dt), _ptr(D), _ptr(ch), _ptr(ct), _ptr(cu), _ptr(cB), _ptr(cC),
+        _ptr(frame_t), _ptr(t_query), _ptr(idx), _ptr(gy), _ptr(gc["h"]), _ptr(gc["t"]),
+        _ptr(gc["u"]), _ptr(gc["B"]), _ptr(gc["C"]), _ptr(gtq), _ptr(dlam), _ptr(dlog), _ptr(dD),
+        B, L, Q, H, N, dt_min, dt_max)
+    return gc, gtq, dlam, dlog, dD
 
 
 def cell_commits(lam, log_dt, u, Bc, Cc, t, D, mean, var, eps, eta, var_eps=1e-5,

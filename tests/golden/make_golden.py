@@ -17,6 +17,8 @@ Reference functions exercised (paths inside the CST-SSM project):
   modules/eacs.py:386-439      run_with_commits (per-frame commits)
   modules/continuous_query.py:12-61  segment_index / readout_from_commits
   modules/streaming.py:45-85   temporal_step (explicit branch state)
+  modules/eacs.py:386-401 + continuous_query.py:20-54  _commit_range and
+                               readout_from_commits under autograd (training)
 
     python tests/golden/make_golden.py --groups query   # rewrite one group only
 """
@@ -348,6 +350,75 @@ def query_cases():
     return out
 
 
+def qtrain_cases():
+    """Training through per-frame commits: EACSLayer._commit_range
+    (eacs.py:386-401) in training mode (STE or soft gate, event_gate.py:84-105)
+    followed by readout_from_commits (continuous_query.py:20-54) at query
+    times and at the frame times, differentiated by autograd with respect to
+    the op-boundary tensors (u, B, C, t, lam, log_dt_scale, D, eps, the query
+    times).  proj_out is the identity, so the readouts are the core's values."""
+    from cst_ssm.modules.continuous_query import readout_from_commits
+    out = {}
+    specs = {
+        # name: (H, N, B, L, Q, seed, use_ste, temperature, target update rate)
+        "qtrain_ste": (6, 4, 2, 12, 9, 30, True, 0.5, 0.5),
+        "qtrain_soft": (5, 3, 2, 10, 7, 31, False, 0.4, 0.5),
+        "qtrain_commit": (8, 4, 2, 9, 6, 32, True, 0.3, None),
+    }
+    for name, (H, N, B, L, Q, seed, ste, T, q) in specs.items():
+        layer, u, Bc, Cc, t = _layer_inputs(H, N, 0.5, 4.0, B, L, seed, dup_frames=True)
+        eps_v = float(layer.gate.eps.detach()) if q is None else _calibrate(layer, u, Bc, Cc, t, q)[0]
+        with torch.no_grad():
+            layer.proj_out.weight.copy_(torch.eye(H))
+            layer.proj_out.bias.zero_()
+        layer.train()
+        layer.gate.use_ste = ste
+        layer.gate.set_temperature(T)
+        eps = torch.tensor(eps_v).requires_grad_(True)
+        orig = layer.step_params
+
+        def step_params(lam, _orig=orig, _eps=eps):
+            p = _orig(lam)
+            p.eps = _eps
+            return p
+
+        layer.step_params = step_params
+        g = torch.Generator().manual_seed(seed + 100)
+        tq = t[:, :1] - 0.3 + (t[:, -1:] - t[:, :1] + 0.8) * torch.rand(B, Q, generator=g)
+        tq[:, 0] = t[:, 0] - 0.2
+        tq[:, 1] = t[:, 4]
+        tq[:, 2] = t[:, -1] + 0.4
+        tq = tq.sort(dim=1).values
+        lam = layer.lam().detach().to(torch.complex64).requires_grad_(True)
+        u_, Bc_, Cc_, t_, tq_ = (x.clone().requires_grad_(True) for x in (u, Bc, Cc, t, tq))
+        state = (torch.zeros(B, H, N, dtype=torch.complex64), t_[:, 0] - layer.dt_init,
+                 u_[:, 0], Bc_[:, 0], Cc_[:, 0])
+        ys, gs, rs, Hc, Tc, Uc, Bs, Cs = layer._commit_range(lam, state, u_, Bc_, Cc_, t_, 0, L)
+        commits = dict(h=Hc, t=Tc, u=Uc, B=Bs, C=Cs, lam=lam, frame_t=t_,
+                       log_dt_scale=layer.log_dt_scale, dt_max=layer.dt_max)
+        yq = readout_from_commits(layer, commits, tq_)
+        yf = readout_from_commits(layer, commits, commits["frame_t"])
+        up = [torch.randn(x.shape, generator=g) for x in (ys, gs, rs, yq, yf)]
+        leaves = [u_, Bc_, Cc_, t_, lam, layer.log_dt_scale, layer.D, eps, tq_]
+        grads = torch.autograd.grad([ys, gs, rs, yq, yf], leaves, up)
+        names = ["du", "dBc", "dCc", "dt", "dlam", "dlog_dt", "dD", "deps", "dtq"]
+        d = dict(lam=_np(lam), log_dt=_np(layer.log_dt_scale), u=_np(u), Bc=_np(Bc), Cc=_np(Cc),
+                 t=_np(t), D=_np(layer.D), mean=_np(layer.obs_norm.running_mean),
+                 var=_np(layer.obs_norm.running_var),
+                 scalars=np.array([eps_v, layer.gate.norm_eta, layer.obs_norm.eps, layer.dt_init,
+                                   1e-3, layer.dt_max, T], np.float64),
+                 gate_mode=np.array([0 if ste else 1]),
+                 y=_np(ys), gate=_np(gs), resid=_np(rs), ch=_np(Hc), ct=_np(Tc), cu=_np(Uc),
+                 cB=_np(Bs), cC=_np(Cs), t_query=_np(tq), yq=_np(yq), yf=_np(yf),
+                 gy=_np(up[0]), ggs=_np(up[1]), grs=_np(up[2]), gq=_np(up[3]), gf=_np(up[4]))
+        for k, v in zip(names, grads):
+            d[k] = _np(v)
+        out[name] = d
+        print(f"{name}: update rate {float(gs.detach().round().mean()):.3f}, "
+              f"min|r-eps| {float((rs.detach() - eps_v).abs().min()):.2e}")
+    return out
+
+
 def stream_cases():
     """temporal_step (streaming.py:45-85) on a one-branch MultiScaleEACS with
     proj_out = identity and out_norm removed, so each step's output is
@@ -431,7 +502,7 @@ def stream_cases():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--groups", default="scan,ssm,cell,train,query,stream",
+    ap.add_argument("--groups", default="scan,ssm,cell,train,query,stream,qtrain",
                     help="comma-separated groups to (re)write")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
@@ -439,10 +510,10 @@ def main():
     gen = torch.Generator().manual_seed(1234)
     makers = {"scan": lambda: scan_cases(gen), "ssm": lambda: ssm_cases(gen),
               "cell": cell_cases, "train": train_cases, "query": query_cases,
-              "stream": stream_cases}
+              "stream": stream_cases, "qtrain": qtrain_cases}
     want = args.groups.split(",")
     groups = {}
-    for name in ("scan", "ssm", "cell", "train", "query", "stream"):  # fixed order: gen is shared
+    for name in ("scan", "ssm", "cell", "train", "query", "stream", "qtrain"):  # fixed order: gen is shared
         cases = makers[name]()
         if name in want:
             groups[name] = cases

@@ -150,3 +150,52 @@ def test_stream_chunk(name):
                                            sl(cpi, mid, K), st1, **kw)
     assert relerr(y2, d["y"][:, mid:]) < 1e-5
     assert relerr(st2[0], d["h"]) < 1e-5
+
+
+QTRAIN = cases("qtrain")
+
+
+def qtrain_grads(d, fwd_from_oracle=True):
+    """The oracle's composition for a commit-training fixture: the readout
+    adjoints of the query and frame-time readouts feed the cell backward as
+    commit adjoints; the parameter and time gradients of the pieces add.
+    Returns (forward, grads) in the fixture's key order."""
+    eps, eta, var_eps, dt_init, dt_min, dt_max, T = [float(v) for v in d["scalars"]]
+    mode = int(d["gate_mode"][0])
+    B, L = d["t"].shape
+    fwd, _ = oracle.cell_train_commits(d["lam"], d["log_dt"], d["u"], d["Bc"], d["Cc"], d["t"],
+                                       d["D"], d["mean"], d["var"], eps, eta, var_eps, dt_init,
+                                       dt_max, T, mode)
+    y, g, r, ch, ct, cu, cB, cC = fwd if fwd_from_oracle else (
+        d["y"], d["gate"], d["resid"], d["ch"], d["ct"], d["cu"], d["cB"], d["cC"])
+    com = (d["lam"], d["log_dt"], d["D"], ch, ct, cu, cB, cC, d["t"])
+    gq, gtq, dlq, dlogq, dDq = oracle.query_readout_bwd(*com, d["t_query"], d["gq"],
+                                                        dt_min=dt_min, dt_max=dt_max)
+    idx = np.broadcast_to(np.arange(L, dtype=np.int32), (B, L))
+    gf, gtf, dlf, dlogf, dDf = oracle.query_readout_bwd(*com, d["t"], d["gf"], idx=idx,
+                                                        dt_min=dt_min, dt_max=dt_max)
+    gc = {k: gq[k] + gf[k] for k in gq}
+    _, (du, dBc, dCc, dt, dlam, dlog, dD, deps) = oracle.cell_train_commits(
+        d["lam"], d["log_dt"], d["u"], d["Bc"], d["Cc"], d["t"], d["D"], d["mean"], d["var"],
+        eps, eta, var_eps, dt_init, dt_max, T, mode, gs=g, gy=d["gy"], ggs=d["ggs"], grs=d["grs"],
+        gc=gc)
+    grads = dict(du=du, dBc=dBc, dCc=dCc, dt=dt + gtf, dlam=dlam + dlq + dlf,
+                 dlog_dt=dlog + dlogq + dlogf, dD=dD + dDq + dDf, deps=deps, dtq=gtq)
+    return fwd, grads
+
+
+@pytest.mark.parametrize("name", sorted(QTRAIN))
+def test_commit_training(name):
+    """_commit_range + readout_from_commits under autograd (eacs.py:386-401,
+    continuous_query.py:20-54): the training forward (gates, commits) and every
+    gradient, including those of the query times, to 1e-4."""
+    d = QTRAIN[name]
+    mode = int(d["gate_mode"][0])
+    (y, g, r, ch, ct, cu, cB, cC), grads = qtrain_grads(d)
+    assert np.max(np.abs(g - d["gate"])) <= (0 if mode == 0 else 1e-5)
+    assert relerr(r, d["resid"]) < 1e-5
+    assert relerr(y, d["y"]) < 1e-5
+    for got, key in zip((ch, ct, cu, cB, cC), ("ch", "ct", "cu", "cB", "cC")):
+        assert relerr(got, d[key]) < 1e-5, key
+    for k, v in grads.items():
+        assert relerr(v, d[k]) < 1e-4, (k, relerr(v, d[k]))
