@@ -341,6 +341,78 @@ EACS_API int eacs_query_readout(const void* lam, const float* log_dt, const floa
                                 int64_t B, int64_t L, int64_t Q, int64_t H, int64_t N,
                                 float dt_min, float dt_max, void* stream);
 
+/* Training through per-frame commits.  Replaces EACSLayer._commit_range
+ * (cst_ssm/modules/eacs.py:386-401) run under autograd by run_with_commits
+ * (:404-439), after the projections: the training forward
+ * (eacs_cell_train_fwd's arguments and outputs: STE gate for gate_mode 0,
+ * soft gate for 1; 2 is the eval-mode hard gate r > eps, whose forward is
+ * the STE forward and whose backward passes no gradient through the gate,
+ * event_gate.py:99-100), then a replay with the decided gates that records the
+ * commits after every step -- commit_h (B,L,H,N) complex64 = h_pi, commit_t
+ * (B,L) = t_pi, commit_u (B,L,H) float32 = u_pi, commit_B, commit_C (B,L,N)
+ * complex64 = B_pi, C_pi (blends of the previous and the new values under a
+ * soft gate) -- and writes the backward's checkpoints into bwd_workspace
+ * (eacs_cell_train_commits_workspace_size bytes, kept until the matching
+ * eacs_cell_train_commits_bwd call).  workspace: eacs_cell_workspace_size. */
+EACS_API size_t eacs_cell_train_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+EACS_API int eacs_cell_train_commits_fwd(const void* lam, const float* log_dt, const void* u, int u_dtype,
+                                         const void* Bc, const void* Cc, const float* t, const float* D,
+                                         const float* mean, const float* var,
+                                         float eps, float eta, float var_eps, float dt_init,
+                                         float dt_min, float dt_max, int gate_mode, float temperature,
+                                         float* y, float* gate, float* resid, float* stats,
+                                         void* commit_h, float* commit_t, float* commit_u,
+                                         void* commit_B, void* commit_C,
+                                         void* workspace, size_t workspace_bytes,
+                                         void* bwd_workspace, size_t bwd_workspace_bytes,
+                                         int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
+
+/* Backward of eacs_cell_train_commits_fwd: eacs_cell_train_bwd_ckpt's
+ * arguments with the forward's gate_mode (no innovation term: _commit_range
+ * does not return one) plus the
+ * upstream adjoints of the commits, g_commit_h (B,L,H,N) complex64,
+ * g_commit_t (B,L), g_commit_u (B,L,H), g_commit_B, g_commit_C (B,L,N)
+ * complex64 (any may be NULL = 0), which join the scan's adjoint at their
+ * step.  workspace: the bwd_workspace eacs_cell_train_commits_fwd filled. */
+EACS_API int eacs_cell_train_commits_bwd(const void* lam, const float* log_dt, const void* u, int u_dtype,
+                                         const void* Bc, const void* Cc, const float* t, const float* D,
+                                         const float* mean, const float* var,
+                                         float eps, float eta, float var_eps, float dt_init,
+                                         float dt_min, float dt_max, int gate_mode, float temperature,
+                                         const float* gate, const float* resid, const float* stats,
+                                         const float* gy, const float* ggs, const float* grs,
+                                         const void* g_commit_h, const float* g_commit_t,
+                                         const float* g_commit_u, const void* g_commit_B,
+                                         const void* g_commit_C,
+                                         float* du, void* dBc, void* dCc, float* dt, void* dlam,
+                                         float* dlog_dt, float* dD, float* deps,
+                                         void* workspace, size_t workspace_bytes,
+                                         int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
+
+/* Adjoint of eacs_query_readout (the backward of readout_from_commits before
+ * proj_out, cst_ssm/modules/continuous_query.py:20-54 under autograd).
+ * gy (B,Q,H) = dLoss/dy; idx (B,Q) int32 must be nondecreasing per row (a
+ * frame's queries contiguous: sort the queries, or pass 0..L-1 for the frame
+ * times); out-of-order indices record EACS_ERR_INVALID in the device status
+ * word.  Outputs, overwritten: the commits' adjoints g_commit_h (B,L,H,N)
+ * complex64, g_commit_t (B,L), g_commit_u (B,L,H), g_commit_B, g_commit_C
+ * (B,L,N) complex64 (zero for frames no query reads), the query times'
+ * g_t_query (B,Q) (may be NULL), dlam (H,N) complex64, dlog_dt (H), dD (H).
+ * Sums run in a fixed order (no atomics).  workspace:
+ * eacs_query_readout_bwd_workspace_size bytes. */
+EACS_API size_t eacs_query_readout_bwd_workspace_size(int64_t B, int64_t L, int64_t Q, int64_t H, int64_t N);
+EACS_API int eacs_query_readout_bwd(const void* lam, const float* log_dt, const float* D,
+                                    const void* commit_h, const float* commit_t,
+                                    const float* commit_u, const void* commit_B,
+                                    const void* commit_C, const float* t_query,
+                                    const int32_t* idx, const float* gy,
+                                    void* g_commit_h, float* g_commit_t, float* g_commit_u,
+                                    void* g_commit_B, void* g_commit_C, float* g_t_query,
+                                    void* dlam, float* dlog_dt, float* dD,
+                                    void* workspace, size_t workspace_bytes,
+                                    int64_t B, int64_t L, int64_t Q, int64_t H, int64_t N,
+                                    float dt_min, float dt_max, void* stream);
+
 /* K steps of one EACS branch with explicit state, per row (streaming).
  * Replaces the per-branch body of temporal_step (cst_ssm/modules/streaming.py:
  * 45-85: first-observation commit, valid masks, CPI-modulated threshold) over

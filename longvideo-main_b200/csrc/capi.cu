@@ -61,10 +61,12 @@ int eacs_device_status(int* status, void* stream) {
     if (rc) return rc;
     rc = eacs::cuda_check(eacs::cell_read_status(&b, s), "eacs_device_status");
     if (rc) return rc;
-    int c = 0;
+    int c = 0, d = 0;
     rc = eacs::cuda_check(eacs::train_read_status(&c, s), "eacs_device_status");
     if (rc) return rc;
-    *status = a ? a : (b ? b : c);
+    rc = eacs::cuda_check(eacs::query_read_status(&d, s), "eacs_device_status");
+    if (rc) return rc;
+    *status = a ? a : (b ? b : (c ? c : d));
     return EACS_OK;
 }
 
@@ -242,6 +244,118 @@ int eacs_cell_train_bwd(const void* lam, const float* log_dt, const void* u, int
                          dCc,   dt,     dlam,  dlog_dt, dD,      deps,   workspace, workspace_bytes,
                          B,     L,      H,     N};
     return eacs::train_bwd(c, static_cast<cudaStream_t>(stream));
+}
+
+size_t eacs_cell_train_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
+    return eacs::train_commits_workspace_size(B, L, H, N);
+}
+
+int eacs_cell_train_commits_fwd(const void* lam, const float* log_dt, const void* u, int u_dtype,
+                                const void* Bc, const void* Cc, const float* t, const float* D,
+                                const float* mean, const float* var, float eps, float eta, float var_eps,
+                                float dt_init, float dt_min, float dt_max, int gate_mode, float temperature,
+                                float* y, float* gate, float* resid, float* stats, void* commit_h,
+                                float* commit_t, float* commit_u, void* commit_B, void* commit_C,
+                                void* workspace, size_t workspace_bytes, void* bwd_workspace,
+                                size_t bwd_workspace_bytes, int64_t B, int64_t L, int64_t H, int64_t N,
+                                void* stream) {
+    const char* fn = "eacs_cell_train_commits_fwd";
+    if (!stats) return eacs::fail(EACS_ERR_INVALID, "%s: null stats", fn);
+    if (gate_mode < 0 || gate_mode > 2) return eacs::fail(EACS_ERR_INVALID, "%s: gate_mode %d not in 0..2", fn, gate_mode);
+    if (gate_mode == 2) gate_mode = 0;  // the hard gate's forward is the STE forward
+    if (B < 0 || L < 0 || H < 0 || N < 0) return eacs::fail(EACS_ERR_INVALID, "%s: negative size", fn);
+    if (B == 0 || L == 0 || H == 0) return EACS_OK;
+    const size_t need = eacs::train_commits_workspace_size(B, L, H, N);
+    if (need == 0)
+        return eacs::fail(EACS_ERR_UNSUPPORTED, "%s: no training backward for B=%lld L=%lld H=%lld N=%lld", fn,
+                          (long long)B, (long long)L, (long long)H, (long long)N);
+    if (!bwd_workspace || bwd_workspace_bytes < need)
+        return eacs::fail(EACS_ERR_WORKSPACE, "%s: backward workspace of %zu bytes needed, %zu given", fn, need,
+                          bwd_workspace_bytes);
+    if (!commit_h || !commit_t || !commit_u || !commit_B || !commit_C)
+        return eacs::fail(EACS_ERR_INVALID, "%s: null commit buffer", fn);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    eacs::CellCall c{lam,  log_dt, u,       u_dtype, Bc,     Cc,      t,      D,
+                     mean, var,    eps,     eta,     var_eps, dt_init, dt_min, dt_max,
+                     0,    3,      2.0f,    0.3f,    gate_mode, temperature, y, gate,
+                     resid, workspace, workspace_bytes, B, L, H, N};
+    c.stats = stats;
+    int rc = eacs::cell_fwd(c, s);
+    if (rc) return rc;
+    eacs::TrainBwdCall r{};
+    r.lam = lam;
+    r.log_dt = log_dt;
+    r.u = u;
+    r.u_dtype = u_dtype;
+    r.Bc = Bc;
+    r.Cc = Cc;
+    r.t = t;
+    r.D = D;
+    r.mean = mean;
+    r.var = var;
+    r.eps = eps;
+    r.eta = eta;
+    r.var_eps = var_eps;
+    r.dt_init = dt_init;
+    r.dt_min = dt_min;
+    r.dt_max = dt_max;
+    r.temperature = temperature;
+    r.gates = gate;
+    r.workspace = bwd_workspace;
+    r.workspace_bytes = bwd_workspace_bytes;
+    r.B = B;
+    r.L = L;
+    r.H = H;
+    r.N = N;
+    eacs::CommitOut out{commit_h, commit_t, commit_u, commit_B, commit_C};
+    return eacs::train_commits_replay(r, out, s);
+}
+
+int eacs_cell_train_commits_bwd(const void* lam, const float* log_dt, const void* u, int u_dtype,
+                                const void* Bc, const void* Cc, const float* t, const float* D,
+                                const float* mean, const float* var, float eps, float eta, float var_eps,
+                                float dt_init, float dt_min, float dt_max, int gate_mode, float temperature,
+                                const float* gate, const float* resid, const float* stats, const float* gy,
+                                const float* ggs, const float* grs, const void* g_commit_h,
+                                const float* g_commit_t, const float* g_commit_u, const void* g_commit_B,
+                                const void* g_commit_C, float* du, void* dBc, void* dCc, float* dt,
+                                void* dlam, float* dlog_dt, float* dD, float* deps, void* workspace,
+                                size_t workspace_bytes, int64_t B, int64_t L, int64_t H, int64_t N,
+                                void* stream) {
+    eacs::TrainBwdCall c{lam,   log_dt, u,     u_dtype, Bc,      Cc,     t,       D,       mean,
+                         var,   eps,    eta,   var_eps, dt_init, dt_min, dt_max,  temperature,
+                         gate,  resid,  stats, gy,      ggs,     grs,    nullptr, du,      dBc,
+                         dCc,   dt,     dlam,  dlog_dt, dD,      deps,   workspace, workspace_bytes,
+                         B,     L,      H,     N};
+    if (gate_mode < 0 || gate_mode > 2)
+        return eacs::fail(EACS_ERR_INVALID, "eacs_cell_train_commits_bwd: gate_mode %d not in 0..2", gate_mode);
+    c.commits = true;
+    c.gate_const = gate_mode == 2;
+    c.gc_h = g_commit_h;
+    c.gc_t = g_commit_t;
+    c.gc_u = g_commit_u;
+    c.gc_B = g_commit_B;
+    c.gc_C = g_commit_C;
+    return eacs::train_bwd(c, static_cast<cudaStream_t>(stream));
+}
+
+size_t eacs_query_readout_bwd_workspace_size(int64_t B, int64_t L, int64_t Q, int64_t H, int64_t N) {
+    return eacs::query_readout_bwd_workspace_size(B, L, Q, H, N);
+}
+
+int eacs_query_readout_bwd(const void* lam, const float* log_dt, const float* D, const void* commit_h,
+                           const float* commit_t, const float* commit_u, const void* commit_B,
+                           const void* commit_C, const float* t_query, const int32_t* idx, const float* gy,
+                           void* g_commit_h, float* g_commit_t, float* g_commit_u, void* g_commit_B,
+                           void* g_commit_C, float* g_t_query, void* dlam, float* dlog_dt, float* dD,
+                           void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t Q,
+                           int64_t H, int64_t N, float dt_min, float dt_max, void* stream) {
+    eacs::QueryBwdCall c{lam,        log_dt,     D,          commit_h,   commit_t,   commit_u,
+                         commit_B,   commit_C,   t_query,    idx,        gy,         g_commit_h,
+                         g_commit_t, g_commit_u, g_commit_B, g_commit_C, g_t_query,  dlam,
+                         dlog_dt,    dD,         workspace,  workspace_bytes, B,     L,
+                         Q,          H,          N,          dt_min,     dt_max};
+    return eacs::query_readout_bwd(c, static_cast<cudaStream_t>(stream));
 }
 
 size_t eacs_cell_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {

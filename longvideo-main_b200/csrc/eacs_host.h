@@ -157,6 +157,38 @@ int query_readout(const void* lam, const float* log_dt, const float* D, const vo
                   const void* commit_C, const float* t_query, const int* idx, float* y, int64_t B,
                   int64_t L, int64_t Q, int64_t H, int64_t N, float dt_min, float dt_max,
                   cudaStream_t stream);
+// adjoint of query_readout: idx nondecreasing per row (a frame's queries
+// contiguous); the commits' adjoints are overwritten (zero where no query
+// reads a frame)
+struct QueryBwdCall {
+    const void* lam;
+    const float* log_dt;
+    const float* D;
+    const void* commit_h;
+    const float* commit_t;
+    const float* commit_u;
+    const void* commit_B;
+    const void* commit_C;
+    const float* t_query;
+    const int* idx;
+    const float* gy;       // (B,Q,H)
+    void* g_commit_h;      // (B,L,H,N) complex64
+    float* g_commit_t;     // (B,L)
+    float* g_commit_u;     // (B,L,H)
+    void* g_commit_B;      // (B,L,N) complex64
+    void* g_commit_C;
+    float* g_t_query;      // (B,Q) or null
+    void* dlam;            // (H,N) complex64
+    float* dlog;           // (H)
+    float* dD;             // (H)
+    void* workspace;
+    size_t workspace_bytes;
+    int64_t B, L, Q, H, N;
+    float dt_min, dt_max;
+};
+size_t query_readout_bwd_workspace_size(int64_t B, int64_t L, int64_t Q, int64_t H, int64_t N);
+int query_readout_bwd(const QueryBwdCall& c, cudaStream_t stream);
+cudaError_t query_read_status(int* out, cudaStream_t stream);
 
 // stream.cu: gated steps with explicit branch state
 struct StreamCall {
@@ -244,8 +276,30 @@ struct TrainBwdCall {
     size_t workspace_bytes;
     int64_t B, L, H, N;
     bool have_ckpt = false;  // the workspace already holds the forward's checkpoints
+    // training through per-frame commits: the workspace holds the checkpoints
+    // train_commits_replay wrote, and the upstream adjoints of the commits
+    // (any may be null = zero) join the backward at their step
+    bool commits = false;
+    bool gate_const = false;     // the gates are constants (no gradient through r > eps)
+    const void* gc_h = nullptr;  // (B,L,H,N) complex64
+    const float* gc_t = nullptr; // (B,L)
+    const float* gc_u = nullptr; // (B,L,H)
+    const void* gc_B = nullptr;  // (B,L,N) complex64
+    const void* gc_C = nullptr;
 };
 size_t train_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+// per-frame commits written by the replay of the training forward
+struct CommitOut {
+    void* h;   // (B,L,H,N) complex64
+    float* t;  // (B,L)
+    float* u;  // (B,L,H)
+    void* B;   // (B,L,N) complex64
+    void* C;
+};
+size_t train_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N);
+// Replays the gated forward with c.gates, writing the commits and the
+// backward's checkpoints into c.workspace (train_commits_workspace_size).
+int train_commits_replay(const TrainBwdCall& c, const CommitOut& out, cudaStream_t stream);
 // Where the training backward's workspace keeps its checkpoints (fills c's
 // ck_* fields); an EACS status code.
 int train_ckpt_layout(int64_t B, int64_t L, int64_t H, int64_t N, void* workspace, size_t workspace_bytes,

@@ -80,9 +80,25 @@ struct TArgs {
     float* plog;          // [B][H]
     float* pD;            // [B][H]
     float* peps;          // [B]
+    // per-frame commits (the state after every step, EACSLayer._commit_range):
+    // written by the checkpoint pass when cm_h is set
+    float2* cm_h;         // (B,L,H,N)
+    float* cm_t;          // (B,L)
+    float* cm_u;          // (B,L,H)
+    float2* cm_B;         // (B,L,N)
+    float2* cm_C;
+    // their upstream adjoints, read by the backward when commit_grads is set
+    // (any may be null = zero)
+    const float2* gc_h;   // (B,L,H,N)
+    const float* gc_t;    // (B,L)
+    const float* gc_u;    // (B,L,H)
+    const float2* gc_B;   // (B,L,N)
+    const float2* gc_C;
     int B, L, H, N, nK, CL, HC;
     int K, Klog;          // steps per checkpoint / recompute chunk (K = 1 << Klog)
     int have_ckpt;        // the forward already wrote the checkpoints
+    int commit_grads;     // the backward adds the commits' adjoints (extra shared memory)
+    int gate_const;       // hard gates that carry no gradient (eval-mode comparison r > eps)
 };
 
 template <int LANES>
@@ -240,6 +256,24 @@ __global__ void __launch_bounds__(kCkThreads) train_ckpt(TArgs a) {
             };
             if (sg[buf][i] == 1.f) step(std::true_type{});
             else step(std::false_type{});
+            if (a.cm_h) {  // the commits of step l: the state after it
+                const size_t rl = rowL + l;
+#pragma unroll
+                for (int j = 0; j < NPT; ++j)
+                    if (nv[j]) a.cm_h[(rl * H + h) * N + ln + LANES * j] = hs[j];
+                if (hv && ln == 0) a.cm_u[rl * H + h] = u_pi;
+                if (row_writer) a.cm_t[rl] = t_pi;
+                if (bc_writer) {
+#pragma unroll
+                    for (int j = 0; j < NPT; ++j) {
+                        const int n = ln + LANES * j;
+                        if (n < N) {
+                            a.cm_B[rl * N + n] = Bp[j];
+                            a.cm_C[rl * N + n] = Cp[j];
+                        }
+                    }
+                }
+            }
         }
     }
 }
@@ -255,7 +289,7 @@ __device__ __forceinline__ void cluster_sync_all() {
 // Backward: one cluster of CL CTAs per row, CTA c owns channels
 // [c*HC, (c+1)*HC); thread (hl, ln) owns chains n = ln + LANES*j.
 // ---------------------------------------------------------------------------
-template <int LANES, int NPT, typename UT, int MAXT = 512>
+template <int LANES, int NPT, typename UT, int MAXT = 512, bool CG = false>
 __global__ void __launch_bounds__(MAXT) train_bwd(TArgs a) {
     constexpr int NP = LANES * NPT;
     extern __shared__ __align__(16) unsigned char smem[];
@@ -288,6 +322,15 @@ __global__ void __launch_bounds__(MAXT) train_bwd(TArgs a) {
     float* sgr = f;   f += kK;                                    // g_rs
     float* sgn = f;   f += kK;                                    // g_ns
     float* sot = f;   f += kK * NW;                               // [kK][NW]
+    // commit adjoints (commit_grads only): u_pi's and t_pi's per step, B_pi's
+    // and C_pi's per step, and a two-step ring of h_pi's prefetched with cp.async
+    constexpr bool cm = CG;
+    float* sgcu = f;  f += cm ? kK * HC : 0;                      // [kK][HC]
+    float* sgct = f;  f += cm ? kK : 0;                           // [kK]
+    f += (reinterpret_cast<uintptr_t>(f) & 7u) ? 1 : 0;
+    float2* sgcB = reinterpret_cast<float2*>(f);                  // [kK][NP]
+    float2* sgcC = sgcB + (cm ? kK * NP : 0);
+    float2* sring = sgcC + (cm ? kK * NP : 0);                    // [2][NPT][T]
 
     cg::cluster_group cluster = cg::this_cluster();
     const int crank = static_cast<int>(cluster.block_rank());
@@ -335,6 +378,19 @@ __global__ void __launch_bounds__(MAXT) train_bwd(TArgs a) {
     }
     int nred = 0;                              // reductions done so far
     bool failed = false;
+    // the adjoint of h_pi's commit at step l into ring slot l & 1 (zero for
+    // padded chains)
+    const bool cmh = cm && a.gc_h != nullptr;
+    auto prefetch_gch = [&](const int l) {
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            cp_async8(&sring[((l & 1) * NPT + j) * T + tid],
+                      nv[j] ? a.gc_h + ((rowL + l) * H + h) * N + n : a.gc_h, nv[j]);
+        }
+        cp_async_commit();
+    };
+    if (cmh) prefetch_gch(L - 1);
 
     for (int k = a.nK - 1; k >= 0; --k) {
         const int l0 = k * kK;
@@ -358,7 +414,7 @@ __global__ void __launch_bounds__(MAXT) train_bwd(TArgs a) {
             stl[i] = a.t[o];
             sgt[i] = a.gates[o];
             const float soft = 1.0f / (1.0f + expf(-((a.resid[o] - a.eps) / a.Tp)));
-            sslp[i] = soft * (1.f - soft) / a.Tp;
+            sslp[i] = a.gate_const ? 0.f : soft * (1.f - soft) / a.Tp;
             const float2 st = a.stats[o];
             const float num = st.x, nobs = st.y, den = nobs + a.eta;
             const float rden = 1.0f / den;
@@ -367,6 +423,19 @@ __global__ void __launch_bounds__(MAXT) train_bwd(TArgs a) {
             sgg[i] = a.ggs ? a.ggs[o] : 0.f;
             sgr[i] = a.grs ? a.grs[o] : 0.f;
             sgn[i] = a.gns ? a.gns[o] : 0.f;
+            if (cm) sgct[i] = a.gc_t ? a.gc_t[o] : 0.f;
+        }
+        if (cm) {
+            for (int idx = tid; idx < steps * HC; idx += T) {
+                const int i = idx / HC, c = idx % HC, hh = crank * HC + c;
+                sgcu[i * HC + c] = (a.gc_u && hh < H) ? a.gc_u[(rowL + l0 + i) * H + hh] : 0.f;
+            }
+            for (int idx = tid; idx < steps * NP; idx += T) {
+                const int i = idx / NP, n = idx % NP;
+                const size_t o = (rowL + l0 + i) * N + n;
+                sgcB[i * NP + n] = (a.gc_B && n < N) ? a.gc_B[o] : make_float2(0.f, 0.f);
+                sgcC[i * NP + n] = (a.gc_C && n < N) ? a.gc_C[o] : make_float2(0.f, 0.f);
+            }
         }
         // ---- forward recompute of the chunk from its checkpoint ----
         float2 hs[NPT], Bp[NPT], Cp[NPT];
@@ -439,6 +508,28 @@ __global__ void __launch_bounds__(MAXT) train_bwd(TArgs a) {
             const float ul = hv ? sul[i * HC + hl] : 0.f;
             const float upi = hv ? supi[i * HC + hl] : 0.f;
             const float yb = hv ? sgy[i * HC + hl] : 0.f;
+            if (cm) {
+                // the commits of step l are the state after it: their upstream
+                // adjoints join the carried ones (u_pi's and t_pi's are kept
+                // per channel on every lane, B_pi's and C_pi's as shares summed
+                // over the row's channels, so channel 0 takes those)
+                if (cmh) {
+                    cp_async_wait_all();
+                    if (l > 0) prefetch_gch(l - 1);
+#pragma unroll
+                    for (int j = 0; j < NPT; ++j) ah[j] = cadd(ah[j], sring[((l & 1) * NPT + j) * T + tid]);
+                }
+                if (hv) vu += sgcu[i * HC + hl];
+                if (crank == 0 && hl == 0) {
+                    vt += sgct[i];
+#pragma unroll
+                    for (int j = 0; j < NPT; ++j) {
+                        const int n = ln + LANES * j;
+                        vB[j] = cadd(vB[j], sgcB[i * NP + n]);
+                        vC[j] = cadd(vC[j], sgcC[i * NP + n]);
+                    }
+                }
+            }
             const float draw = tl - tpi;
             const float delta = fmaxf(draw, 0.f);
             const float mdel = draw >= 0.f ? 1.f : 0.f;
@@ -765,7 +856,7 @@ bool train_shape(int64_t H, int lanes, int64_t B, int* CL, int* HC, int* T) {
     return false;
 }
 
-size_t smem_bytes(int T, int NPT, int NP, int HC, int kK) {
+size_t smem_bytes(int T, int NPT, int NP, int HC, int kK, bool commits) {
     const int NW = T / 32;
     size_t s = 0;
     s += sizeof(float2) * kK * T * NPT * 3;   // h_pi, dA, dB_bar
@@ -774,6 +865,10 @@ size_t smem_bytes(int T, int NPT, int NP, int HC, int kK) {
     s += sizeof(float4) * kK + 16;            // row constants, 2 mbarriers
     s += sizeof(float) * 2 * 16 * 32;         // reduction slots
     s += sizeof(float) * (kK * HC * 3 + kK * 7 + kK * NW);
+    if (commits) {                            // commit adjoints: u_pi, t_pi, B_pi, C_pi, h_pi ring
+        s += sizeof(float) * (kK * HC + kK + 1);
+        s += sizeof(float2) * (kK * NP * 2 + 2 * NPT * T);
+    }
     return s;
 }
 
@@ -781,9 +876,9 @@ size_t al(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 // Chunk length: the largest power of two up to kKMax whose shared-memory
 // footprint fits in 200 KiB.
-int chunk_len(int T, int NPT, int NP, int HC) {
+int chunk_len(int T, int NPT, int NP, int HC, bool commits) {
     for (int k = kKMax; k >= 1; k /= 2)
-        if (smem_bytes(T, NPT, NP, HC, k) <= 200u * 1024u) return k;
+        if (smem_bytes(T, NPT, NP, HC, k, commits) <= 200u * 1024u) return k;
     return 0;
 }
 
@@ -824,17 +919,17 @@ cudaError_t launch_ckpt(TArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-template <int LANES, int NPT, typename UT>
+template <int LANES, int NPT, typename UT, bool CG>
 cudaError_t launch_train(TArgs& a, int T, cudaStream_t s) {
     constexpr int NP = LANES * NPT;
     if (!a.have_ckpt) {
         cudaError_t e = launch_ckpt<UT>(a, s);
         if (e != cudaSuccess) return e;
     }
-    const size_t smem = smem_bytes(T, NPT, NP, a.HC, a.K);
+    const size_t smem = smem_bytes(T, NPT, NP, a.HC, a.K, a.commit_grads != 0);
     // CTAs of at most 384 threads (config 3: 96 channels x 4 lanes) may use up to
     // 168 registers a thread; the 512-thread bound (128) made the kernel spill
-    auto kern = T <= 384 ? train_bwd<LANES, NPT, UT, 384> : train_bwd<LANES, NPT, UT, 512>;
+    auto kern = T <= 384 ? train_bwd<LANES, NPT, UT, 384, CG> : train_bwd<LANES, NPT, UT, 512, CG>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     if (a.CL > 8) {
@@ -868,82 +963,63 @@ cudaError_t launch_train(TArgs& a, int T, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-template <typename UT>
+// the (lanes, chains a thread) pairs lanes_train can return, and no others
+template <typename UT, bool CG>
 cudaError_t train_by_n(TArgs& a, int T, cudaStream_t s) {
     int lanes, npt;
     lanes_train(a.N, &lanes, &npt);
 #if EACS_TRAIN_NPT == 4
     if (npt == 4) {
-        if (lanes == 4) return launch_train<4, 4, UT>(a, T, s);
-        if (lanes == 8) return launch_train<8, 4, UT>(a, T, s);
-        return launch_train<16, 4, UT>(a, T, s);
+        if (lanes == 4) return launch_train<4, 4, UT, CG>(a, T, s);
+        if (lanes == 8) return launch_train<8, 4, UT, CG>(a, T, s);
+        return launch_train<16, 4, UT, CG>(a, T, s);
     }
+    return launch_train<4, 2, UT, CG>(a, T, s);
+#else
+    if (lanes == 4) return launch_train<4, 2, UT, CG>(a, T, s);
+    if (lanes == 8) return launch_train<8, 2, UT, CG>(a, T, s);
+    if (lanes == 16) return launch_train<16, 2, UT, CG>(a, T, s);
+    return launch_train<32, 2, UT, CG>(a, T, s);
 #endif
-    if (lanes == 4) return launch_train<4, 2, UT>(a, T, s);
-    if (lanes == 8) return launch_train<8, 2, UT>(a, T, s);
-    if (lanes == 16) return launch_train<16, 2, UT>(a, T, s);
-    return launch_train<32, 2, UT>(a, T, s);
 }
 
-}  // namespace
-
-size_t train_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
-    int lanes, npt, CL, HC, T;
-    if (B <= 0 || L <= 0 || H <= 0 || N <= 0 || !lanes_train(static_cast<int>(N), &lanes, &npt)) return 0;
-    if (!train_shape(H, lanes, B, &CL, &HC, &T)) return 0;
-    const int K = chunk_len(T, npt, lanes * npt, HC);
-    if (K == 0) return 0;
-    return tws(B, L, H, N, CL, K).total;
+template <typename UT>
+cudaError_t train_by_n(TArgs& a, int T, cudaStream_t s) {
+    return a.commit_grads ? train_by_n<UT, true>(a, T, s) : train_by_n<UT, false>(a, T, s);
 }
 
-int train_ckpt_layout(int64_t B, int64_t L, int64_t H, int64_t N, void* workspace, size_t workspace_bytes,
-                      CellCall* c) {
-    const char* fn = "eacs_cell_train_fwd_ckpt";
-    int lanes, npt, CL, HC, T;
-    if (B <= 0 || L <= 0 || H <= 0 || N <= 0 || !lanes_train(static_cast<int>(N), &lanes, &npt) ||
-        !train_shape(H, lanes, B, &CL, &HC, &T))
-        return fail(EACS_ERR_UNSUPPORTED, "%s: no training backward for B=%lld L=%lld H=%lld N=%lld", fn,
-                    (long long)B, (long long)L, (long long)H, (long long)N);
-    const int K = chunk_len(T, npt, lanes * npt, HC);
-    if (K == 0) return fail(EACS_ERR_UNSUPPORTED, "%s: shared memory too small for H=%lld", fn, (long long)H);
-    const TWs w = tws(B, L, H, N, CL, K);
-    if (!workspace || workspace_bytes < w.total)
-        return fail(EACS_ERR_WORKSPACE, "%s: backward workspace of %zu bytes needed, %zu given", fn, w.total,
-                    workspace_bytes);
-    char* ws = static_cast<char*>(workspace);
-    c->ck_h = ws + w.ck_h;
-    c->ck_u = reinterpret_cast<float*>(ws + w.ck_u);
-    c->ck_row = ws + w.ck_row;
-    c->ck_bc = ws + w.ck_bc;
-    c->ck_K = K;
-    c->ck_nK = static_cast<int>((L + K - 1) / K);
+// Shapes of the backward for (B, L, H, N): lanes and chains a thread, cluster
+// size, channels a CTA, threads a CTA and the checkpoint interval (which the
+// commit-adjoint variant may shorten: its extra shared memory counts).
+struct Layout {
+    int lanes, npt, CL, HC, T, K;
+};
+// With fn null nothing is reported, only the status returned.
+int train_layout(int64_t B, int64_t L, int64_t H, int64_t N, bool commits, const char* fn, Layout* o) {
+#define EACS_LAYOUT_FAIL(code, ...) return fn ? fail(code, __VA_ARGS__) : (code)
+    if (B < 0 || L < 0 || H < 0 || N < 0) EACS_LAYOUT_FAIL(EACS_ERR_INVALID, "%s: negative size", fn);
+    if (N <= 0 || !lanes_train(static_cast<int>(N), &o->lanes, &o->npt))
+        EACS_LAYOUT_FAIL(EACS_ERR_UNSUPPORTED, "%s: N=%lld outside 1..64", fn, (long long)N);
+    if (H <= 0 || !train_shape(H, o->lanes, B, &o->CL, &o->HC, &o->T))
+        EACS_LAYOUT_FAIL(EACS_ERR_UNSUPPORTED, "%s: H=%lld needs more than 16 CTAs of 512 threads per row", fn,
+                         (long long)H);
+    if (B > 65535 || L > (1LL << 30)) EACS_LAYOUT_FAIL(EACS_ERR_UNSUPPORTED, "%s: B or L too large", fn);
+    o->K = chunk_len(o->T, o->npt, o->lanes * o->npt, o->HC, commits);
+    if (o->K == 0)
+        EACS_LAYOUT_FAIL(EACS_ERR_UNSUPPORTED, "%s: shared memory too small for H=%lld", fn, (long long)H);
+#undef EACS_LAYOUT_FAIL
     return EACS_OK;
 }
 
-int train_bwd(const TrainBwdCall& c, cudaStream_t stream) {
-    const char* fn = c.have_ckpt ? "eacs_cell_train_bwd_ckpt" : "eacs_cell_train_bwd";
-    if (c.B < 0 || c.L < 0 || c.H < 0 || c.N < 0) return fail(EACS_ERR_INVALID, "%s: negative size", fn);
-    if (c.B == 0 || c.L == 0 || c.H == 0) return EACS_OK;
-    int lanes, npt, CL, HC, T;
-    if (c.N <= 0 || !lanes_train(static_cast<int>(c.N), &lanes, &npt))
-        return fail(EACS_ERR_UNSUPPORTED, "%s: N=%lld outside 1..64", fn, (long long)c.N);
-    if (!train_shape(c.H, lanes, c.B, &CL, &HC, &T))
-        return fail(EACS_ERR_UNSUPPORTED, "%s: H=%lld needs more than 16 CTAs of 512 threads per row", fn,
-                    (long long)c.H);
-    if (c.B > 65535 || c.L > (1LL << 30)) return fail(EACS_ERR_UNSUPPORTED, "%s: B or L too large", fn);
-    if (c.u_dtype != EACS_DTYPE_F32 && c.u_dtype != EACS_DTYPE_F16 && c.u_dtype != EACS_DTYPE_BF16)
-        return fail(EACS_ERR_INVALID, "%s: unknown u dtype %d", fn, c.u_dtype);
-    if (!c.lam || !c.log_dt || !c.u || !c.Bc || !c.Cc || !c.t || !c.D || !c.mean || !c.var || !c.gates ||
-        !c.resid || !c.stats || !c.gy || !c.du || !c.dBc || !c.dCc || !c.dt || !c.dlam || !c.dlog ||
-        !c.dD || !c.deps)
-        return fail(EACS_ERR_INVALID, "%s: null pointer argument", fn);
-    const int K = chunk_len(T, npt, lanes * npt, HC);
-    if (K == 0) return fail(EACS_ERR_UNSUPPORTED, "%s: shared memory too small for H=%lld", fn, (long long)c.H);
-    const TWs w = tws(c.B, c.L, c.H, c.N, CL, K);
-    if (!c.workspace || c.workspace_bytes < w.total)
-        return fail(EACS_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", fn, w.total,
-                    c.workspace_bytes);
-    TArgs a{};
+size_t layout_bytes(int64_t B, int64_t L, int64_t H, int64_t N, bool commits) {
+    if (B <= 0 || L <= 0 || H <= 0 || N <= 0) return 0;
+    Layout o{};
+    if (train_layout(B, L, H, N, commits, nullptr, &o) != EACS_OK) return 0;
+    return tws(B, L, H, N, o.CL, o.K).total;
+}
+
+// Fills the fields of `a` every pass shares: inputs, workspace, sizes.
+void fill_common(TArgs& a, const TrainBwdCall& c, const Layout& o, const TWs& w) {
     a.lam = static_cast<const float2*>(c.lam);
     a.log_dt = c.log_dt;
     a.u = c.u;
@@ -961,20 +1037,6 @@ int train_bwd(const TrainBwdCall& c, cudaStream_t stream) {
     a.dt_max = c.dt_max;
     a.Tp = c.temperature > 1e-4f ? c.temperature : 1e-4f;
     a.gates = c.gates;
-    a.resid = c.resid;
-    a.stats = static_cast<const float2*>(c.stats);
-    a.gy = c.gy;
-    a.ggs = c.ggs;
-    a.grs = c.grs;
-    a.gns = c.gns;
-    a.du = c.du;
-    a.dBc = static_cast<float2*>(c.dBc);
-    a.dCc = static_cast<float2*>(c.dCc);
-    a.dt = c.dt;
-    a.dlam = static_cast<float2*>(c.dlam);
-    a.dlog = c.dlog;
-    a.dD = c.dD;
-    a.deps = c.deps;
     char* ws = static_cast<char*>(c.workspace);
     a.ck_h = reinterpret_cast<float2*>(ws + w.ck_h);
     a.ck_u = reinterpret_cast<float*>(ws + w.ck_u);
@@ -991,17 +1053,122 @@ int train_bwd(const TrainBwdCall& c, cudaStream_t stream) {
     a.L = static_cast<int>(c.L);
     a.H = static_cast<int>(c.H);
     a.N = static_cast<int>(c.N);
-    a.K = K;
-    a.nK = static_cast<int>((c.L + K - 1) / K);
-    a.CL = CL;
-    a.HC = HC;
-    a.have_ckpt = c.have_ckpt ? 1 : 0;
+    a.K = o.K;
+    a.nK = static_cast<int>((c.L + o.K - 1) / o.K);
+    a.CL = o.CL;
+    a.HC = o.HC;
     a.Klog = 0;
     while ((1 << a.Klog) < a.K) ++a.Klog;
+}
+
+}  // namespace
+
+size_t train_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
+    return layout_bytes(B, L, H, N, false);
+}
+
+size_t train_commits_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N) {
+    return layout_bytes(B, L, H, N, true);
+}
+
+int train_ckpt_layout(int64_t B, int64_t L, int64_t H, int64_t N, void* workspace, size_t workspace_bytes,
+                      CellCall* c) {
+    const char* fn = "eacs_cell_train_fwd_ckpt";
+    Layout o{};
+    if (B <= 0 || L <= 0 || H <= 0 || N <= 0)
+        return fail(EACS_ERR_UNSUPPORTED, "%s: no training backward for B=%lld L=%lld H=%lld N=%lld", fn,
+                    (long long)B, (long long)L, (long long)H, (long long)N);
+    const int rc = train_layout(B, L, H, N, false, fn, &o);
+    if (rc) return rc;
+    const TWs w = tws(B, L, H, N, o.CL, o.K);
+    if (!workspace || workspace_bytes < w.total)
+        return fail(EACS_ERR_WORKSPACE, "%s: backward workspace of %zu bytes needed, %zu given", fn, w.total,
+                    workspace_bytes);
+    char* ws = static_cast<char*>(workspace);
+    c->ck_h = ws + w.ck_h;
+    c->ck_u = reinterpret_cast<float*>(ws + w.ck_u);
+    c->ck_row = ws + w.ck_row;
+    c->ck_bc = ws + w.ck_bc;
+    c->ck_K = o.K;
+    c->ck_nK = static_cast<int>((L + o.K - 1) / o.K);
+    return EACS_OK;
+}
+
+int train_commits_replay(const TrainBwdCall& c, const CommitOut& out, cudaStream_t stream) {
+    const char* fn = "eacs_cell_train_commits_fwd";
+    if (c.B == 0 || c.L == 0 || c.H == 0) return EACS_OK;
+    Layout o{};
+    const int rc = train_layout(c.B, c.L, c.H, c.N, true, fn, &o);
+    if (rc) return rc;
+    if (c.u_dtype != EACS_DTYPE_F32 && c.u_dtype != EACS_DTYPE_F16 && c.u_dtype != EACS_DTYPE_BF16)
+        return fail(EACS_ERR_INVALID, "%s: unknown u dtype %d", fn, c.u_dtype);
+    if (!c.lam || !c.log_dt || !c.u || !c.Bc || !c.Cc || !c.t || !c.gates || !out.h || !out.t || !out.u ||
+        !out.B || !out.C)
+        return fail(EACS_ERR_INVALID, "%s: null pointer argument", fn);
+    const TWs w = tws(c.B, c.L, c.H, c.N, o.CL, o.K);
+    if (!c.workspace || c.workspace_bytes < w.total)
+        return fail(EACS_ERR_WORKSPACE, "%s: backward workspace of %zu bytes needed, %zu given", fn, w.total,
+                    c.workspace_bytes);
+    TArgs a{};
+    fill_common(a, c, o, w);
+    a.cm_h = static_cast<float2*>(out.h);
+    a.cm_t = out.t;
+    a.cm_u = out.u;
+    a.cm_B = static_cast<float2*>(out.B);
+    a.cm_C = static_cast<float2*>(out.C);
     cudaError_t e;
-    if (c.u_dtype == EACS_DTYPE_F16) e = train_by_n<__half>(a, T, stream);
-    else if (c.u_dtype == EACS_DTYPE_BF16) e = train_by_n<__nv_bfloat16>(a, T, stream);
-    else e = train_by_n<float>(a, T, stream);
+    if (c.u_dtype == EACS_DTYPE_F16) e = launch_ckpt<__half>(a, stream);
+    else if (c.u_dtype == EACS_DTYPE_BF16) e = launch_ckpt<__nv_bfloat16>(a, stream);
+    else e = launch_ckpt<float>(a, stream);
+    return cuda_check(e, fn);
+}
+
+int train_bwd(const TrainBwdCall& c, cudaStream_t stream) {
+    const char* fn = c.commits ? "eacs_cell_train_commits_bwd"
+                   : c.have_ckpt ? "eacs_cell_train_bwd_ckpt" : "eacs_cell_train_bwd";
+    if (c.B < 0 || c.L < 0 || c.H < 0 || c.N < 0) return fail(EACS_ERR_INVALID, "%s: negative size", fn);
+    if (c.B == 0 || c.L == 0 || c.H == 0) return EACS_OK;
+    Layout o{};
+    const int rc = train_layout(c.B, c.L, c.H, c.N, c.commits, fn, &o);
+    if (rc) return rc;
+    if (c.u_dtype != EACS_DTYPE_F32 && c.u_dtype != EACS_DTYPE_F16 && c.u_dtype != EACS_DTYPE_BF16)
+        return fail(EACS_ERR_INVALID, "%s: unknown u dtype %d", fn, c.u_dtype);
+    if (!c.lam || !c.log_dt || !c.u || !c.Bc || !c.Cc || !c.t || !c.D || !c.mean || !c.var || !c.gates ||
+        !c.resid || !c.stats || !c.gy || !c.du || !c.dBc || !c.dCc || !c.dt || !c.dlam || !c.dlog ||
+        !c.dD || !c.deps)
+        return fail(EACS_ERR_INVALID, "%s: null pointer argument", fn);
+    const TWs w = tws(c.B, c.L, c.H, c.N, o.CL, o.K);
+    if (!c.workspace || c.workspace_bytes < w.total)
+        return fail(EACS_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", fn, w.total,
+                    c.workspace_bytes);
+    TArgs a{};
+    fill_common(a, c, o, w);
+    a.resid = c.resid;
+    a.stats = static_cast<const float2*>(c.stats);
+    a.gy = c.gy;
+    a.ggs = c.ggs;
+    a.grs = c.grs;
+    a.gns = c.gns;
+    a.du = c.du;
+    a.dBc = static_cast<float2*>(c.dBc);
+    a.dCc = static_cast<float2*>(c.dCc);
+    a.dt = c.dt;
+    a.dlam = static_cast<float2*>(c.dlam);
+    a.dlog = c.dlog;
+    a.dD = c.dD;
+    a.deps = c.deps;
+    a.have_ckpt = (c.have_ckpt || c.commits) ? 1 : 0;
+    a.commit_grads = c.commits ? 1 : 0;
+    a.gate_const = c.gate_const ? 1 : 0;
+    a.gc_h = static_cast<const float2*>(c.gc_h);
+    a.gc_t = c.gc_t;
+    a.gc_u = c.gc_u;
+    a.gc_B = static_cast<const float2*>(c.gc_B);
+    a.gc_C = static_cast<const float2*>(c.gc_C);
+    cudaError_t e;
+    if (c.u_dtype == EACS_DTYPE_F16) e = train_by_n<__half>(a, o.T, stream);
+    else if (c.u_dtype == EACS_DTYPE_BF16) e = train_by_n<__nv_bfloat16>(a, o.T, stream);
+    else e = train_by_n<float>(a, o.T, stream);
     return cuda_check(e, fn);
 }
 

@@ -97,6 +97,19 @@ SIGNATURES = {
                                       _P, _P, _P, _P, _P, _P, _P,
                                       _P, _P, _P, _P, _P, _P, _P, _P,
                                       _P, ctypes.c_size_t, _I64, _I64, _I64, _I64, _P]),
+    "eacs_cell_train_commits_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
+    "eacs_cell_train_commits_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
+                                         _F, _F, _F, _F, _F, _F, _I, _F,
+                                         _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                         _P, _SZ, _P, _SZ, _I64, _I64, _I64, _I64, _P]),
+    "eacs_cell_train_commits_bwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
+                                         _F, _F, _F, _F, _F, _F, _I, _F,
+                                         _P, _P, _P, _P, _P, _P,
+                                         _P, _P, _P, _P, _P,
+                                         _P, _P, _P, _P, _P, _P, _P, _P,
+                                         _P, _SZ, _I64, _I64, _I64, _I64, _P]),
+    "eacs_query_readout_bwd_workspace_size": (_SZ, [_I64] * 5),
+    "eacs_query_readout_bwd": (_I, [_P] * 20 + [_P, _SZ] + [_I64] * 5 + [_F, _F, _P]),
     "eacs_cell_fwd_noalloc": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P,
                                    _F, _F, _F, _F, _F, _F, _I, _I, _F, _F, _I, _F,
                                    _P, _P, _P, _I64, _I64, _I64, _I64, _P]),

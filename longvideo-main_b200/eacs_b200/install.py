@@ -25,8 +25,9 @@ def install(package: str = "cst_ssm", fuse_ungated: bool = False,
     fused kernel instead of the Python step loop.
     queries: also route EACSLayer.run_with_commits and the continuous-query
     functions (segment_index, readout_from_commits) through the commit and
-    readout kernels where no gradient has to flow through the commits; the
-    reference's own code runs otherwise.
+    readout kernels, with gradients through the commits and the readouts
+    (training); the reference's own code runs only for CPI-modulated or
+    non-event gates and non-continuous discretisation.
     streaming: also route temporal_step (modules/streaming.py, and the name
     models/adaptive_path.py imported from it) through the streaming step
     kernel under the same rule.

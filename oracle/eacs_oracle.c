@@ -1110,7 +1110,8 @@ static int cell_bwd_impl(const float* lam, const float* log_dt, const float* u,
                 aCn[n] = cd_scale(aC[n], 1 - g);
             }
             /* gate -> soft -> r, eps */
-            double xbar = gbar * soft * (1 - soft);
+            /* gate_mode 2: the eval-mode gate r > eps, a constant */
+            double xbar = gate_mode == 2 ? 0.0 : gbar * soft * (1 - soft);
             rbar += xbar / Tp;
             acc_eps[bi] += -xbar / Tp;
             double numbar = rbar / den;
@@ -1252,8 +1253,9 @@ int eacs_oracle_cell_bwd(const float* lam, const float* log_dt, const float* u,
 /* ---------------------------------------------------------------------------
  * Training through per-frame commits: EACSLayer._commit_range (eacs.py:386-401)
  * under autograd, i.e. the gated cell of eacs_step (eacs.py:78-142) with the
- * training gate (STE hard forward for gate_mode 0, soft for 1;
- * event_gate.py:84-105), which also returns the state after every step.
+ * training gate (STE hard forward for gate_mode 0, soft for 1; 2 is the
+ * eval-mode gate r > eps, which passes no gradient; event_gate.py:84-105),
+ * which also returns the state after every step.
  * Forward outputs (any may be NULL): y (B,L,H), gate, resid (B,L) and the
  * commits h (B,L,H,N) complex, t (B,L), u (B,L,H), B, C (B,L,N) complex.
  * Backward: the cell backward above with the upstream adjoints of the commits

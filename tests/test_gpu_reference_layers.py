@@ -228,3 +228,66 @@ def test_eacs_layer_fused_train(ref):
             assert p.grad is None or not p.grad.any(), name
             continue
         assert relerr(p.grad.cpu().numpy(), p_ref.grad.cpu().numpy()) < GRAD_TOL, name
+
+
+@pytest.mark.parametrize("train", [True, False])
+def test_continuous_query_gradients(ref, train):
+    """continuous_query (modules/continuous_query.py:56-65) under autograd:
+    run_with_commits (training mode: the STE gate; eval mode: r > eps) and
+    readout_from_commits at query times between, on and around the frames.
+    The loss's gradients with respect to the input and every parameter, the
+    reference's own step loop and autograd against install(queries=True)'s
+    commit and readout kernels (eacs_cell_train_commits_*,
+    eacs_query_readout_bwd).  The threshold is bisected (eps_anneal) to an
+    update rate near one half and moved away from every residual."""
+    from cst_ssm.modules.event_gate import EventGate
+    from cst_ssm.ops.spectral_init import BranchSpec
+    cq = ref["modules.continuous_query"]
+    torch.manual_seed(0)
+    layer = ref["modules.eacs"].EACSLayer(96, BranchSpec("short", 16, 0.5, 4.0),
+                                          gate=EventGate(init_eps=0.12)).to(DEV)
+    x, t = _video(2, 40, 96, 12)
+    g = torch.Generator().manual_seed(13)
+    tq = (t[:, :1] - 0.2 + (t[:, -1:] - t[:, :1] + 0.5) * torch.rand(2, 33, generator=g).to(DEV)).sort(1).values
+    tq[:, 3] = t[:, 7]
+    gq = torch.randn(2, 33, 96, generator=g).to(DEV)
+    layer.eval()
+    with torch.no_grad():
+        base = float(layer.gate.eps) / float(layer.gate.eps_anneal)
+        lo, hi = 0.0, 4.0
+        for _ in range(14):
+            mid = 0.5 * (lo + hi)
+            layer.gate.set_eps_anneal(mid / base)
+            rate = float(layer.run_with_commits(x, t)[0].gates.mean())
+            lo, hi = (mid, hi) if rate > 0.5 else (lo, mid)
+        eps = 0.5 * (lo + hi)
+        for _ in range(200):
+            layer.gate.set_eps_anneal(eps / base)
+            r = layer.run_with_commits(x, t)[0].residual.cpu().numpy()
+            if decisive(r, eps, None, 2e-5).all():
+                break
+            eps *= 1.00002
+    layer.train(train)
+    twin = copy.deepcopy(layer)
+
+    def run(m):
+        xx = x.clone().requires_grad_(True)
+        y = cq.continuous_query(m, xx, t, tq)
+        (y * gq).sum().backward()
+        return y.detach(), xx.grad
+
+    n0 = _launches()
+    y_ref, gx_ref = run(layer)
+    assert _launches() == n0
+    _install(queries=True)
+    y, gx = run(twin)
+    assert _launches() > n0
+    rate = float(twin.run_with_commits(x, t)[0].gates.detach().float().mean())
+    assert 0.2 < rate < 0.8, rate
+    assert relerr(y.cpu().numpy(), y_ref.cpu().numpy()) < FWD_TOL
+    assert relerr(gx.cpu().numpy(), gx_ref.cpu().numpy()) < GRAD_TOL
+    for (name, p), p_ref in zip(twin.named_parameters(), layer.parameters()):
+        if p_ref.grad is None:
+            assert p.grad is None or not p.grad.any(), name
+            continue
+        assert relerr(p.grad.cpu().numpy(), p_ref.grad.cpu().numpy()) < GRAD_TOL, name
