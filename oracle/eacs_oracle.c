@@ -1280,4 +1280,297 @@ int eacs_oracle_cell_bwd_commits(const float* lam, const float* log_dt, const fl
                          ct_out, cu_out, cB_out, cC_out, B, L, H, N);
 }
 
+/* ---------------------------------------------------------------------------
+ * Backward of one streaming step of one branch (the per-branch body of
+ * temporal_step, streaming.py:55-80, over eacs_step, eacs.py:78-142, and
+ * EventGate.forward, event_gate.py:84-105), under autograd: the
+ * vector-Jacobian product with respect to the frame's u (B,H), Bc, Cc (B,N)
+ * complex, t (B), cpi (B), the state in h (B,H,N) complex, t, u, B, C, and
+ * lam (H,N) complex, log_dt (H), D (H), eps (1).  Upstream: gy (B,H) of y
+ * (before proj_out), gg, gr, gn (B) of the gate (1 on the first step), resid
+ * and innov outputs, and gh, gt, gu, gB, gC of the state out (any may be
+ * NULL = 0).  gate_mode 0: STE (hard forward, soft backward); 1: soft; 2:
+ * hard with no gradient through the gate (eval).  gs (B) or NULL: the
+ * forward's gate output to pin for rows past their first observation (hard
+ * modes).  Rows with valid = 0 pass the state's adjoints through.  Outputs
+ * overwritten; dcpi may be NULL.  Double precision throughout.
+ * ------------------------------------------------------------------------- */
+int eacs_oracle_stream_step_bwd(const float* lam, const float* log_dt, const float* D,
+                                const float* mean, const float* var, const float* u,
+                                const float* Bc, const float* Cc, const float* t,
+                                const uint8_t* valid, const float* cpi, const float* h_in,
+                                const float* t_in, const float* u_in, const float* B_in,
+                                const float* C_in, const uint8_t* init_in, const float* gs,
+                                const float* gy, const float* gg, const float* gr,
+                                const float* gn, const float* gh, const float* gt,
+                                const float* gu, const float* gB, const float* gC, float* du,
+                                float* dBc, float* dCc, float* dt, float* dcpi, float* dh_in,
+                                float* dt_in, float* du_in, float* dB_in, float* dC_in,
+                                float* dlam, float* dlog, float* dD, float* deps, float eps,
+                                float eta, float var_eps, float dt_init, float dt_min,
+                                float dt_max, float cpi_mod, int gate_mode, float T, int64_t B,
+                                int64_t H, int64_t N) {
+    const double Tp = T > 1e-4f ? (double)T : 1e-4;
+    const int64_t HN = H * N;
+    double* acc_lam = (double*)calloc((size_t)(B * HN * 2), sizeof(double));
+    double* acc_log = (double*)calloc((size_t)(B * H), sizeof(double));
+    double* acc_D = (double*)calloc((size_t)(B * H), sizeof(double));
+    double* acc_eps = (double*)calloc((size_t)B, sizeof(double));
+#pragma omp parallel for num_threads(nthreads()) schedule(dynamic, 1)
+    for (int64_t bi = 0; bi < B; ++bi) {
+        const int v = valid ? valid[bi] != 0 : 1;
+        const float* hs = h_in + bi * HN * 2;
+        float* dhs = dh_in + bi * HN * 2;
+        if (!v) {  /* masked: the state passes through */
+            for (int64_t i = 0; i < HN * 2; ++i) dhs[i] = gh ? gh[bi * HN * 2 + i] : 0.f;
+            dt_in[bi] = gt ? gt[bi] : 0.f;
+            for (int64_t hh = 0; hh < H; ++hh) {
+                du_in[bi * H + hh] = gu ? gu[bi * H + hh] : 0.f;
+                du[bi * H + hh] = 0.f;
+            }
+            for (int64_t q = 0; q < 2 * N; ++q) {
+                dB_in[bi * 2 * N + q] = gB ? gB[bi * 2 * N + q] : 0.f;
+                dC_in[bi * 2 * N + q] = gC ? gC[bi * 2 * N + q] : 0.f;
+                dBc[bi * 2 * N + q] = 0.f;
+                dCc[bi * 2 * N + q] = 0.f;
+            }
+            dt[bi] = 0.f;
+            if (dcpi) dcpi[bi] = 0.f;
+            continue;
+        }
+        const int first = !init_in[bi];
+        const double tl = t[bi];
+        const double t0 = first ? tl - (double)dt_init : (double)t_in[bi];
+        double* u0 = (double*)malloc(sizeof(double) * (size_t)H);
+        cd* B0 = (cd*)malloc(sizeof(cd) * (size_t)N);
+        cd* C0 = (cd*)malloc(sizeof(cd) * (size_t)N);
+        cd* Bf = (cd*)malloc(sizeof(cd) * (size_t)N);
+        cd* Cf = (cd*)malloc(sizeof(cd) * (size_t)N);
+        for (int64_t hh = 0; hh < H; ++hh) u0[hh] = first ? u[bi * H + hh] : u_in[bi * H + hh];
+        for (int64_t n = 0; n < N; ++n) {
+            Bf[n] = cd_of(Bc + (bi * N + n) * 2);
+            Cf[n] = cd_of(Cc + (bi * N + n) * 2);
+            B0[n] = first ? Bf[n] : cd_of(B_in + (bi * N + n) * 2);
+            C0[n] = first ? Cf[n] : cd_of(C_in + (bi * N + n) * 2);
+        }
+        const double draw = tl - t0, delta = draw > 0 ? draw : 0;
+        cd *dA = (cd*)malloc(sizeof(cd) * (size_t)HN), *E = (cd*)malloc(sizeof(cd) * (size_t)HN);
+        cd *dB = (cd*)malloc(sizeof(cd) * (size_t)HN), *xh = (cd*)malloc(sizeof(cd) * (size_t)HN);
+        cd *hu = (cd*)malloc(sizeof(cd) * (size_t)HN), *il = (cd*)malloc(sizeof(cd) * (size_t)HN);
+        double *dte = (double*)malloc(sizeof(double) * (size_t)H), *sc = (double*)malloc(sizeof(double) * (size_t)H);
+        double *obs = (double*)malloc(sizeof(double) * (size_t)H), *dv = (double*)malloc(sizeof(double) * (size_t)H);
+        double *sd = (double*)malloc(sizeof(double) * (size_t)H), *mdt = (double*)malloc(sizeof(double) * (size_t)H);
+        double sdiff = 0, sobs = 0;
+        for (int64_t hh = 0; hh < H; ++hh) {
+            sc[hh] = exp((double)log_dt[hh]);
+            const double raw = delta * sc[hh];
+            double v2 = raw < dt_min ? dt_min : raw;
+            if (v2 > dt_max) v2 = dt_max;
+            dte[hh] = v2;
+            mdt[hh] = (raw >= dt_min && raw <= (double)dt_max) ? 1.0 : 0.0;
+            double yh = 0;
+            for (int64_t n = 0; n < N; ++n) {
+                const int64_t i = hh * N + n;
+                const cd lm = {lam[2 * i], lam[2 * i + 1]};
+                const double d2 = lm.re * lm.re + lm.im * lm.im;
+                il[i] = (cd){lm.re / d2, -lm.im / d2};
+                const double a = lm.re * dte[hh], b = lm.im * dte[hh], e = exp(a);
+                dA[i] = (cd){e * cos(b), e * sin(b)};
+                E[i] = (cd){expm1(a) * cos(b) - 2 * sin(0.5 * b) * sin(0.5 * b), e * sin(b)};
+                dB[i] = cd_mul(E[i], il[i]);
+                const cd P = cd_mul(dA[i], cd_of(hs + 2 * i));
+                xh[i] = cd_add(P, cd_scale(cd_mul(dB[i], B0[n]), u0[hh]));
+                hu[i] = cd_add(P, cd_scale(cd_mul(dB[i], Bf[n]), u[bi * H + hh]));
+                yh += C0[n].re * xh[i].re - C0[n].im * xh[i].im;
+            }
+            sd[hh] = sqrt((double)var[hh] + (double)var_eps);
+            obs[hh] = (u[bi * H + hh] - mean[hh]) / sd[hh];
+            dv[hh] = obs[hh] - (yh - mean[hh]) / sd[hh];
+            sdiff += dv[hh] * dv[hh];
+            sobs += obs[hh] * obs[hh];
+        }
+        const double num = sqrt(sdiff), nobs = sqrt(sobs), den = nobs + eta, r = num / den;
+        double epsl = first ? -1.0 : (double)eps, e1 = epsl, cc = 0;
+        const int mod = cpi != NULL && cpi_mod > 0.f;
+        if (mod) {
+            cc = cpi[bi] < 0 ? 0 : (cpi[bi] > 1 ? 1 : cpi[bi]);
+            e1 = epsl * (1.0 - cpi_mod * cc);
+            epsl = e1 > 1e-3 ? e1 : 1e-3;
+        }
+        const double soft = 1.0 / (1.0 + exp(-((r - epsl) / Tp)));
+        double g = gate_mode == 1 ? soft : (r > epsl ? 1.0 : 0.0);
+        if (gate_mode != 1 && gs && !first) g = gs[bi];
+        /* ---- adjoints ---- */
+        double gbar = 0, dtl = 0, dt0 = 0;
+        double *dul = (double*)calloc((size_t)H, sizeof(double)), *du0 = (double*)calloc((size_t)H, sizeof(double));
+        cd *dBl = (cd*)calloc((size_t)N, sizeof(cd)), *dCl = (cd*)calloc((size_t)N, sizeof(cd));
+        cd *aB0 = (cd*)calloc((size_t)N, sizeof(cd)), *aC0 = (cd*)calloc((size_t)N, sizeof(cd));
+        cd *ahu = (cd*)calloc((size_t)HN, sizeof(cd)), *axh = (cd*)calloc((size_t)HN, sizeof(cd));
+        cd *ah0 = (cd*)calloc((size_t)HN, sizeof(cd));
+        double* alam = acc_lam + bi * HN * 2;
+        double* alog = acc_log + bi * H;
+        double* aD = acc_D + bi * H;
+        for (int64_t hh = 0; hh < H; ++hh) {
+            const double yb = gy ? gy[bi * H + hh] : 0.0, ul = u[bi * H + hh];
+            dul[hh] += yb * D[hh];
+            aD[hh] += yb * ul;
+            for (int64_t n = 0; n < N; ++n) {
+                const int64_t i = hh * N + n;
+                const cd hc = cd_add(cd_scale(hu[i], g), cd_scale(xh[i], 1 - g));
+                cd ahc = cd_scale(cd_conj(Cf[n]), yb);
+                dCl[n] = cd_add(dCl[n], cd_scale(cd_conj(hc), yb));
+                const cd Ah = gh ? cd_of(gh + (bi * HN + i) * 2) : (cd){0, 0};
+                if (first) {
+                    ahc = cd_add(ahc, Ah);
+                } else {
+                    ahu[i] = cd_add(ahu[i], cd_scale(Ah, g));
+                    ah0[i] = cd_add(ah0[i], cd_scale(Ah, 1 - g));
+                    gbar += cd_redot(Ah, cd_sub(hu[i], cd_of(hs + 2 * i)));
+                }
+                ahu[i] = cd_add(ahu[i], cd_scale(ahc, g));
+                axh[i] = cd_add(axh[i], cd_scale(ahc, 1 - g));
+                gbar += cd_redot(ahc, cd_sub(hu[i], xh[i]));
+            }
+        }
+        const double At = gt ? gt[bi] : 0.0;
+        if (first) {
+            dtl += At;
+            for (int64_t hh = 0; hh < H; ++hh) dul[hh] += gu ? gu[bi * H + hh] : 0.0;
+            for (int64_t n = 0; n < N; ++n) {
+                if (gB) dBl[n] = cd_add(dBl[n], cd_of(gB + (bi * N + n) * 2));
+                if (gC) dCl[n] = cd_add(dCl[n], cd_of(gC + (bi * N + n) * 2));
+            }
+        } else {
+            dtl += g * At;
+            dt0 += (1 - g) * At;
+            gbar += At * (tl - t0);
+            for (int64_t hh = 0; hh < H; ++hh) {
+                const double Au = gu ? gu[bi * H + hh] : 0.0;
+                dul[hh] += g * Au;
+                du0[hh] += (1 - g) * Au;
+                gbar += Au * (u[bi * H + hh] - u0[hh]);
+            }
+            for (int64_t n = 0; n < N; ++n) {
+                const cd AB = gB ? cd_of(gB + (bi * N + n) * 2) : (cd){0, 0};
+                const cd AC = gC ? cd_of(gC + (bi * N + n) * 2) : (cd){0, 0};
+                dBl[n] = cd_add(dBl[n], cd_scale(AB, g));
+                aB0[n] = cd_add(aB0[n], cd_scale(AB, 1 - g));
+                dCl[n] = cd_add(dCl[n], cd_scale(AC, g));
+                aC0[n] = cd_add(aC0[n], cd_scale(AC, 1 - g));
+                gbar += cd_redot(AB, cd_sub(Bf[n], B0[n])) + cd_redot(AC, cd_sub(Cf[n], C0[n]));
+            }
+            if (gg) gbar += gg[bi];
+        }
+        const double xbar = gate_mode == 2 ? 0.0 : gbar * soft * (1 - soft) / Tp;
+        const double rbar = (gr ? gr[bi] : 0.0) + xbar;
+        double dcp = 0;
+        if (!first) {
+            const double ebar = -xbar;
+            if (mod) {
+                if (e1 >= 1e-3) {
+                    acc_eps[bi] += ebar * (1.0 - cpi_mod * cc);
+                    if (cpi[bi] >= 0 && cpi[bi] <= 1) dcp = -ebar * (double)eps * cpi_mod;
+                }
+            } else {
+                acc_eps[bi] += ebar;
+            }
+        }
+        if (dcpi) dcpi[bi] = (float)dcp;
+        const double nbar = (!first && gn) ? gn[bi] : 0.0;
+        const double numbar = rbar / den, denbar = -rbar * num / (den * den), numnbar = nbar / den;
+        double deltabar = 0;
+        for (int64_t hh = 0; hh < H; ++hh) {
+            const double dbar = num > 0 ? numbar * dv[hh] / num : 0.0;
+            const double obar = dbar + (nobs > 0 ? denbar * obs[hh] / nobs : 0.0);
+            const double pbar = -dbar - (num > 0 ? numnbar * dv[hh] / num : 0.0);
+            dul[hh] += obar / sd[hh];
+            const double yhb = pbar / sd[hh];
+            const double ul = u[bi * H + hh];
+            double dtebar = 0;
+            for (int64_t n = 0; n < N; ++n) {
+                const int64_t i = hh * N + n;
+                axh[i] = cd_add(axh[i], cd_scale(cd_conj(C0[n]), yhb));
+                aC0[n] = cd_add(aC0[n], cd_scale(cd_conj(xh[i]), yhb));
+                const cd aP = cd_add(axh[i], ahu[i]);
+                const cd qp = cd_mul(dB[i], B0[n]), qc = cd_mul(dB[i], Bf[n]);
+                const cd aqp = cd_scale(axh[i], u0[hh]), aqc = cd_scale(ahu[i], ul);
+                du0[hh] += cd_redot(axh[i], qp);
+                dul[hh] += cd_redot(ahu[i], qc);
+                const cd adB = cd_add(cd_mul(aqp, cd_conj(B0[n])), cd_mul(aqc, cd_conj(Bf[n])));
+                aB0[n] = cd_add(aB0[n], cd_mul(cd_conj(dB[i]), aqp));
+                dBl[n] = cd_add(dBl[n], cd_mul(cd_conj(dB[i]), aqc));
+                const cd h0 = cd_of(hs + 2 * i);
+                const cd adA = cd_mul(aP, cd_conj(h0));
+                ah0[i] = cd_add(ah0[i], cd_mul(cd_conj(dA[i]), aP));
+                const cd aE = cd_mul(adB, cd_conj(il[i]));
+                const cd ail = cd_mul(adB, cd_conj(E[i]));
+                cd alm = cd_scale(cd_mul(cd_conj(cd_mul(il[i], il[i])), ail), -1.0);
+                const cd az = cd_mul(cd_conj(dA[i]), cd_add(adA, aE));
+                alm = cd_add(alm, cd_scale(az, dte[hh]));
+                const cd lm = {lam[2 * i], lam[2 * i + 1]};
+                dtebar += cd_redot(az, lm);
+                alam[2 * i] += alm.re;
+                alam[2 * i + 1] += alm.im;
+            }
+            const double drb = mdt[hh] * dtebar;
+            alog[hh] += drb * delta * sc[hh];
+            deltabar += drb * sc[hh];
+        }
+        const double mdel = draw >= 0 ? 1.0 : 0.0;
+        dtl += mdel * deltabar;
+        dt0 -= mdel * deltabar;
+        if (first) {
+            dtl += dt0;
+            for (int64_t hh = 0; hh < H; ++hh) dul[hh] += du0[hh];
+            for (int64_t n = 0; n < N; ++n) {
+                dBl[n] = cd_add(dBl[n], aB0[n]);
+                dCl[n] = cd_add(dCl[n], aC0[n]);
+            }
+            dt_in[bi] = 0.f;
+            for (int64_t hh = 0; hh < H; ++hh) du_in[bi * H + hh] = 0.f;
+            for (int64_t q = 0; q < 2 * N; ++q) { dB_in[bi * 2 * N + q] = 0.f; dC_in[bi * 2 * N + q] = 0.f; }
+        } else {
+            dt_in[bi] = (float)dt0;
+            for (int64_t hh = 0; hh < H; ++hh) du_in[bi * H + hh] = (float)du0[hh];
+            for (int64_t n = 0; n < N; ++n) {
+                dB_in[(bi * N + n) * 2] = (float)aB0[n].re;
+                dB_in[(bi * N + n) * 2 + 1] = (float)aB0[n].im;
+                dC_in[(bi * N + n) * 2] = (float)aC0[n].re;
+                dC_in[(bi * N + n) * 2 + 1] = (float)aC0[n].im;
+            }
+        }
+        dt[bi] = (float)dtl;
+        for (int64_t hh = 0; hh < H; ++hh) du[bi * H + hh] = (float)dul[hh];
+        for (int64_t n = 0; n < N; ++n) {
+            dBc[(bi * N + n) * 2] = (float)dBl[n].re;
+            dBc[(bi * N + n) * 2 + 1] = (float)dBl[n].im;
+            dCc[(bi * N + n) * 2] = (float)dCl[n].re;
+            dCc[(bi * N + n) * 2 + 1] = (float)dCl[n].im;
+        }
+        for (int64_t i = 0; i < HN; ++i) {
+            dhs[2 * i] = (float)ah0[i].re;
+            dhs[2 * i + 1] = (float)ah0[i].im;
+        }
+        free(u0); free(B0); free(C0); free(Bf); free(Cf); free(dA); free(E); free(dB); free(xh);
+        free(hu); free(il); free(dte); free(sc); free(obs); free(dv); free(sd); free(mdt);
+        free(dul); free(du0); free(dBl); free(dCl); free(aB0); free(aC0); free(ahu); free(axh); free(ah0);
+    }
+    for (int64_t i = 0; i < HN * 2; ++i) {
+        double s = 0;
+        for (int64_t bi = 0; bi < B; ++bi) s += acc_lam[bi * HN * 2 + i];
+        dlam[i] = (float)s;
+    }
+    for (int64_t hh = 0; hh < H; ++hh) {
+        double s = 0, s2 = 0;
+        for (int64_t bi = 0; bi < B; ++bi) { s += acc_log[bi * H + hh]; s2 += acc_D[bi * H + hh]; }
+        dlog[hh] = (float)s;
+        dD[hh] = (float)s2;
+    }
+    double se = 0;
+    for (int64_t bi = 0; bi < B; ++bi) se += acc_eps[bi];
+    deps[0] = (float)se;
+    free(acc_lam); free(acc_log); free(acc_D); free(acc_eps);
+    return 0;
+}
+
 const char* eacs_oracle_version(void) { return "eacs-oracle 2"; }

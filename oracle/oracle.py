@@ -50,6 +50,7 @@ def lib():
         L.eacs_oracle_cell_bwd_commits.argtypes = ([_P] * 9 + [_F] * 5 + [_F, _I] + [_P] * 4
                                                    + [_P] * 5 + [_P] * 8 + [_P] * 8 + [_I64] * 4)
         L.eacs_oracle_query_readout_bwd.argtypes = [_P] * 21 + [_I64] * 5 + [_F, _F]
+        L.eacs_oracle_stream_step_bwd.argtypes = [_P] * 41 + [_F] * 7 + [_I, _F] + [_I64] * 3
         L.eacs_oracle_stream_chunk.argtypes = [_P] * 27 + [_F] * 7 + [_I, _F] + [_I64] * 4
         L.eacs_oracle_set_threads.argtypes = [_I]
         L.eacs_oracle_version.restype = ctypes.c_char_p
@@ -285,6 +286,42 @@ def query_readout_bwd(lam, log_dt, D, ch, ct, cu, cB, cC, frame_t, t_query, gy, 
         _ptr(gc["u"]), _ptr(gc["B"]), _ptr(gc["C"]), _ptr(gtq), _ptr(dlam), _ptr(dlog), _ptr(dD),
         B, L, Q, H, N, dt_min, dt_max)
     return gc, gtq, dlam, dlog, dD
+
+
+def stream_step_bwd(lam, log_dt, D, mean, var, u, Bc, Cc, t, valid, cpi, state, up, eps, eta,
+                    var_eps=1e-5, dt_init=1.0, dt_min=1e-3, dt_max=1e3, cpi_mod=0.0, gate_mode=0,
+                    T=0.1, gs=None):
+    """Backward of one streaming step of one branch (the per-branch body of
+    temporal_step, cst_ssm/modules/streaming.py:55-80, over eacs_step).
+
+    u (B,H), Bc/Cc (B,N), t (B), valid (B) bool or None, cpi (B) or None;
+    state = (h (B,H,N), t (B), u (B,H), B (B,N), C (B,N), initialized (B));
+    up: dict of upstream gradients with any of y (B,H), gate, resid, innov
+    (B), h, t, u, B, C (the state out).  gate_mode 0 STE, 1 soft, 2 hard
+    (no gradient through the gate).  Returns dict du, dBc, dCc, dt, dcpi,
+    dh, dt_in, du_in, dB_in, dC_in, dlam, dlog_dt, dD, deps."""
+    lam = _c(lam, np.complex64)
+    B, H = np.asarray(u).shape
+    N = lam.shape[1]
+    f = lambda x: None if x is None else _c(x, np.float32)  # noqa: E731
+    c = lambda x: None if x is None else _c(x, np.complex64)  # noqa: E731
+    h0, t0, u0, B0, C0, i0 = state
+    valid = None if valid is None else _c(valid, np.uint8)
+    ins = [lam, f(log_dt), f(D), f(mean), f(var), f(u), c(Bc), c(Cc), f(t)]
+    st = [c(h0), f(t0), f(u0), c(B0), c(C0), _c(i0, np.uint8)]
+    ups = [f(up.get("y")), f(up.get("gate")), f(up.get("resid")), f(up.get("innov")), c(up.get("h")),
+           f(up.get("t")), f(up.get("u")), c(up.get("B")), c(up.get("C"))]
+    out = dict(du=np.empty((B, H), np.float32), dBc=np.empty((B, N), np.complex64),
+               dCc=np.empty((B, N), np.complex64), dt=np.empty(B, np.float32), dcpi=np.empty(B, np.float32),
+               dh=np.empty((B, H, N), np.complex64), dt_in=np.empty(B, np.float32),
+               du_in=np.empty((B, H), np.float32), dB_in=np.empty((B, N), np.complex64),
+               dC_in=np.empty((B, N), np.complex64), dlam=np.empty((H, N), np.complex64),
+               dlog_dt=np.empty(H, np.float32), dD=np.empty(H, np.float32), deps=np.empty(1, np.float32))
+    lib().eacs_oracle_stream_step_bwd(
+        *[_ptr(x) for x in ins], _ptr(valid), _ptr(f(cpi)), *[_ptr(x) for x in st], _ptr(f(gs)),
+        *[_ptr(x) for x in ups], *[_ptr(out[k]) for k in out], eps, eta, var_eps, dt_init, dt_min,
+        dt_max, cpi_mod, int(gate_mode), T, B, H, N)
+    return out
 
 
 def cell_commits(lam, log_dt, u, Bc, Cc, t, D, mean, var, eps, eta, var_eps=1e-5,

@@ -19,6 +19,7 @@ Reference functions exercised (paths inside the CST-SSM project):
   modules/streaming.py:45-85   temporal_step (explicit branch state)
   modules/eacs.py:386-401 + continuous_query.py:20-54  _commit_range and
                                readout_from_commits under autograd (training)
+  modules/streaming.py:45-85   temporal_step under autograd (training)
 
     python tests/golden/make_golden.py --groups query   # rewrite one group only
 """
@@ -499,10 +500,132 @@ def stream_cases():
     return out
 
 
+def sgrad_cases():
+    """temporal_step (streaming.py:45-85) over K steps under autograd, on a
+    one-branch MultiScaleEACS whose projections return op-boundary leaves
+    (u, B, C per step), whose lam() returns a leaf and whose gate threshold is
+    a leaf, with proj_out = identity, out_norm removed and x = 0, so each
+    step's output is the core's y on valid rows.  Gradients of a weighted sum
+    of every step's outputs (y, gate, resid, innov) and the final state with
+    respect to the per-step inputs (u, B, C, t, cpi), the initial state (h, t,
+    u, B, C; rows 0 and 2 start initialised, row 1 does not) and lam,
+    log_dt_scale, D, eps."""
+    from torch import nn
+    from cst_ssm.modules.event_gate import EventGate
+    from cst_ssm.modules.multiscale import MultiScaleEACS
+    from cst_ssm.modules.streaming import BranchState, temporal_step
+    from cst_ssm.ops.spectral_init import BranchSpec
+    out = {}
+    specs = {
+        # name: (H, N, B, K, seed, init_eps, cpi_modulation, mode, T)
+        "sgrad_ste": (12, 8, 3, 6, 40, 0.7, 0.0, "ste", 0.2),
+        "sgrad_cpi": (10, 4, 3, 5, 41, 0.7, 0.5, "ste", 0.2),
+        "sgrad_soft": (8, 5, 3, 5, 42, 0.7, 0.0, "soft", 0.3),
+        "sgrad_eval": (12, 8, 3, 6, 43, 0.7, 0.0, "eval", 0.2),
+    }
+    for name, (H, N, B, K, seed, e0, m, mode, T) in specs.items():
+        torch.manual_seed(seed)
+        temporal = MultiScaleEACS(H, branches=[BranchSpec("s", N, 0.5, 4.0)],
+                                  gate_kwargs=dict(init_eps=e0, eps_max=3.0, cpi_modulation=m,
+                                                   use_ste=mode != "soft", temperature=T))
+        br = temporal.branches[0]
+        with torch.no_grad():
+            br.log_dt_scale.normal_(0.0, 0.2)
+            br.D.normal_(0.0, 1.0)
+            br.obs_norm.running_mean.normal_(0.0, 0.1)
+            br.obs_norm.running_var.uniform_(0.5, 1.5)
+            br.proj_out.weight.copy_(torch.eye(H))
+            br.proj_out.bias.zero_()
+        temporal.out_norm = nn.Identity()
+        br.norm = nn.Identity()
+        temporal.train(mode != "eval")
+        g = torch.Generator().manual_seed(seed + 1)
+        lam = br.lam().detach().to(torch.complex64).requires_grad_(True)
+        br.lam = lambda _l=lam: _l
+        eps = torch.tensor(float(br.gate.eps.detach())).requires_grad_(True)
+
+        eps_leaf = eps
+
+        class Gate(EventGate):
+            @property
+            def eps(self):
+                return eps_leaf
+        br.gate.__class__ = Gate
+        s = 1 / math.sqrt(2 * N)
+        u = torch.randn(B, K, H, generator=g)
+        for k in range(1, K):
+            if k % 3 == 2:  # repeated frames: small residuals, skipped steps
+                u[:, k] = u[:, k - 1] + 0.02 * torch.randn(B, H, generator=g)
+        Bc = torch.complex(torch.randn(B, K, N, generator=g), torch.randn(B, K, N, generator=g)) * s
+        Cc = torch.complex(torch.randn(B, K, N, generator=g), torch.randn(B, K, N, generator=g)) * s
+        t = 1.0 + timestamps_exp(g, B, K)
+        cpi = (torch.rand(B, K, generator=g) * 1.4 - 0.2) if m > 0 else None
+        valid = torch.ones(B, K, dtype=torch.bool)
+        valid[1, :2] = False   # row 1 starts late
+        valid[0, 3] = False
+        valid[2, K - 1] = False
+        init = torch.tensor([True, False, True])
+        h0 = torch.complex(torch.randn(B, H, N, generator=g), torch.randn(B, H, N, generator=g)) * 0.3
+        st0 = [h0, torch.rand(B, generator=g) * 0.5, torch.randn(B, H, generator=g),
+               torch.complex(torch.randn(B, N, generator=g), torch.randn(B, N, generator=g)) * s,
+               torch.complex(torch.randn(B, N, generator=g), torch.randn(B, N, generator=g)) * s]
+        leaves = [x.clone().requires_grad_(True) for x in [u, Bc, Cc, t] + ([cpi] if cpi is not None else [])
+                  + st0]
+        u_, Bc_, Cc_, t_ = leaves[:4]
+        cpi_ = leaves[4] if cpi is not None else None
+        sl = leaves[-5:]
+        states = [BranchState(*sl, init.clone())]
+        outs, ups = [], []
+        x0 = torch.zeros(B, H)
+        rec = dict(gate=[], resid=[], innov=[], y=[])
+        for k in range(K):
+            br._project = lambda xn, _k=k: (u_[:, _k], Bc_[:, _k], Cc_[:, _k])
+            y, gk, rk, nk, w, states = temporal_step(temporal, x0, t_[:, k], states, valid[:, k],
+                                                     None if cpi_ is None else cpi_[:, k])
+            for key, val in (("y", y), ("gate", gk[:, 0]), ("resid", rk[:, 0]), ("innov", nk[:, 0])):
+                rec[key].append(val)
+        for key in ("y", "gate", "resid", "innov"):
+            v = torch.stack(rec[key], 1)
+            outs.append(v)
+            ups.append(torch.randn(v.shape, generator=g))
+        fin = states[0]
+        for v in (fin.h, fin.t, fin.u, fin.B, fin.C):
+            outs.append(v)
+            ups.append(torch.complex(torch.randn(v.shape, generator=g), torch.randn(v.shape, generator=g))
+                       if v.is_complex() else torch.randn(v.shape, generator=g))
+        wrt = leaves + [lam, br.log_dt_scale, br.D, eps]
+        live = [(o, w) for o, w in zip(outs, ups) if o.requires_grad]  # eval: the gate is a constant
+        grads = torch.autograd.grad([o for o, _ in live], wrt, [w for _, w in live], allow_unused=True)
+        names = ["du", "dBc", "dCc", "dt"] + (["dcpi"] if cpi is not None else []) + \
+            ["dh0", "dt0", "du0", "dB0", "dC0", "dlam", "dlog_dt", "dD", "deps"]
+        gates = torch.stack(rec["gate"], 1).detach()
+        rr = torch.stack(rec["resid"], 1).detach()
+        print(f"{name}: gate mean {float(gates.mean()):.3f}, min|r-eps| "
+              f"{float((rr - float(eps))[valid].abs().min()):.2e}")
+        d = dict(lam=_np(lam), log_dt=_np(br.log_dt_scale), D=_np(br.D),
+                 mean=_np(br.obs_norm.running_mean), var=_np(br.obs_norm.running_var),
+                 u=_np(u), Bc=_np(Bc), Cc=_np(Cc), t=_np(t), valid=valid.numpy().astype(np.uint8),
+                 h0=_np(st0[0]), t0=_np(st0[1]), u0=_np(st0[2]), B0=_np(st0[3]), C0=_np(st0[4]),
+                 init0=init.numpy().astype(np.uint8),
+                 scalars=np.array([float(eps), br.gate.norm_eta, br.obs_norm.eps, br.dt_init, 1e-3,
+                                   br.dt_max, m, T], np.float64),
+                 gate_mode=np.array([{"ste": 0, "soft": 1, "eval": 2}[mode]]),
+                 y=_np(outs[0]), gate=_np(outs[1]), resid=_np(outs[2]), innov=_np(outs[3]),
+                 fh=_np(fin.h), ft=_np(fin.t), fu=_np(fin.u), fB=_np(fin.B), fC=_np(fin.C),
+                 gy=_np(ups[0]), gg=_np(ups[1]), gr=_np(ups[2]), gn=_np(ups[3]), gh=_np(ups[4]),
+                 gt=_np(ups[5]), gu=_np(ups[6]), gB=_np(ups[7]), gC=_np(ups[8]))
+        if cpi is not None:
+            d["cpi"] = _np(cpi)
+        for k, v in zip(names, grads):
+            d[k] = np.zeros(1, np.float32) if v is None else _np(v)
+        out[name] = d
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--groups", default="scan,ssm,cell,train,query,stream,qtrain",
+    ap.add_argument("--groups", default="scan,ssm,cell,train,query,stream,qtrain,sgrad",
                     help="comma-separated groups to (re)write")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
@@ -510,10 +633,10 @@ def main():
     gen = torch.Generator().manual_seed(1234)
     makers = {"scan": lambda: scan_cases(gen), "ssm": lambda: ssm_cases(gen),
               "cell": cell_cases, "train": train_cases, "query": query_cases,
-              "stream": stream_cases, "qtrain": qtrain_cases}
+              "stream": stream_cases, "qtrain": qtrain_cases, "sgrad": sgrad_cases}
     want = args.groups.split(",")
     groups = {}
-    for name in ("scan", "ssm", "cell", "train", "query", "stream", "qtrain"):  # fixed order: gen is shared
+    for name in ("scan", "ssm", "cell", "train", "query", "stream", "qtrain", "sgrad"):  # fixed order: gen is shared
         cases = makers[name]()
         if name in want:
             groups[name] = cases

@@ -199,3 +199,63 @@ def test_commit_training(name):
         assert relerr(got, d[key]) < 1e-5, key
     for k, v in grads.items():
         assert relerr(v, d[k]) < 1e-4, (k, relerr(v, d[k]))
+
+
+SGRAD = cases("sgrad")
+
+
+def sgrad_oracle(d, pin=None):
+    """The oracle's K-step streaming scan for a temporal_step-gradient fixture:
+    the steps forward one at a time (eacs_oracle_stream_chunk, K = 1), then
+    their backwards in reverse (eacs_oracle_stream_step_bwd), the state's
+    adjoint passed from step to step.  pin: gate outputs (B,K) to pin in the
+    hard modes.  Returns (outputs (y, gate, resid, innov), final state, grads)."""
+    eps, eta, var_eps, dt_init, dt_min, dt_max, m, T = [float(v) for v in d["scalars"]]
+    mode = int(d["gate_mode"][0])
+    ins = (d["lam"], d["log_dt"], d["D"], d["mean"], d["var"])
+    cpi = d.get("cpi")
+    B, K, H = d["u"].shape
+    kw = dict(var_eps=var_eps, dt_init=dt_init, dt_min=dt_min, dt_max=dt_max)
+    states = [(d["h0"], d["t0"], d["u0"], d["B0"], d["C0"], d["init0"])]
+    outs = []
+    for k in range(K):
+        sl = slice(k, k + 1)
+        y, g, r, n, st = oracle.stream_chunk(*ins, d["u"][:, sl], d["Bc"][:, sl], d["Cc"][:, sl], d["t"][:, sl],
+                                             d["valid"][:, sl], None if cpi is None else cpi[:, sl], states[-1],
+                                             eps, eta, cpi_mod=m, gate_mode=1 if mode == 1 else 0, T=T, **kw)
+        outs.append((y[:, 0], g[:, 0], r[:, 0], n[:, 0]))
+        states.append(st)
+    adj = dict(h=d["gh"], t=d["gt"], u=d["gu"], B=d["gB"], C=d["gC"])
+    per = {k: [None] * K for k in ("du", "dBc", "dCc", "dt", "dcpi")}
+    tot = dict(dlam=0, dlog_dt=0, dD=0, deps=0)
+    for k in reversed(range(K)):
+        up = dict(y=d["gy"][:, k], gate=d["gg"][:, k], resid=d["gr"][:, k], innov=d["gn"][:, k], **adj)
+        o = oracle.stream_step_bwd(*ins, d["u"][:, k], d["Bc"][:, k], d["Cc"][:, k], d["t"][:, k],
+                                   d["valid"][:, k], None if cpi is None else cpi[:, k], states[k], up, eps, eta,
+                                   cpi_mod=m, gate_mode=mode, T=T, gs=None if pin is None else pin[:, k], **kw)
+        for key in per:
+            per[key][k] = o[key]
+        for key in tot:
+            tot[key] = tot[key] + o[key]
+        adj = dict(h=o["dh"], t=o["dt_in"], u=o["du_in"], B=o["dB_in"], C=o["dC_in"])
+    grads = {key: np.stack(v, 1) for key, v in per.items()}
+    grads.update(dh0=adj["h"], dt0=adj["t"], du0=adj["u"], dB0=adj["B"], dC0=adj["C"], **tot)
+    outputs = tuple(np.stack([o[i] for o in outs], 1) for i in range(4))
+    return outputs, states[-1], grads
+
+
+@pytest.mark.parametrize("name", sorted(SGRAD))
+def test_stream_step_gradients(name):
+    """temporal_step under autograd over K steps (streaming.py:45-85): the
+    outputs, the final state and every gradient (per-step inputs, initial
+    state, parameters, threshold, CPI) to 1e-4."""
+    d = SGRAD[name]
+    (y, g, r, n), st, grads = sgrad_oracle(d)
+    for got, key in zip((y, g, r, n), ("y", "gate", "resid", "innov")):
+        assert relerr(got, d[key]) < 1e-5, key
+    for got, key in zip(st[:5], ("fh", "ft", "fu", "fB", "fC")):
+        assert relerr(got, d[key]) < 1e-5, key
+    names = ["du", "dBc", "dCc", "dt"] + (["dcpi"] if "cpi" in d else []) + \
+        ["dh0", "dt0", "du0", "dB0", "dC0", "dlam", "dlog_dt", "dD", "deps"]
+    for k in names:
+        assert relerr(grads[k], d[k]) < 1e-4, (k, relerr(grads[k], d[k]))
