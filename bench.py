@@ -77,9 +77,10 @@ def parse():
                     help="gate threshold override for the cell workload (e.g. ~1.01 skips about "
                     "half the frames of the N(0,1) features and exercises the repair path)")
     ap.add_argument("--shape", default=None,
-                    help="B,L,H,N override for --workload scan, ssm_train, train or longvideo (e.g. a small case for ncu)")
+                    help="B,L,H,N override for --workload scan, ssm_train, train, longvideo or query_train "
+                    "(e.g. a small case for ncu)")
     ap.add_argument("--workload", choices=["cell", "scan", "ssm", "ssm_train", "train", "multiscale",
-                                           "longvideo", "project"],
+                                           "longvideo", "project", "query_train"],
                     default="cell", help="cell (default) is the headline; the others are the "
                     "materialised scan, the fused ungated SSM, the training step, the "
                     "three-branch multiscale cell and the long-video cell (B=64, H=2048, N=32)")

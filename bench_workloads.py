@@ -17,6 +17,7 @@ import json
 import math
 import os
 import statistics
+import time
 
 import torch
 
@@ -519,6 +520,110 @@ def wl_project(args, dev, flush):
     return 0
 
 
+def wl_query_train(args, dev, flush):
+    """Training through per-frame commits and continuous-time queries
+    (EACSLayer._commit_range + readout_from_commits under autograd,
+    eacs.py:386-401, continuous_query.py:20-54) at config 1's widths: B = 8
+    videos of L = 1024 frames, H = 768, N = 16 (--shape B,L,H,N), tau in [0.1, 1] s,
+    Q = L query times per video, STE gate with the threshold at the median
+    residual of an all-commit run (about half the frames commit).  One step =
+    forward and backward of sum(y * gy) + sum(y_q * g_q) with respect to u,
+    B, C, t, lam, log_dt, D, eps and the query times, from op-boundary tensors
+    resident on the GPU.  The reference's own code (its step loop and
+    autograd) runs on the same tensors on the same GPU when its package is
+    present (one step: it takes seconds)."""
+    import sys as _sys
+
+    from eacs_b200.ops.continuous_query import QueryReadoutFunction, cell_commits_train, segment_index
+    B, L, H, N = (8, 1024, 768, 16) if not args.shape else tuple(int(v) for v in args.shape.split(","))
+    Q = L
+    g = torch.Generator().manual_seed(0)
+    d = cell_inputs(g, B, L, H, N, (0.1, 1.0), dev, torch.float32)
+    tq = (d["t"][:, :1] - 0.2 + (d["t"][:, -1:] - d["t"][:, :1] + 0.4)
+          * torch.rand(B, Q, generator=g).to(dev)).sort(1).values
+    gy = torch.randn(B, L, H, generator=g).to(dev)
+    gq = torch.randn(B, Q, H, generator=g).to(dev)
+    from eacs_b200.ops.eacs_gated_scan import eacs_cell_forward
+    _, _, r_all = eacs_cell_forward(d["lam"], d["log_dt"], d["u"], d["Bc"], d["Cc"], d["t"], d["D"],
+                                    d["mean"], d["var"], eps=0.0, eta=1e-6)
+    eps0 = float(r_all.median())
+    names = ("u", "Bc", "Cc", "t", "lam", "log_dt", "D")
+    rate = []
+
+    def ours():
+        lv = {k: d[k].detach().requires_grad_(True) for k in names}
+        eps = torch.tensor(eps0, device=dev, requires_grad=True)
+        tqq = tq.detach().requires_grad_(True)
+        ys, gs, rs, c = cell_commits_train(lv["lam"], lv["log_dt"], lv["u"], lv["Bc"], lv["Cc"], lv["t"],
+                                           lv["D"], d["mean"], d["var"], eps, 1e-6, 0.1, "ste")
+        yq = QueryReadoutFunction.apply(lv["lam"], lv["log_dt"], lv["D"], c["h"], c["t"], c["u"], c["B"],
+                                        c["C"], tqq, segment_index(lv["t"].detach(), tq), 1e-3, 1e3)
+        torch.autograd.backward([ys, yq], [gy, gq])
+        if not rate:
+            rate.append(float(gs.detach().mean()))
+
+    n = max(3, min(args.steps, 10))
+    st, _ = timed(ours, n, 2, flush, False)
+    ms = statistics.median(st)
+    updates = B * L * H * N
+    ref_ms, ref_note = None, "reference package absent"
+    root = None
+    for cand in (os.environ.get("CST_SSM_REFERENCE"), os.path.join(ROOT, "baseline", "_ref")):
+        if cand and os.path.isdir(os.path.join(cand, "cst_ssm")):
+            root = cand
+            break
+    if root is not None:
+        if root not in _sys.path:
+            _sys.path.insert(0, root)
+        from cst_ssm.modules.continuous_query import readout_from_commits
+        from cst_ssm.modules.eacs import EACSLayer
+        from cst_ssm.modules.event_gate import EventGate
+        from cst_ssm.ops.spectral_init import BranchSpec
+        torch.manual_seed(0)
+        layer = EACSLayer(H, BranchSpec("short", N, 0.1, 1.0), gate=EventGate(init_eps=0.12)).to(dev).train()
+        with torch.no_grad():
+            layer.proj_out.weight.copy_(torch.eye(H))
+            layer.proj_out.bias.zero_()
+            layer.log_dt_scale.copy_(d["log_dt"])
+            layer.D.copy_(d["D"])
+            layer.obs_norm.running_mean.copy_(d["mean"])
+            layer.obs_norm.running_var.copy_(d["var"])
+        layer.gate.set_temperature(0.1)
+        orig = layer.step_params
+
+        def ref():
+            lv = {k: d[k].detach().requires_grad_(True) for k in ("u", "Bc", "Cc", "t", "lam")}
+            eps = torch.tensor(eps0, device=dev, requires_grad=True)
+
+            def sp(lam, _o=orig):
+                p = _o(lam)
+                p.eps = eps
+                return p
+            layer.step_params = sp
+            tqq = tq.detach().requires_grad_(True)
+            state = (torch.zeros(B, H, N, dtype=torch.complex64, device=dev), lv["t"][:, 0] - layer.dt_init,
+                     lv["u"][:, 0], lv["Bc"][:, 0], lv["Cc"][:, 0])
+            ys, gs, rs, Hc, Tc, Uc, Bs, Cs = layer._commit_range(lv["lam"], state, lv["u"], lv["Bc"],
+                                                                 lv["Cc"], lv["t"], 0, L)
+            commits = dict(h=Hc, t=Tc, u=Uc, B=Bs, C=Cs, lam=lv["lam"], frame_t=lv["t"],
+                           log_dt_scale=layer.log_dt_scale, dt_max=layer.dt_max)
+            yq = readout_from_commits(layer, commits, tqq)
+            torch.autograd.backward([ys, yq], [gy, gq])
+        t0 = time.perf_counter()
+        ref()
+        torch.cuda.synchronize()
+        ref_ms = (time.perf_counter() - t0) * 1e3
+        ref_note = "the reference's _commit_range + readout_from_commits under autograd on the same GPU, one step (wall clock)"
+    line("training through commits and queries (forward + backward), updates/s",
+         updates / (ms / 1e3) / 1e9, n, 2, ms,
+         {"workload": f"commit-training step, B={B} L={L} H={H} N={N}, Q={Q} query times a video, STE gate",
+          "l2": "flushed between steps"},
+         unit="Gupd/s", dtype="f32", update_rate=rate[0] if rate else None,
+         reference_gpu_ms=ref_ms, speedup_vs_reference_gpu=(ref_ms / ms) if ref_ms else None,
+         note="value: B*L*H*N / step time; " + ref_note)
+    return 0
+
+
 def longvideo_inputs(rows, L, dev, seed, H=2048, N=32):
     """Long-video inputs (H=2048, N=32) for `rows` videos, drawn on the device from one seeded
     generator: fp16 u ~ N(0,1); B, C complex with N(0,1)/sqrt(N) parts;
@@ -659,7 +764,7 @@ def run_workload(args):
     torch.cuda.set_device(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     {"scan": wl_scan, "ssm": wl_ssm, "ssm_train": wl_ssm_train,
-     "multiscale": wl_multiscale, "project": wl_project}[args.workload](
+     "multiscale": wl_multiscale, "project": wl_project, "query_train": wl_query_train}[args.workload](
         args, dev, flush)
     from eacs_b200 import _lib
     assert _lib.device_status() == 0

@@ -440,6 +440,39 @@ EACS_API int eacs_stream_chunk(const void* lam, const float* log_dt, const float
                                int gate_mode, float temperature,
                                int64_t B, int64_t K, int64_t H, int64_t N, void* stream);
 
+/* Backward of one streaming step (eacs_stream_chunk with K = 1, float32 u):
+ * the per-branch body of temporal_step (cst_ssm/modules/streaming.py:55-80,
+ * eacs_step eacs.py:78-142, EventGate.forward event_gate.py:84-105) under
+ * autograd.  Inputs: the step's inputs and state in as eacs_stream_chunk
+ * (u (B,H), Bc/Cc (B,N), t (B), valid/cpi (B) or NULL, h_in (B,H,N), t_in,
+ * u_in, B_in, C_in, init_in), its gate output (B) or NULL (pins the hard
+ * decision), and the upstream gradients of y (B,H) (before proj_out), of the
+ * gate output, resid and innov (B), and of the state out gh (B,H,N), gt,
+ * gu, gB, gC -- any of them NULL = 0.  Outputs (overwritten): du (B,H), dBc,
+ * dCc (B,N), dt (B), dcpi (B) (may be NULL), the state in's dh_in, dt_in,
+ * du_in, dB_in, dC_in, and dlam (H,N), dlog_dt (H), dD (H), deps (1).
+ * gate_mode 0: STE (hard forward, sigmoid slope backward), 1: soft, 2: hard
+ * with no gradient through the gate (eval mode).  One CTA per row; the
+ * parameter sums run in row order (workspace:
+ * eacs_stream_step_bwd_workspace_size bytes). */
+EACS_API size_t eacs_stream_step_bwd_workspace_size(int64_t B, int64_t H, int64_t N);
+EACS_API int eacs_stream_step_bwd(const void* lam, const float* log_dt, const float* D,
+                                  const float* mean, const float* var, const float* u,
+                                  const void* Bc, const void* Cc, const float* t,
+                                  const uint8_t* valid, const float* cpi,
+                                  const void* h_in, const float* t_in, const float* u_in,
+                                  const void* B_in, const void* C_in, const uint8_t* init_in,
+                                  const float* gate, const float* gy, const float* gg,
+                                  const float* gr, const float* gn, const void* gh,
+                                  const float* gt, const float* gu, const void* gB, const void* gC,
+                                  float* du, void* dBc, void* dCc, float* dt, float* dcpi,
+                                  void* dh_in, float* dt_in, float* du_in, void* dB_in, void* dC_in,
+                                  void* dlam, float* dlog_dt, float* dD, float* deps,
+                                  void* workspace, size_t workspace_bytes,
+                                  float eps, float eta, float var_eps, float dt_init, float dt_min,
+                                  float dt_max, float cpi_modulation, int gate_mode, float temperature,
+                                  int64_t B, int64_t H, int64_t N, void* stream);
+
 /* Device workspace bytes eacs_cell_fwd_host needs (0 if unsupported). */
 EACS_API size_t eacs_cell_fwd_host_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N,
                                                   int64_t chunk);

@@ -415,6 +415,32 @@ int eacs_stream_chunk(const void* lam, const float* log_dt, const float* D, cons
     return eacs::stream_chunk(c, static_cast<cudaStream_t>(stream));
 }
 
+size_t eacs_stream_step_bwd_workspace_size(int64_t B, int64_t H, int64_t N) {
+    return eacs::stream_step_bwd_workspace_size(B, H, N);
+}
+
+int eacs_stream_step_bwd(const void* lam, const float* log_dt, const float* D, const float* mean,
+                         const float* var, const float* u, const void* Bc, const void* Cc, const float* t,
+                         const uint8_t* valid, const float* cpi, const void* h_in, const float* t_in,
+                         const float* u_in, const void* B_in, const void* C_in, const uint8_t* init_in,
+                         const float* gate, const float* gy, const float* gg, const float* gr,
+                         const float* gn, const void* gh, const float* gt, const float* gu, const void* gB,
+                         const void* gC, float* du, void* dBc, void* dCc, float* dt, float* dcpi,
+                         void* dh_in, float* dt_in, float* du_in, void* dB_in, void* dC_in, void* dlam,
+                         float* dlog_dt, float* dD, float* deps, void* workspace, size_t workspace_bytes,
+                         float eps, float eta, float var_eps, float dt_init, float dt_min, float dt_max,
+                         float cpi_modulation, int gate_mode, float temperature, int64_t B, int64_t H,
+                         int64_t N, void* stream) {
+    eacs::StreamBwdCall c{lam,   log_dt, D,      mean,    var,    u,     Bc,      Cc,      t,
+                          valid, cpi,    h_in,   t_in,    u_in,   B_in,  C_in,    init_in, gate,
+                          gy,    gg,     gr,     gn,      gh,     gt,    gu,      gB,      gC,
+                          du,    dBc,    dCc,    dt,      dcpi,   dh_in, dt_in,   du_in,   dB_in,
+                          dC_in, dlam,   dlog_dt, dD,     deps,   workspace, workspace_bytes,
+                          eps,   eta,    var_eps, dt_init, dt_min, dt_max, cpi_modulation, temperature,
+                          gate_mode, B,  H,      N};
+    return eacs::stream_step_bwd(c, static_cast<cudaStream_t>(stream));
+}
+
 size_t eacs_cell_fwd_host_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N, int64_t chunk) {
     return eacs::cell_host_workspace_size(B, L, H, N, chunk);
 }

@@ -225,6 +225,57 @@ struct StreamCall {
     int64_t B, K, H, N;
 };
 int stream_chunk(const StreamCall& c, cudaStream_t stream);
+// backward of one step (K = 1), float32 u; upstream pointers may be null (0)
+struct StreamBwdCall {
+    const void* lam;
+    const float* log_dt;
+    const float* D;
+    const float* mean;
+    const float* var;
+    const float* u;        // (B,H)
+    const void* Bc;        // (B,N) complex64
+    const void* Cc;
+    const float* t;        // (B)
+    const uint8_t* valid;  // (B) or null
+    const float* cpi;      // (B) or null
+    const void* h_in;
+    const float* t_in;
+    const float* u_in;
+    const void* B_in;
+    const void* C_in;
+    const uint8_t* init_in;
+    const float* gate;     // (B) the forward's gate output (pins a hard gate) or null
+    const float* gy;       // (B,H)
+    const float* gg;       // (B)
+    const float* gr;
+    const float* gn;
+    const void* gh;        // (B,H,N) complex64: the state out's adjoints
+    const float* gt;
+    const float* gu;
+    const void* gB;
+    const void* gC;
+    float* du;
+    void* dBc;
+    void* dCc;
+    float* dt;
+    float* dcpi;           // or null
+    void* dh_in;
+    float* dt_in;
+    float* du_in;
+    void* dB_in;
+    void* dC_in;
+    void* dlam;
+    float* dlog;
+    float* dD;
+    float* deps;
+    void* workspace;
+    size_t workspace_bytes;
+    float eps, eta, var_eps, dt_init, dt_min, dt_max, cpi_modulation, temperature;
+    int gate_mode;  // 0 STE, 1 soft, 2 hard (no gradient through the gate)
+    int64_t B, H, N;
+};
+size_t stream_step_bwd_workspace_size(int64_t B, int64_t H, int64_t N);
+int stream_step_bwd(const StreamBwdCall& c, cudaStream_t stream);
 
 // fuse.cu: MultiScaleEACS branch epilogue
 struct FuseCall {

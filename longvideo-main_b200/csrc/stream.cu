@@ -244,6 +244,484 @@ cudaError_t launch_stream(const StArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Backward of one step (K = 1: temporal_step under autograd), float32 u.
+// Per row, with the step's forward recomputed in the same order as
+// stream_chunk (so the residual, and with it a hard gate, comes out the same;
+// the forward's gate output also pins it), the vector-Jacobian product with
+// respect to the frame (u, B, C, t, cpi), the state in and the parameters,
+// given the upstream gradients of y (before proj_out), the gate output (1 on
+// a first observation), resid, innov and the state out:
+//   hc = g h_upd + (1-g) x_hat:  g_bar += Re(conj(a_hc)(h_upd - x_hat)),
+//   state' = g new + (1-g) old:   g_bar += sum Re(conj(a')(new - old)),
+//   g = sigmoid((r - eps_l)/T) in the backward (STE / soft; mode 2: none),
+//   r = |obs - pred| / (|obs| + eta), innov with obs held constant,
+//   eps_l = max(eps (1 - m clamp(cpi, 0, 1)), 1e-3) (-1 on a first step),
+// then the readout, prediction and ZOH adjoints as in the cell backward.
+// A first observation takes its own frame as predecessor, so the
+// predecessor's adjoints go to the frame; a masked row passes the state's
+// adjoints through.  Per-row partials of lam, log_dt, D and eps are summed
+// by stream_bwd_post in row order.
+// ---------------------------------------------------------------------------
+struct SbArgs {
+    const float2* lam;
+    const float* log_dt;
+    const float* D;
+    const float* mean;
+    const float* var;
+    const float* u;        // (B,H)
+    const float2* Bc;      // (B,N)
+    const float2* Cc;
+    const float* t;        // (B)
+    const uint8_t* valid;  // (B) or null
+    const float* cpi;      // (B) or null
+    const float2* h_in;    // (B,H,N)
+    const float* t_in;
+    const float* u_in;
+    const float2* B_in;
+    const float2* C_in;
+    const uint8_t* init_in;
+    const float* gate;     // (B) forward gate output or null
+    const float* gy;       // (B,H) or null
+    const float* gg;       // (B) or null
+    const float* gr;
+    const float* gn;
+    const float2* gh;      // (B,H,N) or null
+    const float* gt;       // (B) or null
+    const float* gu;       // (B,H) or null
+    const float2* gB;      // (B,N) or null
+    const float2* gC;
+    float* du;
+    float2* dBc;
+    float2* dCc;
+    float* dt;
+    float* dcpi;           // or null
+    float2* dh_in;
+    float* dt_in;
+    float* du_in;
+    float2* dB_in;
+    float2* dC_in;
+    float2* dlam;
+    float* dlog;
+    float* dD;
+    float* deps;
+    float2* plam;          // [B][H][N] per-row partials
+    float* plog;           // [B][H]
+    float* pD;
+    float* peps;           // [B]
+    float eps, eta, var_eps, dt_init, dt_min, dt_max, cpi_mod, Tp;
+    int gate_mode;         // 0 STE, 1 soft, 2 hard (no gradient through the gate)
+    int B, H, N;
+};
+
+__device__ __forceinline__ float2 conjf2(float2 a) { return make_float2(a.x, -a.y); }
+__device__ __forceinline__ float redot(float2 a, float2 b) { return a.x * b.x + a.y * b.y; }  // Re(conj(a) b)
+
+template <int LANES>
+__device__ __forceinline__ float lane_sum(float v) {
+#pragma unroll
+    for (int o = LANES / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// sum over the CTA in a fixed order (warps, then warp 0..NW-1); every thread
+// gets the total
+__device__ __forceinline__ float cta_sum(float v, float* sred, float* sout) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) sred[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.f;
+        for (int w = 0; w < kST / 32; ++w) s += sred[w];
+        *sout = s;
+    }
+    __syncthreads();
+    return *sout;
+}
+
+template <int LANES, int NPT>
+__global__ void __launch_bounds__(kST) stream_step_bwd_k(SbArgs a) {
+    constexpr int HG = kST / LANES;
+    constexpr int NP = LANES * NPT;
+    constexpr int NW = kST / 32;
+    extern __shared__ __align__(16) unsigned char sdyn[];
+    float2* sacc = reinterpret_cast<float2*>(sdyn);                // [4][NW][NP]
+    float* sdv = reinterpret_cast<float*>(sacc + 4 * NW * NP);     // [H] residual terms, then obs' adjoint / sd
+    float* sob = sdv + a.H;                                       // [H] obs, then pred's adjoint / sd
+    __shared__ float2 sB0[NP], sC0[NP], sBf[NP], sCf[NP];
+    __shared__ float2 sred2[NW];
+    __shared__ float sred[NW];
+    __shared__ float sv[12];
+
+    const int b = blockIdx.x;
+    const int tid = threadIdx.x, ln = tid % LANES, hg = tid / LANES;
+    const int lane = tid & 31, wid = tid >> 5;
+    const int H = a.H, N = a.N;
+    const size_t HN = static_cast<size_t>(H) * N;
+    const size_t bHN = static_cast<size_t>(b) * HN;
+    const size_t bH = static_cast<size_t>(b) * H;
+    const bool v = a.valid ? a.valid[b] != 0 : true;
+    if (!v) {  // masked row: the state passes through, nothing else
+        for (size_t i = tid; i < HN; i += kST) {
+            a.dh_in[bHN + i] = a.gh ? a.gh[bHN + i] : make_float2(0.f, 0.f);
+            a.plam[bHN + i] = make_float2(0.f, 0.f);
+        }
+        for (int h = tid; h < H; h += kST) {
+            a.du_in[bH + h] = a.gu ? a.gu[bH + h] : 0.f;
+            a.du[bH + h] = 0.f;
+            a.plog[bH + h] = 0.f;
+            a.pD[bH + h] = 0.f;
+        }
+        for (int n = tid; n < N; n += kST) {
+            const size_t o = static_cast<size_t>(b) * N + n;
+            a.dB_in[o] = a.gB ? a.gB[o] : make_float2(0.f, 0.f);
+            a.dC_in[o] = a.gC ? a.gC[o] : make_float2(0.f, 0.f);
+            a.dBc[o] = a.dCc[o] = make_float2(0.f, 0.f);
+        }
+        if (tid == 0) {
+            a.dt_in[b] = a.gt ? a.gt[b] : 0.f;
+            a.dt[b] = 0.f;
+            if (a.dcpi) a.dcpi[b] = 0.f;
+            a.peps[b] = 0.f;
+        }
+        return;
+    }
+    const bool first = a.init_in[b] == 0;
+    const float tl = a.t[b];
+    const float t0 = first ? tl - a.dt_init : a.t_in[b];
+    for (int n = tid; n < NP; n += kST) {
+        const size_t o = static_cast<size_t>(b) * N + n;
+        const float2 z = make_float2(0.f, 0.f);
+        sBf[n] = n < N ? a.Bc[o] : z;
+        sCf[n] = n < N ? a.Cc[o] : z;
+        sB0[n] = n < N ? (first ? a.Bc[o] : a.B_in[o]) : z;
+        sC0[n] = n < N ? (first ? a.Cc[o] : a.C_in[o]) : z;
+    }
+    __syncthreads();
+    const float draw = tl - t0;
+    const float delta = fmaxf(draw, 0.f);
+    const float mdel = draw >= 0.f ? 1.f : 0.f;
+    auto u0_of = [&](int h) { return first ? a.u[bH + h] : a.u_in[bH + h]; };
+
+    // ---- pass 1: prediction and residual (stream_chunk's order) ----
+    float acc1 = 0.f, acc2 = 0.f;
+    for (int h0 = 0; h0 < H; h0 += HG) {
+        const int h = h0 + hg;
+        const bool hv = h < H;
+        float yhp = 0.f, dte = 0.f, upv = 0.f;
+        if (hv) {
+            dte = eff_dt(delta, expf(a.log_dt[h]), a.dt_min, a.dt_max);
+            upv = u0_of(h);
+        }
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            if (hv && n < N) {
+                const float2 lm = a.lam[static_cast<size_t>(h) * N + n];
+                float2 dA, dB;
+                zoh(lm, crecip(lm), dte, dA, dB);
+                const float2 P = cmul(dA, a.h_in[bHN + static_cast<size_t>(h) * N + n]);
+                const float2 q = cmul(dB, sB0[n]);
+                const float2 xh = make_float2(fmaf(q.x, upv, P.x), fmaf(q.y, upv, P.y));
+                yhp += cre_mul(sC0[n], xh);
+            }
+        }
+        yhp = lane_sum<LANES>(yhp);
+        if (ln == 0 && hv) {
+            const float sd = sqrtf(a.var[h] + a.var_eps);
+            const float obs = (a.u[bH + h] - a.mean[h]) / sd;
+            const float pred = (yhp - a.mean[h]) / sd;
+            const float d = obs - pred;
+            sdv[h] = d;
+            sob[h] = obs;
+            acc1 += d * d;
+            acc2 += obs * obs;
+        }
+    }
+    acc1 = warp_sum(acc1);
+    acc2 = warp_sum(acc2);
+    if (lane == 0) sred2[wid] = make_float2(acc1, acc2);
+    __syncthreads();
+    const bool mod = a.cpi != nullptr && a.cpi_mod > 0.f;
+    if (tid == 0) {
+        float s1 = 0.f, s2 = 0.f;
+        for (int w = 0; w < NW; ++w) {
+            s1 += sred2[w].x;
+            s2 += sred2[w].y;
+        }
+        const float num = sqrtf(s1), nobs = sqrtf(s2), den = nobs + a.eta;
+        const float r = num / den;
+        float epsl = first ? -1.f : a.eps, e1 = epsl, c = 0.f;
+        if (mod) {
+            c = fminf(fmaxf(a.cpi[b], 0.f), 1.f);
+            e1 = epsl * (1.f - a.cpi_mod * c);
+            epsl = fmaxf(e1, 1e-3f);
+        }
+        const float soft = 1.0f / (1.0f + expf(-((r - epsl) / a.Tp)));
+        float g = a.gate_mode == 1 ? soft : (r > epsl ? 1.f : 0.f);
+        if (a.gate_mode != 1 && a.gate && !first) g = a.gate[b];
+        sv[0] = g;
+        sv[1] = soft;
+        sv[2] = num;
+        sv[3] = nobs;
+        sv[4] = den;
+        sv[5] = e1;
+        sv[6] = c;
+    }
+    __syncthreads();
+    const float g = sv[0], soft = sv[1], num = sv[2], nobs = sv[3], den = sv[4];
+
+    // ---- pass 2: the gate's adjoint ----
+    float gl = 0.f;
+    for (int h0 = 0; h0 < H; h0 += HG) {
+        const int h = h0 + hg;
+        const bool hv = h < H;
+        float dte = 0.f, upv = 0.f, ul = 0.f, yb = 0.f;
+        if (hv) {
+            dte = eff_dt(delta, expf(a.log_dt[h]), a.dt_min, a.dt_max);
+            upv = u0_of(h);
+            ul = a.u[bH + h];
+            yb = a.gy ? a.gy[bH + h] : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            if (hv && n < N) {
+                const size_t o = bHN + static_cast<size_t>(h) * N + n;
+                const float2 lm = a.lam[static_cast<size_t>(h) * N + n];
+                float2 dA, dB;
+                zoh(lm, crecip(lm), dte, dA, dB);
+                const float2 h0v = a.h_in[o];
+                const float2 P = cmul(dA, h0v);
+                const float2 qp = cmul(dB, sB0[n]), qc = cmul(dB, sBf[n]);
+                const float2 xh = make_float2(fmaf(qp.x, upv, P.x), fmaf(qp.y, upv, P.y));
+                const float2 hu = make_float2(fmaf(qc.x, ul, P.x), fmaf(qc.y, ul, P.y));
+                float2 ahc = cscale(conjf2(sCf[n]), yb);
+                const float2 Ah = a.gh ? a.gh[o] : make_float2(0.f, 0.f);
+                if (first) ahc = cadd(ahc, Ah);
+                else gl += redot(Ah, make_float2(hu.x - h0v.x, hu.y - h0v.y));
+                gl += redot(ahc, make_float2(hu.x - xh.x, hu.y - xh.y));
+            }
+        }
+        if (!first && hv && ln == 0 && a.gu) gl += a.gu[bH + h] * (ul - upv);
+    }
+    float gbar = cta_sum(gl, sred, &sv[7]);
+    if (tid == 0) {
+        if (!first) {
+            if (a.gt) gbar += a.gt[b] * (tl - t0);
+            for (int n = 0; n < N; ++n) {
+                const size_t o = static_cast<size_t>(b) * N + n;
+                if (a.gB) gbar += redot(a.gB[o], make_float2(sBf[n].x - sB0[n].x, sBf[n].y - sB0[n].y));
+                if (a.gC) gbar += redot(a.gC[o], make_float2(sCf[n].x - sC0[n].x, sCf[n].y - sC0[n].y));
+            }
+            if (a.gg) gbar += a.gg[b];
+        }
+        const float xbar = a.gate_mode == 2 ? 0.f : gbar * soft * (1.f - soft) / a.Tp;
+        const float rbar = (a.gr ? a.gr[b] : 0.f) + xbar;
+        float pe = 0.f, dc = 0.f;
+        if (!first) {
+            const float ebar = -xbar;
+            if (mod) {
+                if (sv[5] >= 1e-3f) {
+                    pe = ebar * (1.f - a.cpi_mod * sv[6]);
+                    const float cr = a.cpi[b];
+                    if (cr >= 0.f && cr <= 1.f) dc = -ebar * a.eps * a.cpi_mod;
+                }
+            } else {
+                pe = ebar;
+            }
+        }
+        a.peps[b] = pe;
+        if (a.dcpi) a.dcpi[b] = dc;
+        const float nbar = (!first && a.gn) ? a.gn[b] : 0.f;
+        sv[8] = rbar / den;                 // num's adjoint
+        sv[9] = -rbar * num / (den * den);  // den's adjoint
+        sv[10] = nbar / den;                // innov's num's adjoint
+    }
+    __syncthreads();
+    {
+        const float numbar = sv[8], denbar = sv[9], numnbar = sv[10];
+        for (int h = tid; h < H; h += kST) {
+            const float d = sdv[h], obs = sob[h];
+            const float dbar = num > 0.f ? numbar * d / num : 0.f;
+            const float obar = dbar + (nobs > 0.f ? denbar * obs / nobs : 0.f);
+            const float pbar = -dbar - (num > 0.f ? numnbar * d / num : 0.f);
+            const float sd = sqrtf(a.var[h] + a.var_eps);
+            sdv[h] = obar / sd;
+            sob[h] = pbar / sd;
+        }
+    }
+    __syncthreads();
+
+    // ---- pass 3: readout, prediction and ZOH adjoints ----
+    float2 aBf[NPT], aCf[NPT], aB0[NPT], aC0[NPT];
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) aBf[j] = aCf[j] = aB0[j] = aC0[j] = make_float2(0.f, 0.f);
+    float dsum = 0.f;
+    for (int h0 = 0; h0 < H; h0 += HG) {
+        const int h = h0 + hg;
+        const bool hv = h < H;
+        float sc = 1.f, dte = 0.f, mdt = 0.f, upv = 0.f, ul = 0.f, yb = 0.f, yhb = 0.f;
+        if (hv) {
+            sc = expf(a.log_dt[h]);
+            const float raw = delta * sc;
+            dte = fminf(fmaxf(raw, a.dt_min), a.dt_max);
+            mdt = (raw >= a.dt_min && raw <= a.dt_max) ? 1.f : 0.f;
+            upv = u0_of(h);
+            ul = a.u[bH + h];
+            yb = a.gy ? a.gy[bH + h] : 0.f;
+            yhb = sob[h];
+        }
+        float s_u0 = 0.f, s_ul = 0.f, s_dte = 0.f;
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            if (hv && n < N) {
+                const size_t o = bHN + static_cast<size_t>(h) * N + n;
+                const float2 lm = a.lam[static_cast<size_t>(h) * N + n];
+                const float2 il = crecip(lm);
+                float2 dA, dB;
+                zoh(lm, il, dte, dA, dB);
+                const float2 h0v = a.h_in[o];
+                const float2 P = cmul(dA, h0v);
+                const float2 qp = cmul(dB, sB0[n]), qc = cmul(dB, sBf[n]);
+                const float2 xh = make_float2(fmaf(qp.x, upv, P.x), fmaf(qp.y, upv, P.y));
+                const float2 hu = make_float2(fmaf(qc.x, ul, P.x), fmaf(qc.y, ul, P.y));
+                const float2 hc = cadd(cscale(hu, g), cscale(xh, 1.f - g));
+                const float2 Ah = a.gh ? a.gh[o] : make_float2(0.f, 0.f);
+                float2 ahc = cscale(conjf2(sCf[n]), yb);
+                float2 ahu, ah0;
+                if (first) {
+                    ahc = cadd(ahc, Ah);
+                    ahu = cscale(ahc, g);
+                    ah0 = make_float2(0.f, 0.f);
+                } else {
+                    ahu = cscale(cadd(ahc, Ah), g);
+                    ah0 = cscale(Ah, 1.f - g);
+                }
+                const float2 axh = cadd(cscale(ahc, 1.f - g), cscale(conjf2(sC0[n]), yhb));
+                aCf[j] = cadd(aCf[j], cscale(conjf2(hc), yb));
+                aC0[j] = cadd(aC0[j], cscale(conjf2(xh), yhb));
+                const float2 aP = cadd(axh, ahu);
+                const float2 aqp = cscale(axh, upv), aqc = cscale(ahu, ul);
+                s_u0 += redot(axh, qp);
+                s_ul += redot(ahu, qc);
+                const float2 adB = cadd(cmul(aqp, conjf2(sB0[n])), cmul(aqc, conjf2(sBf[n])));
+                const float2 cdA = conjf2(dA), cdB = conjf2(dB);
+                aB0[j] = cadd(aB0[j], cmul(cdB, aqp));
+                aBf[j] = cadd(aBf[j], cmul(cdB, aqc));
+                const float2 adA = cmul(aP, conjf2(h0v));
+                a.dh_in[o] = cadd(ah0, cmul(cdA, aP));
+                const float2 aE = cmul(adB, conjf2(il));
+                float2 alm = cmul(make_float2(-aE.x, -aE.y), cdB);
+                const float2 az = cmul(cdA, cadd(adA, aE));
+                alm = cadd(alm, cscale(az, dte));
+                a.plam[o] = alm;
+                s_dte += az.x * lm.x + az.y * lm.y;
+            }
+        }
+        s_u0 = lane_sum<LANES>(s_u0);
+        s_ul = lane_sum<LANES>(s_ul);
+        s_dte = lane_sum<LANES>(s_dte);
+        if (hv && ln == 0) {
+            const float drb = mdt * s_dte;
+            a.plog[bH + h] = drb * delta * sc;
+            dsum += drb * sc;
+            const float Au = a.gu ? a.gu[bH + h] : 0.f;
+            const float dul = yb * a.D[h] + (first ? Au : g * Au) + sdv[h] + s_ul;
+            const float du0 = (first ? 0.f : (1.f - g) * Au) + s_u0;
+            a.du[bH + h] = first ? dul + du0 : dul;
+            a.du_in[bH + h] = first ? 0.f : du0;
+            a.pD[bH + h] = yb * ul;
+        }
+    }
+    // B's and C's adjoints summed over the channels (frame and predecessor)
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) {
+        float2* q[4] = {&aBf[j], &aCf[j], &aB0[j], &aC0[j]};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+#pragma unroll
+            for (int o = LANES; o < 32; o <<= 1) {
+                q[k]->x += __shfl_xor_sync(0xffffffffu, q[k]->x, o);
+                q[k]->y += __shfl_xor_sync(0xffffffffu, q[k]->y, o);
+            }
+            if (lane < LANES) sacc[(k * NW + wid) * NP + ln + LANES * j] = *q[k];
+        }
+    }
+    const float deltabar = cta_sum(dsum, sred, &sv[11]);  // its barriers also publish sacc
+    for (int n = tid; n < N; n += kST) {
+        float2 s4[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float2 sum = make_float2(0.f, 0.f);
+            for (int w = 0; w < NW; ++w) sum = cadd(sum, sacc[(k * NW + w) * NP + n]);
+            s4[k] = sum;
+        }
+        const size_t o = static_cast<size_t>(b) * N + n;
+        const float2 AB = a.gB ? a.gB[o] : make_float2(0.f, 0.f);
+        const float2 AC = a.gC ? a.gC[o] : make_float2(0.f, 0.f);
+        if (first) {
+            a.dBc[o] = cadd(cadd(s4[0], AB), s4[2]);
+            a.dCc[o] = cadd(cadd(s4[1], AC), s4[3]);
+            a.dB_in[o] = a.dC_in[o] = make_float2(0.f, 0.f);
+        } else {
+            a.dBc[o] = cadd(s4[0], cscale(AB, g));
+            a.dCc[o] = cadd(s4[1], cscale(AC, g));
+            a.dB_in[o] = cadd(cscale(AB, 1.f - g), s4[2]);
+            a.dC_in[o] = cadd(cscale(AC, 1.f - g), s4[3]);
+        }
+    }
+    if (tid == 0) {
+        const float At = a.gt ? a.gt[b] : 0.f;
+        const float dtl = (first ? At : g * At) + mdel * deltabar;
+        const float dt0 = (first ? 0.f : (1.f - g) * At) - mdel * deltabar;
+        a.dt[b] = first ? dtl + dt0 : dtl;
+        a.dt_in[b] = first ? 0.f : dt0;
+    }
+}
+
+__global__ void stream_bwd_post(SbArgs a) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t HN = static_cast<int64_t>(a.H) * a.N;
+    if (i < HN) {
+        float2 s = make_float2(0.f, 0.f);
+        for (int b = 0; b < a.B; ++b) s = cadd(s, a.plam[b * HN + i]);
+        a.dlam[i] = s;
+    }
+    if (i < a.H) {
+        float s1 = 0.f, s2 = 0.f;
+        for (int b = 0; b < a.B; ++b) {
+            s1 += a.plog[static_cast<size_t>(b) * a.H + i];
+            s2 += a.pD[static_cast<size_t>(b) * a.H + i];
+        }
+        a.dlog[i] = s1;
+        a.dD[i] = s2;
+    }
+    if (i == 0) {
+        float s = 0.f;
+        for (int b = 0; b < a.B; ++b) s += a.peps[b];
+        a.deps[0] = s;
+    }
+}
+
+size_t als(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+template <int LANES, int NPT>
+cudaError_t launch_step_bwd(const SbArgs& a, cudaStream_t s) {
+    const size_t smem = sizeof(float2) * 4 * (kST / 32) * LANES * NPT + sizeof(float) * 2 * a.H;
+    cudaError_t e = cudaFuncSetAttribute(stream_step_bwd_k<LANES, NPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    stream_step_bwd_k<LANES, NPT><<<a.B, kST, smem, s>>>(a);
+    note_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const int64_t n = std::max<int64_t>(static_cast<int64_t>(a.H) * a.N, 1);
+    stream_bwd_post<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(a);
+    note_launch();
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 int stream_chunk(const StreamCall& c, cudaStream_t stream) {
@@ -310,6 +788,101 @@ int stream_chunk(const StreamCall& c, cudaStream_t stream) {
     if (c.u_dtype == EACS_DTYPE_F16) e = launch_stream<__half>(a, stream);
     else if (c.u_dtype == EACS_DTYPE_BF16) e = launch_stream<__nv_bfloat16>(a, stream);
     else e = launch_stream<float>(a, stream);
+    return cuda_check(e, fn);
+}
+
+}  // namespace eacs
+
+namespace eacs {
+
+size_t stream_step_bwd_workspace_size(int64_t B, int64_t H, int64_t N) {
+    if (B <= 0 || H <= 0 || N <= 0) return 0;
+    return als(sizeof(float2) * B * H * N) + 2 * als(sizeof(float) * B * H) + als(sizeof(float) * B);
+}
+
+int stream_step_bwd(const StreamBwdCall& c, cudaStream_t stream) {
+    const char* fn = "eacs_stream_step_bwd";
+    if (c.B < 0 || c.H < 0 || c.N < 0) return fail(EACS_ERR_INVALID, "%s: negative size", fn);
+    if (c.N > 64) return fail(EACS_ERR_UNSUPPORTED, "%s: N=%lld > 64 is not supported", fn, (long long)c.N);
+    if (c.B > (1LL << 31) - 1 || c.H > 20000)
+        return fail(EACS_ERR_UNSUPPORTED, "%s: B or H too large", fn);
+    if (c.gate_mode < 0 || c.gate_mode > 2) return fail(EACS_ERR_INVALID, "%s: gate_mode %d not in 0..2", fn, c.gate_mode);
+    if (c.B == 0) return EACS_OK;
+    if (c.H == 0 || c.N == 0) return fail(EACS_ERR_INVALID, "%s: H and N must be positive", fn);
+    if (!c.lam || !c.log_dt || !c.D || !c.mean || !c.var || !c.u || !c.Bc || !c.Cc || !c.t || !c.h_in ||
+        !c.t_in || !c.u_in || !c.B_in || !c.C_in || !c.init_in || !c.du || !c.dBc || !c.dCc || !c.dt ||
+        !c.dh_in || !c.dt_in || !c.du_in || !c.dB_in || !c.dC_in || !c.dlam || !c.dlog || !c.dD || !c.deps)
+        return fail(EACS_ERR_INVALID, "%s: null pointer argument", fn);
+    const size_t need = stream_step_bwd_workspace_size(c.B, c.H, c.N);
+    if (!c.workspace || c.workspace_bytes < need)
+        return fail(EACS_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", fn, need, c.workspace_bytes);
+    SbArgs a{};
+    a.lam = static_cast<const float2*>(c.lam);
+    a.log_dt = c.log_dt;
+    a.D = c.D;
+    a.mean = c.mean;
+    a.var = c.var;
+    a.u = c.u;
+    a.Bc = static_cast<const float2*>(c.Bc);
+    a.Cc = static_cast<const float2*>(c.Cc);
+    a.t = c.t;
+    a.valid = c.valid;
+    a.cpi = c.cpi;
+    a.h_in = static_cast<const float2*>(c.h_in);
+    a.t_in = c.t_in;
+    a.u_in = c.u_in;
+    a.B_in = static_cast<const float2*>(c.B_in);
+    a.C_in = static_cast<const float2*>(c.C_in);
+    a.init_in = c.init_in;
+    a.gate = c.gate;
+    a.gy = c.gy;
+    a.gg = c.gg;
+    a.gr = c.gr;
+    a.gn = c.gn;
+    a.gh = static_cast<const float2*>(c.gh);
+    a.gt = c.gt;
+    a.gu = c.gu;
+    a.gB = static_cast<const float2*>(c.gB);
+    a.gC = static_cast<const float2*>(c.gC);
+    a.du = c.du;
+    a.dBc = static_cast<float2*>(c.dBc);
+    a.dCc = static_cast<float2*>(c.dCc);
+    a.dt = c.dt;
+    a.dcpi = c.dcpi;
+    a.dh_in = static_cast<float2*>(c.dh_in);
+    a.dt_in = c.dt_in;
+    a.du_in = c.du_in;
+    a.dB_in = static_cast<float2*>(c.dB_in);
+    a.dC_in = static_cast<float2*>(c.dC_in);
+    a.dlam = static_cast<float2*>(c.dlam);
+    a.dlog = c.dlog;
+    a.dD = c.dD;
+    a.deps = c.deps;
+    char* ws = static_cast<char*>(c.workspace);
+    const size_t o1 = als(sizeof(float2) * c.B * c.H * c.N), o2 = als(sizeof(float) * c.B * c.H);
+    a.plam = reinterpret_cast<float2*>(ws);
+    a.plog = reinterpret_cast<float*>(ws + o1);
+    a.pD = reinterpret_cast<float*>(ws + o1 + o2);
+    a.peps = reinterpret_cast<float*>(ws + o1 + 2 * o2);
+    a.eps = c.eps;
+    a.eta = c.eta;
+    a.var_eps = c.var_eps;
+    a.dt_init = c.dt_init;
+    a.dt_min = c.dt_min;
+    a.dt_max = c.dt_max;
+    a.cpi_mod = c.cpi_modulation;
+    a.Tp = c.temperature > 1e-4f ? c.temperature : 1e-4f;
+    a.gate_mode = c.gate_mode;
+    a.B = static_cast<int>(c.B);
+    a.H = static_cast<int>(c.H);
+    a.N = static_cast<int>(c.N);
+    cudaError_t e;
+    const int64_t N = c.N;
+    if (N <= 4) e = launch_step_bwd<4, 1>(a, stream);
+    else if (N <= 8) e = launch_step_bwd<8, 1>(a, stream);
+    else if (N <= 16) e = launch_step_bwd<16, 1>(a, stream);
+    else if (N <= 32) e = launch_step_bwd<32, 1>(a, stream);
+    else e = launch_step_bwd<32, 2>(a, stream);
     return cuda_check(e, fn);
 }
 

@@ -30,7 +30,9 @@ def install(package: str = "cst_ssm", fuse_ungated: bool = False,
     non-event gates and non-continuous discretisation.
     streaming: also route temporal_step (modules/streaming.py, and the name
     models/adaptive_path.py imported from it) through the streaming step
-    kernel under the same rule.
+    kernel and its backward (gradients through the state from step to step);
+    the reference's own code runs only for CPU tensors, non-event gates and
+    non-continuous discretisation.
     multiscale: also route MultiScaleEACS.forward's epilogue (fusion softmax,
     blend, LayerNorm) through the one-pass branch-fuse kernel, under the same
     rule."""

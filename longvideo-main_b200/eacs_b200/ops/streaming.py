@@ -8,9 +8,13 @@ readout and the new state -- is one kernel launch (eacs_stream_chunk) instead
 of the reference's ~40 tensor operations.  `stream_chunk` runs K known steps
 of one branch in one launch with the same semantics.
 
-Inference path: no autograd through the state.  install(..., streaming=True)
-binds `temporal_step` with a dispatcher that keeps the reference's own code
-where gradients are needed or the tensors are on the CPU.
+Under autograd each branch's step is `StreamStepFunction` (forward: the
+same kernel with K = 1; backward: eacs_stream_step_bwd, one launch per row
+and branch plus a parameter sum), so gradients flow through the state from
+step to step as in the reference's per-step autograd graph.
+install(..., streaming=True) binds `temporal_step` with a dispatcher that
+keeps the reference's own code only for CPU tensors, non-event gates and
+non-continuous discretisation.
 """
 from __future__ import annotations
 
@@ -73,10 +77,111 @@ def stream_chunk(lam, log_dt_scale, D, mean, var, u, Bc, Cc, t, valid, cpi, stat
 
 
 def _gate_mode(br) -> str:
+    """The branch gate's forward kind: "soft" (training without STE) or "hard"."""
     return "soft" if (br.training and not br.gate.use_ste) else "hard"
 
 
-@torch.no_grad()
+def _grad_mode(br) -> str:
+    """Its backward kind: "ste" / "soft" in training, "hard" (no gradient
+    through r > eps) in eval (event_gate.py:98-105)."""
+    if not br.training:
+        return "hard"
+    return "ste" if br.gate.use_ste else "soft"
+
+
+_GRAD_MODES = {"ste": 0, "soft": 1, "hard": 2}
+
+
+class StreamStepFunction(torch.autograd.Function):
+    """One streaming step of one branch under autograd (the per-branch body of
+    temporal_step, streaming.py:55-80): (y before proj_out, gate, resid,
+    innov, h', t', u', B', C', initialized') from the frame (u, B, C, t, cpi),
+    the state and the parameters.  The backward is eacs_stream_step_bwd."""
+
+    @staticmethod
+    def forward(ctx, u, Bc, Cc, t, cpi, h, st_t, st_u, st_B, st_C, lam, log_dt, D, eps, init, valid,
+                mean, var, hp):
+        ctx.set_materialize_grads(False)
+        eta, var_eps, dt_init, dt_min, dt_max, cpi_mod, mode, T = hp
+        st = (h, st_t, st_u, st_B, st_C, init)
+        y, g, r, n, st1 = stream_chunk(
+            lam, log_dt, D, mean, var, u.float()[:, None], Bc[:, None], Cc[:, None], t.float()[:, None],
+            None if valid is None else valid[:, None], None if cpi is None else cpi.float()[:, None], st,
+            float(eps), eta, var_eps, dt_init, dt_min, dt_max, cpi_mod, "soft" if mode == "soft" else "hard", T)
+        h1, t1, u1, B1, C1, i1 = st1
+        ctx.mark_non_differentiable(i1)
+        keep = [u.float().contiguous(), _c64(Bc), _c64(Cc), _f32(t), None if cpi is None else _f32(cpi),
+                _c64(h), _f32(st_t), _f32(st_u), _c64(st_B), _c64(st_C), _c64(lam), _f32(log_dt), _f32(D),
+                _f32(mean), _f32(var), init.to(torch.uint8).contiguous(),
+                None if valid is None else valid.to(torch.uint8).contiguous(), g[:, 0].contiguous()]
+        ctx.keep = keep
+        ctx.hp = (float(eps), float(eta), float(var_eps), float(dt_init), float(dt_min), float(dt_max),
+                  float(cpi_mod), _GRAD_MODES[mode], float(T))
+        ctx.dtypes = (u.dtype, Bc.dtype, Cc.dtype, t.dtype, None if cpi is None else cpi.dtype, h.dtype,
+                      st_t.dtype, st_u.dtype, st_B.dtype, st_C.dtype, lam.dtype, log_dt.dtype, D.dtype,
+                      eps.dtype if torch.is_tensor(eps) else None, eps.shape if torch.is_tensor(eps) else None)
+        return y[:, 0], g[:, 0], r[:, 0], n[:, 0], h1, t1, u1, B1, C1, i1
+
+    @staticmethod
+    def backward(ctx, gy, gg, gr, gn, gh, gt, gu, gB, gC, _gi):
+        (u, Bc, Cc, t, cpi, h, st_t, st_u, st_B, st_C, lam, log_dt, D, mean, var, init, valid,
+         gate) = ctx.keep
+        eps, eta, var_eps, dt_init, dt_min, dt_max, cpi_mod, mode, T = ctx.hp
+        dev = u.device
+        B, H = u.shape
+        N = lam.shape[1]
+        f = lambda x: None if x is None else x.float().contiguous()  # noqa: E731
+        c = lambda x: None if x is None else x.to(torch.complex64).contiguous()  # noqa: E731
+        ups = [f(gy), f(gg), f(gr), f(gn), c(gh), f(gt), f(gu), c(gB), c(gC)]
+        f32 = dict(dtype=torch.float32, device=dev)
+        c64 = dict(dtype=torch.complex64, device=dev)
+        out = [torch.empty(B, H, **f32), torch.empty(B, N, **c64), torch.empty(B, N, **c64),
+               torch.empty(B, **f32), None if cpi is None else torch.empty(B, **f32),
+               torch.empty(B, H, N, **c64), torch.empty(B, **f32), torch.empty(B, H, **f32),
+               torch.empty(B, N, **c64), torch.empty(B, N, **c64), torch.empty(H, N, **c64),
+               torch.empty(H, **f32), torch.empty(H, **f32), torch.empty(1, **f32)]
+        L_ = _lib.lib()
+        ws = torch.empty(int(L_.eacs_stream_step_bwd_workspace_size(B, H, N)), dtype=torch.uint8, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(L_.eacs_stream_step_bwd(
+                lam.data_ptr(), log_dt.data_ptr(), D.data_ptr(), mean.data_ptr(), var.data_ptr(), u.data_ptr(),
+                Bc.data_ptr(), Cc.data_ptr(), t.data_ptr(), _lib.ptr(valid), _lib.ptr(cpi), h.data_ptr(),
+                st_t.data_ptr(), st_u.data_ptr(), st_B.data_ptr(), st_C.data_ptr(), init.data_ptr(),
+                gate.data_ptr(), *[_lib.ptr(x) for x in ups], *[_lib.ptr(x) for x in out],
+                ws.data_ptr(), ws.numel(), eps, eta, var_eps, dt_init, dt_min, dt_max, cpi_mod, mode, T,
+                B, H, N, _lib.stream_ptr(dev)), "eacs_stream_step_bwd")
+        dt_ = ctx.dtypes
+        du, dBc, dCc, dt, dcpi, dh, dt_in, du_in, dB_in, dC_in, dlam, dlog, dD, deps = out
+        grads = [du.to(dt_[0]), dBc.to(dt_[1]), dCc.to(dt_[2]), dt.to(dt_[3]),
+                 None if dcpi is None else dcpi.to(dt_[4]), dh.to(dt_[5]), dt_in.to(dt_[6]),
+                 du_in.to(dt_[7]), dB_in.to(dt_[8]), dC_in.to(dt_[9]), dlam.to(dt_[10]), dlog.to(dt_[11]),
+                 dD.to(dt_[12]), None if dt_[13] is None else deps.to(dt_[13]).reshape(dt_[14])]
+        return (*grads, None, None, None, None, None)
+
+
+def stream_step(br, u, Bc, Cc, t, valid, cpi, state, eps):
+    """One step of branch `br` (an EACSLayer) from `state` (h, t, u, B, C,
+    initialized): (y (B,H) before proj_out, gate, resid, innov, state').
+    Differentiable where any input needs a gradient."""
+    mode = _grad_mode(br)
+    hp = (br.gate.norm_eta, br.obs_norm.eps, br.dt_init, 1e-3, float(br.dt_max),
+          float(br.gate.cpi_modulation) if cpi is not None else 0.0, mode, float(br.gate.temperature))
+    lam = br.lam()
+    h, st_t, st_u, st_B, st_C, init = state
+    ins = (u, Bc, Cc, t, cpi, h, st_t, st_u, st_B, st_C, lam, br.log_dt_scale, br.D, eps)
+    if torch.is_grad_enabled() and any(torch.is_tensor(x) and x.requires_grad for x in ins):
+        y, g, r, n, h1, t1, u1, B1, C1, i1 = StreamStepFunction.apply(
+            u, Bc, Cc, t, cpi, h, st_t, st_u, st_B, st_C, lam, br.log_dt_scale, br.D, eps, init, valid,
+            br.obs_norm.running_mean, br.obs_norm.running_var, hp)
+        return y, g, r, n, (h1, t1, u1, B1, C1, i1.bool())
+    with torch.no_grad():
+        y, g, r, n, st1 = stream_chunk(
+            lam, br.log_dt_scale, br.D, br.obs_norm.running_mean, br.obs_norm.running_var, u[:, None],
+            Bc[:, None], Cc[:, None], t.float()[:, None], None if valid is None else valid[:, None],
+            None if cpi is None else cpi.float()[:, None], state, float(eps), *hp[:6], _gate_mode(br), hp[7])
+    return y[:, 0], g[:, 0], r[:, 0], n[:, 0], st1
+
+
 def temporal_step(temporal, x: Tensor, t: Tensor, states: list, valid: Tensor,
                   cpi: Tensor | None = None):
     """streaming.py:45-85: one observation for every branch; returns
@@ -90,19 +195,14 @@ def temporal_step(temporal, x: Tensor, t: Tensor, states: list, valid: Tensor,
         if bool((vb & state.initialized & (t < state.t)).any()):
             raise ValueError("timestamps must not precede the last committed observation")
         st = (state.h, state.t, state.u, state.B, state.C, state.initialized)
-        y, g, r, n, st1 = stream_chunk(
-            br.lam(), br.log_dt_scale, br.D, br.obs_norm.running_mean, br.obs_norm.running_var,
-            u[:, None], Bc[:, None], Cc[:, None], t.float()[:, None], vb[:, None],
-            None if cpi is None else cpi.float()[:, None], st, float(br.gate.eps.item()),
-            br.gate.norm_eta, br.obs_norm.eps, br.dt_init, 1e-3, float(br.dt_max),
-            float(br.gate.cpi_modulation) if cpi is not None else 0.0, _gate_mode(br),
-            float(br.gate.temperature))
+        y, g, r, n, st1 = stream_step(br, u, Bc, Cc, t.float(), vb, None if cpi is None else cpi.float(), st,
+                                      br.gate.eps)
         new.append(type(state)(*st1))
-        delta = br.proj_out(y[:, 0].to(x.dtype))
+        delta = br.proj_out(y.to(x.dtype))
         ys.append(delta * vb[:, None])
-        gs.append(g[:, 0])
-        rs.append(r[:, 0])
-        ns.append(n[:, 0])
+        gs.append(g)
+        rs.append(r)
+        ns.append(n)
     weights = temporal.fusion(x).softmax(-1)
     fused = (torch.stack(ys, -1) * weights[:, None, :]).sum(-1)
     y = temporal.out_norm(x + fused) * vb[:, None]
@@ -114,11 +214,6 @@ def streaming_fusable(temporal, x: Tensor, states) -> bool:
         return False
     for br in temporal.branches:
         if br.disc_mode != "continuous" or getattr(br.gate, "gate_kind", "event") != "event":
-            return False
-    if torch.is_grad_enabled():
-        if x.requires_grad or any(p.requires_grad for p in temporal.parameters()):
-            return False
-        if any(s.h.requires_grad or s.u.requires_grad for s in states):
             return False
     return True
 
