@@ -311,7 +311,8 @@ def run_with_commits(layer, x: Tensor, timestamps: Tensor, cpi: Tensor | None = 
     lam = layer.lam().to(torch.complex64)
     t = timestamps.float()
     train_gate = layer.training
-    if train_gate or _needs_grad(x, u, Bc, Cc, t, lam, layer.log_dt_scale, layer.D, layer.gate.eps_raw):
+    if train_gate or _needs_grad(x, u, Bc, Cc, t, lam, layer.log_dt_scale, layer.D,
+                                 getattr(layer.gate, "eps_raw", None)):
         gate = layer.gate
         mode = ("ste" if gate.use_ste else "soft") if train_gate else "hard"
         eps = gate.eps
