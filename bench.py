@@ -80,7 +80,7 @@ def parse():
                     help="B,L,H,N override for --workload scan, ssm_train, train, longvideo or query_train "
                     "(e.g. a small case for ncu)")
     ap.add_argument("--workload", choices=["cell", "scan", "ssm", "ssm_train", "train", "multiscale",
-                                           "longvideo", "project", "query_train"],
+                                           "longvideo", "project", "query_train", "stream"],
                     default="cell", help="cell (default) is the headline; the others are the "
                     "materialised scan, the fused ungated SSM, the training step, the "
                     "three-branch multiscale cell and the long-video cell (B=64, H=2048, N=32)")

@@ -624,6 +624,96 @@ def wl_query_train(args, dev, flush):
     return 0
 
 
+def wl_stream(args, dev, flush):
+    """Streaming steps (temporal_step, streaming.py:45-85), one frame at a
+    time through a MultiScaleEACS with config 2's three branch bands (tau in
+    [0.5, 4], [4, 32], [32, 256] s, N = 16) at d = 1024, B = 4 videos, 64
+    frames: inference (no autograd) and training (the STE gate, forward over
+    the 64 frames then backward through the state), this library's
+    temporal_step against the reference's own on the same module, inputs and
+    GPU.  Needs the reference package (its module classes hold the
+    parameters); timed on the device with CUDA events around the frame loop."""
+    import sys as _sys
+    root = None
+    for cand in (os.environ.get("CST_SSM_REFERENCE"), os.path.join(ROOT, "baseline", "_ref")):
+        if cand and os.path.isdir(os.path.join(cand, "cst_ssm")):
+            root = cand
+            break
+    if root is None:
+        print(json.dumps({"metric": "streaming frames/s", "unavailable": "reference package absent"}))
+        return 0
+    if root not in _sys.path:
+        _sys.path.insert(0, root)
+    from cst_ssm.modules.multiscale import MultiScaleEACS
+    from cst_ssm.modules.streaming import initial_states
+    from cst_ssm.modules.streaming import temporal_step as ref_step
+    from cst_ssm.ops import eacs_gated_scan, scan_cuda
+    from cst_ssm.ops.spectral_init import BranchSpec
+
+    from eacs_b200.ops.streaming import temporal_step as our_step
+    scan_cuda._EXT, scan_cuda._TRIED = None, True
+    eacs_gated_scan._EXT, eacs_gated_scan._TRIED = None, True
+    B, K, d = 4, 64, 1024
+    torch.manual_seed(0)
+    temporal = MultiScaleEACS(d, branches=[BranchSpec("short", 16, 0.5, 4.0), BranchSpec("mid", 16, 4.0, 32.0),
+                                           BranchSpec("long", 16, 32.0, 256.0)],
+                              gate_kwargs={"init_eps": 0.12}).to(dev)
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(B, K, d, generator=g).to(dev)
+    dt = 0.25 + 1.75 * torch.rand(B, K, generator=g)
+    dt[torch.rand(B, K, generator=g) < 0.1] = 0.25
+    t = torch.cumsum(dt, 1).to(dev)
+    valid = torch.ones(B, K, dtype=torch.bool, device=dev)
+    gy = torch.randn(B, K, d, generator=g).to(dev)
+
+    def scan(step, train):
+        states = initial_states(temporal, B, dev)
+        ys, gs = [], []
+        for k in range(K):
+            y, gk, r, n, w, states = step(temporal, x[:, k], t[:, k], states, valid[:, k])
+            ys.append(y)
+            gs.append(gk)
+        if train:
+            (torch.stack(ys, 1) * gy).sum().backward()
+        return torch.stack(gs, 1)
+
+    def timed_scan(step, train, reps):
+        temporal.train(train)
+        out = []
+        for i in range(reps + 1):
+            temporal.zero_grad(set_to_none=True)
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            s0.record()
+            with torch.set_grad_enabled(train):
+                gates = scan(step, train)
+            s1.record()
+            torch.cuda.synchronize()
+            if i:  # the first is a warm-up
+                out.append(s0.elapsed_time(s1))
+        return statistics.median(out), gates
+
+    n = max(3, min(args.steps, 10))
+    res = {}
+    for train in (False, True):
+        ours_ms, g_ours = timed_scan(our_step, train, n)
+        ref_ms, g_ref = timed_scan(ref_step, train, 2)
+        res["training" if train else "inference"] = {
+            "ours_ms_per_frame": ours_ms / K, "reference_ms_per_frame": ref_ms / K,
+            "speedup": ref_ms / ours_ms, "gates_equal": bool(torch.equal(g_ours.float(), g_ref.float())),
+            "update_rate": float(g_ours.float().mean())}
+    inf = res["inference"]
+    line("streaming steps (temporal_step), frames/s over B videos", B / (inf["ours_ms_per_frame"] / 1e3), n, 1,
+         inf["ours_ms_per_frame"] * K,
+         {"workload": f"temporal_step frame by frame: MultiScaleEACS d={d}, three branches N=16 "
+                      f"(config 2's bands), B={B} videos, {K} frames", "cases": res},
+         unit="frames/s", dtype="f32",
+         note="value: inference frames/s (B videos a frame); cases: per-frame device time of this "
+              "library's temporal_step and of the reference's on the same module and GPU, inference "
+              "and training (STE gate, forward over the frames then backward through the state)")
+    return 0
+
+
 def longvideo_inputs(rows, L, dev, seed, H=2048, N=32):
     """Long-video inputs (H=2048, N=32) for `rows` videos, drawn on the device from one seeded
     generator: fp16 u ~ N(0,1); B, C complex with N(0,1)/sqrt(N) parts;
@@ -764,7 +854,8 @@ def run_workload(args):
     torch.cuda.set_device(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     {"scan": wl_scan, "ssm": wl_ssm, "ssm_train": wl_ssm_train,
-     "multiscale": wl_multiscale, "project": wl_project, "query_train": wl_query_train}[args.workload](
+     "multiscale": wl_multiscale, "project": wl_project, "query_train": wl_query_train,
+     "stream": wl_stream}[args.workload](
         args, dev, flush)
     from eacs_b200 import _lib
     assert _lib.device_status() == 0

@@ -102,12 +102,13 @@ class StreamStepFunction(torch.autograd.Function):
     def forward(ctx, u, Bc, Cc, t, cpi, h, st_t, st_u, st_B, st_C, lam, log_dt, D, eps, init, valid,
                 mean, var, hp):
         ctx.set_materialize_grads(False)
-        eta, var_eps, dt_init, dt_min, dt_max, cpi_mod, mode, T = hp
+        eta, var_eps, dt_init, dt_min, dt_max, cpi_mod, mode, T = hp[:8]
+        eps_v = hp[8] if len(hp) > 8 else float(eps)  # the threshold's value, when the caller has it
         st = (h, st_t, st_u, st_B, st_C, init)
         y, g, r, n, st1 = stream_chunk(
             lam, log_dt, D, mean, var, u.float()[:, None], Bc[:, None], Cc[:, None], t.float()[:, None],
             None if valid is None else valid[:, None], None if cpi is None else cpi.float()[:, None], st,
-            float(eps), eta, var_eps, dt_init, dt_min, dt_max, cpi_mod, "soft" if mode == "soft" else "hard", T)
+            eps_v, eta, var_eps, dt_init, dt_min, dt_max, cpi_mod, "soft" if mode == "soft" else "hard", T)
         h1, t1, u1, B1, C1, i1 = st1
         ctx.mark_non_differentiable(i1)
         keep = [u.float().contiguous(), _c64(Bc), _c64(Cc), _f32(t), None if cpi is None else _f32(cpi),
@@ -115,7 +116,7 @@ class StreamStepFunction(torch.autograd.Function):
                 _f32(mean), _f32(var), init.to(torch.uint8).contiguous(),
                 None if valid is None else valid.to(torch.uint8).contiguous(), g[:, 0].contiguous()]
         ctx.keep = keep
-        ctx.hp = (float(eps), float(eta), float(var_eps), float(dt_init), float(dt_min), float(dt_max),
+        ctx.hp = (eps_v, float(eta), float(var_eps), float(dt_init), float(dt_min), float(dt_max),
                   float(cpi_mod), _GRAD_MODES[mode], float(T))
         ctx.dtypes = (u.dtype, Bc.dtype, Cc.dtype, t.dtype, None if cpi is None else cpi.dtype, h.dtype,
                       st_t.dtype, st_u.dtype, st_B.dtype, st_C.dtype, lam.dtype, log_dt.dtype, D.dtype,
@@ -159,13 +160,52 @@ class StreamStepFunction(torch.autograd.Function):
         return (*grads, None, None, None, None, None)
 
 
-def stream_step(br, u, Bc, Cc, t, valid, cpi, state, eps):
+_EPS_CACHE: dict = {}
+_SCALAR_CACHE: dict = {}
+
+
+def host_float(x) -> float:
+    """float(x) for a number; for a one-element tensor (a buffer such as the
+    gate temperature) its value, read from the device only when the tensor
+    changed since the last read (its version counter or storage)."""
+    if not torch.is_tensor(x):
+        return float(x)
+    key = (x.data_ptr(), x._version)
+    hit = _SCALAR_CACHE.get(id(x))
+    if hit is None or hit[0] != key:
+        hit = (key, float(x.detach()))
+        _SCALAR_CACHE[id(x)] = hit
+    return hit[1]
+
+
+def eps_value(gate) -> float:
+    """The gate threshold as a Python float, read from the device only when
+    its parameters changed since the last read (EventGate.eps is
+    eps_min + (eps_max - eps_min) sigmoid(eps_raw), times eps_anneal): a
+    stream of frames then takes no host synchronisation for it."""
+    raw, anneal = getattr(gate, "eps_raw", None), getattr(gate, "eps_anneal", None)
+    if not (torch.is_tensor(raw) and torch.is_tensor(anneal)):
+        return float(gate.eps)
+    key = (raw._version, anneal._version, raw.data_ptr(), anneal.data_ptr(), gate.eps_min, gate.eps_max)
+    hit = _EPS_CACHE.get(id(gate))
+    if hit is None or hit[0] != key:
+        hit = (key, float(gate.eps.detach()))
+        _EPS_CACHE[id(gate)] = hit
+    return hit[1]
+
+
+def stream_step(br, u, Bc, Cc, t, valid, cpi, state, eps=None):
     """One step of branch `br` (an EACSLayer) from `state` (h, t, u, B, C,
     initialized): (y (B,H) before proj_out, gate, resid, innov, state').
-    Differentiable where any input needs a gradient."""
+    eps: the threshold (default: the branch gate's).  Differentiable where
+    any input needs a gradient."""
     mode = _grad_mode(br)
-    hp = (br.gate.norm_eta, br.obs_norm.eps, br.dt_init, 1e-3, float(br.dt_max),
-          float(br.gate.cpi_modulation) if cpi is not None else 0.0, mode, float(br.gate.temperature))
+    if eps is None:
+        eps, eps_v = br.gate.eps, eps_value(br.gate)
+    else:
+        eps_v = float(eps)
+    hp = (br.gate.norm_eta, br.obs_norm.eps, br.dt_init, 1e-3, host_float(br.dt_max),
+          float(br.gate.cpi_modulation) if cpi is not None else 0.0, mode, host_float(br.gate.temperature), eps_v)
     lam = br.lam()
     h, st_t, st_u, st_B, st_C, init = state
     ins = (u, Bc, Cc, t, cpi, h, st_t, st_u, st_B, st_C, lam, br.log_dt_scale, br.D, eps)
@@ -178,7 +218,7 @@ def stream_step(br, u, Bc, Cc, t, valid, cpi, state, eps):
         y, g, r, n, st1 = stream_chunk(
             lam, br.log_dt_scale, br.D, br.obs_norm.running_mean, br.obs_norm.running_var, u[:, None],
             Bc[:, None], Cc[:, None], t.float()[:, None], None if valid is None else valid[:, None],
-            None if cpi is None else cpi.float()[:, None], state, float(eps), *hp[:6], _gate_mode(br), hp[7])
+            None if cpi is None else cpi.float()[:, None], state, hp[8], *hp[:6], _gate_mode(br), hp[7])
     return y[:, 0], g[:, 0], r[:, 0], n[:, 0], st1
 
 
@@ -188,15 +228,21 @@ def temporal_step(temporal, x: Tensor, t: Tensor, states: list, valid: Tensor,
     (y, gates (B,S), resid, innov, fusion weights, new states)."""
     ys, gs, rs, ns, new = [], [], [], [], []
     vb = valid.bool()
-    for br, state in zip(temporal.branches, states):
+    for br in temporal.branches:
         if br.robust_guard:
             raise ValueError("streaming CPIB does not support robust_guard; disable it explicitly")
+    # the reference checks each branch's state in turn; one check over all
+    # branches (one host synchronisation) raises the same error
+    bad = None
+    for state in states:
+        b = vb & state.initialized & (t < state.t)
+        bad = b if bad is None else bad | b
+    if bad is not None and bool(bad.any()):
+        raise ValueError("timestamps must not precede the last committed observation")
+    for br, state in zip(temporal.branches, states):
         u, Bc, Cc = br._project(br.norm(x))
-        if bool((vb & state.initialized & (t < state.t)).any()):
-            raise ValueError("timestamps must not precede the last committed observation")
         st = (state.h, state.t, state.u, state.B, state.C, state.initialized)
-        y, g, r, n, st1 = stream_step(br, u, Bc, Cc, t.float(), vb, None if cpi is None else cpi.float(), st,
-                                      br.gate.eps)
+        y, g, r, n, st1 = stream_step(br, u, Bc, Cc, t.float(), vb, None if cpi is None else cpi.float(), st)
         new.append(type(state)(*st1))
         delta = br.proj_out(y.to(x.dtype))
         ys.append(delta * vb[:, None])
