@@ -123,3 +123,61 @@ def test_project_rejects_bad_arguments_without_device():
     # workspace too small (checked before any launch)
     assert lib.eacs_project(p, 1, p, p, 1e-5, p, 1, 256, p, p, 1, p, p, p, 8, 10, 16, 8, 4, None) == _lib.EACS_ERR_WORKSPACE
     assert lib.eacs_project_workspace_size(10) == 80
+
+
+def test_commit_training_rejects_bad_arguments_without_device():
+    """eacs_cell_train_commits_fwd/_bwd check the gate mode, the backward
+    workspace and the commit buffers before anything touches the device."""
+    L = _lib.lib()
+    p = 256
+    B, Ln, H, N = 2, 16, 8, 16
+    need = L.eacs_cell_train_commits_workspace_size(B, Ln, H, N)
+    assert need > 0 and L.eacs_cell_train_commits_workspace_size(B, Ln, H, 65) == 0
+    head = (p, p, p, 0, p, p, p, p, p, p, 0.1, 1e-6, 1e-5, 1.0, 1e-3, 1e3)
+
+    def fwd(gate_mode=0, commits=(p,) * 5, bws=p, bwn=None):
+        return L.eacs_cell_train_commits_fwd(*head, gate_mode, 0.1, p, p, p, p, *commits, p, 1 << 30,
+                                             bws, need if bwn is None else bwn, B, Ln, H, N, None)
+    assert fwd(gate_mode=3) == _lib.EACS_ERR_INVALID and "gate_mode" in _lib.last_error()
+    assert fwd(bws=None, bwn=0) == _lib.EACS_ERR_WORKSPACE
+    assert fwd(bwn=need - 1) == _lib.EACS_ERR_WORKSPACE
+    assert fwd(commits=(p, None, p, p, p)) == _lib.EACS_ERR_INVALID
+
+    def bwd(gate_mode=0, ws=p, wn=None):
+        return L.eacs_cell_train_commits_bwd(*head, gate_mode, 0.1, p, p, p, p, None, None, None, None, None,
+                                             None, None, p, p, p, p, p, p, p, p, ws, need if wn is None else wn,
+                                             B, Ln, H, N, None)
+    assert bwd(gate_mode=-1) == _lib.EACS_ERR_INVALID
+    assert bwd(ws=None, wn=0) == _lib.EACS_ERR_WORKSPACE
+
+
+def test_query_readout_bwd_rejects_bad_arguments_without_device():
+    L = _lib.lib()
+    p = 256
+    B, Ln, Q, H, N = 2, 16, 5, 8, 16
+    need = L.eacs_query_readout_bwd_workspace_size(B, Ln, Q, H, N)
+    assert need > 0 and L.eacs_query_readout_bwd_workspace_size(B, Ln, Q, H, 65) == 0
+
+    def call(ptrs=(p,) * 20, ws=p, wn=None, n=N, b=B):
+        return L.eacs_query_readout_bwd(*ptrs, ws, need if wn is None else wn, b, Ln, Q, H, n, 1e-3, 1e3, None)
+    assert call(n=65) == _lib.EACS_ERR_UNSUPPORTED
+    assert call(ptrs=(p,) * 10 + (None,) + (p,) * 9) == _lib.EACS_ERR_INVALID   # gy
+    assert call(wn=need - 1) == _lib.EACS_ERR_WORKSPACE
+    assert call(b=0) == _lib.EACS_OK
+
+
+def test_stream_step_bwd_rejects_bad_arguments_without_device():
+    L = _lib.lib()
+    p = 256
+    B, H, N = 2, 8, 16
+    need = L.eacs_stream_step_bwd_workspace_size(B, H, N)
+    assert need > 0 and L.eacs_stream_step_bwd_workspace_size(0, H, N) == 0
+
+    def call(ptrs=(p,) * 41, wn=None, gate_mode=0, n=N, b=B):
+        return L.eacs_stream_step_bwd(*ptrs, p, need if wn is None else wn, 0.1, 1e-6, 1e-5, 1.0, 1e-3, 1e3, 0.0,
+                                      gate_mode, 0.1, b, H, n, None)
+    assert call(gate_mode=3) == _lib.EACS_ERR_INVALID
+    assert call(n=65) == _lib.EACS_ERR_UNSUPPORTED
+    assert call(ptrs=(None,) + (p,) * 40) == _lib.EACS_ERR_INVALID
+    assert call(wn=need - 1) == _lib.EACS_ERR_WORKSPACE
+    assert call(b=0) == _lib.EACS_OK

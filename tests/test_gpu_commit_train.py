@@ -180,3 +180,27 @@ def test_unsorted_queries_and_workspace_reuse():
     (gl0, gu0, gt0), (gl1, gu1, gt1) = res
     assert relerr(gl1, gl0) < 1e-5 and relerr(gu1, gu0) < 1e-5
     assert relerr(gt1, np.take_along_axis(gt0, perm, 1)) < 1e-5
+
+
+def test_edge_shapes():
+    """One frame (L = 1), a row's queries all before its first frame, and no
+    queries at all (Q = 0: the commits' adjoints are zero)."""
+    from eacs_b200.ops.continuous_query import QueryReadoutFunction, cell_commits_train
+    for L, Q in ((1, 3), (5, 0), (7, 4)):
+        d, up = _inputs(2, L, 16, 8, max(Q, 1), 40 + L)
+        d["scalars"] = np.array([0.5, 1e-6, 1e-5, 1.0, 1e-3, 1e3, 0.3])
+        if Q:
+            d["t_query"] = d["t_query"][:, :Q] if L > 1 else np.stack([d["t"][:, 0] - 0.5, d["t"][:, 0],
+                                                                       d["t"][:, 0] + 0.3], 1).astype(np.float32)
+            if L == 7:
+                d["t_query"] = (d["t"][:, :1] - 1.0 - np.arange(Q)[None, :] * 0.1).astype(np.float32)
+            up["gq"] = up["gq"][:, :Q]
+        else:
+            d["t_query"] = np.zeros((2, 0), np.float32)
+            up["gq"] = np.zeros((2, 0, 16), np.float32)
+        fwd, grads = _run_gpu(d, "ste", up["gq"], up["gf"], up["gy"], up["ggs"], up["grs"])
+        _, ograds = _oracle(d, fwd[1], "ste", up)
+        for k in NAMES:
+            if k == "dtq" and Q == 0:
+                continue
+            assert relerr(grads[k], ograds[k]) < GRAD_TOL, (L, Q, k, relerr(grads[k], ograds[k]))

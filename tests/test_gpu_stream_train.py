@@ -221,3 +221,19 @@ def test_reference_temporal_step_gradients(ref, train):
             assert p.grad is None or not p.grad.any(), name
             continue
         assert relerr(p.grad.cpu().numpy(), p_ref.grad.cpu().numpy()) < GRAD_TOL, name
+
+
+def test_all_rows_masked_and_first_steps():
+    """A step where no row is valid passes the state's adjoints through and
+    gives the frame none; a step where every row starts (first observation)."""
+    d = _random_case(3, 3, 32, 8, "ste", 11)
+    d["valid"][:] = 1
+    d["valid"][:, 1] = 0
+    d["init0"][:] = 0
+    d["scalars"] = np.array([0.5, 1e-6, 1e-5, 1.0, 1e-3, 1e3, 0.0, 0.3])
+    outs, st, grads = _scan_gpu(d)
+    (oy, og, orr, on), ost, ograds = sgrad_oracle(d, pin=outs["gate"])
+    assert np.all(outs["gate"][:, 0] == 1.0) and np.all(outs["gate"][:, 1] == 0.0)
+    assert not grads["du"][:, 1].any() and not grads["dt"][:, 1].any()
+    for k, v in grads.items():
+        assert relerr(v, ograds[k]) < GRAD_TOL, (k, relerr(v, ograds[k]))
