@@ -580,6 +580,43 @@ EACS_API int eacs_cell_fwd_noalloc(const void* lam, const float* log_dt, const v
                                    float* y, float* gate, float* resid,
                                    int64_t B, int64_t L, int64_t H, int64_t N, void* stream);
 
+/* One streaming frame of a MultiScaleEACS, inference (temporal_step,
+ * cst_ssm/modules/streaming.py:45-85, with the branches' norm, _project and
+ * proj_out, modules/eacs.py:261-267, and the module's fusion softmax and
+ * out_norm, modules/multiscale.py:45-46, :177-179), in S + 3 launches:
+ * the norms, input projections and fusion logits of all branches, each
+ * branch's cell step (as eacs_stream_chunk with K = 1), each branch's proj_out
+ * blended with the fusion weights plus the residual, and out_norm.  x (B,d)
+ * float32 with B <= 8, t (B), valid (B) uint8 or NULL, cpi (B) or NULL; the
+ * weights are the modules' float32 tensors: per branch the LayerNorm (d),
+ * proj_u (H,d), proj_B and proj_C (2N,d) with biases, proj_out (d,H) with its
+ * bias; the fusion layer (S,d), (S) and out_norm (d).  State in and out as
+ * eacs_stream_chunk, per branch.  Outputs: y (B,d), the fusion weights (B,S),
+ * and gate, resid, innov (S,B).  1 <= S <= 4. */
+typedef struct {
+    const float* ln_w; const float* ln_b; float ln_eps;       /* the branch's norm */
+    const float* wu; const float* bu;                         /* proj_u (H,d), (H) */
+    const float* wB; const float* bB;                         /* proj_B (2N,d), (2N) */
+    const float* wC; const float* bC;                         /* proj_C (2N,d), (2N) */
+    const float* wo; const float* bo;                         /* proj_out (d,H), (d) */
+    const void* lam; const float* log_dt; const float* D; const float* mean; const float* var;
+    float eps, eta, var_eps, dt_init, dt_min, dt_max, cpi_modulation, temperature;
+    int gate_mode;                                            /* 0 hard, 1 soft */
+    int H, N;
+    const void* h_in; const float* t_in; const float* u_in; const void* B_in; const void* C_in;
+    const uint8_t* init_in;
+    void* h_out; float* t_out; float* u_out; void* B_out; void* C_out; uint8_t* init_out;
+} EacsFrameBranch;
+
+EACS_API size_t eacs_stream_frame_workspace_size(const EacsFrameBranch* branches, int S, int64_t B,
+                                                 int64_t d);
+EACS_API int eacs_stream_frame(const float* x, const float* t, const uint8_t* valid, const float* cpi,
+                               const EacsFrameBranch* branches, int S, const float* fusion_w,
+                               const float* fusion_b, const float* out_norm_w, const float* out_norm_b,
+                               float out_norm_eps, float* y, float* weights, float* gate, float* resid,
+                               float* innov, void* workspace, size_t workspace_bytes, int64_t B,
+                               int64_t d, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -441,6 +441,21 @@ int eacs_stream_step_bwd(const void* lam, const float* log_dt, const float* D, c
     return eacs::stream_step_bwd(c, static_cast<cudaStream_t>(stream));
 }
 
+size_t eacs_stream_frame_workspace_size(const EacsFrameBranch* branches, int S, int64_t B, int64_t d) {
+    return eacs::stream_frame_workspace_size(branches, S, B, d);
+}
+
+int eacs_stream_frame(const float* x, const float* t, const uint8_t* valid, const float* cpi,
+                      const EacsFrameBranch* branches, int S, const float* fusion_w, const float* fusion_b,
+                      const float* out_norm_w, const float* out_norm_b, float out_norm_eps, float* y,
+                      float* weights, float* gate, float* resid, float* innov, void* workspace,
+                      size_t workspace_bytes, int64_t B, int64_t d, void* stream) {
+    eacs::FrameCall c{x,        t,          valid,      cpi,   branches, S,      fusion_w, fusion_b,
+                      out_norm_w, out_norm_b, out_norm_eps, y,   weights,  gate,   resid,    innov,
+                      workspace, workspace_bytes, B,    d};
+    return eacs::stream_frame(c, static_cast<cudaStream_t>(stream));
+}
+
 size_t eacs_cell_fwd_host_workspace_size(int64_t B, int64_t L, int64_t H, int64_t N, int64_t chunk) {
     return eacs::cell_host_workspace_size(B, L, H, N, chunk);
 }

@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "../../include/eacs_b200.h"
+
 namespace eacs {
 
 // Records `msg` as the calling thread's last error and returns `code`.
@@ -276,6 +278,34 @@ struct StreamBwdCall {
 };
 size_t stream_step_bwd_workspace_size(int64_t B, int64_t H, int64_t N);
 int stream_step_bwd(const StreamBwdCall& c, cudaStream_t stream);
+
+// frame.cu: one streaming frame of a MultiScaleEACS (inference)
+constexpr int kFrameMaxBranches = 4;
+constexpr int kFrameMaxRows = 8;
+using FrameBranch = EacsFrameBranch;
+struct FrameCall {
+    const float* x;
+    const float* t;
+    const uint8_t* valid;
+    const float* cpi;
+    const FrameBranch* br;
+    int S;
+    const float* wf;
+    const float* bf;
+    const float* out_w;
+    const float* out_b;
+    float out_eps;
+    float* y;
+    float* weights;
+    float* gate;
+    float* resid;
+    float* innov;
+    void* workspace;
+    size_t workspace_bytes;
+    int64_t B, d;
+};
+size_t stream_frame_workspace_size(const FrameBranch* br, int S, int64_t B, int64_t d);
+int stream_frame(const FrameCall& c, cudaStream_t stream);
 
 // fuse.cu: MultiScaleEACS branch epilogue
 struct FuseCall {

@@ -67,6 +67,8 @@ SIGNATURES = {
                            + [_P] * 4 + [_SZ] + [_I64] * 5 + [_P]),
     "eacs_stream_chunk": (_I, [_P] * 6 + [_I] + [_P] * 21 + [_F] * 7 + [_I, _F]
                           + [_I64] * 4 + [_P]),
+    "eacs_stream_frame_workspace_size": (_SZ, [_P, _I, _I64, _I64]),
+    "eacs_stream_frame": (_I, [_P] * 5 + [_I] + [_P] * 4 + [_F] + [_P] * 6 + [_SZ, _I64, _I64, _P]),
     "eacs_stream_step_bwd_workspace_size": (_SZ, [_I64] * 3),
     "eacs_stream_step_bwd": (_I, [_P] * 41 + [_P, _SZ] + [_F] * 7 + [_I, _F] + [_I64] * 3 + [_P]),
     "eacs_ssm_bwd_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),

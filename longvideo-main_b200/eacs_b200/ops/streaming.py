@@ -18,6 +18,8 @@ non-continuous discretisation.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 from torch import Tensor
 
@@ -222,15 +224,28 @@ def stream_step(br, u, Bc, Cc, t, valid, cpi, state, eps=None):
     return y[:, 0], g[:, 0], r[:, 0], n[:, 0], st1
 
 
+def _needs_grad_frame(temporal, x, t, states, cpi) -> bool:
+    if not torch.is_grad_enabled():
+        return False
+    if any(torch.is_tensor(z) and z.requires_grad for z in (x, t, cpi)):
+        return True
+    if any(p.requires_grad for p in temporal.parameters()):
+        return True
+    return any(z.requires_grad for st in states for z in (st.h, st.t, st.u, st.B, st.C))
+
+
 def temporal_step(temporal, x: Tensor, t: Tensor, states: list, valid: Tensor,
                   cpi: Tensor | None = None):
     """streaming.py:45-85: one observation for every branch; returns
-    (y, gates (B,S), resid, innov, fusion weights, new states)."""
-    ys, gs, rs, ns, new = [], [], [], [], []
-    vb = valid.bool()
+    (y, gates (B,S), resid, innov, fusion weights, new states).  Without
+    autograd a frame the fused path takes runs as eacs_stream_frame."""
     for br in temporal.branches:
         if br.robust_guard:
             raise ValueError("streaming CPIB does not support robust_guard; disable it explicitly")
+    if not _needs_grad_frame(temporal, x, t, states, cpi) and frame_fusable(temporal, x, states):
+        return temporal_step_frame(temporal, x, t, states, valid, cpi)
+    ys, gs, rs, ns, new = [], [], [], [], []
+    vb = valid.bool()
     # the reference checks each branch's state in turn; one check over all
     # branches (one host synchronisation) raises the same error
     bad = None
@@ -253,6 +268,122 @@ def temporal_step(temporal, x: Tensor, t: Tensor, states: list, valid: Tensor,
     fused = (torch.stack(ys, -1) * weights[:, None, :]).sum(-1)
     y = temporal.out_norm(x + fused) * vb[:, None]
     return y, torch.stack(gs, 1), torch.stack(rs, 1), torch.stack(ns, 1), weights, new
+
+
+_CP, _CF = ctypes.c_void_p, ctypes.c_float
+
+
+class FrameBranch(ctypes.Structure):
+    """EacsFrameBranch (include/eacs_b200.h): one branch's weights, cell
+    parameters and state buffers for eacs_stream_frame."""
+    _fields_ = ([("ln_w", _CP), ("ln_b", _CP), ("ln_eps", _CF)]
+                + [(k, _CP) for k in ("wu", "bu", "wB", "bB", "wC", "bC", "wo", "bo",
+                                      "lam", "log_dt", "D", "mean", "var")]
+                + [(k, _CF) for k in ("eps", "eta", "var_eps", "dt_init", "dt_min", "dt_max",
+                                      "cpi_modulation", "temperature")]
+                + [("gate_mode", ctypes.c_int), ("H", ctypes.c_int), ("N", ctypes.c_int)]
+                + [(k, _CP) for k in ("h_in", "t_in", "u_in", "B_in", "C_in", "init_in",
+                                      "h_out", "t_out", "u_out", "B_out", "C_out", "init_out")])
+
+
+def _f32_param(t) -> bool:
+    return t is not None and t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()
+
+
+def frame_fusable(temporal, x: Tensor, states) -> bool:
+    """Whether one frame can run as eacs_stream_frame: float32 CUDA rows
+    (at most 8) of width d (B*d <= 51200), 1-4 continuous event-gate branches
+    without robust_guard, float32 contiguous weights with LayerNorm affines."""
+    if not (x.is_cuda and x.dim() == 2 and x.dtype == torch.float32 and 1 <= x.shape[0] <= 8
+            and x.shape[0] * x.shape[1] <= 51200):
+        return False
+    if not 1 <= len(temporal.branches) <= 4:
+        return False
+    mods = [temporal.fusion, temporal.out_norm]
+    if not isinstance(temporal.out_norm, torch.nn.LayerNorm):
+        return False
+    for br in temporal.branches:
+        if (br.robust_guard or br.disc_mode != "continuous" or getattr(br.gate, "gate_kind", "event") != "event"
+                or not isinstance(br.norm, torch.nn.LayerNorm) or br.N > 64):
+            return False
+        mods += [br.norm, br.proj_u, br.proj_B, br.proj_C, br.proj_out]
+    return all(_f32_param(m.weight) and _f32_param(m.bias) for m in mods)
+
+
+_LAM_CACHE: dict = {}
+
+
+def _frame_lam(br) -> Tensor:
+    """br.lam() as contiguous complex64, recomputed only when one of the
+    layer's own parameters changed (without autograd the value is all that
+    is needed)."""
+    key = tuple((p.data_ptr(), p._version) for p in br.parameters(recurse=False))
+    hit = _LAM_CACHE.get(id(br))
+    if hit is None or hit[0] != key:
+        hit = (key, br.lam().detach().to(torch.complex64).contiguous())
+        _LAM_CACHE[id(br)] = hit
+    return hit[1]
+
+
+def temporal_step_frame(temporal, x: Tensor, t: Tensor, states: list, valid: Tensor,
+                        cpi: Tensor | None = None):
+    """temporal_step (streaming.py:45-85) for one frame without autograd, as
+    eacs_stream_frame: S + 3 launches for the whole module (norms, projections,
+    cell steps, proj_out, fusion, out_norm).  Same returns as temporal_step."""
+    vb = valid.bool()
+    bad = None
+    for state in states:
+        b = vb & state.initialized & (t < state.t)
+        bad = b if bad is None else bad | b
+    if bad is not None and bool(bad.any()):
+        raise ValueError("timestamps must not precede the last committed observation")
+    B, d = x.shape
+    S = len(temporal.branches)
+    dev = x.device
+    keep = [x.contiguous(), t.float().contiguous(), vb.contiguous().view(torch.uint8),
+            None if cpi is None else cpi.float().contiguous()]
+    arr = (FrameBranch * S)()
+    new = []
+    ptr = lambda z: None if z is None else z.data_ptr()  # noqa: E731
+    for s, (br, st) in enumerate(zip(temporal.branches, states)):
+        ins = [_frame_lam(br), _f32(br.log_dt_scale), _f32(br.D),
+               _f32(br.obs_norm.running_mean), _f32(br.obs_norm.running_var),
+               _c64(st.h), _f32(st.t), _f32(st.u), _c64(st.B), _c64(st.C),
+               st.initialized.bool().contiguous().view(torch.uint8)]
+        outs = [torch.empty_like(z) for z in ins[5:]]
+        keep += ins + outs
+        f = arr[s]
+        f.ln_w, f.ln_b, f.ln_eps = br.norm.weight.data_ptr(), br.norm.bias.data_ptr(), float(br.norm.eps)
+        f.wu, f.bu = br.proj_u.weight.data_ptr(), br.proj_u.bias.data_ptr()
+        f.wB, f.bB = br.proj_B.weight.data_ptr(), br.proj_B.bias.data_ptr()
+        f.wC, f.bC = br.proj_C.weight.data_ptr(), br.proj_C.bias.data_ptr()
+        f.wo, f.bo = br.proj_out.weight.data_ptr(), br.proj_out.bias.data_ptr()
+        f.lam, f.log_dt, f.D, f.mean, f.var = [z.data_ptr() for z in ins[:5]]
+        f.eps, f.eta, f.var_eps = eps_value(br.gate), br.gate.norm_eta, br.obs_norm.eps
+        f.dt_init, f.dt_min, f.dt_max = br.dt_init, 1e-3, host_float(br.dt_max)
+        f.cpi_modulation = float(br.gate.cpi_modulation) if cpi is not None else 0.0
+        f.temperature = host_float(br.gate.temperature)
+        f.gate_mode = 1 if _gate_mode(br) == "soft" else 0
+        f.H, f.N = br.H, br.N
+        f.h_in, f.t_in, f.u_in, f.B_in, f.C_in, f.init_in = [z.data_ptr() for z in ins[5:]]
+        f.h_out, f.t_out, f.u_out, f.B_out, f.C_out, f.init_out = [z.data_ptr() for z in outs]
+        new.append((type(st), outs))
+    y = torch.empty(B, d, dtype=torch.float32, device=dev)
+    weights = torch.empty(B, S, dtype=torch.float32, device=dev)
+    gate, resid, innov = (torch.empty(S, B, dtype=torch.float32, device=dev) for _ in range(3))
+    L_ = _lib.lib()
+    nbytes = int(L_.eacs_stream_frame_workspace_size(ctypes.byref(arr), S, B, d))
+    require(nbytes > 0, "eacs_stream_frame: unsupported sizes")
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(L_.eacs_stream_frame(
+            keep[0].data_ptr(), keep[1].data_ptr(), keep[2].data_ptr(), ptr(keep[3]), ctypes.byref(arr), S,
+            temporal.fusion.weight.data_ptr(), temporal.fusion.bias.data_ptr(), temporal.out_norm.weight.data_ptr(),
+            temporal.out_norm.bias.data_ptr(), float(temporal.out_norm.eps), y.data_ptr(), weights.data_ptr(),
+            gate.data_ptr(), resid.data_ptr(), innov.data_ptr(), ws.data_ptr(), ws.numel(), B, d,
+            _lib.stream_ptr(dev)), "eacs_stream_frame")
+    new = [cls(*outs[:5], outs[5].view(torch.bool)) for cls, outs in new]  # the kernel wrote 0 / 1
+    return y, gate.t(), resid.t(), innov.t(), weights, new
 
 
 def streaming_fusable(temporal, x: Tensor, states) -> bool:
