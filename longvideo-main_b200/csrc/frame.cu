@@ -108,11 +108,36 @@ __global__ void __launch_bounds__(kFT) frame_proj_k(ProjArgs a) {
     float rstd[kFrameMaxRows];
 #pragma unroll
     for (int b = 0; b < kFrameMaxRows; ++b) rstd[b] = b < B ? 1.0f / sqrtf(svar[b] + p.ln_eps) : 0.f;
-    for (int k = lane; k < d; k += 32) {
-        const float wk = w[k], g = p.ln_w[k], be = p.ln_b[k];
+    if ((d & 3) == 0 &&
+        ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(p.ln_w) | reinterpret_cast<uintptr_t>(p.ln_b)) &
+         15u) == 0) {
+        // 16-byte loads, several in flight per lane
+        const float4* w4 = reinterpret_cast<const float4*>(w);
+        const float4* g4 = reinterpret_cast<const float4*>(p.ln_w);
+        const float4* be4 = reinterpret_cast<const float4*>(p.ln_b);
+        const float4* sx4 = reinterpret_cast<const float4*>(sx);
+        const int d4 = d >> 2;
+#pragma unroll 2
+        for (int k = lane; k < d4; k += 32) {
+            const float4 wk = w4[k], g = g4[k], be = be4[k];
 #pragma unroll
-        for (int b = 0; b < kFrameMaxRows; ++b)
-            if (b < B) acc[b] = fmaf(wk, fmaf(sx[b * d + k] * rstd[b], g, be), acc[b]);
+            for (int b = 0; b < kFrameMaxRows; ++b)
+                if (b < B) {
+                    const float4 xv = sx4[b * d4 + k];
+                    float t = acc[b];
+                    t = fmaf(wk.x, fmaf(xv.x * rstd[b], g.x, be.x), t);
+                    t = fmaf(wk.y, fmaf(xv.y * rstd[b], g.y, be.y), t);
+                    t = fmaf(wk.z, fmaf(xv.z * rstd[b], g.z, be.z), t);
+                    acc[b] = fmaf(wk.w, fmaf(xv.w * rstd[b], g.w, be.w), t);
+                }
+        }
+    } else {
+        for (int k = lane; k < d; k += 32) {
+            const float wk = w[k], g = p.ln_w[k], be = p.ln_b[k];
+#pragma unroll
+            for (int b = 0; b < kFrameMaxRows; ++b)
+                if (b < B) acc[b] = fmaf(wk, fmaf(sx[b * d + k] * rstd[b], g, be), acc[b]);
+        }
     }
 #pragma unroll
     for (int b = 0; b < kFrameMaxRows; ++b) {
@@ -175,11 +200,27 @@ __global__ void __launch_bounds__(kFT) frame_out_k(OutArgs a) {
         float dot[kFrameMaxRows];
 #pragma unroll
         for (int b = 0; b < kFrameMaxRows; ++b) dot[b] = 0.f;
-        for (int k = lane; k < p.H; k += 32) {
-            const float wk = w[k];
+        if ((p.H & 3) == 0 && ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(p.y)) & 15u) == 0) {
+            // 16-byte loads, several in flight per lane (the weights stream from L2)
+            const float4* w4 = reinterpret_cast<const float4*>(w);
+            const int H4 = p.H >> 2;
+#pragma unroll 4
+            for (int k = lane; k < H4; k += 32) {
+                const float4 wk = w4[k];
 #pragma unroll
-            for (int b = 0; b < kFrameMaxRows; ++b)
-                if (b < B) dot[b] = fmaf(wk, p.y[static_cast<size_t>(b) * p.H + k], dot[b]);
+                for (int b = 0; b < kFrameMaxRows; ++b)
+                    if (b < B) {
+                        const float4 yv = reinterpret_cast<const float4*>(p.y + static_cast<size_t>(b) * p.H)[k];
+                        dot[b] = fmaf(wk.x, yv.x, fmaf(wk.y, yv.y, fmaf(wk.z, yv.z, fmaf(wk.w, yv.w, dot[b]))));
+                    }
+            }
+        } else {
+            for (int k = lane; k < p.H; k += 32) {
+                const float wk = w[k];
+#pragma unroll
+                for (int b = 0; b < kFrameMaxRows; ++b)
+                    if (b < B) dot[b] = fmaf(wk, p.y[static_cast<size_t>(b) * p.H + k], dot[b]);
+            }
         }
 #pragma unroll
         for (int b = 0; b < kFrameMaxRows; ++b) {

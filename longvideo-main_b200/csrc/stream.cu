@@ -17,6 +17,8 @@
 // One CTA per row runs the chunk's K steps in order (K = 1 is temporal_step);
 // state in and state out are separate buffers, so a caller may replay a step
 // from the same state.
+#include <cooperative_groups.h>
+
 #include <algorithm>
 
 #include "eacs_common.cuh"
@@ -231,9 +233,203 @@ __global__ void __launch_bounds__(kST) stream_chunk(StArgs a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// One step (K = 1) with a row spread over a cluster of kSCL CTAs: CTA r owns
+// channels [r*HC, (r+1)*HC).  Same semantics as stream_chunk; the row's two
+// residual sums are added over the cluster through distributed shared memory
+// (one hardware cluster barrier before the CTAs read one another's partials,
+// one after, so that no CTA leaves while its partial may still be read), in
+// rank order in every CTA, so all take the same gate decision.  State in and
+// state out are separate buffers; nothing is copied in place.
+// ---------------------------------------------------------------------------
+constexpr int kSCL = 8;     // CTAs a row
+constexpr int kSCT = 256;   // threads a CTA
+
+template <int LANES, int NPT, typename UT>
+__global__ void __cluster_dims__(kSCL, 1, 1) __launch_bounds__(kSCT) stream_step_cl(StArgs a) {
+    namespace cg = cooperative_groups;
+    constexpr int HG = kSCT / LANES;
+    constexpr int NP = LANES * NPT;
+    __shared__ float2 sBp[NP], sCp[NP];
+    __shared__ float2 sred[kSCT / 32];
+    __shared__ float2 spart;
+    __shared__ float sg;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = static_cast<int>(cluster.block_rank());
+    const int b = blockIdx.y;
+    const int tid = threadIdx.x, ln = tid % LANES, hg = tid / LANES;
+    const int lane = tid & 31, wid = tid >> 5;
+    const int H = a.H, N = a.N;
+    const int HC = (H + kSCL - 1) / kSCL;
+    const int c0 = rank * HC, c1 = min(H, c0 + HC);
+    const UT* u = static_cast<const UT*>(a.u);
+    const size_t HN = static_cast<size_t>(H) * N;
+    const size_t bH = static_cast<size_t>(b) * H;
+    const bool v = a.valid ? a.valid[b] != 0 : true;
+    if (!v) {  // masked row (the whole cluster): state through, zero outputs
+        for (size_t i = static_cast<size_t>(c0) * N + tid; i < static_cast<size_t>(c1) * N; i += kSCT)
+            a.h_out[b * HN + i] = a.h_in[b * HN + i];
+        for (int h = c0 + tid; h < c1; h += kSCT) {
+            a.u_out[bH + h] = a.u_in[bH + h];
+            a.y[bH + h] = 0.f;
+        }
+        if (rank == 0) {
+            for (int n = tid; n < N; n += kSCT) {
+                a.B_out[static_cast<size_t>(b) * N + n] = a.B_in[static_cast<size_t>(b) * N + n];
+                a.C_out[static_cast<size_t>(b) * N + n] = a.C_in[static_cast<size_t>(b) * N + n];
+            }
+            if (tid == 0) {
+                a.t_out[b] = a.t_in[b];
+                a.init_out[b] = a.init_in[b] ? 1 : 0;
+                a.gate[b] = a.resid[b] = a.innov[b] = 0.f;
+            }
+        }
+        return;
+    }
+    const bool init = a.init_in[b] != 0;
+    const bool first = !init;
+    const float tl = a.t[b];
+    const float t_pi = first ? tl - a.dt_init : a.t_in[b];
+    for (int n = tid; n < NP; n += kSCT) {
+        const size_t o = static_cast<size_t>(b) * N + n;
+        sBp[n] = n < N ? (first ? a.Bc[o] : a.B_in[o]) : make_float2(0.f, 0.f);
+        sCp[n] = n < N ? (first ? a.Cc[o] : a.C_in[o]) : make_float2(0.f, 0.f);
+    }
+    __syncthreads();
+    const float delta = fmaxf(tl - t_pi, 0.f);
+    auto upi_of = [&](int h) { return first ? to_f32(u[bH + h]) : a.u_in[bH + h]; };
+    // prediction and this CTA's share of the residual sums
+    float acc1 = 0.f, acc2 = 0.f;
+    for (int h0 = c0; h0 < c1; h0 += HG) {
+        const int h = h0 + hg;
+        const bool hv = h < c1;
+        float yhp = 0.f, dte = 0.f, upv = 0.f;
+        if (hv) {
+            dte = eff_dt(delta, expf(a.log_dt[h]), a.dt_min, a.dt_max);
+            upv = upi_of(h);
+        }
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            if (hv && n < N) {
+                const float2 lm = a.lam[static_cast<size_t>(h) * N + n];
+                float2 dA, dB;
+                zoh(lm, crecip(lm), dte, dA, dB);
+                const float2 P = cmul(dA, a.h_in[b * HN + static_cast<size_t>(h) * N + n]);
+                const float2 q = cmul(dB, sBp[n]);
+                const float2 xh = make_float2(fmaf(q.x, upv, P.x), fmaf(q.y, upv, P.y));
+                yhp += cre_mul(sCp[n], xh);
+            }
+        }
+#pragma unroll
+        for (int o = LANES / 2; o > 0; o >>= 1) yhp += __shfl_xor_sync(0xffffffffu, yhp, o);
+        if (ln == 0 && hv) {
+            const float sd = sqrtf(a.var[h] + a.var_eps);
+            const float obs = (to_f32(u[bH + h]) - a.mean[h]) / sd;
+            const float pred = (yhp - a.mean[h]) / sd;
+            const float d = obs - pred;
+            acc1 += d * d;
+            acc2 += obs * obs;
+        }
+    }
+    acc1 = warp_sum(acc1);
+    acc2 = warp_sum(acc2);
+    if (lane == 0) sred[wid] = make_float2(acc1, acc2);
+    __syncthreads();
+    if (tid == 0) {
+        float s1 = 0.f, s2 = 0.f;
+        for (int w = 0; w < kSCT / 32; ++w) {
+            s1 += sred[w].x;
+            s2 += sred[w].y;
+        }
+        spart = make_float2(s1, s2);
+    }
+    cluster.sync();  // every CTA's partial is in place
+    if (tid == 0) {
+        float s1 = 0.f, s2 = 0.f;
+        for (int r = 0; r < kSCL; ++r) {
+            const float2 p = *cluster.map_shared_rank(&spart, r);
+            s1 += p.x;
+            s2 += p.y;
+        }
+        const float r = sqrtf(s1) / (sqrtf(s2) + a.eta);
+        float eps_l = first ? -1.f : a.eps;
+        if (a.cpi && a.cpi_mod > 0.f)
+            eps_l = fmaxf(eps_l * (1.f - a.cpi_mod * fminf(fmaxf(a.cpi[b], 0.f), 1.f)), 1e-3f);
+        const float g = a.gate_mode == 1 ? 1.0f / (1.0f + expf(-((r - eps_l) / a.Tp))) : (r > eps_l ? 1.f : 0.f);
+        sg = g;
+        if (rank == 0) {
+            a.gate[b] = first ? 1.f : g;
+            a.resid[b] = r;
+            a.innov[b] = init ? r : 0.f;
+        }
+    }
+    cluster.sync();  // all partials read: a CTA may now leave; sg is published
+    const float g = sg;
+    // update, blend, readout, state out for this CTA's channels
+    for (int h0 = c0; h0 < c1; h0 += HG) {
+        const int h = h0 + hg;
+        const bool hv = h < c1;
+        float yp = 0.f, dte = 0.f, upv = 0.f, ul = 0.f;
+        if (hv) {
+            dte = eff_dt(delta, expf(a.log_dt[h]), a.dt_min, a.dt_max);
+            upv = upi_of(h);
+            ul = to_f32(u[bH + h]);
+        }
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int n = ln + LANES * j;
+            if (hv && n < N) {
+                const size_t o = static_cast<size_t>(h) * N + n;
+                const float2 lm = a.lam[o];
+                float2 dA, dB;
+                zoh(lm, crecip(lm), dte, dA, dB);
+                const float2 hp = a.h_in[b * HN + o];
+                const float2 P = cmul(dA, hp);
+                const float2 qp = cmul(dB, sBp[n]);
+                const float2 xh = make_float2(fmaf(qp.x, upv, P.x), fmaf(qp.y, upv, P.y));
+                const float2 qc = cmul(dB, a.Bc[static_cast<size_t>(b) * N + n]);
+                const float2 hu = make_float2(fmaf(qc.x, ul, P.x), fmaf(qc.y, ul, P.y));
+                const float2 gu = cscale(hu, g);
+                const float2 hc = cadd(gu, cscale(xh, 1.f - g));
+                a.h_out[b * HN + o] = first ? hc : cadd(gu, cscale(hp, 1.f - g));
+                yp += cre_mul(a.Cc[static_cast<size_t>(b) * N + n], hc);
+            }
+        }
+#pragma unroll
+        for (int o = LANES / 2; o > 0; o >>= 1) yp += __shfl_xor_sync(0xffffffffu, yp, o);
+        if (ln == 0 && hv) {
+            a.y[bH + h] = yp + a.D[h] * ul;
+            a.u_out[bH + h] = first ? ul : g * ul + (1.f - g) * upv;
+        }
+    }
+    if (rank == 0) {
+        for (int n = tid; n < N; n += kSCT) {
+            const size_t o = static_cast<size_t>(b) * N + n;
+            const float2 Bl = a.Bc[o], Cl = a.Cc[o];
+            a.B_out[o] = first ? Bl : cadd(cscale(Bl, g), cscale(sBp[n], 1.f - g));
+            a.C_out[o] = first ? Cl : cadd(cscale(Cl, g), cscale(sCp[n], 1.f - g));
+        }
+        if (tid == 0) {
+            a.t_out[b] = first ? tl : g * tl + (1.f - g) * t_pi;
+            a.init_out[b] = 1;
+        }
+    }
+}
+
 template <typename UT>
 cudaError_t launch_stream(const StArgs& a, cudaStream_t s) {
     const int N = a.N;
+    if (a.K == 1 && a.H >= 128 && a.B <= 65535) {  // one step: a row over a cluster of kSCL CTAs
+        const dim3 grid(kSCL, a.B);
+        if (N <= 4) stream_step_cl<4, 1, UT><<<grid, kSCT, 0, s>>>(a);
+        else if (N <= 8) stream_step_cl<8, 1, UT><<<grid, kSCT, 0, s>>>(a);
+        else if (N <= 16) stream_step_cl<16, 1, UT><<<grid, kSCT, 0, s>>>(a);
+        else if (N <= 32) stream_step_cl<32, 1, UT><<<grid, kSCT, 0, s>>>(a);
+        else stream_step_cl<32, 2, UT><<<grid, kSCT, 0, s>>>(a);
+        note_launch();
+        return cudaGetLastError();
+    }
     // lanes per channel and chains per lane (one pass covers kST / LANES channels)
     if (N <= 4) stream_chunk<4, 1, UT><<<a.B, kST, 0, s>>>(a);
     else if (N <= 8) stream_chunk<8, 1, UT><<<a.B, kST, 0, s>>>(a);
@@ -246,9 +442,9 @@ cudaError_t launch_stream(const StArgs& a, cudaStream_t s) {
 
 // ---------------------------------------------------------------------------
 // Backward of one step (K = 1: temporal_step under autograd), float32 u.
-// Per row, with the step's forward recomputed in the same order as
-// stream_chunk (so the residual, and with it a hard gate, comes out the same;
-// the forward's gate output also pins it), the vector-Jacobian product with
+// Per row, with the step's forward recomputed (one CTA a row, so the residual
+// may differ from the forward's in the last bits; the forward's gate output
+// pins a hard gate), the vector-Jacobian product with
 // respect to the frame (u, B, C, t, cpi), the state in and the parameters,
 // given the upstream gradients of y (before proj_out), the gate output (1 on
 // a first observation), resid, innov and the state out:
@@ -403,7 +599,7 @@ __global__ void __launch_bounds__(kST) stream_step_bwd_k(SbArgs a) {
     const float mdel = draw >= 0.f ? 1.f : 0.f;
     auto u0_of = [&](int h) { return first ? a.u[bH + h] : a.u_in[bH + h]; };
 
-    // ---- pass 1: prediction and residual (stream_chunk's order) ----
+    // ---- pass 1: prediction and residual (one CTA a row) ----
     float acc1 = 0.f, acc2 = 0.f;
     for (int h0 = 0; h0 < H; h0 += HG) {
         const int h = h0 + hg;
