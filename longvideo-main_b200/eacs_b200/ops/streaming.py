@@ -331,12 +331,6 @@ def temporal_step_frame(temporal, x: Tensor, t: Tensor, states: list, valid: Ten
     eacs_stream_frame: S + 3 launches for the whole module (norms, projections,
     cell steps, proj_out, fusion, out_norm).  Same returns as temporal_step."""
     vb = valid.bool()
-    bad = None
-    for state in states:
-        b = vb & state.initialized & (t < state.t)
-        bad = b if bad is None else bad | b
-    if bad is not None and bool(bad.any()):
-        raise ValueError("timestamps must not precede the last committed observation")
     B, d = x.shape
     S = len(temporal.branches)
     dev = x.device
@@ -375,6 +369,15 @@ def temporal_step_frame(temporal, x: Tensor, t: Tensor, states: list, valid: Ten
     nbytes = int(L_.eacs_stream_frame_workspace_size(ctypes.byref(arr), S, B, d))
     require(nbytes > 0, "eacs_stream_frame: unsupported sizes")
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    # the timestamp check (streaming.py:60-61) reads the previous frame's state, so
+    # its host synchronisation comes last: the frame above was prepared while the
+    # previous one still ran on the GPU
+    bad = None
+    for state in states:
+        b = vb & state.initialized & (t < state.t)
+        bad = b if bad is None else bad | b
+    if bad is not None and bool(bad.any()):
+        raise ValueError("timestamps must not precede the last committed observation")
     with torch.cuda.device(dev):
         _lib.check(L_.eacs_stream_frame(
             keep[0].data_ptr(), keep[1].data_ptr(), keep[2].data_ptr(), ptr(keep[3]), ctypes.byref(arr), S,
