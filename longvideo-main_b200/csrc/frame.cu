@@ -13,8 +13,8 @@
 //   2. the cell step of each branch: stream_chunk with K = 1 (stream.cu);
 //   3. frame_out_k: each branch's proj_out, masked by valid, blended with the
 //      softmax of the fusion logits, plus the residual x: one warp per output
-//      feature;
-//   4. frame_ln_k: out_norm and the valid mask, one warp per row.
+//      feature and branch, the blend through shared memory;
+//   4. frame_ln_k: out_norm and the valid mask, one CTA per row.
 // The frame's GEMVs read the weights once (fp32, ~26 MB for config 2's three
 // branches at d = 1024, resident in L2 from frame to frame).
 #include <algorithm>
@@ -170,8 +170,11 @@ struct OutArgs {
     int B, d, S;
 };
 
-__global__ void __launch_bounds__(kFT) frame_out_k(OutArgs a) {
+constexpr int kFOut = 8;  // output features a CTA; one warp per (feature, branch)
+
+__global__ void __launch_bounds__(kFOut * kFrameMaxBranches * 32) frame_out_k(OutArgs a) {
     __shared__ float sw[kFrameMaxRows][kFrameMaxBranches];
+    __shared__ float sdelta[kFOut][kFrameMaxBranches][kFrameMaxRows];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int B = a.B, d = a.d, S = a.S;
     if (threadIdx.x < B) {  // softmax over the branches, one thread a row
@@ -188,13 +191,10 @@ __global__ void __launch_bounds__(kFT) frame_out_k(OutArgs a) {
             if (blockIdx.x == 0) a.weights[b * S + s] = sw[b][s];
         }
     }
-    __syncthreads();
-    const int o = blockIdx.x * kFW + warp;
-    if (o >= d) return;
-    float acc[kFrameMaxRows];
-#pragma unroll
-    for (int b = 0; b < kFrameMaxRows; ++b) acc[b] = 0.f;
-    for (int s = 0; s < S; ++s) {
+    // this warp's (feature, branch): proj_out's dot product for every row
+    const int ol = warp / S, s = warp % S;
+    const int o = blockIdx.x * kFOut + ol;
+    if (o < d) {
         const OutBranch& p = a.br[s];
         const float* w = p.w + static_cast<size_t>(o) * p.H;
         float dot[kFrameMaxRows];
@@ -224,34 +224,49 @@ __global__ void __launch_bounds__(kFT) frame_out_k(OutArgs a) {
         }
 #pragma unroll
         for (int b = 0; b < kFrameMaxRows; ++b) {
-            const float v = warp_sum(dot[b]) + p.b[o];
-            const float m = (a.valid && !a.valid[b < B ? b : 0]) ? 0.f : 1.f;
-            acc[b] += (v * m) * sw[b < B ? b : 0][s];
+            const float v = warp_sum(dot[b]);
+            if (lane == 0 && b < B) sdelta[ol][s][b] = v + p.b[o];
         }
     }
-    if (lane == 0)
-#pragma unroll
-        for (int b = 0; b < kFrameMaxRows; ++b)
-            if (b < B) a.z[static_cast<size_t>(b) * d + o] = a.x[static_cast<size_t>(b) * d + o] + acc[b];
+    __syncthreads();
+    // blend the branches (masked by valid, weighted by the softmax) and add x
+    for (int i = threadIdx.x; i < kFOut * B; i += blockDim.x) {
+        const int l = i / B, b = i % B, oo = blockIdx.x * kFOut + l;
+        if (oo >= d) continue;
+        const float m = (a.valid && !a.valid[b]) ? 0.f : 1.f;
+        float acc = 0.f;
+        for (int t = 0; t < S; ++t) acc += (sdelta[l][t][b] * m) * sw[b][t];
+        a.z[static_cast<size_t>(b) * d + oo] = a.x[static_cast<size_t>(b) * d + oo] + acc;
+    }
 }
 
-// out_norm and the valid mask: one warp a row
+// out_norm and the valid mask: one CTA a row
 __global__ void __launch_bounds__(kFT) frame_ln_k(const float* z, const uint8_t* valid, const float* g,
                                                    const float* be, float eps, float* y, int B, int d) {
-    const int b = blockIdx.x * kFW + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (b >= B) return;
+    __shared__ float sred[kFW];
+    const int b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float* zr = z + static_cast<size_t>(b) * d;
+    auto cta_sum = [&](float v) {  // every thread gets the sum, in a fixed order
+        v = warp_sum(v);
+        if (lane == 0) sred[warp] = v;
+        __syncthreads();
+        float t = 0.f;
+        for (int w = 0; w < kFW; ++w) t += sred[w];
+        __syncthreads();
+        return t;
+    };
     float s = 0.f;
-    for (int k = lane; k < d; k += 32) s += zr[k];
-    const float mean = warp_sum(s) / d;
+    for (int k = threadIdx.x; k < d; k += kFT) s += zr[k];
+    const float mean = cta_sum(s) / d;
     float v = 0.f;
-    for (int k = lane; k < d; k += 32) {
+    for (int k = threadIdx.x; k < d; k += kFT) {
         const float c = zr[k] - mean;
         v += c * c;
     }
-    const float rstd = 1.0f / sqrtf(warp_sum(v) / d + eps);
+    const float rstd = 1.0f / sqrtf(cta_sum(v) / d + eps);
     const float m = (valid && !valid[b]) ? 0.f : 1.f;
-    for (int k = lane; k < d; k += 32) y[static_cast<size_t>(b) * d + k] = fmaf((zr[k] - mean) * rstd, g[k], be[k]) * m;
+    for (int k = threadIdx.x; k < d; k += kFT)
+        y[static_cast<size_t>(b) * d + k] = fmaf((zr[k] - mean) * rstd, g[k], be[k]) * m;
 }
 
 size_t alf(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -375,12 +390,12 @@ int stream_frame(const FrameCall& c, cudaStream_t stream) {
     oa.d = d;
     oa.S = S;
     for (int s = 0; s < S; ++s) oa.br[s] = OutBranch{c.br[s].wo, c.br[s].bo, yb[s], c.br[s].H};
-    frame_out_k<<<(d + kFW - 1) / kFW, kFT, 0, stream>>>(oa);
+    frame_out_k<<<(d + kFOut - 1) / kFOut, kFOut * S * 32, 0, stream>>>(oa);
     note_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_check(e, fn);
 
     // 4. out_norm
-    frame_ln_k<<<(B + kFW - 1) / kFW, kFT, 0, stream>>>(z, c.valid, c.out_w, c.out_b, c.out_eps, c.y, B, d);
+    frame_ln_k<<<B, kFT, 0, stream>>>(z, c.valid, c.out_w, c.out_b, c.out_eps, c.y, B, d);
     note_launch();
     return cuda_check(cudaGetLastError(), fn);
 }
